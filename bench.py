@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark: MoE-layer decode tokens/s and MXFP4 matvec HBM GB/s on B200.
+
+Workload: one MoE layer at decode -- 384 routed + 1 shared
+MXFP4 expert (hidden 7168, intermediate 2048), bf16 router [384, 7168] ~ N(0, 0.02),
+sigmoid top-8, renormalised weights x 2.5 -- on M tokens (default 8) of bf16 x ~ N(0, 1).
+Synthetic data with random-init weights of that architecture (seeded). A step is one
+layer forward through ``LatentMoE.__call__`` (router + every routed expert + the shared
+expert + weighted scatter-add).
+
+    python bench.py [--gpus N --steps K --warmup W --tokens M] [--impl reference]
+
+Timing: ``value`` replays one CUDA graph per token batch with inputs resident in HBM,
+bracketed by CUDA events; every step uses a fresh token batch so it reads a fresh set of
+experts out of a 9 GB pool (inputs larger than L2). ``e2e`` times the public API call on
+pinned host tensors with the host->device copy of x and the device->host copy of y inside
+the timed region. ``roofline`` covers the dominant kernel (the grouped gate/up matvec),
+timed per launch with CUDA events on its launch stream in a second pass. Multi-GPU runs
+are weak-scaled replicas (each rank its own tokens and a full copy of the layer); the
+time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+H, I_, E, TOPK, SCALE = 7168, 2048, 384, 8, 2.5
+PROJ_BYTES = I_ * H // 2 + I_ * H // 32                   # 7,798,784 B per MXFP4 projection
+EXPERT_BYTES = 3 * PROJ_BYTES                              # 23,396,352 B
+ROUTER_BYTES = E * H * 2
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ distributed
+
+def dist_init(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def dist_max(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ----------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU every 200 ms while the timed region runs."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, local_rank: int):
+        import torch
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={uuid}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------- CPU baseline (oracle)
+
+def cpu_baseline(M: int, seed: int, steps: int, budget_s: float = 20.0):
+    """The reference path restated on the host cores (oracle port): fp32 router in numpy,
+    then the reference fused kernel's loop in C (OpenMP over rows) for every expert the
+    step routes to, plus the shared expert. Weights are a pool of 8 synthetic experts
+    reused by id (the work per expert does not depend on the values); at most
+    ``budget_s`` of expert compute is spent and the step time is extrapolated to all
+    U + 1 experts. Returns (tokens/s, cores, sample description)."""
+    from oracle import mxfp4_oracle as O
+    rng = np.random.default_rng(seed)
+    gate = O.bf16_bits_to_f32(O.f32_to_bf16_bits((rng.standard_normal((E, H)) * 0.02).astype(np.float32)))
+    pool = [(O.random_mxfp4(rng, I_, H), O.random_mxfp4(rng, I_, H), O.random_mxfp4(rng, H, I_))
+            for _ in range(8)]
+    t_route, t_exp, n_exp, n_steps, U_tot = 0.0, 0.0, 0, 0, 0
+    spent = 0.0
+    for s in range(max(1, steps)):
+        x = O.bf16_bits_to_f32(O.f32_to_bf16_bits(rng.standard_normal((M, H)).astype(np.float32)))
+        t0 = time.perf_counter()
+        r = O.route(x, gate, None, TOPK, True, SCALE)
+        t_route += time.perf_counter() - t0
+        experts = sorted(set(r.expert_indices.reshape(-1).tolist()))
+        U_tot += len(experts) + 1
+        n_steps += 1
+        for j, e in enumerate(experts + [-1]):
+            tok = np.arange(M) if e < 0 else np.nonzero(r.expert_indices == e)[0]
+            (p1, s1), (p3, s3), (p2, s2) = pool[j % len(pool)]
+            t0 = time.perf_counter()
+            g = O.matvec_fused(x[tok], p1, s1)
+            u = O.matvec_fused(x[tok], p3, s3)
+            O.matvec_fused(O.silu(g) * u, p2, s2)
+            dt = time.perf_counter() - t0
+            t_exp += dt
+            spent += dt
+            n_exp += 1
+            if spent > budget_s:
+                break
+        if spent > budget_s:
+            break
+    per_step = t_route / n_steps + (U_tot / n_steps) * (t_exp / n_exp)
+    sample = (f"{n_steps} decode step(s) of M={M}: numpy fp32 router + C port of the reference "
+              f"fused-kernel loop over {n_exp} expert FFNs (of {U_tot} routed+shared); step time = "
+              f"router + (U+1) x mean expert time")
+    return M / per_step, O.oracle_threads(), sample
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path (oracle port) on this box's host cores."""
+    if rank != 0:
+        return
+    M = args.tokens
+    t0 = time.perf_counter()
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, cores, sample = cpu_baseline(M, args.seed + i, 1, budget_s=4.0)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals) if vals else 0.0
+    line = {
+        "impl": "reference", "metric": "moe_layer_decode_tokens_per_s", "value": value,
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * M / value if value else None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"BASELINE configs[2]: MoE layer decode, M={M}, 384+1 MXFP4 experts "
+                               "7168/2048, top-8", "tokens": M},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": time.perf_counter() - t0,
+    }
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------------ B200 arm
+
+def traffic_from_profiles():
+    """Per-launch DRAM bytes of the gate/up kernel from the committed ncu summary."""
+    f = ROOT / "profiles" / "gemv_gateup_config2.md"
+    if not f.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch_full:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+def run_b200(args, rank, world, local):
+    import torch
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+
+    torch.cuda.set_device(local)
+    M, K, W = args.tokens, args.steps, args.warmup
+    nb = K + W
+    lay = synthetic.baseline_layer(seed=args.seed, E=E, H=H, I=I_, top_k=TOPK, scale=SCALE)
+    moe = lay.moe()
+    _ = moe.pool
+    xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, M, H) for i in range(nb)]
+    U = []
+    for x in xs:
+        U.append(int(torch.unique(moe.route(x).expert_indices).numel()))
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing: one CUDA graph per token batch
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        for i in range(2):
+            moe(xs[i])
+    torch.cuda.synchronize()
+    graphs, ys = [], []
+    for i in range(nb):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            ys.append(moe(xs[i]))
+        graphs.append(g)
+    for i in range(W):
+        graphs[i].replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = ClockSampler(local)
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    for i in range(W, nb):
+        graphs[i].replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    barrier(world)
+    ms = dist_max(ev0.elapsed_time(ev1) / K, world)
+    value = world * M / (ms / 1e3)
+
+    # ---- per-kernel timing of the same steps (eager launches, events per kernel)
+    L.profile_enable(True)
+    L.profile_collect()
+    torch.cuda.synchronize()
+    for i in range(W, nb):
+        moe(xs[i])
+    torch.cuda.synchronize()
+    prof = L.profile_collect()
+    L.profile_enable(False)
+    gu_ms, gu_n = prof["gateup"]
+    dn_ms, dn_n = prof["down"]
+    U_t = U[W:]
+    gu_bytes = np.mean([(u + 1) * 2 * PROJ_BYTES for u in U_t]) + M * H * 2
+    dn_bytes = np.mean([(u + 1) * PROJ_BYTES for u in U_t])
+    layer_bytes = np.mean([(u + 1) * EXPERT_BYTES for u in U_t]) + ROUTER_BYTES
+    peak, peak_kind = measured_peaks()
+    gu_gbs = gu_bytes / (gu_ms / gu_n / 1e3) / 1e9
+    dn_gbs = dn_bytes / (dn_ms / dn_n / 1e3) / 1e9
+
+    # ---- end to end through the public API with host buffers
+    xh = torch.stack([x.cpu() for x in xs]).pin_memory()
+    yh = torch.empty((M, H), dtype=torch.float32).pin_memory()
+    xd = torch.empty((M, H), dtype=torch.bfloat16, device="cuda")
+    for i in range(W):
+        xd.copy_(xh[i], non_blocking=True)
+        yh.copy_(moe(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(W, nb):
+        xd.copy_(xh[i], non_blocking=True)
+        yh.copy_(moe(xd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = dist_max(e0.elapsed_time(e1) / K, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline(M, args.seed, 2)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+
+    for g in graphs:
+        g.reset()
+    if rank != 0:
+        return
+    line = {
+        "metric": "moe_layer_decode_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1+f16 mma, f32 accumulate",
+        "data": "synthetic (seeded random-init weights of the BASELINE layer)",
+        "config": {"workload": f"BASELINE configs[2]: one MoE layer decode, M={M} tokens per GPU, "
+                               "384 routed + 1 shared MXFP4 expert (7168/2048), bf16 router, "
+                               "top-8, x2.5",
+                   "tokens_per_gpu": M, "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2: 9.0 GB expert pool, fresh token batch per step",
+                   "timing": "CUDA graph per batch, events around K replays"},
+        "unique_experts_mean": float(np.mean(U_t)),
+        "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<gate/up> (grouped MXFP4 matvec)",
+                     "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
+                     "peak_kind": peak_kind, "traffic": traffic_from_profiles(),
+                     "algorithmic_bytes_per_launch": gu_bytes,
+                     "launch_ms": gu_ms / gu_n},
+        "down_kernel": {"achieved": dn_gbs, "frac": dn_gbs / peak, "launch_ms": dn_ms / dn_n},
+        "kernel_ms_per_step": {k: v[0] / K for k, v in prof.items() if v[1]},
+        "e2e": {"value": world * M / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
+                "ms_per_step": e2e_ms, "api": "LatentMoE.__call__ (k3_moe_decode)"},
+        "gpu_launches": 4 * K,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_init(args)
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_b200(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,173 @@
+/*
+ * k3b200 -- C ABI of the B200 (sm_100a) MXFP4 quantized-expert path.
+ *
+ * Drop-in for the hot path of sjdthree/kimi-k3-mlx-macmini: the fused MXFP4
+ * dequant-matvec that runs every routed and shared expert projection, the sigmoid
+ * top-k router, and the token->expert gather / weighted scatter-add around them.
+ *
+ * Conventions (every entry point):
+ *  - Returns 0 (K3_OK) or a K3_ERR_* code; never aborts. k3_last_error() gives the
+ *    message of the calling thread's last failure.
+ *  - Tensor arguments are DEVICE pointers, row-major and contiguous, unless noted.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream); all work is enqueued
+ *    on it, nothing blocks the host.
+ *  - Scratch ("workspace") is caller-owned device memory of at least the size the
+ *    matching *_workspace() function returns, 256-byte aligned. Its contents need no
+ *    initialisation and are not preserved between calls; calls that share one
+ *    workspace must not overlap on the GPU.
+ *
+ * MXFP4 layout (the reference's, air_llm/models/kimi_k3/mxfp4.py:3-12): packed u8
+ * [rows][cols/2], low nibble = even element; code bit 3 = sign, bits 0-2 index
+ * {0,.5,1,1.5,2,3,4,6}; scales u8 [rows][cols/32], E8M0 value 2**(byte-127).
+ */
+#ifndef K3B200_H
+#define K3B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define K3_API __attribute__((visibility("default")))
+#else
+#define K3_API
+#endif
+
+enum {
+    K3_OK = 0,
+    K3_ERR_INVALID = 1,      /* bad argument: shape, dtype, NULL pointer (reference: ValueError) */
+    K3_ERR_UNSUPPORTED = 2,  /* valid request outside what this build implements */
+    K3_ERR_CUDA = 3,         /* a CUDA runtime call failed */
+    K3_ERR_WORKSPACE = 4,    /* workspace missing, too small or misaligned */
+    K3_ERR_TIMEOUT = 5       /* a bounded device-side wait gave up */
+};
+
+enum { K3_F32 = 0, K3_BF16 = 1, K3_F16 = 2 };             /* element types */
+enum { K3_ACT_SILU = 0, K3_ACT_SITU = 1 };                 /* expert activation */
+
+K3_API int k3_abi_version(void);
+K3_API const char* k3_last_error(void);
+/* Number of streaming multiprocessors of the current device (grid sizing / tests). */
+K3_API int k3_device_sms(void);
+
+/* Kernel timing diagnostics (no counterpart in the reference, which times with wall
+ * clocks around mx.eval -- tools/profile_compute.py:26-33). While enabled, every kernel
+ * launch of this library is bracketed by CUDA events on its launch stream;
+ * k3_profile_collect waits for them and returns, per kernel kind, the summed device
+ * milliseconds and the launch count since the previous collect. */
+enum {
+    K3_PROF_ROUTER = 0,      /* router logits GEMV                                */
+    K3_PROF_TOPK = 1,        /* top-k / routing plan / activation conversion      */
+    K3_PROF_GATEUP = 2,      /* grouped MXFP4 matvec: gate+up projections + act   */
+    K3_PROF_DOWN = 3,        /* grouped MXFP4 matvec: down projection + combine   */
+    K3_PROF_MATVEC = 4,      /* single-matrix MXFP4 matvec                        */
+    K3_PROF_OTHER = 5,       /* codec and generic kernels                         */
+    K3_PROF_KINDS = 6
+};
+K3_API int k3_profile_enable(int on);
+K3_API int k3_profile_collect(double* ms_out, int64_t* launches_out, int n);
+
+/* ------------------------------------------------------------------ codec ----- */
+
+/* Full dequantisation, bit-exact: out[r][c] = E2M1(code) * 2**(scale-127) as f32 or
+ * bf16 (lossless for scale bytes 1..254 -- air_llm/models/kimi_k3/mxfp4.py:8-10).
+ * Replaces decode_mxfp4_reference (air_llm/models/kimi_k3/mxfp4.py:26-36), the
+ * k3ref decoder (k3ref/weights.py:29-37) and decode_mxfp4_mlx (mxfp4.py:68-81).
+ * group_size must be 32. */
+K3_API int k3_mxfp4_dequant(const uint8_t* packed, const uint8_t* scales, int64_t rows,
+                            int64_t cols, int group_size, void* out, int out_dtype,
+                            void* stream);
+
+/* minmax_out (device int32[2]) <- {min, max} of n scale bytes. The reduction half of
+ * assert_scales_representable (air_llm/models/kimi_k3/mxfp4.py:58-65); the caller
+ * applies the 2..252 rule. */
+K3_API int k3_mxfp4_scale_minmax(const uint8_t* scales, int64_t n, int32_t* minmax_out,
+                                 void* stream);
+
+/* ------------------------------------------------------------- fused matvec --- */
+
+/* out[M][N] = x[M][K] . dequant(packed[N][K/2], scales[N][K/32])^T with fp32
+ * accumulation; x is f32 or bf16, out f32 or bf16. Any M >= 1; K a multiple of 32.
+ * Replaces mxfp4_matvec_fused (air_llm/kernels/metal/mxfp4_matvec.py:75-96) and its
+ * MSL kernel (:29-63); K mismatch is the caller's ValueError (:85-86). */
+K3_API size_t k3_mxfp4_matvec_workspace(int64_t M, int64_t K, int64_t N);
+K3_API int k3_mxfp4_matvec(const void* x, int x_dtype, int64_t M, int64_t K,
+                           const uint8_t* packed, const uint8_t* scales, int64_t N,
+                           void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* ------------------------------------------------------------------- router --- */
+
+/* Sigmoid top-k router of LatentMoE.route (air_llm/models/kimi_k3/moe.py:65-76;
+ * oracle k3ref/layers.py:214-224): logits = x_f32 . W_g^T (fp32), raw = sigmoid,
+ * corrected = raw + bias (selection only), idx = top-k(corrected) in descending order
+ * (ties: lower index), w = raw[idx], renormalised by sum + 1e-20 when top_k > 1 and
+ * renormalize != 0, times routed_scaling_factor.
+ * x [M][H] f32|bf16; gate_w bf16 bits [E][H]; bias f32 [E] or NULL (zeros);
+ * idx_out int32 [M][top_k]; weight_out f32 [M][top_k]; raw/corrected f32 [M][E] or
+ * NULL. Limits: E <= 1024, 1 <= top_k <= 32, H % 8 == 0. */
+K3_API size_t k3_moe_route_workspace(int64_t M, int64_t E);
+K3_API int k3_moe_route(const void* x, int x_dtype, int64_t M, int64_t H,
+                        const uint16_t* gate_w_bf16, const float* bias, int64_t E, int top_k,
+                        int renormalize, float routed_scaling_factor, int32_t* idx_out,
+                        float* weight_out, float* raw_out, float* corrected_out,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------ MoE experts ----- */
+
+/* One expert's three MXFP4 projections (device pointers), as expert_source returns
+ * them (air_llm/models/kimi_k3/moe.py:79-88, loader.py:229-266): w1 = gate [I][H],
+ * w3 = up [I][H], w2 = down [H][I]; each packed [rows][cols/2] + scales [rows][cols/32]. */
+typedef struct k3_expert_ptrs {
+    const uint8_t* w1_packed;
+    const uint8_t* w1_scales;
+    const uint8_t* w3_packed;
+    const uint8_t* w3_scales;
+    const uint8_t* w2_packed;
+    const uint8_t* w2_scales;
+} k3_expert_ptrs;
+
+/* Static description of one MoE layer's expert set (host struct). */
+typedef struct k3_moe_params {
+    int64_t hidden;               /* H: w1/w3 input dim, w2 output dim               */
+    int64_t inter;                /* I: expert intermediate size                     */
+    int64_t num_experts;          /* E routed experts                                */
+    int32_t top_k;                /* routed experts per token                        */
+    int32_t renormalize;          /* moe_renormalize                                 */
+    float routed_scaling_factor;
+    int32_t has_shared;           /* 1: experts[E] is an MXFP4 shared expert applied
+                                     to every token with weight 1                    */
+    int32_t activation;           /* K3_ACT_SILU (silu(g)*u) or K3_ACT_SITU           */
+    float situ_beta;              /* situ only (air_llm/models/kimi_k3/ops.py:17-28)  */
+    float situ_linear_beta;       /* situ only; <= 0 means None                      */
+    const k3_expert_ptrs* experts;/* DEVICE array [E + has_shared]                   */
+} k3_moe_params;
+
+/* Decode (M <= 8 tokens) MoE block without the latent wrapper: route, then for every
+ * routed expert y[t] += w[t,slot] * act(x W1^T, x W3^T) W2^T, summed in ascending
+ * expert id, plus the shared expert. Replaces LatentMoE.__call__'s route + expert loop
+ * + shared expert (air_llm/models/kimi_k3/moe.py:110-132; oracle k3ref/layers.py:
+ * 241-261) for the BASELINE layer. y [M][H] f32|bf16; idx_out/weight_out as in
+ * k3_moe_route (may be NULL). Limits: M <= 8, H % 128 == 0, I % 128 == 0, E <= 1024,
+ * top_k <= 16. */
+K3_API size_t k3_moe_decode_workspace(const k3_moe_params* p, int64_t M);
+K3_API int k3_moe_decode(const k3_moe_params* p, const void* x, int x_dtype, int64_t M,
+                         const uint16_t* gate_w_bf16, const float* bias, void* y_out,
+                         int y_dtype, int32_t* idx_out, float* weight_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Same expert computation with routing supplied (idx int32 [M][top_k], w f32
+ * [M][top_k], e.g. from k3_moe_route): the expert loop of moe.py:115-127 + shared
+ * expert (:131) alone. The input x here is the expert input h (latent or hidden). */
+K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* x, int x_dtype, int64_t M,
+                                 const int32_t* idx, const float* w, void* y_out, int y_dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* K3B200_H */

@@ -1,0 +1,977 @@
+// Decode path: router, routing plan, and the MXFP4 grouped matvec (sm_100a).
+//
+// Work decomposition. A warp-item is 64 weight rows (four m16 tiles) x one k-chunk of
+// one expert projection. Each warp streams its items through a private 3-stage
+// cp.async ring in shared memory (64 packed bytes = 128 k per row per stage),
+// reads the tiles with ldmatrix so that the four lanes of a quad hold the same
+// 32-element scale group, converts E2M1 -> f16 in hardware, and issues
+// mma.m16n8k16 with the tokens (<= 8) as the n8 dimension. Every 32-element group
+// is accumulated into a temporary and added to the fp32 accumulator with its exact
+// scale 2**(s-127) * 2**e_col (E8M0 weight scale times the power-of-two scale of the
+// activation piece), so weights are never rounded and activations keep ~22 bits.
+// Partial sums of k-chunks meet in global scratch; the last warp to finish a row
+// block (atomic counter) reduces them in a fixed order, so results are deterministic.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "k3_moe.cuh"
+
+namespace k3 {
+
+// ================================================================== router
+
+// logits[m][e] = sum_k x[m][k] * W[e][k] for m < Mc (<= 8): one warp per expert row,
+// lanes walk 8-element chunks, fp32 fma in chunk order, then a xor-tree reduction.
+template <int XDT>
+__global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, int Mc,
+                                                            int64_t H,
+                                                            const uint16_t* __restrict__ W,
+                                                            int64_t E, float* __restrict__ logits) {
+    const int64_t e = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (e >= E) return;
+    const uint16_t* wr = W + e * H;
+    float acc[kMaxTok];
+#pragma unroll
+    for (int m = 0; m < kMaxTok; ++m) acc[m] = 0.0f;
+    for (int64_t k = int64_t(lane) * 8; k < H; k += 256) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + k));
+        float wf[8];
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            wf[2 * j] = __uint_as_float(ww[j] << 16);
+            wf[2 * j + 1] = __uint_as_float(ww[j] & 0xffff0000u);
+        }
+#pragma unroll
+        for (int m = 0; m < kMaxTok; ++m) {
+            if (m < Mc) {
+                float xf[8];
+                if (XDT == K3_BF16) {
+                    const uint4 xv = __ldg(reinterpret_cast<const uint4*>(
+                        reinterpret_cast<const uint16_t*>(x) + m * H + k));
+                    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        xf[2 * j] = __uint_as_float(xw[j] << 16);
+                        xf[2 * j + 1] = __uint_as_float(xw[j] & 0xffff0000u);
+                    }
+                } else {
+                    const float4* xp =
+                        reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + m * H + k);
+                    const float4 a = __ldg(xp), b = __ldg(xp + 1);
+                    xf[0] = a.x; xf[1] = a.y; xf[2] = a.z; xf[3] = a.w;
+                    xf[4] = b.x; xf[5] = b.y; xf[6] = b.z; xf[7] = b.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[m] = fmaf(xf[j], wf[j], acc[m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < kMaxTok; ++m) {
+        if (m < Mc) {
+            const float s = warp_sum(acc[m]);
+            if (lane == 0) logits[int64_t(m) * E + e] = s;
+        }
+    }
+}
+
+// Top-k of one token's row by one warp: raw = sigmoid(logit), corrected = raw + bias;
+// k rounds of a warp argmax on (corrected desc, index asc); weights gathered from raw.
+__device__ void topk_row(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
+                         int k, int renorm, float scale, int32_t* __restrict__ idx_out,
+                         float* __restrict__ w_out, float* __restrict__ raw_out,
+                         float* __restrict__ cor_out, int lane, int* status) {
+    float raw[32], cor[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E) {
+            const float l = lrow[e];
+            const float r = 1.0f / (1.0f + expf(-l));
+            const float c = r + (bias ? bias[e] : 0.0f);
+            raw[i] = r;
+            cor[i] = c;
+            if (raw_out) raw_out[e] = r;
+            if (cor_out) cor_out[e] = c;
+        } else {
+            raw[i] = 0.0f;
+            cor[i] = -INFINITY;
+        }
+    }
+    float wsel[kMaxTopK > 32 ? kMaxTopK : 32];
+    int isel[kMaxTopK > 32 ? kMaxTopK : 32];
+    for (int s = 0; s < 32; ++s) {
+        if (s >= k) break;
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && (cor[i] > bv || (cor[i] == bv && e < bi))) {
+                bv = cor[i];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi >= E) {            // only NaN rows get here: report, pick a valid index
+            if (lane == 0) atomicExch(status, K3_ERR_INVALID);
+            bi = 0;
+        }
+        // the owner lane reads the raw score and retires the entry: a NaN never compares
+        // greater or equal, so it cannot win again even when every other entry is -inf
+        float mine = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (lane + 32 * i == bi) {
+                mine = raw[i];
+                cor[i] = __int_as_float(0x7fc00000u);
+            }
+        }
+        wsel[s] = __shfl_sync(0xffffffffu, mine, bi & 31);
+        isel[s] = bi;
+    }
+    // w / (sum + 1e-20) then * scale, as moe.py:74-76 / k3ref/layers.py:221-224
+    float sum = 0.0f;
+    for (int s = 0; s < k; ++s) sum += wsel[s];
+    const float den = sum + 1e-20f;
+    if (lane == 0) {
+        for (int s = 0; s < k; ++s) {
+            idx_out[s] = isel[s];
+            w_out[s] = ((k > 1 && renorm) ? wsel[s] / den : wsel[s]) * scale;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int M, int E,
+                                                   const float* __restrict__ bias, int k, int renorm,
+                                                   float scale, int32_t* __restrict__ idx,
+                                                   float* __restrict__ w, float* __restrict__ raw,
+                                                   float* __restrict__ cor, int* status) {
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (t >= M) return;
+    topk_row(logits + int64_t(t) * E, bias, E, k, renorm, scale, idx + int64_t(t) * k,
+             w + int64_t(t) * k, raw ? raw + int64_t(t) * E : nullptr,
+             cor ? cor + int64_t(t) * E : nullptr, lane, status);
+}
+
+// ==================================================================== prep
+
+struct PrepArgs {
+    // routing (CTA 0)
+    int mode;                      // 0: plan from idx/w; 1: identity plan (matvec)
+    const float* logits;           // non-null: run the top-k first (writes idx/w)
+    const float* bias;
+    int E, k, renorm;
+    float scale;
+    int32_t* idx;
+    float* w;
+    int has_shared;
+    Plan* plan;
+    unsigned* cntA;
+    int64_t n_cntA;
+    unsigned* cntB;
+    int64_t n_cntB;
+    // activation conversion (CTAs >= 1)
+    const void* x;
+    int x_dtype;
+    int M;
+    int64_t K;                     // x row length
+    __half* xq_hi;
+    __half* xq_lo;                 // null when the source is bf16 (hi is exact)
+    float* xq_ts;
+};
+
+__global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (blockIdx.x > 0) {
+        // x[t][k] -> (hi, lo) f16 pieces of x * 2**-e with one exponent per 32-group.
+        const int64_t groups = a.K / 32;
+        const int64_t total = int64_t(a.M) * groups;
+        const int64_t nw = int64_t(gridDim.x - 1) * (blockDim.x >> 5);
+        for (int64_t gw = int64_t(blockIdx.x - 1) * (blockDim.x >> 5) + warp; gw < total; gw += nw) {
+            const int64_t t = gw / groups, g = gw % groups;
+            const int64_t i = t * a.K + g * 32 + lane;
+            const float v = load_as_f32(a.x, a.x_dtype, i);
+            const int e = f16_group_exponent(warp_max(fabsf(v)));
+            __half hi, lo;
+            split_f16(ldexpf(v, -e), hi, lo);
+            a.xq_hi[i] = hi;
+            if (a.xq_lo) a.xq_lo[i] = lo;
+            if (lane == 0) a.xq_ts[t * groups + g] = ldexpf(1.0f, e);
+        }
+        return;
+    }
+    Plan* P = a.plan;
+    __shared__ uint32_t bitmap[kMaxExperts / 32];
+    __shared__ int cnt[kMaxActive];
+    __shared__ int n_routed;
+    if (threadIdx.x == 0) P->status = K3_OK;
+    for (int64_t i = threadIdx.x; i < a.n_cntA; i += blockDim.x) a.cntA[i] = 0;
+    for (int64_t i = threadIdx.x; i < a.n_cntB; i += blockDim.x) a.cntB[i] = 0;
+    if (a.mode == 1) {                             // matvec: one "expert", pairs = tokens
+        if (threadIdx.x == 0) {
+            P->M = a.M;
+            P->n_active = 1;
+            P->n_pairs = a.M;
+            P->expert[0] = 0;
+            P->pair_start[0] = 0;
+            P->pair_start[1] = a.M;
+        }
+        for (int t = threadIdx.x; t < a.M; t += blockDim.x) {
+            P->pair_tok[t] = t;
+            P->pair_w[t] = 1.0f;
+        }
+        return;
+    }
+    __syncthreads();
+    if (a.logits && warp < a.M) {
+        topk_row(a.logits + int64_t(warp) * a.E, a.bias, a.E, a.k, a.renorm, a.scale,
+                 a.idx + warp * a.k, a.w + warp * a.k, nullptr, nullptr, lane, &P->status);
+    }
+    for (int i = threadIdx.x; i < kMaxExperts / 32; i += blockDim.x) bitmap[i] = 0;
+    __syncthreads();                               // top-k results and zeroed bitmap visible
+    const int nsel = a.M * a.k;
+    for (int i = threadIdx.x; i < nsel; i += blockDim.x) {
+        const int e = a.idx[i];
+        if (e < 0 || e >= a.E) {
+            P->status = K3_ERR_INVALID;
+            continue;
+        }
+        atomicOr(&bitmap[e >> 5], 1u << (e & 31));
+    }
+    __syncthreads();
+    if (warp == 0) {                               // ascending unique expert list
+        const uint32_t word = bitmap[lane];
+        const int c = __popc(word);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int pos = incl - c;
+        uint32_t wv = word;
+        while (wv) {
+            const int b = __ffs(wv) - 1;
+            wv &= wv - 1;
+            P->expert[pos++] = lane * 32 + b;
+        }
+        if (lane == 31) n_routed = incl;
+    }
+    __syncthreads();
+    const int nr = n_routed;
+    const int na = nr + (a.has_shared ? 1 : 0);
+    for (int u = threadIdx.x; u < na; u += blockDim.x) {
+        int c = 0;
+        if (u < nr) {
+            const int e = P->expert[u];
+            for (int i = 0; i < nsel; ++i) c += (a.idx[i] == e);
+            if (c > kMaxTok) {          // a token listed the same expert twice: invalid routing
+                P->status = K3_ERR_INVALID;
+                c = kMaxTok;
+            }
+        } else {
+            c = a.M;
+            P->expert[u] = a.E;                    // shared expert slot in the table
+        }
+        cnt[u] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0;
+        for (int u = 0; u < na; ++u) {
+            P->pair_start[u] = s;
+            s += cnt[u];
+        }
+        P->pair_start[na] = s;
+        P->n_active = na;
+        P->n_pairs = s;
+        P->M = a.M;
+    }
+    __syncthreads();
+    for (int u = threadIdx.x; u < na; u += blockDim.x) {
+        int p = P->pair_start[u];
+        if (u < nr) {
+            const int e = P->expert[u];
+            const int pend = P->pair_start[u + 1];
+            for (int t = 0; t < a.M; ++t)
+                for (int s = 0; s < a.k; ++s)
+                    if (a.idx[t * a.k + s] == e && p < pend) {
+                        P->pair_tok[p] = t;
+                        P->pair_w[p] = a.w[t * a.k + s];
+                        ++p;
+                    }
+        } else {
+            for (int t = 0; t < a.M; ++t) {
+                P->pair_tok[p] = t;
+                P->pair_w[p] = 1.0f;
+                ++p;
+            }
+        }
+    }
+}
+
+// ========================================================== grouped matvec
+
+struct GemvArgs {
+    const Plan* plan;
+    const k3_expert_ptrs* table;
+    const uint8_t* mat_packed;     // PROJ over one plain matrix (matvec) instead of w2
+    const uint8_t* mat_scales;
+    int64_t K;                     // reduction length of this phase
+    int64_t rows;                  // rows of one projection (I for gate/up, H or N for PROJ)
+    int C;                         // k-chunks per row block
+    int hilo;                      // B operand carries lo pieces
+    const __half* bh;              // B pieces: row r at bh + r*K
+    const __half* bl;
+    const float* bts;              // B group scales: row r at bts + r*(K/32)
+    float* part;                   // partial sums
+    unsigned* cnt;                 // arrival counters
+    int Pmax;                      // PROJ partial stride (pairs)
+    // GATEUP epilogue
+    __half* act_hi;
+    __half* act_lo;
+    float* act_ts;
+    int act_kind;
+    float beta, lbeta;
+    // PROJ epilogue
+    void* y;
+    int y_dtype;
+};
+
+__device__ __forceinline__ float apply_act(int kind, float g, float u, float beta, float lbeta) {
+    if (kind == K3_ACT_SITU) {
+        const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
+        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
+        return a * v;
+    }
+    return g / (1.0f + expf(-g)) * u;
+}
+
+template <bool GATEUP>
+__global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    Stage* ring = reinterpret_cast<Stage*>(smem_raw + size_t(warp) * kSmemPerWarp);
+    const Plan* P = a.plan;
+    const int n_active = P->n_active;
+    const int64_t nRb = GATEUP ? a.rows / 32 : a.rows / kItemRows;
+    const int64_t n_items = int64_t(n_active) * nRb * a.C;
+    const int64_t wstride = a.K / 2, sstride = a.K / 32;
+    const int64_t kchunk = a.K / a.C;
+    const int nst = int(kchunk / kStageK);
+    const int g = lane >> 2, q = lane & 3;
+    const int64_t total_warps = int64_t(gridDim.x) * kWarps;
+
+    for (int64_t item = int64_t(blockIdx.x) * kWarps + warp; item < n_items; item += total_warps) {
+        const int kc = int(item % a.C);
+        const int64_t rest = item / a.C;
+        const int rb = int(rest % nRb);
+        const int u = int(rest / nRb);
+        const int ps = P->pair_start[u];
+        const int ncols = P->pair_start[u + 1] - ps;
+        const int64_t k0 = int64_t(kc) * kchunk;
+
+        const uint8_t* wp[kTiles];
+        const uint8_t* sp[kTiles];
+        if (GATEUP) {
+            const k3_expert_ptrs ep = a.table[P->expert[u]];
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t) {
+                const int64_t r0 = int64_t(rb) * 32 + (t & 1) * 16;
+                wp[t] = (t < 2 ? ep.w1_packed : ep.w3_packed) + r0 * wstride;
+                sp[t] = (t < 2 ? ep.w1_scales : ep.w3_scales) + r0 * sstride;
+            }
+        } else {
+            const uint8_t* W;
+            const uint8_t* S;
+            if (a.mat_packed) {
+                W = a.mat_packed;
+                S = a.mat_scales;
+            } else {
+                const k3_expert_ptrs ep = a.table[P->expert[u]];
+                W = ep.w2_packed;
+                S = ep.w2_scales;
+            }
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t) {
+                const int64_t r0 = int64_t(rb) * kItemRows + t * 16;
+                wp[t] = W + r0 * wstride;
+                sp[t] = S + r0 * sstride;
+            }
+        }
+        // B rows of this lane's copy chunks: column (lane>>4) + 2i, and ts column lane&7.
+        const __half* bsrc[4];
+        const __half* blsrc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int j = (lane >> 4) + 2 * i;
+            bsrc[i] = nullptr;
+            blsrc[i] = nullptr;
+            if (j < ncols) {
+                const int64_t row = GATEUP ? P->pair_tok[ps + j] : ps + j;
+                bsrc[i] = a.bh + row * a.K + k0 + (lane & 15) * 8;
+                if (a.hilo) blsrc[i] = a.bl + row * a.K + k0 + (lane & 15) * 8;
+            }
+        }
+        const float* tssrc = nullptr;
+        {
+            const int j = lane & 7;
+            if (j < ncols) {
+                const int64_t row = GATEUP ? P->pair_tok[ps + j] : ps + j;
+                tssrc = a.bts + row * sstride + k0 / 32 + (lane >> 3);
+            }
+        }
+
+        auto issue = [&](int s) {
+            Stage& st = ring[s % kStages];
+            const int64_t kb = (k0 + int64_t(s) * kStageK) / 2;     // packed byte offset
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int t = i >> 1, r = (lane >> 2) + 8 * (i & 1), cc = lane & 3;
+                cp_async_16_cg(smem_u32(&st.w[t][r][(cc ^ ((r >> 1) & 3)) * 16]),
+                               wp[t] + r * wstride + kb + cc * 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int c = lane + 32 * i, t = c >> 4, r = c & 15;
+                cp_async_4(smem_u32(&st.s[t][r][0]), sp[t] + r * sstride + kb / 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int j = (lane >> 4) + 2 * i, ch = lane & 15;
+                const int pc = (ch ^ ((j & 1) << 2)) * 8;
+                if (bsrc[i]) cp_async_16_ca(smem_u32(&st.bh[j][pc]), bsrc[i] + s * kStageK);
+                if (blsrc[i]) cp_async_16_ca(smem_u32(&st.bl[j][pc]), blsrc[i] + s * kStageK);
+            }
+            if (tssrc) cp_async_4(smem_u32(&st.ts[lane >> 3][lane & 7]), tssrc + s * (kStageK / 32));
+            else st.ts[lane >> 3][lane & 7] = 0.0f;
+        };
+
+        float acc[kTiles][4];
+#pragma unroll
+        for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[t][i] = 0.0f;
+
+#pragma unroll
+        for (int s = 0; s < kStages - 1; ++s) {
+            if (s < nst) issue(s);
+            cp_async_commit();
+        }
+        for (int s = 0; s < nst; ++s) {
+            if (s + kStages - 1 < nst) issue(s + kStages - 1);
+            cp_async_commit();
+            cp_async_wait<kStages - 1>();
+            __syncwarp();
+            const Stage& st = ring[s % kStages];
+#pragma unroll
+            for (int gp = 0; gp < 2; ++gp) {
+                uint4 X[2], XL[2];
+                float2 tsv[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int G = 2 * gp + h;
+                    const int pc = (((G * 4 + q) ^ ((g & 1) << 2))) * 8;
+                    X[h] = make_uint4(0, 0, 0, 0);
+                    XL[h] = make_uint4(0, 0, 0, 0);
+                    if (g < ncols) {
+                        X[h] = *reinterpret_cast<const uint4*>(&st.bh[g][pc]);
+                        if (a.hilo) XL[h] = *reinterpret_cast<const uint4*>(&st.bl[g][pc]);
+                    }
+                    tsv[h] = *reinterpret_cast<const float2*>(&st.ts[G][2 * q]);
+                }
+#pragma unroll
+                for (int t = 0; t < kTiles; ++t) {
+                    uint32_t R0, R1, R2, R3;
+                    {
+                        const int m = lane >> 3, r = (lane & 7) + 8 * (m & 1), cc = 2 * gp + (m >> 1);
+                        ldmatrix_x4(smem_u32(&st.w[t][r][(cc ^ ((r >> 1) & 3)) * 16]), R0, R1, R2, R3);
+                    }
+                    const uint32_t swg = *reinterpret_cast<const uint32_t*>(&st.s[t][g][0]);
+                    const uint32_t swg8 = *reinterpret_cast<const uint32_t*>(&st.s[t][g + 8][0]);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int G = 2 * gp + h;
+                        uint32_t f0, f1, f2, f3, e0, e1, e2, e3;
+                        e2m1x8_to_f16x8(h ? R2 : R0, f0, f1, f2, f3);
+                        e2m1x8_to_f16x8(h ? R3 : R1, e0, e1, e2, e3);
+                        float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        mma_f16_16816(tmp, f0, e0, f1, e1, X[h].x, X[h].y);
+                        mma_f16_16816(tmp, f2, e2, f3, e3, X[h].z, X[h].w);
+                        if (a.hilo) {
+                            mma_f16_16816(tmp, f0, e0, f1, e1, XL[h].x, XL[h].y);
+                            mma_f16_16816(tmp, f2, e2, f3, e3, XL[h].z, XL[h].w);
+                        }
+                        const float rs0 = e8m0_to_f32((swg >> (8 * G)) & 0xffu);
+                        const float rs1 = e8m0_to_f32((swg8 >> (8 * G)) & 0xffu);
+                        acc[t][0] = fmaf(rs0 * tsv[h].x, tmp[0], acc[t][0]);
+                        acc[t][1] = fmaf(rs0 * tsv[h].y, tmp[1], acc[t][1]);
+                        acc[t][2] = fmaf(rs1 * tsv[h].x, tmp[2], acc[t][2]);
+                        acc[t][3] = fmaf(rs1 * tsv[h].y, tmp[3], acc[t][3]);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+
+        // ---- partial sums to scratch, then the last arrival reduces them
+        unsigned* counter;
+        unsigned target;
+        if (GATEUP) {
+            float* base = a.part + (rest * a.C + kc) * (kMaxTok * kItemRows);
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t) {
+                const int r0 = t * 16 + g, c0 = 2 * q;
+                if (c0 < ncols) {
+                    base[c0 * kItemRows + r0] = acc[t][0];
+                    base[c0 * kItemRows + r0 + 8] = acc[t][2];
+                }
+                if (c0 + 1 < ncols) {
+                    base[(c0 + 1) * kItemRows + r0] = acc[t][1];
+                    base[(c0 + 1) * kItemRows + r0 + 8] = acc[t][3];
+                }
+            }
+            counter = a.cnt + rest;
+            target = unsigned(a.C);
+        } else {
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t) {
+                const int64_t r0 = int64_t(rb) * kItemRows + t * 16 + g;
+                const int c0 = 2 * q;
+                if (c0 < ncols) {
+                    float* b = a.part + (int64_t(kc) * a.Pmax + ps + c0) * a.rows;
+                    b[r0] = acc[t][0];
+                    b[r0 + 8] = acc[t][2];
+                }
+                if (c0 + 1 < ncols) {
+                    float* b = a.part + (int64_t(kc) * a.Pmax + ps + c0 + 1) * a.rows;
+                    b[r0] = acc[t][1];
+                    b[r0 + 8] = acc[t][3];
+                }
+            }
+            counter = a.cnt + rb;
+            target = unsigned(n_active) * unsigned(a.C);
+        }
+        __threadfence();
+        __syncwarp();
+        unsigned old = 0;
+        if (lane == 0) old = atomicAdd(counter, 1u);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old + 1 != target) continue;
+        __threadfence();
+        if (lane == 0) *counter = 0u;                  // ready for the next call
+
+        if (GATEUP) {
+            // lane = act row; gate rows are partial rows 0..31, up rows 32..63
+            const int64_t I = a.rows;
+            for (int j = 0; j < ncols; ++j) {
+                float gs = 0.0f, us = 0.0f;
+                for (int c = 0; c < a.C; ++c) {
+                    const float* base = a.part + (rest * a.C + c) * (kMaxTok * kItemRows) + j * kItemRows;
+                    gs += __ldcg(base + lane);
+                    us += __ldcg(base + 32 + lane);
+                }
+                const int p = ps + j;
+                const float v = apply_act(a.act_kind, gs, us, a.beta, a.lbeta) * P->pair_w[p];
+                const int e = f16_group_exponent(warp_max(fabsf(v)));
+                __half hi, lo;
+                split_f16(ldexpf(v, -e), hi, lo);
+                const int64_t o = int64_t(p) * I + int64_t(rb) * 32 + lane;
+                a.act_hi[o] = hi;
+                a.act_lo[o] = lo;
+                if (lane == 0) a.act_ts[int64_t(p) * (I / 32) + rb] = ldexpf(1.0f, e);
+            }
+        } else {
+            const int np = P->n_pairs, M = P->M;
+            for (int t = 0; t < M; ++t) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int64_t row = int64_t(rb) * kItemRows + lane + 32 * h;
+                    float yv = 0.0f;
+                    for (int p = 0; p < np; ++p) {
+                        if (P->pair_tok[p] != t) continue;
+                        for (int c = 0; c < a.C; ++c)
+                            yv += __ldcg(a.part + (int64_t(c) * a.Pmax + p) * a.rows + row);
+                    }
+                    store_from_f32(a.y, a.y_dtype, int64_t(t) * a.rows + row, yv);
+                }
+            }
+        }
+    }
+}
+
+// ================================================================== host side
+
+namespace {
+
+// Smallest k-split C (a divisor of K/128 leaving >= 2 stages per item) that gives at
+// least `target` items; falls back to the largest allowed split.
+int choose_split(int64_t base_items, int64_t K, int64_t target) {
+    const int64_t nst = K / kStageK;
+    int best = 1;
+    for (int64_t c = 1; c <= nst; ++c) {
+        if (nst % c) continue;
+        if (nst / c < 2 && c > 1) break;
+        best = int(c);
+        if (base_items * c >= target) break;
+    }
+    return best;
+}
+
+bool smem_configured = false;
+int configure_smem() {
+    if (smem_configured) return K3_OK;
+    int rc = cuda_check(cudaFuncSetAttribute(gemv_kernel<true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(kSmemBytes)),
+                        "cudaFuncSetAttribute(gemv gate/up)");
+    if (rc) return rc;
+    rc = cuda_check(cudaFuncSetAttribute(gemv_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         int(kSmemBytes)),
+                    "cudaFuncSetAttribute(gemv proj)");
+    if (rc) return rc;
+    smem_configured = true;
+    return K3_OK;
+}
+
+size_t carve(size_t& off, size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+}
+
+DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
+    DecodeLayout L{};
+    L.M = M;
+    L.H = p.hidden;
+    L.I = p.inter;
+    L.E = p.num_experts;
+    L.U = std::min<int64_t>(p.num_experts, M * p.top_k) + (p.has_shared ? 1 : 0);
+    L.P = M * p.top_k + (p.has_shared ? M : 0);
+    const int64_t target = int64_t(sms) * kWarps * 4;
+    L.CA = choose_split(L.U * (L.I / 32), L.H, target);
+    L.CB = choose_split(L.U * (L.H / kItemRows), L.I, target);
+    size_t off = 0;
+    L.plan = carve(off, sizeof(Plan));
+    L.logits = carve(off, sizeof(float) * M * L.E);
+    L.route_idx = carve(off, sizeof(int32_t) * M * p.top_k);   // when the caller passes NULL
+    L.route_w = carve(off, sizeof(float) * M * p.top_k);
+    L.xq_hi = carve(off, sizeof(__half) * kMaxTok * L.H);
+    L.xq_lo = carve(off, sizeof(__half) * kMaxTok * L.H);
+    L.xq_ts = carve(off, sizeof(float) * kMaxTok * (L.H / 32));
+    L.act_hi = carve(off, sizeof(__half) * L.P * L.I);
+    L.act_lo = carve(off, sizeof(__half) * L.P * L.I);
+    L.act_ts = carve(off, sizeof(float) * L.P * (L.I / 32));
+    L.partA = carve(off, sizeof(float) * L.U * (L.I / 32) * L.CA * kMaxTok * kItemRows);
+    L.cntA = carve(off, sizeof(unsigned) * L.U * (L.I / 32));
+    L.partB = carve(off, sizeof(float) * L.CB * L.P * L.H);
+    L.cntB = carve(off, sizeof(unsigned) * (L.H / kItemRows));
+    L.total = off;
+    return L;
+}
+
+int check_moe_params(const k3_moe_params* p, int64_t M) {
+    if (!p) return fail(K3_ERR_INVALID, "k3_moe_params is NULL");
+    if (M < 1 || M > kMaxTok) return fail(K3_ERR_UNSUPPORTED, "decode path takes 1..8 tokens, got M=" + std::to_string(M));
+    if (p->hidden <= 0 || p->hidden % 128) return fail(K3_ERR_UNSUPPORTED, "hidden must be a positive multiple of 128");
+    if (p->inter <= 0 || p->inter % 128) return fail(K3_ERR_UNSUPPORTED, "inter must be a positive multiple of 128");
+    if (p->num_experts < 1 || p->num_experts > kMaxExperts) return fail(K3_ERR_UNSUPPORTED, "num_experts must be 1..1024");
+    if (p->top_k < 1 || p->top_k > kMaxTopK || p->top_k > p->num_experts) return fail(K3_ERR_UNSUPPORTED, "top_k must be 1..min(16, E)");
+    if (!p->experts) return fail(K3_ERR_INVALID, "expert table is NULL");
+    if (p->activation != K3_ACT_SILU && p->activation != K3_ACT_SITU) return fail(K3_ERR_INVALID, "unknown activation");
+    return K3_OK;
+}
+
+int check_ws(void* ws, size_t bytes, size_t need) {
+    if (!ws) return fail(K3_ERR_WORKSPACE, "workspace is NULL");
+    if (reinterpret_cast<uintptr_t>(ws) % 256) return fail(K3_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    if (bytes < need) return fail(K3_ERR_WORKSPACE, "workspace too small: need " + std::to_string(need) + " bytes");
+    return K3_OK;
+}
+
+int launch_router_logits(const void* x, int xdt, int Mc, int64_t H, const uint16_t* W, int64_t E,
+                         float* logits, cudaStream_t s) {
+    const int blocks = int((E * 32 + 255) / 256);
+    prof_begin(K3_PROF_ROUTER, s);
+    if (xdt == K3_BF16)
+        router_logits_kernel<K3_BF16><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+    else
+        router_logits_kernel<K3_F32><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+    prof_end(K3_PROF_ROUTER, s);
+    K3_CHECK_LAUNCH("router_logits_kernel");
+    return K3_OK;
+}
+
+// Decode experts given routing; `logits` non-null also runs the top-k inside prep.
+int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M, const float* logits,
+                const float* bias, int32_t* idx, float* w, void* y, int ydt, uint8_t* ws,
+                const DecodeLayout& L, cudaStream_t s) {
+    int rc = configure_smem();
+    if (rc) return rc;
+    Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
+    __half* xq_hi = reinterpret_cast<__half*>(ws + L.xq_hi);
+    __half* xq_lo = reinterpret_cast<__half*>(ws + L.xq_lo);
+    float* xq_ts = reinterpret_cast<float*>(ws + L.xq_ts);
+    const bool x_hilo = (xdt == K3_F32);
+    PrepArgs pa{};
+    pa.mode = 0;
+    pa.logits = logits;
+    pa.bias = bias;
+    pa.E = int(p->num_experts);
+    pa.k = p->top_k;
+    pa.renorm = p->renormalize;
+    pa.scale = p->routed_scaling_factor;
+    pa.idx = idx;
+    pa.w = w;
+    pa.has_shared = p->has_shared;
+    pa.plan = plan;
+    pa.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
+    pa.n_cntA = L.U * (L.I / 32);
+    pa.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
+    pa.n_cntB = L.H / kItemRows;
+    pa.x = x;
+    pa.x_dtype = xdt;
+    pa.M = int(M);
+    pa.K = L.H;
+    pa.xq_hi = xq_hi;
+    pa.xq_lo = x_hilo ? xq_lo : nullptr;
+    pa.xq_ts = xq_ts;
+    const int64_t conv_warps = M * (L.H / 32);
+    const int conv_blocks = int(std::min<int64_t>((conv_warps + 7) / 8, 1024));
+    prof_begin(K3_PROF_TOPK, s);
+    prep_kernel<<<1 + conv_blocks, 256, 0, s>>>(pa);
+    prof_end(K3_PROF_TOPK, s);
+    K3_CHECK_LAUNCH("prep_kernel");
+
+    const int sms = num_sms();
+    GemvArgs ga{};
+    ga.plan = plan;
+    ga.table = p->experts;
+    ga.K = L.H;
+    ga.rows = L.I;
+    ga.C = L.CA;
+    ga.hilo = x_hilo ? 1 : 0;
+    ga.bh = xq_hi;
+    ga.bl = xq_lo;
+    ga.bts = xq_ts;
+    ga.part = reinterpret_cast<float*>(ws + L.partA);
+    ga.cnt = reinterpret_cast<unsigned*>(ws + L.cntA);
+    ga.act_hi = reinterpret_cast<__half*>(ws + L.act_hi);
+    ga.act_lo = reinterpret_cast<__half*>(ws + L.act_lo);
+    ga.act_ts = reinterpret_cast<float*>(ws + L.act_ts);
+    ga.act_kind = p->activation;
+    ga.beta = p->situ_beta;
+    ga.lbeta = p->situ_linear_beta;
+    prof_begin(K3_PROF_GATEUP, s);
+    gemv_kernel<true><<<sms, kWarps * 32, kSmemBytes, s>>>(ga);
+    prof_end(K3_PROF_GATEUP, s);
+    K3_CHECK_LAUNCH("gemv_kernel<gate/up>");
+
+    GemvArgs gb{};
+    gb.plan = plan;
+    gb.table = p->experts;
+    gb.K = L.I;
+    gb.rows = L.H;
+    gb.C = L.CB;
+    gb.hilo = 1;
+    gb.bh = ga.act_hi;
+    gb.bl = ga.act_lo;
+    gb.bts = ga.act_ts;
+    gb.part = reinterpret_cast<float*>(ws + L.partB);
+    gb.cnt = reinterpret_cast<unsigned*>(ws + L.cntB);
+    gb.Pmax = int(L.P);
+    gb.y = y;
+    gb.y_dtype = ydt;
+    prof_begin(K3_PROF_DOWN, s);
+    gemv_kernel<false><<<sms, kWarps * 32, kSmemBytes, s>>>(gb);
+    prof_end(K3_PROF_DOWN, s);
+    K3_CHECK_LAUNCH("gemv_kernel<down>");
+    return K3_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+// Matvec pieces (used by k3_capi.cu's k3_mxfp4_matvec fast path).
+struct MatvecLayout {
+    int C;
+    size_t plan, xq_hi, xq_lo, xq_ts, part, cnt, total;
+};
+
+MatvecLayout matvec_layout(int64_t M, int64_t K, int64_t N, int sms) {
+    MatvecLayout L{};
+    const int64_t Mc = std::min<int64_t>(M, kMaxTok);
+    L.C = choose_split(N / kItemRows, K, int64_t(sms) * kWarps * 4);
+    size_t off = 0;
+    L.plan = carve(off, sizeof(Plan));
+    L.xq_hi = carve(off, sizeof(__half) * Mc * K);
+    L.xq_lo = carve(off, sizeof(__half) * Mc * K);
+    L.xq_ts = carve(off, sizeof(float) * Mc * (K / 32));
+    L.part = carve(off, sizeof(float) * L.C * Mc * N);
+    L.cnt = carve(off, sizeof(unsigned) * (N / kItemRows));
+    L.total = off;
+    return L;
+}
+
+bool matvec_fast_ok(int64_t K, int64_t N, const void* x, const uint8_t* packed,
+                    const uint8_t* scales) {
+    return K % 128 == 0 && N % kItemRows == 0 && aligned16(packed) &&
+           (reinterpret_cast<uintptr_t>(scales) & 3) == 0 && x != nullptr;
+}
+
+int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* packed,
+                const uint8_t* scales, int64_t N, void* out, int odt, uint8_t* ws,
+                cudaStream_t s) {
+    int rc = configure_smem();
+    if (rc) return rc;
+    const int sms = num_sms();
+    const MatvecLayout L = matvec_layout(M, K, N, sms);
+    const size_t esz = (xdt == K3_BF16 || xdt == K3_F16) ? 2 : 4;
+    const size_t osz = (odt == K3_BF16 || odt == K3_F16) ? 2 : 4;
+    const bool hilo = (xdt == K3_F32);
+    for (int64_t m0 = 0; m0 < M; m0 += kMaxTok) {
+        const int Mc = int(std::min<int64_t>(kMaxTok, M - m0));
+        PrepArgs pa{};
+        pa.mode = 1;
+        pa.plan = reinterpret_cast<Plan*>(ws + L.plan);
+        pa.cntB = reinterpret_cast<unsigned*>(ws + L.cnt);
+        pa.n_cntB = N / kItemRows;
+        pa.x = static_cast<const uint8_t*>(x) + size_t(m0) * K * esz;
+        pa.x_dtype = xdt;
+        pa.M = Mc;
+        pa.K = K;
+        pa.xq_hi = reinterpret_cast<__half*>(ws + L.xq_hi);
+        pa.xq_lo = hilo ? reinterpret_cast<__half*>(ws + L.xq_lo) : nullptr;
+        pa.xq_ts = reinterpret_cast<float*>(ws + L.xq_ts);
+        const int64_t conv_warps = int64_t(Mc) * (K / 32);
+        const int conv_blocks = int(std::min<int64_t>((conv_warps + 7) / 8, 1024));
+        prof_begin(K3_PROF_TOPK, s);
+        prep_kernel<<<1 + conv_blocks, 256, 0, s>>>(pa);
+        prof_end(K3_PROF_TOPK, s);
+        K3_CHECK_LAUNCH("prep_kernel(matvec)");
+        GemvArgs g{};
+        g.plan = pa.plan;
+        g.mat_packed = packed;
+        g.mat_scales = scales;
+        g.K = K;
+        g.rows = N;
+        g.C = L.C;
+        g.hilo = hilo ? 1 : 0;
+        g.bh = pa.xq_hi;
+        g.bl = reinterpret_cast<__half*>(ws + L.xq_lo);
+        g.bts = pa.xq_ts;
+        g.part = reinterpret_cast<float*>(ws + L.part);
+        g.cnt = pa.cntB;
+        g.Pmax = Mc;
+        g.y = static_cast<uint8_t*>(out) + size_t(m0) * N * osz;
+        g.y_dtype = odt;
+        prof_begin(K3_PROF_MATVEC, s);
+        gemv_kernel<false><<<sms, kWarps * 32, kSmemBytes, s>>>(g);
+        prof_end(K3_PROF_MATVEC, s);
+        K3_CHECK_LAUNCH("gemv_kernel<matvec>");
+    }
+    return K3_OK;
+}
+
+size_t matvec_fast_workspace(int64_t M, int64_t K, int64_t N) {
+    return matvec_layout(M, K, N, num_sms()).total;
+}
+
+}  // namespace k3
+
+using namespace k3;
+
+// ================================================================ C ABI
+
+extern "C" K3_API size_t k3_moe_route_workspace(int64_t M, int64_t E) {
+    return align_up(sizeof(float) * size_t(std::max<int64_t>(M, 1)) * size_t(std::max<int64_t>(E, 1)), 256) + 256;
+}
+
+extern "C" K3_API int k3_moe_route(const void* x, int x_dtype, int64_t M, int64_t H,
+                                   const uint16_t* gate_w_bf16, const float* bias, int64_t E,
+                                   int top_k, int renormalize, float routed_scaling_factor,
+                                   int32_t* idx_out, float* weight_out, float* raw_out,
+                                   float* corrected_out, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    if (!x || !gate_w_bf16 || !idx_out || !weight_out) return fail(K3_ERR_INVALID, "k3_moe_route: NULL tensor");
+    if (x_dtype != K3_F32 && x_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_route: x must be f32 or bf16");
+    if (M < 1 || H < 8 || H % 8) return fail(K3_ERR_INVALID, "k3_moe_route: need M >= 1 and H % 8 == 0");
+    if (E < 1 || E > kMaxExperts) return fail(K3_ERR_UNSUPPORTED, "k3_moe_route: E must be 1..1024");
+    if (top_k < 1 || top_k > 32 || top_k > E) return fail(K3_ERR_UNSUPPORTED, "k3_moe_route: top_k must be 1..min(32, E)");
+    if (!aligned16(x) || !aligned16(gate_w_bf16)) return fail(K3_ERR_INVALID, "k3_moe_route: x and gate_w must be 16-byte aligned");
+    const size_t need = k3_moe_route_workspace(M, E);
+    if (int rc = check_ws(workspace, workspace_bytes, need)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* logits = static_cast<float*>(workspace);
+    int* status = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + need - 256);
+    const size_t esz = x_dtype == K3_BF16 ? 2 : 4;
+    if (int rc = cuda_check(cudaMemsetAsync(status, 0, sizeof(int), s), "cudaMemsetAsync")) return rc;
+    for (int64_t m0 = 0; m0 < M; m0 += kMaxTok) {
+        const int Mc = int(std::min<int64_t>(kMaxTok, M - m0));
+        if (int rc = launch_router_logits(static_cast<const uint8_t*>(x) + size_t(m0) * H * esz,
+                                          x_dtype, Mc, H, gate_w_bf16, E, logits + m0 * E, s))
+            return rc;
+    }
+    prof_begin(K3_PROF_TOPK, s);
+    topk_kernel<<<int((M + 7) / 8), 256, 0, s>>>(logits, int(M), int(E), bias, top_k, renormalize,
+                                                 routed_scaling_factor, idx_out, weight_out,
+                                                 raw_out, corrected_out, status);
+    prof_end(K3_PROF_TOPK, s);
+    K3_CHECK_LAUNCH("topk_kernel");
+    return K3_OK;
+}
+
+extern "C" K3_API size_t k3_moe_decode_workspace(const k3_moe_params* p, int64_t M) {
+    if (check_moe_params(p, M) != K3_OK) return 0;
+    return decode_layout(*p, M, num_sms()).total;
+}
+
+extern "C" K3_API int k3_moe_decode(const k3_moe_params* p, const void* x, int x_dtype, int64_t M,
+                                    const uint16_t* gate_w_bf16, const float* bias, void* y_out,
+                                    int y_dtype, int32_t* idx_out, float* weight_out,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = check_moe_params(p, M)) return rc;
+    if (!x || !gate_w_bf16 || !y_out) return fail(K3_ERR_INVALID, "k3_moe_decode: NULL tensor");
+    if (x_dtype != K3_F32 && x_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_decode: x must be f32 or bf16");
+    if (y_dtype != K3_F32 && y_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_decode: y must be f32 or bf16");
+    if (!aligned16(x) || !aligned16(gate_w_bf16)) return fail(K3_ERR_INVALID, "k3_moe_decode: x and gate_w must be 16-byte aligned");
+    const DecodeLayout L = decode_layout(*p, M, num_sms());
+    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* logits = reinterpret_cast<float*>(ws + L.logits);
+    int32_t* idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + L.route_idx);
+    float* w = weight_out ? weight_out : reinterpret_cast<float*>(ws + L.route_w);
+    if (int rc = launch_router_logits(x, x_dtype, int(M), p->hidden, gate_w_bf16, p->num_experts, logits, s)) return rc;
+    return decode_impl(p, x, x_dtype, M, logits, bias, idx, w, y_out, y_dtype, ws, L, s);
+}
+
+extern "C" K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* x, int x_dtype,
+                                            int64_t M, const int32_t* idx, const float* w,
+                                            void* y_out, int y_dtype, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+    if (int rc = check_moe_params(p, M)) return rc;
+    if (!x || !idx || !w || !y_out) return fail(K3_ERR_INVALID, "k3_moe_experts_decode: NULL tensor");
+    if (x_dtype != K3_F32 && x_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_experts_decode: x must be f32 or bf16");
+    if (y_dtype != K3_F32 && y_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_experts_decode: y must be f32 or bf16");
+    const DecodeLayout L = decode_layout(*p, M, num_sms());
+    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
+    return decode_impl(p, x, x_dtype, M, nullptr, nullptr, const_cast<int32_t*>(idx),
+                       const_cast<float*>(w), y_out, y_dtype, static_cast<uint8_t*>(workspace), L,
+                       static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,334 @@
+"""Router + MoE block on the B200 -- the drop-in for ``air_llm/models/kimi_k3/moe.py``.
+
+``LatentMoE(cfg, layer, w, expert_source, fused=True)`` keeps the reference's
+constructor, methods (``route``, ``expert_forward``, ``shared_forward``, ``__call__``)
+and semantics (``moe.py:40-132``; oracle ``k3ref/layers.py:188-261``):
+
+* router: sigmoid scores, correction bias for SELECTION only, weights gathered from the
+  raw scores, renormalised by sum + 1e-20, times ``routed_scaling_factor``;
+* routed experts visited in ascending id order, ``y[tok] += out * w[tok, slot]``;
+* with the latent wrapper (``routed_expert_down_proj``/``up_proj``/``norm`` in ``w``):
+  hidden -> latent before the experts, rmsnorm + latent -> hidden after;
+* shared experts act on the ORIGINAL hidden: dense when ``w`` holds
+  ``shared_experts.*`` weights (Kimi-K3), MXFP4 when ``expert_source(layer, "shared",
+  which)`` provides them (the BASELINE layer), absent otherwise.
+
+The expert weights returned by ``expert_source`` are uploaded once into HBM (the
+reference streams them per call from SSD; on a B200 the whole layer fits) and bound
+into a device pointer table that the fused kernels index. Activation: ``cfg.activation``
+("situ" for Kimi-K3 -- the default -- or "silu" for SwiGLU).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .mxfp4 import decode_mxfp4, mxfp4_matvec_fused, scale_minmax
+
+SHARED = "shared"
+WHICH = ("w1", "w3", "w2")
+MAX_DECODE_TOKENS = 8
+
+
+@dataclass
+class MoEConfig:
+    """The MoE fields of ``K3Config`` (``air_llm/models/kimi_k3/config.py:11-41``) plus the
+    activation choice; any object with these attributes works."""
+    hidden_size: int
+    num_experts: int
+    num_experts_per_token: int
+    moe_intermediate_size: int
+    routed_expert_hidden_size: int
+    routed_scaling_factor: float = 1.0
+    moe_renormalize: bool = True
+    situ_beta: float = 4.0
+    situ_linear_beta: Optional[float] = 25.0
+    rms_norm_eps: float = 1e-5
+    num_shared_experts: int = 1
+    activation: str = "situ"
+
+
+@dataclass
+class RouterResult:
+    """``moe.py:32-37``."""
+    expert_indices: torch.Tensor    # [N, top_k] int64, descending corrected score
+    expert_weights: torch.Tensor    # [N, top_k] fp32
+    raw_scores: torch.Tensor        # [N, num_experts] sigmoid(logits)
+    corrected_scores: torch.Tensor  # raw + e_score_correction_bias
+
+
+def _as_device_u8(a, device) -> torch.Tensor:
+    if isinstance(a, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(a))
+    if not isinstance(a, torch.Tensor):
+        a = torch.as_tensor(np.asarray(a))
+    if a.dtype != torch.uint8:
+        raise ValueError(f"MXFP4 tensors must be uint8, got {a.dtype}")
+    return a.to(device, non_blocking=False).contiguous()
+
+
+def _as_device(a, device, dtype=None) -> torch.Tensor:
+    if isinstance(a, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(a))
+    a = torch.as_tensor(a)
+    return a.to(device=device, dtype=dtype or a.dtype).contiguous()
+
+
+class ExpertPool:
+    """HBM-resident MXFP4 expert weights of one layer plus the device pointer table
+    (``k3_expert_ptrs[E (+1 shared)]``) the fused kernels read.
+
+    ``expert_source(layer, e, which) -> (packed, scales)`` is called once per projection
+    (the reference calls it on every use, ``moe.py:86``). Scale ranges are checked at
+    upload like ``loader.py:246-247``.
+    """
+
+    def __init__(self, layer: int, num_experts: int, expert_source: Callable, device,
+                 with_shared: bool, check_scales: bool = True):
+        self.layer, self.E, self.device = layer, num_experts, torch.device(device)
+        self.with_shared = with_shared
+        self.tensors: list[tuple] = []
+        ids = list(range(num_experts)) + ([SHARED] if with_shared else [])
+        lo, hi = 255, 0
+        for e in ids:
+            trip = []
+            for which in WHICH:
+                p, s = expert_source(layer, e, which)
+                p, s = _as_device_u8(p, self.device), _as_device_u8(s, self.device)
+                if check_scales:
+                    a, b = scale_minmax(s)
+                    lo, hi = min(lo, a), max(hi, b)
+                trip.append((p, s))
+            self.tensors.append(tuple(trip))
+        if check_scales and (lo < 2 or hi > 252):
+            raise ValueError(f"Unsupported MXFP4 scale range {lo}..{hi}; require 2..252 "
+                             "to avoid Metal subnormal flushing, overflow, and E8M0 NaN")
+        table = torch.tensor([[t.data_ptr() for pair in trip for t in pair] for trip in self.tensors],
+                             dtype=torch.int64)
+        self.table = table.to(self.device)
+        g1, s1 = self.tensors[0][0]
+        self.inter, self.hidden = g1.shape[0], g1.shape[1] * 2
+
+    def get(self, e, which: str):
+        i = self.E if e == SHARED else int(e)
+        return self.tensors[i][WHICH.index(which)]
+
+    def nbytes(self) -> int:
+        return sum(t.numel() for trip in self.tensors for pair in trip for t in pair)
+
+
+class LatentMoE:
+    """Drop-in for ``air_llm.models.kimi_k3.moe.LatentMoE`` on CUDA tensors."""
+
+    def __init__(self, cfg, layer: int, w: dict, expert_source: Callable, fused: bool = True,
+                 device=None):
+        self.cfg, self.L, self.src, self.fused = cfg, layer, expert_source, fused
+        self.device = torch.device(device) if device is not None else torch.device("cuda")
+        self.act = getattr(cfg, "activation", "situ")
+        if self.act not in ("silu", "situ"):
+            raise ValueError(f"unknown activation {self.act!r}")
+        gw = _as_device(w["gate.weight"], self.device)
+        self.gate_w = gw.to(torch.bfloat16).contiguous()       # stored bf16 on disk
+        if gw.dtype == torch.float32 and not torch.equal(self.gate_w.float(), gw):
+            raise ValueError("gate.weight is not bf16-representable; the router reads bf16 weights")
+        b = w.get("gate.e_score_correction_bias")
+        self.gate_b = None if b is None else _as_device(b, self.device, torch.float32)
+        self.latent = "routed_expert_down_proj.weight" in w
+        if self.latent:
+            self.down = _as_device(w["routed_expert_down_proj.weight"], self.device, torch.float32)
+            self.up = _as_device(w["routed_expert_up_proj.weight"], self.device, torch.float32)
+            self.norm_w = _as_device(w["routed_expert_norm.weight"], self.device, torch.float32)
+        self.dense_shared = "shared_experts.gate_proj.weight" in w
+        if self.dense_shared:
+            self.sh_gate = _as_device(w["shared_experts.gate_proj.weight"], self.device, torch.float32)
+            self.sh_up = _as_device(w["shared_experts.up_proj.weight"], self.device, torch.float32)
+            self.sh_down = _as_device(w["shared_experts.down_proj.weight"], self.device, torch.float32)
+        self.mxfp4_shared = (not self.dense_shared) and getattr(cfg, "num_shared_experts", 0) > 0
+        self._pool: Optional[ExpertPool] = None
+
+    # ------------------------------------------------------------------ plumbing
+    @property
+    def pool(self) -> ExpertPool:
+        if self._pool is None:
+            self._pool = ExpertPool(self.L, self.cfg.num_experts, self.src, self.device,
+                                    with_shared=self.mxfp4_shared)
+        return self._pool
+
+    @property
+    def tiled(self) -> bool:
+        """True when the fused decode kernels tile this layer (H, I multiples of 128,
+        <= 1024 experts, top-k <= 16); otherwise experts run one by one through
+        ``mxfp4_matvec_fused`` (still on the GPU)."""
+        c, p = self.cfg, self.pool
+        return (p.hidden % 128 == 0 and p.inter % 128 == 0 and c.num_experts <= 1024
+                and c.num_experts_per_token <= 16)
+
+    def _params(self, *, num_experts=None, top_k=None, has_shared=None) -> L.K3MoEParams:
+        c, pool = self.cfg, self.pool
+        lb = getattr(c, "situ_linear_beta", None)
+        return L.K3MoEParams(
+            hidden=pool.hidden, inter=pool.inter,
+            num_experts=self.cfg.num_experts if num_experts is None else num_experts,
+            top_k=c.num_experts_per_token if top_k is None else top_k,
+            renormalize=int(bool(c.moe_renormalize)),
+            routed_scaling_factor=float(c.routed_scaling_factor),
+            has_shared=int(self.mxfp4_shared if has_shared is None else has_shared),
+            activation=L.K3_ACT_SITU if self.act == "situ" else L.K3_ACT_SILU,
+            situ_beta=float(getattr(c, "situ_beta", 4.0)),
+            situ_linear_beta=-1.0 if lb is None else float(lb),
+            experts=pool.table.data_ptr())
+
+    def _experts_decode(self, h: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
+                        params: L.K3MoEParams) -> torch.Tensor:
+        """y[t] = sum_slot w[t,slot] * expert_{idx[t,slot]}(h[t]) (+ MXFP4 shared), fp32."""
+        lib = L.load_library()
+        out = torch.empty((h.shape[0], self.pool.hidden), dtype=torch.float32, device=h.device)
+        for m0 in range(0, h.shape[0], MAX_DECODE_TOKENS):
+            hc = h[m0:m0 + MAX_DECODE_TOKENS].contiguous()
+            ic = idx[m0:m0 + MAX_DECODE_TOKENS].to(torch.int32).contiguous()
+            wc = w[m0:m0 + MAX_DECODE_TOKENS].to(torch.float32).contiguous()
+            M = hc.shape[0]
+            need = lib.k3_moe_decode_workspace(params, M)
+            L.check(0 if need else L.K3_ERR_INVALID, "k3_moe_decode_workspace")
+            ws = L.workspace(h.device, need)
+            oc = out[m0:m0 + M]
+            L.check(lib.k3_moe_experts_decode(params, hc.data_ptr(), L.dtype_code(hc), M,
+                                              ic.data_ptr(), wc.data_ptr(), oc.data_ptr(), L.K3_F32,
+                                              ws.data_ptr(), ws.numel(), L.stream_of(hc)),
+                    "k3_moe_experts_decode")
+        return out
+
+    def _activation(self, g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+        if self.act == "silu":
+            return torch.nn.functional.silu(g) * u
+        c = self.cfg
+        beta, lb = float(c.situ_beta), getattr(c, "situ_linear_beta", None)
+        a = beta * torch.tanh(g / beta) * torch.sigmoid(g)
+        if lb is not None:
+            u = lb * torch.tanh(u / lb)
+        return a * u
+
+    # -------------------------------------------------------------------- routing
+    def route(self, x: torch.Tensor) -> RouterResult:
+        """``moe.py:65-76`` on the device (``k3_moe_route``)."""
+        L.require_cuda(x, "x")
+        c = self.cfg
+        flat = x.reshape(-1, x.shape[-1])
+        if flat.dtype not in (torch.float32, torch.bfloat16):
+            flat = flat.float()
+        flat = flat.contiguous()
+        N, E, k = flat.shape[0], c.num_experts, c.num_experts_per_token
+        dev = flat.device
+        idx = torch.empty((N, k), dtype=torch.int32, device=dev)
+        w = torch.empty((N, k), dtype=torch.float32, device=dev)
+        raw = torch.empty((N, E), dtype=torch.float32, device=dev)
+        cor = torch.empty((N, E), dtype=torch.float32, device=dev)
+        lib = L.load_library()
+        ws = L.workspace(dev, lib.k3_moe_route_workspace(N, E))
+        L.check(lib.k3_moe_route(flat.data_ptr(), L.dtype_code(flat), N, flat.shape[1],
+                                 self.gate_w.data_ptr(),
+                                 None if self.gate_b is None else self.gate_b.data_ptr(), E, k,
+                                 int(bool(c.moe_renormalize)), float(c.routed_scaling_factor),
+                                 idx.data_ptr(), w.data_ptr(), raw.data_ptr(), cor.data_ptr(),
+                                 ws.data_ptr(), ws.numel(), L.stream_of(flat)), "k3_moe_route")
+        return RouterResult(idx.long(), w, raw, cor)
+
+    # -------------------------------------------------------------------- experts
+    def _proj(self, h: torch.Tensor, e, which: str) -> torch.Tensor:
+        """``moe.py:79-88``: h @ W.T for one MXFP4 projection."""
+        p, s = self.pool.get(e, which)
+        if self.fused:
+            return mxfp4_matvec_fused(h, p, s)
+        return h.float() @ decode_mxfp4(p, s, out_dtype=torch.bfloat16).float().T
+
+    def expert_forward(self, h: torch.Tensor, e: int) -> torch.Tensor:
+        """One routed expert, unweighted (``moe.py:90-103``): act(h W1^T, h W3^T) W2^T."""
+        L.require_cuda(h, "h")
+        if not self.fused or not self.tiled:
+            return self._proj(self._activation(self._proj(h, e, "w1"), self._proj(h, e, "w3")), e, "w2")
+        h2 = h.reshape(-1, h.shape[-1])
+        if h2.dtype not in (torch.float32, torch.bfloat16):
+            h2 = h2.float()
+        M = h2.shape[0]
+        idx = torch.full((M, 1), int(e), dtype=torch.int32, device=h.device)
+        w = torch.ones((M, 1), dtype=torch.float32, device=h.device)
+        y = self._experts_decode(h2, idx, w, self._params(top_k=1, has_shared=0))
+        return y.reshape(*h.shape[:-1], y.shape[-1])
+
+    def shared_forward(self, x: torch.Tensor) -> torch.Tensor:
+        """Shared experts on the original hidden (``moe.py:105-107``)."""
+        if self.dense_shared:
+            xf = x.float()
+            return self._activation(xf @ self.sh_gate.T, xf @ self.sh_up.T) @ self.sh_down.T
+        if not self.mxfp4_shared:
+            return torch.zeros((*x.shape[:-1], self.cfg.hidden_size), dtype=torch.float32,
+                               device=x.device)
+        if not self.tiled:
+            xf = x.float()
+            return self._proj(self._activation(self._proj(xf, SHARED, "w1"),
+                                               self._proj(xf, SHARED, "w3")), SHARED, "w2")
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype not in (torch.float32, torch.bfloat16):
+            x2 = x2.float()
+        M = x2.shape[0]
+        E = self.cfg.num_experts
+        idx = torch.full((M, 1), E, dtype=torch.int32, device=x.device)
+        w = torch.ones((M, 1), dtype=torch.float32, device=x.device)
+        y = self._experts_decode(x2, idx, w, self._params(num_experts=E + 1, top_k=1, has_shared=0))
+        return y.reshape(*x.shape[:-1], y.shape[-1])
+
+    # -------------------------------------------------------------------- forward
+    def _fused_decode(self, flat: torch.Tensor):
+        """route + routed experts + MXFP4 shared expert in one library call per <= 8 tokens."""
+        lib = L.load_library()
+        params = self._params()
+        k = self.cfg.num_experts_per_token
+        y = torch.empty((flat.shape[0], self.pool.hidden), dtype=torch.float32, device=flat.device)
+        idx = torch.empty((flat.shape[0], k), dtype=torch.int32, device=flat.device)
+        w = torch.empty((flat.shape[0], k), dtype=torch.float32, device=flat.device)
+        for m0 in range(0, flat.shape[0], MAX_DECODE_TOKENS):
+            xc = flat[m0:m0 + MAX_DECODE_TOKENS]
+            M = xc.shape[0]
+            ws = L.workspace(flat.device, lib.k3_moe_decode_workspace(params, M))
+            L.check(lib.k3_moe_decode(params, xc.data_ptr(), L.dtype_code(xc), M,
+                                      self.gate_w.data_ptr(),
+                                      None if self.gate_b is None else self.gate_b.data_ptr(),
+                                      y[m0:m0 + M].data_ptr(), L.K3_F32, idx[m0:m0 + M].data_ptr(),
+                                      w[m0:m0 + M].data_ptr(), ws.data_ptr(), ws.numel(),
+                                      L.stream_of(xc)), "k3_moe_decode")
+        return y, idx, w
+
+    def __call__(self, x: torch.Tensor, return_router: bool = False):
+        """``moe.py:110-132``: returns y shaped like x (fp32), and the RouterResult if asked."""
+        L.require_cuda(x, "x")
+        orig = x.shape
+        flat = x.reshape(-1, orig[-1])
+        if flat.dtype not in (torch.float32, torch.bfloat16):
+            flat = flat.float()
+        flat = flat.contiguous()
+        if (not self.latent and not self.dense_shared and not return_router and self.fused
+                and self.tiled):
+            y, _, _ = self._fused_decode(flat)
+            return y.reshape(*orig[:-1], y.shape[-1])
+        r = self.route(flat)
+        h = flat if not self.latent else flat.float() @ self.down.T
+        if self.fused and self.tiled:
+            y = self._experts_decode(h.contiguous(), r.expert_indices, r.expert_weights,
+                                     self._params(has_shared=0))
+        else:
+            y = torch.zeros((flat.shape[0], h.shape[1]), dtype=torch.float32, device=x.device)
+            for e in sorted(set(r.expert_indices.reshape(-1).tolist())):
+                tok, slot = (r.expert_indices == e).nonzero(as_tuple=True)
+                y.index_add_(0, tok, self.expert_forward(h[tok].float(), e)
+                             * r.expert_weights[tok, slot, None])
+        if self.latent:
+            yf = y.float()
+            y = self.norm_w * (yf * torch.rsqrt(yf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps))
+            y = y @ self.up.T
+        y = y + self.shared_forward(flat)
+        y = y.reshape(*orig[:-1], y.shape[-1])
+        return (y, r) if return_router else y

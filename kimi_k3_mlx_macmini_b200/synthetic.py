@@ -1,0 +1,72 @@
+"""Seeded synthetic MoE layers with BASELINE.json's shapes and value distributions,
+generated directly in HBM (there is no checkpoint; random-init weights of the stated
+architecture stand in for it):
+
+* E2M1 codes uniform over all 16 values, packed two per byte (low nibble = even
+  element), E8M0 scale bytes uniform in [120, 130];
+* router weight bf16 ~ N(0, 0.02), correction bias 0; x bf16 ~ N(0, 1).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .moe import SHARED, LatentMoE, MoEConfig
+
+
+def random_mxfp4(gen: torch.Generator, rows: int, cols: int, device, scale_lo: int = 120,
+                 scale_hi: int = 130):
+    packed = torch.randint(0, 256, (rows, cols // 2), generator=gen, device=device, dtype=torch.uint8)
+    scales = torch.randint(scale_lo, scale_hi + 1, (rows, cols // 32), generator=gen, device=device,
+                           dtype=torch.uint8)
+    return packed, scales
+
+
+def bf16_normal(gen: torch.Generator, shape, std: float, device) -> torch.Tensor:
+    return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+@dataclass
+class SyntheticLayer:
+    cfg: MoEConfig
+    gate: torch.Tensor            # bf16 [E, H]
+    bias: torch.Tensor            # f32 [E]
+    experts: list                 # [(w1, w3, w2)] with each (packed, scales)
+    shared: tuple                 # (w1, w3, w2) or None
+
+    def source(self, layer: int, e, which: str):
+        trip = self.shared if e == SHARED else self.experts[int(e)]
+        return trip[("w1", "w3", "w2").index(which)]
+
+    def moe(self, device="cuda") -> LatentMoE:
+        w = {"gate.weight": self.gate, "gate.e_score_correction_bias": self.bias}
+        return LatentMoE(self.cfg, 0, w, self.source, fused=True, device=device)
+
+    def nbytes_expert(self) -> int:
+        return sum(t.numel() for pair in self.experts[0] for t in pair)
+
+
+def baseline_layer(seed: int = 0, E: int = 384, H: int = 7168, I: int = 2048, top_k: int = 8,
+                   scale: float = 2.5, shared: bool = True, device="cuda") -> SyntheticLayer:
+    """BASELINE configs[2]/[3]: 384 routed + 1 shared MXFP4 expert, hidden 7168,
+    intermediate 2048, sigmoid top-8, renormalised weights x 2.5."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    cfg = MoEConfig(hidden_size=H, num_experts=E, num_experts_per_token=top_k,
+                    moe_intermediate_size=I, routed_expert_hidden_size=H,
+                    routed_scaling_factor=scale, moe_renormalize=True,
+                    num_shared_experts=1 if shared else 0, activation="silu")
+    gate = bf16_normal(gen, (E, H), 0.02, device)
+    bias = torch.zeros(E, dtype=torch.float32, device=device)
+    experts = [(random_mxfp4(gen, I, H, device), random_mxfp4(gen, I, H, device),
+                random_mxfp4(gen, H, I, device)) for _ in range(E)]
+    sh = ((random_mxfp4(gen, I, H, device), random_mxfp4(gen, I, H, device),
+           random_mxfp4(gen, H, I, device)) if shared else None)
+    return SyntheticLayer(cfg, gate, bias, experts, sh)
+
+
+def tokens(seed: int, M: int, H: int, device="cuda") -> torch.Tensor:
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    return bf16_normal(gen, (M, H), 1.0, device)

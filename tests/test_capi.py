@@ -1,0 +1,76 @@
+"""The C-ABI library loads and exports every symbol ``include/k3b200.h`` declares, and
+argument validation answers before any CUDA call (no GPU needed)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def header_symbols():
+    text = (ROOT / "include" / "k3b200.h").read_text()
+    return sorted(set(re.findall(r"K3_API\s+[\w\s\*]+?\b(k3_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from kimi_k3_mlx_macmini_b200 import build
+    build.build()
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    return L.load_library()
+
+
+def test_header_declares_entry_points():
+    syms = header_symbols()
+    assert "k3_mxfp4_matvec" in syms and "k3_moe_decode" in syms and len(syms) >= 12
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    for name in header_symbols():
+        assert hasattr(lib, name), f"{name} not exported"
+        assert name in L.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_error_string(lib):
+    assert lib.k3_abi_version() == 1
+    assert isinstance(lib.k3_last_error(), bytes)
+
+
+def test_null_and_shape_errors_before_cuda(lib):
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    rc = lib.k3_mxfp4_matvec(None, L.K3_F32, 1, 64, None, None, 4, None, L.K3_F32, None, 0, None)
+    assert rc == L.K3_ERR_INVALID and b"NULL" in lib.k3_last_error()
+    # non-NULL placeholders are never dereferenced: validation fails first
+    fake = ctypes.c_void_p(16)
+    assert lib.k3_mxfp4_matvec(fake, L.K3_F32, 1, 48, fake, fake, 4, fake, L.K3_F32, None, 0,
+                               None) == L.K3_ERR_INVALID
+    assert b"multiple of 32" in lib.k3_last_error()
+    assert lib.k3_mxfp4_matvec(fake, 7, 1, 64, fake, fake, 4, fake, L.K3_F32, None, 0, None) == L.K3_ERR_INVALID
+    assert lib.k3_mxfp4_dequant(fake, fake, 4, 64, 16, fake, L.K3_F32, None) == L.K3_ERR_UNSUPPORTED
+    assert lib.k3_moe_route(fake, L.K3_F32, 1, 64, fake, None, 2000, 8, 1, 1.0, fake, fake, None,
+                            None, None, 0, None) == L.K3_ERR_UNSUPPORTED
+
+
+def test_moe_params_validation(lib):
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    p = L.K3MoEParams(hidden=7168, inter=2048, num_experts=384, top_k=8, renormalize=1,
+                      routed_scaling_factor=2.5, has_shared=1, activation=L.K3_ACT_SILU,
+                      situ_beta=4.0, situ_linear_beta=25.0, experts=None)
+    assert lib.k3_moe_decode_workspace(p, 1) == 0          # NULL table rejected
+    p.experts = 16
+    assert lib.k3_moe_decode_workspace(p, 9) == 0          # decode takes <= 8 tokens
+    p.hidden = 7000
+    assert lib.k3_moe_decode_workspace(p, 1) == 0          # hidden % 128
+    assert b"hidden" in lib.k3_last_error()
+
+
+def test_python_layer_refuses_cpu_tensors():
+    import numpy as np
+    import torch
+    from kimi_k3_mlx_macmini_b200 import mxfp4_matvec_fused
+    with pytest.raises(ValueError, match="CUDA"):
+        mxfp4_matvec_fused(torch.zeros(1, 64), torch.zeros(4, 32, dtype=torch.uint8),
+                           torch.zeros(4, 2, dtype=torch.uint8))

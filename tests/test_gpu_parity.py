@@ -1,0 +1,291 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle and the
+reference's golden vectors.
+
+Bars: dequantised weights and router top-k index sets
+bit-exact (rows whose k-th/(k+1)-th score gap is a near-tie are counted apart); expert
+and block outputs within rel-L2 1e-3 under fp32 accumulation. The tests also assert the
+tighter figure this design is expected to meet (rel-L2 1e-5), and the reference kernel
+gate's rel-max 1e-6 vs fp64 (``tests/test_mxfp4_kernel.py:52``).
+"""
+import numpy as np
+import pytest
+import torch
+
+import goldens as G
+import inputs as I
+from oracle import mxfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+NORTH_STAR_REL_L2 = 1e-3       # expert outputs within rel-L2 1e-3
+EXPECTED_REL_L2 = 1e-5         # fp32 accumulation with exact weights
+
+
+@pytest.fixture(scope="module")
+def k3():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    from kimi_k3_mlx_macmini_b200 import build
+    build.build()
+    import kimi_k3_mlx_macmini_b200 as k
+    return k
+
+
+def cu(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def bf16_cu(bits):
+    return cu(np.ascontiguousarray(bits, dtype=np.uint16)).view(torch.bfloat16)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy() if t.dtype == torch.bfloat16 else t.detach().cpu().numpy()
+
+
+# --------------------------------------------------------------------- codec
+
+def test_dequant_all_codes_and_scale_bytes(k3):
+    g = G.load("codec_kat")
+    got = host(k3.decode_mxfp4(cu(g["all256_packed"]), cu(g["all256_scales"])))
+    assert np.array_equal(got, g["all256_decoded"]) and np.array_equal(got, g["all256_ct"])
+    got = host(k3.decode_mxfp4(cu(g["scales_packed"]), cu(g["scales_bytes"])))
+    assert np.array_equal(got, g["scales_decoded"])          # all 256 bytes incl. 0 and 255
+    gb = host(k3.decode_mxfp4(cu(g["scales_packed"]), cu(g["scales_bytes"]), out_dtype=torch.bfloat16))
+    assert np.array_equal(gb[1:255], g["scales_decoded"][1:255])   # bf16 lossless on 1..254
+    e = cu(g["scale_bytes_1_254"])
+    assert np.array_equal(host(k3.decode_scale(e)), g["scale_values_1_254"])
+
+
+def test_dequant_full_projection_bit_exact(k3):
+    rng = np.random.default_rng(4)
+    p, s = O.random_mxfp4(rng, 2048, 7168)
+    want = O.decode_mxfp4(p, s)
+    assert np.array_equal(host(k3.decode_mxfp4(cu(p), cu(s))), want)
+    assert np.array_equal(host(k3.decode_mxfp4(cu(p), cu(s), out_dtype=torch.bfloat16)), want)
+
+
+def test_scale_guard(k3):
+    k3.assert_scales_representable(cu(np.array([[2, 127, 252]], np.uint8)))
+    with pytest.raises(ValueError):
+        k3.assert_scales_representable(cu(np.array([[2, 253]], np.uint8)))
+
+
+# -------------------------------------------------------------------- matvec
+
+@pytest.mark.parametrize("M", [1, 2, 4])
+def test_matvec_reference_kernel_gate(k3, M):
+    """``tests/test_mxfp4_kernel.py:42-54``: rng(0) N=128 K=256, rel-max < 1e-6 vs fp64."""
+    g = G.load("matvec_kat")
+    got = host(k3.mxfp4_matvec_fused(cu(g[f"x{M}"]), cu(g["packed"]), cu(g["scales"])))
+    assert O.rel_max(got, g[f"want{M}"]) < 1e-6
+
+
+SHAPES = [  # (M, K, N, x dtype, out dtype)
+    (1, 7168, 2048, "bf16", "f32"),     # config 1 gate/up, M=1
+    (8, 7168, 2048, "bf16", "f32"),     # config 1 gate/up, M=8
+    (1, 2048, 7168, "f32", "f32"),      # config 1 down (fp32 activations)
+    (8, 2048, 7168, "f32", "bf16"),
+    (5, 1024, 512, "bf16", "f32"),      # config 0 gate/up shape
+    (11, 256, 128, "f32", "f32"),       # M > 8: token chunks
+    (2, 96, 100, "f32", "f32"),         # K % 128, N % 64: generic kernel
+    (3, 160, 64, "bf16", "f32"),
+]
+
+
+@pytest.mark.parametrize("M,K,N,xdt,odt", SHAPES)
+def test_matvec_shapes(k3, M, K, N, xdt, odt):
+    rng = np.random.default_rng(M * 1000 + K + N)
+    p, s = O.random_mxfp4(rng, N, K)
+    xf = rng.standard_normal((M, K)).astype(np.float32)
+    if xdt == "bf16":
+        xb = O.f32_to_bf16_bits(xf)
+        x, xf = bf16_cu(xb), O.bf16_bits_to_f32(xb)
+    else:
+        x = cu(xf)
+    out = k3.mxfp4_matvec_fused(x, cu(p), cu(s),
+                                out_dtype=torch.bfloat16 if odt == "bf16" else torch.float32)
+    got = host(out)
+    want = O.matvec_fp64(xf, p, s)
+    if odt == "bf16":
+        assert O.rel_l2(got, want) < 4e-3                        # bf16 output rounding only
+        want_b = O.bf16_bits_to_f32(O.f32_to_bf16_bits(want.astype(np.float32)))
+        assert np.mean(got == want_b) > 0.95
+    else:
+        assert O.rel_l2(got, want) < EXPECTED_REL_L2
+        assert O.rel_max(got, want) < 1e-5
+        assert O.rel_l2(got, O.matvec_fused(xf, p, s)) < EXPECTED_REL_L2
+
+
+def test_matvec_k_mismatch_raises(k3):
+    with pytest.raises(ValueError, match="K mismatch"):
+        k3.mxfp4_matvec_fused(torch.zeros(1, 64, device="cuda"), torch.zeros(4, 16, dtype=torch.uint8, device="cuda"),
+                              torch.zeros(4, 1, dtype=torch.uint8, device="cuda"))
+
+
+def test_expert_projection_1d(k3):
+    g = G.load("matvec_kat")
+    y = k3.expert_projection(cu(g["x1"][0]), cu(g["packed"]), cu(g["scales"]))
+    assert y.shape == (128,) and O.rel_max(host(y)[None], g["want1"]) < 1e-6
+
+
+# ----------------------------------------------------------------- MoE (small)
+
+def _baseline_moe(k3, d, spec):
+    sh = d["shared"]
+
+    def source(layer, e, which):
+        trip = sh if e == "shared" else d["experts"][int(e)]
+        return trip[("w1", "w3", "w2").index(which)]
+
+    E = spec.num_experts
+    H = d["x_bf16"].shape[1]
+    I_ = d["experts"][0][0][0].shape[0]
+    cfg = k3.MoEConfig(hidden_size=H, num_experts=E, num_experts_per_token=spec.top_k,
+                       moe_intermediate_size=I_, routed_expert_hidden_size=H,
+                       routed_scaling_factor=spec.routed_scaling_factor, moe_renormalize=True,
+                       num_shared_experts=1, activation="silu")
+    w = {"gate.weight": bf16_cu(d["gate_bf16"]), "gate.e_score_correction_bias": cu(d["bias"])}
+    return k3.LatentMoE(cfg, 1, w, source)
+
+
+@pytest.mark.parametrize("name", ["moe_small_m1", "moe_small_m5", "moe_small_m8"])
+def test_router_matches_reference(k3, name):
+    d, g, spec, _, _ = G.moe_case(name)
+    moe = _baseline_moe(k3, d, spec)
+    r = moe.route(bf16_cu(d["x_bf16"]))
+    bad, ties = G.index_sets_match(host(r.expert_indices), g["idx_sorted"], g["corrected"], spec.top_k)
+    assert bad == 0 and ties == 0
+    assert np.abs(G.canon_weights(host(r.expert_indices), host(r.expert_weights)) - g["w_canon"]).max() <= 1e-5
+    assert np.abs(host(r.raw_scores) - g["raw"]).max() <= 1e-5
+    assert np.abs(host(r.corrected_scores) - g["corrected"]).max() <= 1e-5
+
+
+@pytest.mark.parametrize("name", ["moe_small_m1", "moe_small_m5", "moe_small_m8"])
+def test_moe_block_matches_reference(k3, name):
+    d, g, spec, _, _ = G.moe_case(name)
+    moe = _baseline_moe(k3, d, spec)
+    x = bf16_cu(d["x_bf16"])
+    y = moe(x)                                               # fused route + experts + shared
+    y2, r = moe(x, return_router=True)                       # route, then experts
+    assert O.rel_l2(host(y), g["y"]) < NORTH_STAR_REL_L2
+    assert O.rel_l2(host(y), g["y"]) < EXPECTED_REL_L2
+    assert O.rel_l2(host(y2), host(y)) < 1e-6
+    bad, ties = G.index_sets_match(host(r.expert_indices), g["idx_sorted"], g["corrected"], spec.top_k)
+    assert bad == 0 and ties == 0
+
+
+def test_config0_expert_ffn(k3):
+    d, g = G.config0()
+    spec = O.MoESpec(num_experts=1, top_k=1, activation="silu")
+    dd = {"x_bf16": d["x_bf16"], "experts": [(d["w1"], d["w3"], d["w2"])], "shared": (d["w1"], d["w3"], d["w2"]),
+          "gate_bf16": np.zeros((1, 1024), np.uint16), "bias": np.zeros(1, np.float32)}
+    moe = _baseline_moe(k3, dd, spec)
+    y = host(moe.expert_forward(bf16_cu(d["x_bf16"]), 0))
+    assert O.rel_l2(y, g["y"]) < NORTH_STAR_REL_L2
+    assert O.rel_l2(y, g["y"]) < EXPECTED_REL_L2
+
+
+def test_latent_moe_matches_reference(k3):
+    d, g, spec, _, latent, shared = G.latent_case()
+    E = spec.num_experts
+    H = d["x_bf16"].shape[1]
+    cfg = k3.MoEConfig(hidden_size=H, num_experts=E, num_experts_per_token=spec.top_k,
+                       moe_intermediate_size=d["experts"][0][0][0].shape[0],
+                       routed_expert_hidden_size=latent["down"].shape[0], routed_scaling_factor=1.0,
+                       situ_beta=4.0, situ_linear_beta=25.0, activation="situ")
+    w = {"gate.weight": bf16_cu(d["gate_bf16"]), "gate.e_score_correction_bias": cu(d["bias"]),
+         "routed_expert_down_proj.weight": cu(latent["down"]), "routed_expert_up_proj.weight": cu(latent["up"]),
+         "routed_expert_norm.weight": cu(latent["norm"]),
+         "shared_experts.gate_proj.weight": cu(shared["gate"]), "shared_experts.up_proj.weight": cu(shared["up"]),
+         "shared_experts.down_proj.weight": cu(shared["down"])}
+    src = lambda L_, e, wh: d["experts"][int(e)][("w1", "w3", "w2").index(wh)]  # noqa: E731
+    moe = k3.LatentMoE(cfg, 1, w, src)
+    assert moe.tiled
+    y, r = moe(bf16_cu(d["x_bf16"]).reshape(1, -1, H), return_router=True)
+    assert y.shape == (1, d["x_bf16"].shape[0], H)
+    assert O.rel_l2(host(y).reshape(-1, H), g["y"]) < NORTH_STAR_REL_L2
+    assert O.rel_l2(host(y).reshape(-1, H), g["y"]) < EXPECTED_REL_L2
+    bad, ties = G.index_sets_match(host(r.expert_indices), g["idx_sorted"], g["corrected"], spec.top_k)
+    assert bad == 0 and ties == 0
+
+
+def test_reference_mini_k3_layer(k3):
+    """Layer 1 of the reference's own synthetic mini-K3 (latent 96, inter 64): shapes the
+    tiled kernels do not cover, so experts run through the generic CUDA matvec."""
+    g, meta, spec, src, latent, shared, gate, bias, experts = G.mini_k3_case()
+    H = int(meta["hidden_size"])
+    cfg = k3.MoEConfig(hidden_size=H, num_experts=spec.num_experts, num_experts_per_token=spec.top_k,
+                       moe_intermediate_size=int(meta["moe_intermediate_size"]),
+                       routed_expert_hidden_size=int(meta["routed_expert_hidden_size"]),
+                       routed_scaling_factor=spec.routed_scaling_factor, moe_renormalize=spec.renormalize,
+                       situ_beta=spec.situ_beta, situ_linear_beta=spec.situ_linear_beta,
+                       rms_norm_eps=spec.rms_norm_eps, activation="situ")
+    w = {"gate.weight": bf16_cu(gate), "gate.e_score_correction_bias": cu(bias),
+         "routed_expert_down_proj.weight": cu(latent["down"]), "routed_expert_up_proj.weight": cu(latent["up"]),
+         "routed_expert_norm.weight": cu(latent["norm"]),
+         "shared_experts.gate_proj.weight": cu(shared["gate"]), "shared_experts.up_proj.weight": cu(shared["up"]),
+         "shared_experts.down_proj.weight": cu(shared["down"])}
+    moe = k3.LatentMoE(cfg, 1, w, lambda L_, e, wh: src(e, wh))
+    assert not moe.tiled
+    y, r = moe(bf16_cu(g["x_bf16"]), return_router=True)
+    assert O.rel_l2(host(y), g["y"]) < NORTH_STAR_REL_L2
+    assert O.rel_l2(host(y), g["y"]) < EXPECTED_REL_L2
+    bad, ties = G.index_sets_match(host(r.expert_indices), g["idx_sorted"], g["corrected"], spec.top_k)
+    assert bad == 0 and ties == 0
+
+
+# ------------------------------------------------- MoE at BASELINE full size
+
+@pytest.fixture(scope="module")
+def full_layer(k3):
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay = synthetic.baseline_layer(seed=123)
+    return lay, lay.moe()
+
+
+def _oracle_layer_output(lay, x_bits_host, idx, w):
+    """C-oracle (reference fused-kernel order) for the selected experts + shared expert."""
+    xf = O.bf16_bits_to_f32(x_bits_host)
+    H = xf.shape[1]
+    y = np.zeros((xf.shape[0], H), np.float64)
+    h = lambda t: t.cpu().numpy()  # noqa: E731
+    for e in sorted(set(idx.reshape(-1).tolist())):
+        tok, slot = np.nonzero(idx == e)
+        (p1, s1), (p3, s3), (p2, s2) = lay.experts[e]
+        g = O.matvec_fused(xf[tok], h(p1), h(s1))
+        u = O.matvec_fused(xf[tok], h(p3), h(s3))
+        out = O.matvec_fused(O.silu(g) * u, h(p2), h(s2))
+        np.add.at(y, tok, out.astype(np.float64) * w[tok, slot][:, None])
+    (p1, s1), (p3, s3), (p2, s2) = lay.shared
+    y += O.matvec_fused(O.silu(O.matvec_fused(xf, h(p1), h(s1))) * O.matvec_fused(xf, h(p3), h(s3)),
+                        h(p2), h(s2))
+    return y
+
+
+@pytest.mark.parametrize("M", [1, 8])
+def test_full_size_decode_layer(k3, full_layer, M):
+    """BASELINE configs[2] at full size (384 + 1 experts, 7168/2048, top-8, x2.5)."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay, moe = full_layer
+    x = synthetic.tokens(1000 + M, M, 7168)
+    y, r = moe(x, return_router=True)
+    yf = moe(x)
+    torch.cuda.synchronize()
+    xb = x.view(torch.uint16).cpu().numpy()
+    rr = O.route(O.bf16_bits_to_f32(xb), host(lay.gate), None, 8, True, 2.5)
+    bad, ties = G.index_sets_match(host(r.expert_indices), np.sort(rr.expert_indices, -1), rr.corrected_scores, 8)
+    assert bad == 0
+    idx, w = host(r.expert_indices), host(r.expert_weights)
+    want = _oracle_layer_output(lay, xb, idx, w)
+    assert O.rel_l2(host(y), want) < NORTH_STAR_REL_L2
+    assert O.rel_l2(host(y), want) < EXPECTED_REL_L2
+    assert torch.equal(y, yf)
+
+
+def test_full_size_decode_deterministic(k3, full_layer):
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    _, moe = full_layer
+    x = synthetic.tokens(77, 8, 7168)
+    a, b = moe(x), moe(x)
+    assert torch.equal(a, b)
