@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--experts", type=int, default=E,
+                    help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -236,7 +238,7 @@ def run_b200(args, rank, world, local):
     torch.cuda.set_device(local)
     M, K, W = args.tokens, args.steps, args.warmup
     nb = K + W
-    lay = synthetic.baseline_layer(seed=args.seed, E=E, H=H, I=I_, top_k=TOPK, scale=SCALE)
+    lay = synthetic.baseline_layer(seed=args.seed, E=args.experts, H=H, I=I_, top_k=TOPK, scale=SCALE)
     moe = lay.moe()
     _ = moe.pool
     xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, M, H) for i in range(nb)]
@@ -289,7 +291,7 @@ def run_b200(args, rank, world, local):
     U_t = U[W:]
     gu_bytes = np.mean([(u + 1) * 2 * PROJ_BYTES for u in U_t]) + M * H * 2
     dn_bytes = np.mean([(u + 1) * PROJ_BYTES for u in U_t])
-    layer_bytes = np.mean([(u + 1) * EXPERT_BYTES for u in U_t]) + ROUTER_BYTES
+    layer_bytes = np.mean([(u + 1) * EXPERT_BYTES for u in U_t]) + args.experts * H * 2
     peak, peak_kind = measured_peaks()
     gu_gbs = gu_bytes / (gu_ms / gu_n / 1e3) / 1e9
     dn_gbs = dn_bytes / (dn_ms / dn_n / 1e3) / 1e9
@@ -328,7 +330,7 @@ def run_b200(args, rank, world, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "e2m1+f16 mma, f32 accumulate",
         "data": "synthetic (seeded random-init weights of the BASELINE layer)",
         "config": {"workload": f"BASELINE configs[2]: one MoE layer decode, M={M} tokens per GPU, "
-                               "384 routed + 1 shared MXFP4 expert (7168/2048), bf16 router, "
+                               f"{args.experts} routed + 1 shared MXFP4 expert (7168/2048), bf16 router, "
                                "top-8, x2.5",
                    "tokens_per_gpu": M, "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2: 9.0 GB expert pool, fresh token batch per step",

@@ -280,7 +280,8 @@ def test_full_size_decode_layer(k3, full_layer, M):
     want = _oracle_layer_output(lay, xb, idx, w)
     assert O.rel_l2(host(y), want) < NORTH_STAR_REL_L2
     assert O.rel_l2(host(y), want) < EXPECTED_REL_L2
-    assert torch.equal(y, yf)
+    # the fused call sums the shared expert inside the combine, route+experts adds it after
+    assert O.rel_l2(host(yf), host(y)) < 1e-6
 
 
 def test_full_size_decode_deterministic(k3, full_layer):
