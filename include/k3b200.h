@@ -99,6 +99,25 @@ K3_API int k3_mxfp4_matvec(const void* x, int x_dtype, int64_t M, int64_t K,
                            void* out, int out_dtype, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* k3_mxfp4_matvec for callers that cannot allocate device memory. No counterpart in the
+ * reference (its mxfp4_matvec_fused gets its output from MLX's allocator).
+ * Who needs it: a host that hands this path only its own input and output buffers --
+ * e.g. an FFI binding of the three-argument mxfp4_matvec_fused inside a runtime whose
+ * device memory belongs to another allocator (a caching allocator, or a fixed arena
+ * holding the free memory) -- cannot call cudaMalloc: that memory would go behind its
+ * allocator's back or not exist, and cudaMalloc/cudaFree synchronise the device.
+ * This call allocates nothing. Its scratch is one file-scope device array of 4 MiB,
+ * which every GPU that loads this library holds until the process exits; shapes that
+ * need more scratch than that (see k3_mxfp4_matvec_workspace) return K3_ERR_INVALID.
+ * The first call on a device looks the array's address up (cudaGetSymbolAddress, with
+ * that device current); make that first call before any stream capture. Every call
+ * shares the one array, so calls that overlap on the GPU (other streams, other host
+ * threads) race; each call re-initialises what it reads from the array. Arguments and
+ * results are those of k3_mxfp4_matvec. */
+K3_API int k3_mxfp4_matvec_noalloc(const void* x, int x_dtype, int64_t M, int64_t K,
+                                   const uint8_t* packed, const uint8_t* scales, int64_t N,
+                                   void* out, int out_dtype, void* stream);
+
 /* ------------------------------------------------------------------- router --- */
 
 /* Sigmoid top-k router of LatentMoE.route (air_llm/models/kimi_k3/moe.py:65-76;

@@ -48,6 +48,7 @@ SIGNATURES = {
     "k3_mxfp4_scale_minmax": (_i32, [_vp, _i64, _vp, _vp]),
     "k3_mxfp4_matvec_workspace": (_sz, [_i64, _i64, _i64]),
     "k3_mxfp4_matvec": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp, _sz, _vp]),
+    "k3_mxfp4_matvec_noalloc": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),
     "k3_moe_route_workspace": (_sz, [_i64, _i64]),
     "k3_moe_route": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _i32, _i32, _f32, _vp, _vp,
                             _vp, _vp, _vp, _sz, _vp]),
