@@ -149,6 +149,20 @@ typedef struct k3_expert_ptrs {
     const uint8_t* w2_scales;
 } k3_expert_ptrs;
 
+/* Optional contiguous expert pools (device pointers): slot e holds expert e, slot E the
+ * shared expert. w1/w3 packed [slots][I][H/2], scales [slots][I][H/32]; w2 packed
+ * [slots][H][I/2], scales [slots][H][I/32]. With a pool (and H, I multiples of 512) the
+ * decode runs on the TMA-fed kernels; without one, on the pointer-table kernels. */
+typedef struct k3_expert_pool {
+    const uint8_t* w1_packed;
+    const uint8_t* w1_scales;
+    const uint8_t* w3_packed;
+    const uint8_t* w3_scales;
+    const uint8_t* w2_packed;
+    const uint8_t* w2_scales;
+    int64_t num_slots;
+} k3_expert_pool;
+
 /* Static description of one MoE layer's expert set (host struct). */
 typedef struct k3_moe_params {
     int64_t hidden;               /* H: w1/w3 input dim, w2 output dim               */
@@ -163,6 +177,7 @@ typedef struct k3_moe_params {
     float situ_beta;              /* situ only (air_llm/models/kimi_k3/ops.py:17-28)  */
     float situ_linear_beta;       /* situ only; <= 0 means None                      */
     const k3_expert_ptrs* experts;/* DEVICE array [E + has_shared]                   */
+    const k3_expert_pool* pool;   /* HOST pointer to pool descriptors, or NULL       */
 } k3_moe_params;
 
 /* Decode (M <= 8 tokens) MoE block without the latent wrapper: route, then for every

@@ -28,13 +28,18 @@ class K3ExpertPtrs(ctypes.Structure):
                                                "w2_packed", "w2_scales")]
 
 
+class K3ExpertPool(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("w1_packed", "w1_scales", "w3_packed", "w3_scales",
+                                               "w2_packed", "w2_scales")] + [("num_slots", ctypes.c_int64)]
+
+
 class K3MoEParams(ctypes.Structure):
     _fields_ = [("hidden", ctypes.c_int64), ("inter", ctypes.c_int64),
                 ("num_experts", ctypes.c_int64), ("top_k", ctypes.c_int32),
                 ("renormalize", ctypes.c_int32), ("routed_scaling_factor", ctypes.c_float),
                 ("has_shared", ctypes.c_int32), ("activation", ctypes.c_int32),
                 ("situ_beta", ctypes.c_float), ("situ_linear_beta", ctypes.c_float),
-                ("experts", ctypes.c_void_p)]
+                ("experts", ctypes.c_void_p), ("pool", ctypes.POINTER(K3ExpertPool))]
 
 
 # name -> (restype, argtypes); mirrors include/k3b200.h

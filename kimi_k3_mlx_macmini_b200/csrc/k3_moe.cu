@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "k3_moe.cuh"
+#include "k3_tma.cuh"
 
 namespace k3 {
 
@@ -23,8 +24,9 @@ namespace k3 {
 
 // logits[m][e] = sum_k x[m][k] * W[e][k] for m < Mc (<= 8): one warp per expert row,
 // lanes walk 8-element chunks, fp32 fma in chunk order, then a xor-tree reduction.
+// (Generic form for H % 64 != 0; router_logits_kernel below is the fast form.)
 template <int XDT>
-__global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, int Mc,
+__global__ void __launch_bounds__(256) router_logits_rowwarp_kernel(const void* __restrict__ x, int Mc,
                                                             int64_t H,
                                                             const uint16_t* __restrict__ W,
                                                             int64_t E, float* __restrict__ logits) {
@@ -75,6 +77,89 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
             const float s = warp_sum(acc[m]);
             if (lane == 0) logits[int64_t(m) * E + e] = s;
         }
+    }
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float (&f)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        f[2 * j] = __uint_as_float(w[j] << 16);
+        f[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+}
+
+// logits[m][e] = sum_k x[m][k] * W[e][k], m < Mc (<= 8), H % 64 == 0. One CTA per
+// kRouterRows expert rows; its 8 warps each take a contiguous eighth of k, lanes walk
+// 8-element chunks of it (fp32 fma in k order), so every x chunk loaded is used by all
+// rows of the CTA. Lane partials meet in a fixed butterfly reduce-scatter, warp
+// partials in warp order: the result is deterministic.
+constexpr int kRouterRows = 4;
+template <int XDT>
+__global__ void __launch_bounds__(256) router_logits_kernel(const void* __restrict__ x, int Mc,
+                                                            int64_t H,
+                                                            const uint16_t* __restrict__ W,
+                                                            int64_t E, float* __restrict__ logits) {
+    static_assert(kRouterRows * kMaxTok == 32, "one reduced value per lane");
+    __shared__ float part[8][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t e0 = int64_t(blockIdx.x) * kRouterRows;
+    const int64_t slice = H / 8, kb = warp * slice;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+    for (int64_t k = kb + lane * 8; k < kb + slice; k += 256) {
+        float wf[kRouterRows][8];
+#pragma unroll
+        for (int r = 0; r < kRouterRows; ++r) {
+            if (e0 + r < E) {
+                bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(W + (e0 + r) * H + k)), wf[r]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) wf[r][j] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < kMaxTok; ++m) {
+            if (m < Mc) {
+                float xf[8];
+                if (XDT == K3_BF16) {
+                    bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(
+                                      reinterpret_cast<const uint16_t*>(x) + m * H + k)), xf);
+                } else {
+                    const float4* xp =
+                        reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + m * H + k);
+                    const float4 a = __ldg(xp), b = __ldg(xp + 1);
+                    xf[0] = a.x; xf[1] = a.y; xf[2] = a.z; xf[3] = a.w;
+                    xf[4] = b.x; xf[5] = b.y; xf[6] = b.z; xf[7] = b.w;
+                }
+#pragma unroll
+                for (int r = 0; r < kRouterRows; ++r)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[r * kMaxTok + m] = fmaf(xf[j], wf[r][j], v[r * kMaxTok + m]);
+            }
+        }
+    }
+    // butterfly reduce-scatter: after the step with offset o every lane keeps the half
+    // of its values selected by its bit o; lane l ends with the sum of value index l
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const bool upper = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+            const float send = upper ? v[i] : v[i + o];
+            const float keep = upper ? v[i + o] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    part[warp][lane] = v[0];
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        const int r = lane / kMaxTok, m = lane % kMaxTok;
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sum += part[w][lane];
+        if (m < Mc && e0 + r < E) logits[int64_t(m) * E + e0 + r] = sum;
     }
 }
 
@@ -191,26 +276,49 @@ struct PrepArgs {
     __half* xq_hi;
     __half* xq_lo;                 // null when the source is bf16 (hi is exact)
     float* xq_ts;
+    int blocked;                   // pieces in [k/32][8 rows][32] order (TMA kernels);
+                                   // rows M..7 are written as zeros
 };
 
 __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x > 0) {
-        // x[t][k] -> (hi, lo) f16 pieces of x * 2**-e with one exponent per 32-group.
-        const int64_t groups = a.K / 32;
-        const int64_t total = int64_t(a.M) * groups;
-        const int64_t nw = int64_t(gridDim.x - 1) * (blockDim.x >> 5);
-        for (int64_t gw = int64_t(blockIdx.x - 1) * (blockDim.x >> 5) + warp; gw < total; gw += nw) {
-            const int64_t t = gw / groups, g = gw % groups;
-            const int64_t i = t * a.K + g * 32 + lane;
-            const float v = load_as_f32(a.x, a.x_dtype, i);
-            const int e = f16_group_exponent(warp_max(fabsf(v)));
-            __half hi, lo;
-            split_f16(ldexpf(v, -e), hi, lo);
-            a.xq_hi[i] = hi;
-            if (a.xq_lo) a.xq_lo[i] = lo;
-            if (lane == 0) a.xq_ts[t * groups + g] = ldexpf(1.0f, e);
+        // CTA 1+t: x[t][:] -> (hi, lo) f16 pieces of x * 2**-e with one exponent per
+        // token, chosen from the row maximum (the matvec applies 2**e at the end).
+        const int t = blockIdx.x - 1;
+        if (t >= a.M) {
+            if (a.blocked && t < kMaxTok) {
+                for (int64_t i = threadIdx.x; i < a.K; i += blockDim.x) {
+                    const int64_t o = ((i >> 5) * kMaxTok + t) * 32 + (i & 31);
+                    a.xq_hi[o] = __float2half_rn(0.0f);
+                    if (a.xq_lo) a.xq_lo[o] = __float2half_rn(0.0f);
+                }
+            }
+            return;
         }
+        __shared__ float red[8];
+        const int64_t base = int64_t(t) * a.K;
+        float mx = 0.0f;
+        for (int64_t i = threadIdx.x; i < a.K; i += blockDim.x)
+            mx = fmaxf(mx, fabsf(load_as_f32(a.x, a.x_dtype, base + i)));
+        mx = warp_max(mx);
+        if (lane == 0) red[warp] = mx;
+        __syncthreads();
+        mx = red[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+        const int e = f16_group_exponent(mx);
+        const float sc = ldexpf(1.0f, -e);
+        const bool normal_sc = isfinite(sc) && sc >= 1.17549435e-38f;
+        for (int64_t i = threadIdx.x; i < a.K; i += blockDim.x) {
+            const float v = load_as_f32(a.x, a.x_dtype, base + i);
+            __half hi, lo;
+            split_f16(normal_sc ? v * sc : ldexpf(v, -e), hi, lo);
+            const int64_t o = a.blocked ? ((i >> 5) * kMaxTok + t) * 32 + (i & 31) : base + i;
+            a.xq_hi[o] = hi;
+            if (a.xq_lo) a.xq_lo[o] = lo;
+        }
+        if (threadIdx.x == 0) a.xq_ts[t] = ldexpf(1.0f, e);
         return;
     }
     Plan* P = a.plan;
@@ -360,11 +468,16 @@ __device__ __forceinline__ float apply_act(int kind, float g, float u, float bet
     return g / (1.0f + expf(-g)) * u;
 }
 
-template <bool GATEUP>
+// GATEUP: gate+up items with the activation epilogue; otherwise plain projection items
+// with the combine epilogue. GROUP_TS: the B operand carries one power-of-two scale per
+// (column, 32-group) -- applied per group -- instead of one per column (applied once).
+template <bool GATEUP, bool GROUP_TS, bool HILO>
 __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs a) {
+    using Stage = StageT<HILO>;
+    constexpr int kStages = stages_for<HILO>();
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    Stage* ring = reinterpret_cast<Stage*>(smem_raw + size_t(warp) * kSmemPerWarp);
+    Stage* ring = reinterpret_cast<Stage*>(smem_raw + size_t(warp) * sizeof(Stage) * kStages);
     const Plan* P = a.plan;
     const int n_active = P->n_active;
     const int64_t nRb = GATEUP ? a.rows / 32 : a.rows / kItemRows;
@@ -423,11 +536,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs a) {
             if (j < ncols) {
                 const int64_t row = GATEUP ? P->pair_tok[ps + j] : ps + j;
                 bsrc[i] = a.bh + row * a.K + k0 + (lane & 15) * 8;
-                if (a.hilo) blsrc[i] = a.bl + row * a.K + k0 + (lane & 15) * 8;
+                if (HILO) blsrc[i] = a.bl + row * a.K + k0 + (lane & 15) * 8;
             }
         }
         const float* tssrc = nullptr;
-        {
+        if (GROUP_TS) {
             const int j = lane & 7;
             if (j < ncols) {
                 const int64_t row = GATEUP ? P->pair_tok[ps + j] : ps + j;
@@ -454,10 +567,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs a) {
                 const int j = (lane >> 4) + 2 * i, ch = lane & 15;
                 const int pc = (ch ^ ((j & 1) << 2)) * 8;
                 if (bsrc[i]) cp_async_16_ca(smem_u32(&st.bh[j][pc]), bsrc[i] + s * kStageK);
-                if (blsrc[i]) cp_async_16_ca(smem_u32(&st.bl[j][pc]), blsrc[i] + s * kStageK);
+                if (HILO && blsrc[i]) cp_async_16_ca(smem_u32(&st.bl[j][pc]), blsrc[i] + s * kStageK);
             }
-            if (tssrc) cp_async_4(smem_u32(&st.ts[lane >> 3][lane & 7]), tssrc + s * (kStageK / 32));
-            else st.ts[lane >> 3][lane & 7] = 0.0f;
+            if (GROUP_TS) {
+                if (tssrc) cp_async_4(smem_u32(&st.ts[lane >> 3][lane & 7]), tssrc + s * (kStageK / 32));
+                else st.ts[lane >> 3][lane & 7] = 0.0f;
+            }
         };
 
         float acc[kTiles][4];
@@ -489,9 +604,10 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs a) {
                     XL[h] = make_uint4(0, 0, 0, 0);
                     if (g < ncols) {
                         X[h] = *reinterpret_cast<const uint4*>(&st.bh[g][pc]);
-                        if (a.hilo) XL[h] = *reinterpret_cast<const uint4*>(&st.bl[g][pc]);
+                        if (HILO) XL[h] = *reinterpret_cast<const uint4*>(&st.bl[g][pc]);
                     }
-                    tsv[h] = *reinterpret_cast<const float2*>(&st.ts[G][2 * q]);
+                    if (GROUP_TS) tsv[h] = *reinterpret_cast<const float2*>(&st.ts[G][2 * q]);
+                    else tsv[h] = make_float2(1.0f, 1.0f);
                 }
 #pragma unroll
                 for (int t = 0; t < kTiles; ++t) {
@@ -508,23 +624,44 @@ __global__ void __launch_bounds__(kWarps * 32, 1) gemv_kernel(GemvArgs a) {
                         uint32_t f0, f1, f2, f3, e0, e1, e2, e3;
                         e2m1x8_to_f16x8(h ? R2 : R0, f0, f1, f2, f3);
                         e2m1x8_to_f16x8(h ? R3 : R1, e0, e1, e2, e3);
-                        float tmp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                        mma_f16_16816(tmp, f0, e0, f1, e1, X[h].x, X[h].y);
+                        float tmp[4];
+                        mma_f16_16816_zc(tmp, f0, e0, f1, e1, X[h].x, X[h].y);
                         mma_f16_16816(tmp, f2, e2, f3, e3, X[h].z, X[h].w);
-                        if (a.hilo) {
+                        if (HILO) {
                             mma_f16_16816(tmp, f0, e0, f1, e1, XL[h].x, XL[h].y);
                             mma_f16_16816(tmp, f2, e2, f3, e3, XL[h].z, XL[h].w);
                         }
                         const float rs0 = e8m0_to_f32((swg >> (8 * G)) & 0xffu);
                         const float rs1 = e8m0_to_f32((swg8 >> (8 * G)) & 0xffu);
-                        acc[t][0] = fmaf(rs0 * tsv[h].x, tmp[0], acc[t][0]);
-                        acc[t][1] = fmaf(rs0 * tsv[h].y, tmp[1], acc[t][1]);
-                        acc[t][2] = fmaf(rs1 * tsv[h].x, tmp[2], acc[t][2]);
-                        acc[t][3] = fmaf(rs1 * tsv[h].y, tmp[3], acc[t][3]);
+                        if (GROUP_TS) {
+                            acc[t][0] = fmaf(rs0 * tsv[h].x, tmp[0], acc[t][0]);
+                            acc[t][1] = fmaf(rs0 * tsv[h].y, tmp[1], acc[t][1]);
+                            acc[t][2] = fmaf(rs1 * tsv[h].x, tmp[2], acc[t][2]);
+                            acc[t][3] = fmaf(rs1 * tsv[h].y, tmp[3], acc[t][3]);
+                        } else {
+                            acc[t][0] = fmaf(rs0, tmp[0], acc[t][0]);
+                            acc[t][1] = fmaf(rs0, tmp[1], acc[t][1]);
+                            acc[t][2] = fmaf(rs1, tmp[2], acc[t][2]);
+                            acc[t][3] = fmaf(rs1, tmp[3], acc[t][3]);
+                        }
                     }
                 }
             }
             __syncwarp();
+        }
+
+        if (!GROUP_TS) {                       // one scale per column: apply it once
+            float c0s = 0.0f, c1s = 0.0f;
+            const int c0 = 2 * q;
+            if (c0 < ncols) c0s = a.bts[GATEUP ? P->pair_tok[ps + c0] : ps + c0];
+            if (c0 + 1 < ncols) c1s = a.bts[GATEUP ? P->pair_tok[ps + c0 + 1] : ps + c0 + 1];
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t) {
+                acc[t][0] *= c0s;
+                acc[t][1] *= c1s;
+                acc[t][2] *= c0s;
+                acc[t][3] *= c1s;
+            }
         }
 
         // ---- partial sums to scratch, then the last arrival reduces them
@@ -631,19 +768,22 @@ int choose_split(int64_t base_items, int64_t K, int64_t target) {
     return best;
 }
 
+template <bool G, bool T, bool H>
+int set_smem(const char* what) {
+    return cuda_check(cudaFuncSetAttribute(gemv_kernel<G, T, H>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           int(smem_bytes_for<H>())),
+                      what);
+}
+
 bool smem_configured = false;
 int configure_smem() {
     if (smem_configured) return K3_OK;
-    int rc = cuda_check(cudaFuncSetAttribute(gemv_kernel<true>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             int(kSmemBytes)),
-                        "cudaFuncSetAttribute(gemv gate/up)");
-    if (rc) return rc;
-    rc = cuda_check(cudaFuncSetAttribute(gemv_kernel<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(kSmemBytes)),
-                    "cudaFuncSetAttribute(gemv proj)");
-    if (rc) return rc;
+    if (int rc = set_smem<true, false, false>("cudaFuncSetAttribute(gemv gate/up bf16)")) return rc;
+    if (int rc = set_smem<true, false, true>("cudaFuncSetAttribute(gemv gate/up f32)")) return rc;
+    if (int rc = set_smem<false, true, true>("cudaFuncSetAttribute(gemv down)")) return rc;
+    if (int rc = set_smem<false, false, false>("cudaFuncSetAttribute(gemv matvec bf16)")) return rc;
+    if (int rc = set_smem<false, false, true>("cudaFuncSetAttribute(gemv matvec f32)")) return rc;
     smem_configured = true;
     return K3_OK;
 }
@@ -654,6 +794,33 @@ size_t carve(size_t& off, size_t bytes) {
     return o;
 }
 
+// k-split for the TMA kernels: the smallest divisor C of K/512 for which n_base*C items
+// split into `grid` contiguous ranges keep the longest range within 5% of the mean
+// (else the best balance found).
+int choose_split_tma(int64_t n_base, int64_t K, int64_t grid) {
+    const int64_t nst = K / kTStageK;
+    int best = 1;
+    double best_eff = -1.0;
+    for (int64_t c = 1; c <= nst; ++c) {
+        if (nst % c) continue;
+        const int64_t n = n_base * c;
+        const double eff = double(n) / double(((n + grid - 1) / grid) * grid);
+        if (eff >= 0.95) return int(c);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = int(c);
+        }
+    }
+    return best;
+}
+
+bool pool_usable(const k3_moe_params& p) {
+    const k3_expert_pool* pl = p.pool;
+    return pl && pl->w1_packed && pl->w1_scales && pl->w3_packed && pl->w3_scales &&
+           pl->w2_packed && pl->w2_scales && pl->num_slots >= p.num_experts + (p.has_shared ? 1 : 0) &&
+           p.hidden % kTStageK == 0 && p.inter % kTStageK == 0;
+}
+
 DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
     DecodeLayout L{};
     L.M = M;
@@ -662,17 +829,41 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
     L.E = p.num_experts;
     L.U = std::min<int64_t>(p.num_experts, M * p.top_k) + (p.has_shared ? 1 : 0);
     L.P = M * p.top_k + (p.has_shared ? M : 0);
+    L.tma = pool_usable(p);
+    size_t off = 0;
+    if (L.tma) {
+        // keys: gate/up = (active expert, 64-row block); down = 128-row block of y
+        L.CA = choose_split_tma(L.U * (L.I / 64), L.H, sms);
+        L.CB = choose_split_tma(L.U * (L.H / kTRows), L.I, sms);
+        L.ppad = L.U * kMaxTok;             // rows of the token-space activation tensors
+        L.tspad = L.I / 32;
+        L.plan = carve(off, sizeof(Plan));
+        L.logits = carve(off, sizeof(float) * M * L.E);
+        L.route_idx = carve(off, sizeof(int32_t) * M * p.top_k);
+        L.route_w = carve(off, sizeof(float) * M * p.top_k);
+        L.xq_hi = carve(off, sizeof(__half) * kMaxTok * L.H);
+        L.xq_lo = carve(off, sizeof(__half) * kMaxTok * L.H);
+        L.xq_ts = carve(off, sizeof(float) * kMaxTok);
+        L.act_hi = carve(off, sizeof(__half) * L.ppad * L.I);
+        L.act_lo = carve(off, sizeof(__half) * L.ppad * L.I);
+        L.act_ts = carve(off, sizeof(float) * L.ppad * L.tspad);
+        L.partA = carve(off, sizeof(float) * L.U * (L.I / 64) * L.CA * kMaxTok * kTRows);
+        L.cntA = carve(off, sizeof(unsigned) * L.U * (L.I / 64));
+        L.partB = carve(off, sizeof(float) * (L.H / kTRows) * L.U * L.CB * kMaxTok * kTRows);
+        L.cntB = carve(off, sizeof(unsigned) * (L.H / kTRows));
+        L.total = off;
+        return L;
+    }
     const int64_t target = int64_t(sms) * kWarps * 4;
     L.CA = choose_split(L.U * (L.I / 32), L.H, target);
     L.CB = choose_split(L.U * (L.H / kItemRows), L.I, target);
-    size_t off = 0;
     L.plan = carve(off, sizeof(Plan));
     L.logits = carve(off, sizeof(float) * M * L.E);
     L.route_idx = carve(off, sizeof(int32_t) * M * p.top_k);   // when the caller passes NULL
     L.route_w = carve(off, sizeof(float) * M * p.top_k);
     L.xq_hi = carve(off, sizeof(__half) * kMaxTok * L.H);
     L.xq_lo = carve(off, sizeof(__half) * kMaxTok * L.H);
-    L.xq_ts = carve(off, sizeof(float) * kMaxTok * (L.H / 32));
+    L.xq_ts = carve(off, sizeof(float) * kMaxTok);
     L.act_hi = carve(off, sizeof(__half) * L.P * L.I);
     L.act_lo = carve(off, sizeof(__half) * L.P * L.I);
     L.act_ts = carve(off, sizeof(float) * L.P * (L.I / 32));
@@ -705,15 +896,115 @@ int check_ws(void* ws, size_t bytes, size_t need) {
 
 int launch_router_logits(const void* x, int xdt, int Mc, int64_t H, const uint16_t* W, int64_t E,
                          float* logits, cudaStream_t s) {
-    const int blocks = int((E * 32 + 255) / 256);
     prof_begin(K3_PROF_ROUTER, s);
-    if (xdt == K3_BF16)
-        router_logits_kernel<K3_BF16><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
-    else
-        router_logits_kernel<K3_F32><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+    if (H % 64 == 0) {
+        const int blocks = int((E + kRouterRows - 1) / kRouterRows);
+        if (xdt == K3_BF16)
+            router_logits_kernel<K3_BF16><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+        else
+            router_logits_kernel<K3_F32><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+    } else {
+        const int blocks = int((E * 32 + 255) / 256);
+        if (xdt == K3_BF16)
+            router_logits_rowwarp_kernel<K3_BF16><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+        else
+            router_logits_rowwarp_kernel<K3_F32><<<blocks, 256, 0, s>>>(x, Mc, H, W, E, logits);
+    }
     prof_end(K3_PROF_ROUTER, s);
     K3_CHECK_LAUNCH("router_logits_kernel");
     return K3_OK;
+}
+
+// Tensor maps over a [slots][rows][bytes] pool and its [slots][rows][cols/32] scales.
+int pool_maps(CUtensorMap* wmap, CUtensorMap* smap, const uint8_t* packed, const uint8_t* scales,
+              int64_t rows, int64_t cols, int64_t slots, uint32_t box_rows) {
+    const uint64_t dp[3] = {uint64_t(cols / 2), uint64_t(rows), uint64_t(slots)};
+    const uint64_t sp[2] = {uint64_t(cols / 2), uint64_t(rows * cols / 2)};
+    const uint32_t bp[3] = {128, box_rows, 1};
+    if (int rc = encode_map(wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, packed, dp, sp, bp,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    const uint64_t ds[3] = {uint64_t(cols / 32), uint64_t(rows), uint64_t(slots)};
+    const uint64_t ss[2] = {uint64_t(cols / 32), uint64_t(rows * cols / 32)};
+    const uint32_t bs[3] = {uint32_t(kTGroups), box_rows, 1};
+    return encode_map(smap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, scales, ds, ss, bs,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Map over activation pieces in the blocked [k/32][column][32] layout.
+int blocked_map(CUtensorMap* m, const __half* base, int64_t cols, int64_t K) {
+    const uint64_t d[3] = {32, uint64_t(cols), uint64_t(K / 32)};
+    const uint64_t st[2] = {64, uint64_t(cols) * 64};
+    const uint32_t b[3] = {32, uint32_t(kMaxTok), uint32_t(kTGroups)};
+    return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, d, st, b,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+int decode_tma(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, bool x_hilo, void* y,
+               int ydt, int sms, cudaStream_t s) {
+    const k3_expert_pool& pl = *p->pool;
+    Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
+    __half* act_hi = reinterpret_cast<__half*>(ws + L.act_hi);
+    __half* act_lo = reinterpret_cast<__half*>(ws + L.act_lo);
+    float* act_ts = reinterpret_cast<float*>(ws + L.act_ts);
+
+    TMaps ma{};
+    if (int rc = pool_maps(&ma.wA, &ma.sA, pl.w1_packed, pl.w1_scales, L.I, L.H, pl.num_slots, 64)) return rc;
+    if (int rc = pool_maps(&ma.wB, &ma.sB, pl.w3_packed, pl.w3_scales, L.I, L.H, pl.num_slots, 64)) return rc;
+    if (int rc = blocked_map(&ma.bh, reinterpret_cast<__half*>(ws + L.xq_hi), kMaxTok, L.H)) return rc;
+    if (x_hilo)
+        if (int rc = blocked_map(&ma.bl, reinterpret_cast<__half*>(ws + L.xq_lo), kMaxTok, L.H)) return rc;
+    TArgs ta{};
+    ta.plan = plan;
+    ta.K = L.H;
+    ta.rows = L.I;
+    ta.C = L.CA;
+    ta.status = &plan->status;
+    ta.part = reinterpret_cast<float*>(ws + L.partA);
+    ta.cnt = reinterpret_cast<unsigned*>(ws + L.cntA);
+    ta.maxseg = L.CA;
+    ta.act_hi = act_hi;
+    ta.act_lo = act_lo;
+    ta.act_ts = act_ts;
+    ta.act_rows = L.ppad;
+    ta.act_groups = int(L.tspad);
+    ta.act_kind = p->activation;
+    ta.beta = p->situ_beta;
+    ta.lbeta = p->situ_linear_beta;
+    ta.bts_tok = reinterpret_cast<float*>(ws + L.xq_ts);
+    prof_begin(K3_PROF_GATEUP, s);
+    int rc = launch_tma_gateup(ma, ta, x_hilo, sms, s);
+    prof_end(K3_PROF_GATEUP, s);
+    if (rc) return rc;
+
+    TMaps mb{};
+    if (int rc2 = pool_maps(&mb.wA, &mb.sA, pl.w2_packed, pl.w2_scales, L.H, L.I, pl.num_slots, kTRows)) return rc2;
+    if (int rc2 = blocked_map(&mb.bh, act_hi, L.ppad, L.I)) return rc2;
+    if (int rc2 = blocked_map(&mb.bl, act_lo, L.ppad, L.I)) return rc2;
+    {
+        // [expert*8 + token][group] with the group innermost: x = kg, a multiple of 16 floats
+        const uint64_t d[2] = {uint64_t(L.tspad), uint64_t(L.ppad)};
+        const uint64_t st[1] = {uint64_t(L.tspad) * 4};
+        const uint32_t b[2] = {uint32_t(kTGroups), uint32_t(kMaxTok)};
+        if (int rc2 = encode_map(&mb.bts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, act_ts, d, st, b,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE))
+            return rc2;
+    }
+    TArgs tb{};
+    tb.plan = plan;
+    tb.K = L.I;
+    tb.rows = L.H;
+    tb.C = L.CB;
+    tb.status = &plan->status;
+    tb.part = reinterpret_cast<float*>(ws + L.partB);
+    tb.cnt = reinterpret_cast<unsigned*>(ws + L.cntB);
+    tb.maxseg = int(L.U * L.CB);
+    tb.y = y;
+    tb.y_dtype = ydt;
+    prof_begin(K3_PROF_DOWN, s);
+    rc = launch_tma_proj(mb, tb, true, true, sms, s);
+    prof_end(K3_PROF_DOWN, s);
+    return rc;
 }
 
 // Decode experts given routing; `logits` non-null also runs the top-k inside prep.
@@ -750,14 +1041,18 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M, const
     pa.xq_hi = xq_hi;
     pa.xq_lo = x_hilo ? xq_lo : nullptr;
     pa.xq_ts = xq_ts;
-    const int64_t conv_warps = M * (L.H / 32);
-    const int conv_blocks = int(std::min<int64_t>((conv_warps + 7) / 8, 1024));
+    pa.blocked = L.tma ? 1 : 0;
+    if (L.tma) {
+        pa.n_cntA = L.U * (L.I / 64);
+        pa.n_cntB = L.H / kTRows;
+    }
     prof_begin(K3_PROF_TOPK, s);
-    prep_kernel<<<1 + conv_blocks, 256, 0, s>>>(pa);
+    prep_kernel<<<1 + (L.tma ? kMaxTok : int(M)), 256, 0, s>>>(pa);
     prof_end(K3_PROF_TOPK, s);
     K3_CHECK_LAUNCH("prep_kernel");
 
     const int sms = num_sms();
+    if (L.tma) return decode_tma(p, L, ws, x_hilo, y, ydt, sms, s);
     GemvArgs ga{};
     ga.plan = plan;
     ga.table = p->experts;
@@ -777,7 +1072,10 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M, const
     ga.beta = p->situ_beta;
     ga.lbeta = p->situ_linear_beta;
     prof_begin(K3_PROF_GATEUP, s);
-    gemv_kernel<true><<<sms, kWarps * 32, kSmemBytes, s>>>(ga);
+    if (x_hilo)
+        gemv_kernel<true, false, true><<<sms, kWarps * 32, smem_bytes_for<true>(), s>>>(ga);
+    else
+        gemv_kernel<true, false, false><<<sms, kWarps * 32, smem_bytes_for<false>(), s>>>(ga);
     prof_end(K3_PROF_GATEUP, s);
     K3_CHECK_LAUNCH("gemv_kernel<gate/up>");
 
@@ -797,7 +1095,7 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M, const
     gb.y = y;
     gb.y_dtype = ydt;
     prof_begin(K3_PROF_DOWN, s);
-    gemv_kernel<false><<<sms, kWarps * 32, kSmemBytes, s>>>(gb);
+    gemv_kernel<false, true, true><<<sms, kWarps * 32, smem_bytes_for<true>(), s>>>(gb);
     prof_end(K3_PROF_DOWN, s);
     K3_CHECK_LAUNCH("gemv_kernel<down>");
     return K3_OK;
@@ -810,20 +1108,25 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // Matvec pieces (used by k3_capi.cu's k3_mxfp4_matvec fast path).
 struct MatvecLayout {
     int C;
+    bool tma;
     size_t plan, xq_hi, xq_lo, xq_ts, part, cnt, total;
 };
 
 MatvecLayout matvec_layout(int64_t M, int64_t K, int64_t N, int sms) {
     MatvecLayout L{};
     const int64_t Mc = std::min<int64_t>(M, kMaxTok);
-    L.C = choose_split(N / kItemRows, K, int64_t(sms) * kWarps * 4);
+    L.tma = (K % kTStageK == 0) && (N % kTRows == 0);
+    L.C = L.tma ? choose_split_tma(N / kTRows, K, sms)
+                : choose_split(N / kItemRows, K, int64_t(sms) * kWarps * 4);
+    const int64_t xrows = L.tma ? kMaxTok : Mc;
     size_t off = 0;
     L.plan = carve(off, sizeof(Plan));
-    L.xq_hi = carve(off, sizeof(__half) * Mc * K);
-    L.xq_lo = carve(off, sizeof(__half) * Mc * K);
-    L.xq_ts = carve(off, sizeof(float) * Mc * (K / 32));
-    L.part = carve(off, sizeof(float) * L.C * Mc * N);
-    L.cnt = carve(off, sizeof(unsigned) * (N / kItemRows));
+    L.xq_hi = carve(off, sizeof(__half) * xrows * K);
+    L.xq_lo = carve(off, sizeof(__half) * xrows * K);
+    L.xq_ts = carve(off, sizeof(float) * kMaxTok);
+    L.part = carve(off, L.tma ? sizeof(float) * (N / kTRows) * L.C * kMaxTok * kTRows
+                              : sizeof(float) * L.C * Mc * N);
+    L.cnt = carve(off, sizeof(unsigned) * (N / (L.tma ? kTRows : kItemRows)));
     L.total = off;
     return L;
 }
@@ -858,12 +1161,37 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
         pa.xq_hi = reinterpret_cast<__half*>(ws + L.xq_hi);
         pa.xq_lo = hilo ? reinterpret_cast<__half*>(ws + L.xq_lo) : nullptr;
         pa.xq_ts = reinterpret_cast<float*>(ws + L.xq_ts);
-        const int64_t conv_warps = int64_t(Mc) * (K / 32);
-        const int conv_blocks = int(std::min<int64_t>((conv_warps + 7) / 8, 1024));
+        pa.blocked = L.tma ? 1 : 0;
+        if (L.tma) pa.n_cntB = N / kTRows;
         prof_begin(K3_PROF_TOPK, s);
-        prep_kernel<<<1 + conv_blocks, 256, 0, s>>>(pa);
+        prep_kernel<<<1 + (L.tma ? kMaxTok : Mc), 256, 0, s>>>(pa);
         prof_end(K3_PROF_TOPK, s);
         K3_CHECK_LAUNCH("prep_kernel(matvec)");
+        if (L.tma) {
+            TMaps mm{};
+            if (int rc2 = pool_maps(&mm.wA, &mm.sA, packed, scales, N, K, 1, kTRows)) return rc2;
+            if (int rc2 = blocked_map(&mm.bh, pa.xq_hi, kMaxTok, K)) return rc2;
+            if (hilo)
+                if (int rc2 = blocked_map(&mm.bl, reinterpret_cast<__half*>(ws + L.xq_lo), kMaxTok, K)) return rc2;
+            TArgs ta{};
+            ta.plan = pa.plan;
+            ta.matvec = 1;
+            ta.K = K;
+            ta.rows = N;
+            ta.C = L.C;
+            ta.part = reinterpret_cast<float*>(ws + L.part);
+            ta.cnt = pa.cntB;
+            ta.maxseg = L.C;
+            ta.status = &pa.plan->status;
+            ta.bts_tok = pa.xq_ts;
+            ta.y = static_cast<uint8_t*>(out) + size_t(m0) * N * osz;
+            ta.y_dtype = odt;
+            prof_begin(K3_PROF_MATVEC, s);
+            const int rc2 = launch_tma_proj(mm, ta, hilo, false, sms, s);
+            prof_end(K3_PROF_MATVEC, s);
+            if (rc2) return rc2;
+            continue;
+        }
         GemvArgs g{};
         g.plan = pa.plan;
         g.mat_packed = packed;
@@ -881,7 +1209,10 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
         g.y = static_cast<uint8_t*>(out) + size_t(m0) * N * osz;
         g.y_dtype = odt;
         prof_begin(K3_PROF_MATVEC, s);
-        gemv_kernel<false><<<sms, kWarps * 32, kSmemBytes, s>>>(g);
+        if (hilo)
+            gemv_kernel<false, false, true><<<sms, kWarps * 32, smem_bytes_for<true>(), s>>>(g);
+        else
+            gemv_kernel<false, false, false><<<sms, kWarps * 32, smem_bytes_for<false>(), s>>>(g);
         prof_end(K3_PROF_MATVEC, s);
         K3_CHECK_LAUNCH("gemv_kernel<matvec>");
     }

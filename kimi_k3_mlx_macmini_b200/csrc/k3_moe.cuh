@@ -31,23 +31,33 @@ constexpr int kWarps = 8;          // warps per CTA; every warp runs its own ite
 constexpr int kTiles = 4;          // m16 row tiles per item -> 64 weight rows
 constexpr int kItemRows = 16 * kTiles;
 constexpr int kStageK = 128;       // k per pipeline stage: 64 packed bytes per row
-constexpr int kStages = 3;         // cp.async ring depth per warp
-
-struct Stage {
-    uint8_t w[kTiles][16][64];     // packed rows, 16-byte chunks XOR-swizzled
-    uint8_t s[kTiles][16][4];      // E8M0 scales of the stage's 4 groups per row
-    __half bh[kMaxTok][kStageK];   // B operand hi pieces, per column (swizzled chunks)
-    __half bl[kMaxTok][kStageK];   // B operand lo pieces (fp32 sources only)
-    float ts[4][kMaxTok];          // B group scale 2**e, [group][column]
+// Pipeline stage of one warp: 64 packed bytes (128 k) of each of its 64 weight rows,
+// their scales, and the B operand pieces of the same k range. HILO stages also carry
+// the lo pieces of fp32 activations; bf16 activations need only the hi piece, which
+// leaves room for a deeper ring.
+template <bool HILO>
+struct StageT {
+    uint8_t w[kTiles][16][64];                         // packed rows, XOR-swizzled chunks
+    uint8_t s[kTiles][16][4];                          // E8M0 scales of the 4 groups per row
+    __half bh[kMaxTok][kStageK];                       // B hi pieces (swizzled chunks)
+    __half bl[HILO ? kMaxTok : 1][HILO ? kStageK : 8]; // B lo pieces
+    float ts[4][kMaxTok];                              // B group scale 2**e, [group][column]
 };
-static_assert(sizeof(Stage) % 16 == 0, "stage must keep 16-byte alignment");
-constexpr size_t kSmemPerWarp = sizeof(Stage) * kStages;
-constexpr size_t kSmemBytes = kSmemPerWarp * kWarps;
+static_assert(sizeof(StageT<true>) % 16 == 0 && sizeof(StageT<false>) % 16 == 0,
+              "stages must keep 16-byte alignment");
+template <bool HILO>
+constexpr int stages_for() { return HILO ? 3 : 4; }
+template <bool HILO>
+constexpr size_t smem_bytes_for() { return sizeof(StageT<HILO>) * stages_for<HILO>() * kWarps; }
+static_assert(smem_bytes_for<true>() <= 227 * 1024 && smem_bytes_for<false>() <= 227 * 1024,
+              "ring exceeds shared memory");
 
 // Workspace layout of the decode calls; every region is 256-byte aligned.
 struct DecodeLayout {
     int64_t M, H, I, E, U, P;      // tokens, hidden, inter, experts, max active, max pairs
     int CA, CB;                    // k-chunks of the gate/up and down phases
+    bool tma;                      // TMA-fed kernels over contiguous expert pools
+    int64_t ppad, tspad;           // column strides of the blocked activation buffers
     size_t plan, logits, route_idx, route_w, xq_hi, xq_lo, xq_ts, act_hi, act_lo, act_ts, partA, cntA, partB,
         cntB, total;
 };

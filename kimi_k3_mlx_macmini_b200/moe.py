@@ -20,6 +20,7 @@ into a device pointer table that the fused kernels index. Activation: ``cfg.acti
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable, Optional
 
@@ -79,8 +80,13 @@ def _as_device(a, device, dtype=None) -> torch.Tensor:
 
 
 class ExpertPool:
-    """HBM-resident MXFP4 expert weights of one layer plus the device pointer table
-    (``k3_expert_ptrs[E (+1 shared)]``) the fused kernels read.
+    """HBM-resident MXFP4 expert weights of one layer.
+
+    Each projection kind lives in one contiguous pool -- w1/w3 packed ``[slots][I][H/2]``
+    and scales ``[slots][I][H/32]``, w2 packed ``[slots][H][I/2]`` and scales
+    ``[slots][H][I/32]`` -- with slot e = expert e and slot E = the shared expert. The
+    pools feed the TMA kernels (``k3_expert_pool``); a device pointer table
+    (``k3_expert_ptrs[slots]``) into the same memory feeds the generic kernels.
 
     ``expert_source(layer, e, which) -> (packed, scales)`` is called once per projection
     (the reference calls it on every use, ``moe.py:86``). Scale ranges are checked at
@@ -91,34 +97,45 @@ class ExpertPool:
                  with_shared: bool, check_scales: bool = True):
         self.layer, self.E, self.device = layer, num_experts, torch.device(device)
         self.with_shared = with_shared
-        self.tensors: list[tuple] = []
         ids = list(range(num_experts)) + ([SHARED] if with_shared else [])
-        lo, hi = 255, 0
-        for e in ids:
-            trip = []
-            for which in WHICH:
-                p, s = expert_source(layer, e, which)
-                p, s = _as_device_u8(p, self.device), _as_device_u8(s, self.device)
-                if check_scales:
-                    a, b = scale_minmax(s)
-                    lo, hi = min(lo, a), max(hi, b)
-                trip.append((p, s))
-            self.tensors.append(tuple(trip))
-        if check_scales and (lo < 2 or hi > 252):
-            raise ValueError(f"Unsupported MXFP4 scale range {lo}..{hi}; require 2..252 "
-                             "to avoid Metal subnormal flushing, overflow, and E8M0 NaN")
+        self.slots = len(ids)
+        self.pools = None
+        for i, e in enumerate(ids):
+            trip = [expert_source(layer, e, which) for which in WHICH]
+            if self.pools is None:
+                self.pools = [(torch.empty((self.slots, *np.shape(pk)), dtype=torch.uint8, device=self.device),
+                               torch.empty((self.slots, *np.shape(sc)), dtype=torch.uint8, device=self.device))
+                              for pk, sc in trip]
+            for (pp, sp), (pk, sc) in zip(self.pools, trip):
+                if tuple(np.shape(pk)) != tuple(pp.shape[1:]) or tuple(np.shape(sc)) != tuple(sp.shape[1:]):
+                    raise ValueError(f"expert {e}: projection shape {tuple(np.shape(pk))} differs from expert 0")
+                pp[i].copy_(_as_device_u8(pk, self.device))
+                sp[i].copy_(_as_device_u8(sc, self.device))
+        if check_scales:
+            lo, hi = 255, 0
+            for _, sp in self.pools:
+                a, b = scale_minmax(sp)
+                lo, hi = min(lo, a), max(hi, b)
+            if lo < 2 or hi > 252:
+                raise ValueError(f"Unsupported MXFP4 scale range {lo}..{hi}; require 2..252 "
+                                 "to avoid Metal subnormal flushing, overflow, and E8M0 NaN")
+        self.tensors = [tuple((pp[i], sp[i]) for pp, sp in self.pools) for i in range(self.slots)]
         table = torch.tensor([[t.data_ptr() for pair in trip for t in pair] for trip in self.tensors],
                              dtype=torch.int64)
         self.table = table.to(self.device)
-        g1, s1 = self.tensors[0][0]
-        self.inter, self.hidden = g1.shape[0], g1.shape[1] * 2
+        (w1p, w1s), (w3p, w3s), (w2p, w2s) = self.pools
+        self.desc = L.K3ExpertPool(w1_packed=w1p.data_ptr(), w1_scales=w1s.data_ptr(),
+                                   w3_packed=w3p.data_ptr(), w3_scales=w3s.data_ptr(),
+                                   w2_packed=w2p.data_ptr(), w2_scales=w2s.data_ptr(),
+                                   num_slots=self.slots)
+        self.inter, self.hidden = w1p.shape[1], w1p.shape[2] * 2
 
     def get(self, e, which: str):
         i = self.E if e == SHARED else int(e)
         return self.tensors[i][WHICH.index(which)]
 
     def nbytes(self) -> int:
-        return sum(t.numel() for trip in self.tensors for pair in trip for t in pair)
+        return sum(pp.numel() + sp.numel() for pp, sp in self.pools)
 
 
 class LatentMoE:
@@ -149,6 +166,8 @@ class LatentMoE:
             self.sh_down = _as_device(w["shared_experts.down_proj.weight"], self.device, torch.float32)
         self.mxfp4_shared = (not self.dense_shared) and getattr(cfg, "num_shared_experts", 0) > 0
         self._pool: Optional[ExpertPool] = None
+        # the contiguous pools feed the TMA kernels; False forces the pointer-table kernels
+        self.use_pool = True
 
     # ------------------------------------------------------------------ plumbing
     @property
@@ -180,7 +199,8 @@ class LatentMoE:
             activation=L.K3_ACT_SITU if self.act == "situ" else L.K3_ACT_SILU,
             situ_beta=float(getattr(c, "situ_beta", 4.0)),
             situ_linear_beta=-1.0 if lb is None else float(lb),
-            experts=pool.table.data_ptr())
+            experts=pool.table.data_ptr(),
+            pool=ctypes.pointer(pool.desc) if self.use_pool else None)
 
     def _experts_decode(self, h: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
                         params: L.K3MoEParams) -> torch.Tensor:

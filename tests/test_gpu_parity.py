@@ -290,3 +290,18 @@ def test_full_size_decode_deterministic(k3, full_layer):
     x = synthetic.tokens(77, 8, 7168)
     a, b = moe(x), moe(x)
     assert torch.equal(a, b)
+
+
+def test_full_size_pool_and_table_paths_agree(k3, full_layer):
+    """The TMA kernels (contiguous pools) and the pointer-table kernels compute the same
+    layer; only the k-chunking and summation order differ."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    _, moe = full_layer
+    for M in (1, 8):
+        x = synthetic.tokens(4242 + M, M, 7168)
+        moe.use_pool = True
+        a = moe(x)
+        moe.use_pool = False
+        b = moe(x)
+        moe.use_pool = True
+        assert O.rel_l2(host(a), host(b)) < 1e-6
