@@ -281,6 +281,8 @@ def run_b200(args, rank, world, local):
     L.profile_enable(True)
     L.profile_collect()
     torch.cuda.synchronize()
+    # keep the GPU busy while the host enqueues, so each event pair brackets device time
+    torch.cuda._sleep(int(4e7))
     for i in range(W, nb):
         moe(xs[i])
     torch.cuda.synchronize()
@@ -347,7 +349,7 @@ def run_b200(args, rank, world, local):
         "e2e": {"value": world * M / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
                 "ms_per_step": e2e_ms, "api": "LatentMoE.__call__ (k3_moe_decode)"},
-        "gpu_launches": 4 * K,
+        "gpu_launches": int(sum(c for _, c in prof.values())),
         "clocks": clocks,
         "cpu_baseline": cpu,
     }

@@ -16,7 +16,9 @@
 #include <vector>
 
 #include "k3_moe.cuh"
+#include "k3_plan.cuh"
 #include "k3_tma.cuh"
+#include "k3_route.cuh"
 
 namespace k3 {
 
@@ -163,81 +165,6 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const void* __restri
     }
 }
 
-// Top-k of one token's row by one warp: raw = sigmoid(logit), corrected = raw + bias;
-// k rounds of a warp argmax on (corrected desc, index asc); weights gathered from raw.
-__device__ void topk_row(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
-                         int k, int renorm, float scale, int32_t* __restrict__ idx_out,
-                         float* __restrict__ w_out, float* __restrict__ raw_out,
-                         float* __restrict__ cor_out, int lane, int* status) {
-    float raw[32], cor[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E) {
-            const float l = lrow[e];
-            const float r = 1.0f / (1.0f + expf(-l));
-            const float c = r + (bias ? bias[e] : 0.0f);
-            raw[i] = r;
-            cor[i] = c;
-            if (raw_out) raw_out[e] = r;
-            if (cor_out) cor_out[e] = c;
-        } else {
-            raw[i] = 0.0f;
-            cor[i] = -INFINITY;
-        }
-    }
-    float wsel[kMaxTopK > 32 ? kMaxTopK : 32];
-    int isel[kMaxTopK > 32 ? kMaxTopK : 32];
-    for (int s = 0; s < 32; ++s) {
-        if (s >= k) break;
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int e = lane + 32 * i;
-            if (e < E && (cor[i] > bv || (cor[i] == bv && e < bi))) {
-                bv = cor[i];
-                bi = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (bi >= E) {            // only NaN rows get here: report, pick a valid index
-            if (lane == 0) atomicExch(status, K3_ERR_INVALID);
-            bi = 0;
-        }
-        // the owner lane reads the raw score and retires the entry: a NaN never compares
-        // greater or equal, so it cannot win again even when every other entry is -inf
-        float mine = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            if (lane + 32 * i == bi) {
-                mine = raw[i];
-                cor[i] = __int_as_float(0x7fc00000u);
-            }
-        }
-        wsel[s] = __shfl_sync(0xffffffffu, mine, bi & 31);
-        isel[s] = bi;
-    }
-    // w / (sum + 1e-20) then * scale, as moe.py:74-76 / k3ref/layers.py:221-224
-    float sum = 0.0f;
-    for (int s = 0; s < k; ++s) sum += wsel[s];
-    const float den = sum + 1e-20f;
-    if (lane == 0) {
-        for (int s = 0; s < k; ++s) {
-            idx_out[s] = isel[s];
-            w_out[s] = ((k > 1 && renorm) ? wsel[s] / den : wsel[s]) * scale;
-        }
-    }
-}
-
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int M, int E,
                                                    const float* __restrict__ bias, int k, int renorm,
                                                    float scale, int32_t* __restrict__ idx,
@@ -254,20 +181,10 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
 // ==================================================================== prep
 
 struct PrepArgs {
-    // routing (CTA 0)
-    int mode;                      // 0: plan from idx/w; 1: identity plan (matvec)
-    const float* logits;           // non-null: run the top-k first (writes idx/w)
-    const float* bias;
-    int E, k, renorm;
-    float scale;
-    int32_t* idx;
-    float* w;
-    int has_shared;
-    Plan* plan;
-    unsigned* cntA;
-    int64_t n_cntA;
-    unsigned* cntB;
-    int64_t n_cntB;
+    int mode;                      // 0: plan from idx/w (after a top-k when logits != null);
+                                   // 1: identity plan (matvec)
+    const float* logits;
+    PlanArgs pl;
     // activation conversion (CTAs >= 1)
     const void* x;
     int x_dtype;
@@ -276,26 +193,23 @@ struct PrepArgs {
     __half* xq_hi;
     __half* xq_lo;                 // null when the source is bf16 (hi is exact)
     float* xq_ts;
-    int blocked;                   // pieces in [k/32][8 rows][32] order (TMA kernels);
-                                   // rows M..7 are written as zeros
+    int blocked;                   // blocked pieces with one exponent per (token, 512-k)
+                                   // block, rows M..7 zeros (TMA kernels); else row-major
+                                   // with one exponent per token (generic kernels)
 };
 
 __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x > 0) {
-        // CTA 1+t: x[t][:] -> (hi, lo) f16 pieces of x * 2**-e with one exponent per
-        // token, chosen from the row maximum (the matvec applies 2**e at the end).
-        const int t = blockIdx.x - 1;
-        if (t >= a.M) {
-            if (a.blocked && t < kMaxTok) {
-                for (int64_t i = threadIdx.x; i < a.K; i += blockDim.x) {
-                    const int64_t o = ((i >> 5) * kMaxTok + t) * 32 + (i & 31);
-                    a.xq_hi[o] = __float2half_rn(0.0f);
-                    if (a.xq_lo) a.xq_lo[o] = __float2half_rn(0.0f);
-                }
-            }
+        if (a.blocked) {                   // CTA 1+kb: block kb of every token (warp t)
+            const int64_t kb = blockIdx.x - 1;
+            if (kb < a.K / 512)
+                convert_block(a.x, a.x_dtype, a.M, a.K, warp, kb, a.xq_hi, a.xq_lo, a.xq_ts, lane);
             return;
         }
+        // CTA 1+t: x[t][:] -> (hi, lo) f16 pieces of x * 2**-e, one exponent per token
+        const int t = blockIdx.x - 1;
+        if (t >= a.M) return;
         __shared__ float red[8];
         const int64_t base = int64_t(t) * a.K;
         float mx = 0.0f;
@@ -314,121 +228,14 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
             const float v = load_as_f32(a.x, a.x_dtype, base + i);
             __half hi, lo;
             split_f16(normal_sc ? v * sc : ldexpf(v, -e), hi, lo);
-            const int64_t o = a.blocked ? ((i >> 5) * kMaxTok + t) * 32 + (i & 31) : base + i;
-            a.xq_hi[o] = hi;
-            if (a.xq_lo) a.xq_lo[o] = lo;
+            a.xq_hi[base + i] = hi;
+            if (a.xq_lo) a.xq_lo[base + i] = lo;
         }
         if (threadIdx.x == 0) a.xq_ts[t] = ldexpf(1.0f, e);
         return;
     }
-    Plan* P = a.plan;
-    __shared__ uint32_t bitmap[kMaxExperts / 32];
-    __shared__ int cnt[kMaxActive];
-    __shared__ int n_routed;
-    if (threadIdx.x == 0) P->status = K3_OK;
-    for (int64_t i = threadIdx.x; i < a.n_cntA; i += blockDim.x) a.cntA[i] = 0;
-    for (int64_t i = threadIdx.x; i < a.n_cntB; i += blockDim.x) a.cntB[i] = 0;
-    if (a.mode == 1) {                             // matvec: one "expert", pairs = tokens
-        if (threadIdx.x == 0) {
-            P->M = a.M;
-            P->n_active = 1;
-            P->n_pairs = a.M;
-            P->expert[0] = 0;
-            P->pair_start[0] = 0;
-            P->pair_start[1] = a.M;
-        }
-        for (int t = threadIdx.x; t < a.M; t += blockDim.x) {
-            P->pair_tok[t] = t;
-            P->pair_w[t] = 1.0f;
-        }
-        return;
-    }
-    __syncthreads();
-    if (a.logits && warp < a.M) {
-        topk_row(a.logits + int64_t(warp) * a.E, a.bias, a.E, a.k, a.renorm, a.scale,
-                 a.idx + warp * a.k, a.w + warp * a.k, nullptr, nullptr, lane, &P->status);
-    }
-    for (int i = threadIdx.x; i < kMaxExperts / 32; i += blockDim.x) bitmap[i] = 0;
-    __syncthreads();                               // top-k results and zeroed bitmap visible
-    const int nsel = a.M * a.k;
-    for (int i = threadIdx.x; i < nsel; i += blockDim.x) {
-        const int e = a.idx[i];
-        if (e < 0 || e >= a.E) {
-            P->status = K3_ERR_INVALID;
-            continue;
-        }
-        atomicOr(&bitmap[e >> 5], 1u << (e & 31));
-    }
-    __syncthreads();
-    if (warp == 0) {                               // ascending unique expert list
-        const uint32_t word = bitmap[lane];
-        const int c = __popc(word);
-        int incl = c;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-        }
-        int pos = incl - c;
-        uint32_t wv = word;
-        while (wv) {
-            const int b = __ffs(wv) - 1;
-            wv &= wv - 1;
-            P->expert[pos++] = lane * 32 + b;
-        }
-        if (lane == 31) n_routed = incl;
-    }
-    __syncthreads();
-    const int nr = n_routed;
-    const int na = nr + (a.has_shared ? 1 : 0);
-    for (int u = threadIdx.x; u < na; u += blockDim.x) {
-        int c = 0;
-        if (u < nr) {
-            const int e = P->expert[u];
-            for (int i = 0; i < nsel; ++i) c += (a.idx[i] == e);
-            if (c > kMaxTok) {          // a token listed the same expert twice: invalid routing
-                P->status = K3_ERR_INVALID;
-                c = kMaxTok;
-            }
-        } else {
-            c = a.M;
-            P->expert[u] = a.E;                    // shared expert slot in the table
-        }
-        cnt[u] = c;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int s = 0;
-        for (int u = 0; u < na; ++u) {
-            P->pair_start[u] = s;
-            s += cnt[u];
-        }
-        P->pair_start[na] = s;
-        P->n_active = na;
-        P->n_pairs = s;
-        P->M = a.M;
-    }
-    __syncthreads();
-    for (int u = threadIdx.x; u < na; u += blockDim.x) {
-        int p = P->pair_start[u];
-        if (u < nr) {
-            const int e = P->expert[u];
-            const int pend = P->pair_start[u + 1];
-            for (int t = 0; t < a.M; ++t)
-                for (int s = 0; s < a.k; ++s)
-                    if (a.idx[t * a.k + s] == e && p < pend) {
-                        P->pair_tok[p] = t;
-                        P->pair_w[p] = a.w[t * a.k + s];
-                        ++p;
-                    }
-        } else {
-            for (int t = 0; t < a.M; ++t) {
-                P->pair_tok[p] = t;
-                P->pair_w[p] = 1.0f;
-                ++p;
-            }
-        }
-    }
+    if (a.mode == 1) identity_plan_cta(a.pl);
+    else build_plan_cta(a.pl, a.logits, warp, lane);
 }
 
 // ========================================================== grouped matvec
@@ -843,7 +650,15 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
         L.route_w = carve(off, sizeof(float) * M * p.top_k);
         L.xq_hi = carve(off, sizeof(__half) * kMaxTok * L.H);
         L.xq_lo = carve(off, sizeof(__half) * kMaxTok * L.H);
-        L.xq_ts = carve(off, sizeof(float) * kMaxTok);
+        L.xq_ts = carve(off, sizeof(float) * kMaxTok * (L.H / 512));
+        L.KQ = 1;
+        for (int64_t c = 1; c <= L.H / 512; ++c) {        // router k-slices: >= one CTA per SM
+            if ((L.H / 512) % c) continue;
+            L.KQ = int(c);
+            if (((L.E + 15) / 16) * c >= sms) break;
+        }
+        L.logit_part = carve(off, sizeof(float) * L.KQ * M * L.E);
+        L.route_done = carve(off, sizeof(unsigned) * (1 + (L.E + 15) / 16));
         L.act_hi = carve(off, sizeof(__half) * L.ppad * L.I);
         L.act_lo = carve(off, sizeof(__half) * L.ppad * L.I);
         L.act_ts = carve(off, sizeof(float) * L.ppad * L.tspad);
@@ -982,10 +797,10 @@ int decode_tma(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, bool 
     if (int rc2 = blocked_map(&mb.bh, act_hi, L.ppad, L.I)) return rc2;
     if (int rc2 = blocked_map(&mb.bl, act_lo, L.ppad, L.I)) return rc2;
     {
-        // [expert*8 + token][group] with the group innermost: x = kg, a multiple of 16 floats
-        const uint64_t d[2] = {uint64_t(L.tspad), uint64_t(L.ppad)};
-        const uint64_t st[1] = {uint64_t(L.tspad) * 4};
-        const uint32_t b[2] = {uint32_t(kTGroups), uint32_t(kMaxTok)};
+        // [group][expert*8 + token] with the column innermost: x = 8u, a multiple of 8 floats
+        const uint64_t d[2] = {uint64_t(L.ppad), uint64_t(L.tspad)};
+        const uint64_t st[1] = {uint64_t(L.ppad) * 4};
+        const uint32_t b[2] = {uint32_t(kMaxTok), uint32_t(kTGroups)};
         if (int rc2 = encode_map(&mb.bts, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, act_ts, d, st, b,
                                  CU_TENSOR_MAP_SWIZZLE_NONE))
             return rc2;
@@ -1008,32 +823,67 @@ int decode_tma(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, bool 
 }
 
 // Decode experts given routing; `logits` non-null also runs the top-k inside prep.
-int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M, const float* logits,
-                const float* bias, int32_t* idx, float* w, void* y, int ydt, uint8_t* ws,
-                const DecodeLayout& L, cudaStream_t s) {
+int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
+                const uint16_t* gate_w, const float* bias, int32_t* idx, float* w, void* y,
+                int ydt, uint8_t* ws, const DecodeLayout& L, cudaStream_t s) {
     int rc = configure_smem();
     if (rc) return rc;
     Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
     __half* xq_hi = reinterpret_cast<__half*>(ws + L.xq_hi);
     __half* xq_lo = reinterpret_cast<__half*>(ws + L.xq_lo);
     float* xq_ts = reinterpret_cast<float*>(ws + L.xq_ts);
+    float* logits = reinterpret_cast<float*>(ws + L.logits);
     const bool x_hilo = (xdt == K3_F32);
+    PlanArgs pl{};
+    pl.bias = bias;
+    pl.E = int(p->num_experts);
+    pl.k = p->top_k;
+    pl.renorm = p->renormalize;
+    pl.scale = p->routed_scaling_factor;
+    pl.idx = idx;
+    pl.w = w;
+    pl.has_shared = p->has_shared;
+    pl.plan = plan;
+    pl.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
+    pl.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
+    pl.n_cntA = L.tma ? L.U * (L.I / 64) : L.U * (L.I / 32);
+    pl.n_cntB = L.tma ? L.H / kTRows : L.H / kItemRows;
+    pl.M = int(M);
+    const int sms = num_sms();
+
+    if (L.tma && gate_w) {
+        // one launch: router logits + x conversion + (last CTA) top-k and plan
+        RouteArgs ra{};
+        ra.x = x;
+        ra.x_dtype = xdt;
+        ra.M = int(M);
+        ra.H = L.H;
+        ra.W = gate_w;
+        ra.E = L.E;
+        ra.logit_part = reinterpret_cast<float*>(ws + L.logit_part);
+        ra.logits = logits;
+        ra.done = reinterpret_cast<unsigned*>(ws + L.route_done);
+        ra.xq_hi = xq_hi;
+        ra.xq_lo = x_hilo ? xq_lo : nullptr;
+        ra.xq_ts = xq_ts;
+        ra.plan_args = pl;
+        ra.plan = plan;
+        if (int rc2 = cuda_check(cudaMemsetAsync(ra.done, 0, sizeof(unsigned) * (1 + (L.E + 15) / 16), s),
+                                 "route counters"))
+            return rc2;
+        prof_begin(K3_PROF_ROUTER, s);
+        rc = launch_route_fused(ra, L.KQ, s);
+        prof_end(K3_PROF_ROUTER, s);
+        if (rc) return rc;
+        return decode_tma(p, L, ws, x_hilo, y, ydt, sms, s);
+    }
+    if (gate_w) {
+        if (int rc2 = launch_router_logits(x, xdt, int(M), L.H, gate_w, L.E, logits, s)) return rc2;
+    }
     PrepArgs pa{};
     pa.mode = 0;
-    pa.logits = logits;
-    pa.bias = bias;
-    pa.E = int(p->num_experts);
-    pa.k = p->top_k;
-    pa.renorm = p->renormalize;
-    pa.scale = p->routed_scaling_factor;
-    pa.idx = idx;
-    pa.w = w;
-    pa.has_shared = p->has_shared;
-    pa.plan = plan;
-    pa.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
-    pa.n_cntA = L.U * (L.I / 32);
-    pa.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
-    pa.n_cntB = L.H / kItemRows;
+    pa.logits = gate_w ? logits : nullptr;
+    pa.pl = pl;
     pa.x = x;
     pa.x_dtype = xdt;
     pa.M = int(M);
@@ -1042,16 +892,11 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M, const
     pa.xq_lo = x_hilo ? xq_lo : nullptr;
     pa.xq_ts = xq_ts;
     pa.blocked = L.tma ? 1 : 0;
-    if (L.tma) {
-        pa.n_cntA = L.U * (L.I / 64);
-        pa.n_cntB = L.H / kTRows;
-    }
     prof_begin(K3_PROF_TOPK, s);
-    prep_kernel<<<1 + (L.tma ? kMaxTok : int(M)), 256, 0, s>>>(pa);
+    prep_kernel<<<1 + (L.tma ? int(L.H / 512) : int(M)), 256, 0, s>>>(pa);
     prof_end(K3_PROF_TOPK, s);
     K3_CHECK_LAUNCH("prep_kernel");
 
-    const int sms = num_sms();
     if (L.tma) return decode_tma(p, L, ws, x_hilo, y, ydt, sms, s);
     GemvArgs ga{};
     ga.plan = plan;
@@ -1123,7 +968,7 @@ MatvecLayout matvec_layout(int64_t M, int64_t K, int64_t N, int sms) {
     L.plan = carve(off, sizeof(Plan));
     L.xq_hi = carve(off, sizeof(__half) * xrows * K);
     L.xq_lo = carve(off, sizeof(__half) * xrows * K);
-    L.xq_ts = carve(off, sizeof(float) * kMaxTok);
+    L.xq_ts = carve(off, sizeof(float) * kMaxTok * (K / 512 > 0 ? K / 512 : 1));
     L.part = carve(off, L.tma ? sizeof(float) * (N / kTRows) * L.C * kMaxTok * kTRows
                               : sizeof(float) * L.C * Mc * N);
     L.cnt = carve(off, sizeof(unsigned) * (N / (L.tma ? kTRows : kItemRows)));
@@ -1151,9 +996,10 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
         const int Mc = int(std::min<int64_t>(kMaxTok, M - m0));
         PrepArgs pa{};
         pa.mode = 1;
-        pa.plan = reinterpret_cast<Plan*>(ws + L.plan);
-        pa.cntB = reinterpret_cast<unsigned*>(ws + L.cnt);
-        pa.n_cntB = N / kItemRows;
+        pa.pl.plan = reinterpret_cast<Plan*>(ws + L.plan);
+        pa.pl.cntB = reinterpret_cast<unsigned*>(ws + L.cnt);
+        pa.pl.n_cntB = N / kItemRows;
+        pa.pl.M = Mc;
         pa.x = static_cast<const uint8_t*>(x) + size_t(m0) * K * esz;
         pa.x_dtype = xdt;
         pa.M = Mc;
@@ -1162,9 +1008,9 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
         pa.xq_lo = hilo ? reinterpret_cast<__half*>(ws + L.xq_lo) : nullptr;
         pa.xq_ts = reinterpret_cast<float*>(ws + L.xq_ts);
         pa.blocked = L.tma ? 1 : 0;
-        if (L.tma) pa.n_cntB = N / kTRows;
+        if (L.tma) pa.pl.n_cntB = N / kTRows;
         prof_begin(K3_PROF_TOPK, s);
-        prep_kernel<<<1 + (L.tma ? kMaxTok : Mc), 256, 0, s>>>(pa);
+        prep_kernel<<<1 + (L.tma ? int(K / 512) : Mc), 256, 0, s>>>(pa);
         prof_end(K3_PROF_TOPK, s);
         K3_CHECK_LAUNCH("prep_kernel(matvec)");
         if (L.tma) {
@@ -1174,15 +1020,15 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
             if (hilo)
                 if (int rc2 = blocked_map(&mm.bl, reinterpret_cast<__half*>(ws + L.xq_lo), kMaxTok, K)) return rc2;
             TArgs ta{};
-            ta.plan = pa.plan;
+            ta.plan = pa.pl.plan;
             ta.matvec = 1;
             ta.K = K;
             ta.rows = N;
             ta.C = L.C;
             ta.part = reinterpret_cast<float*>(ws + L.part);
-            ta.cnt = pa.cntB;
+            ta.cnt = pa.pl.cntB;
             ta.maxseg = L.C;
-            ta.status = &pa.plan->status;
+            ta.status = &pa.pl.plan->status;
             ta.bts_tok = pa.xq_ts;
             ta.y = static_cast<uint8_t*>(out) + size_t(m0) * N * osz;
             ta.y_dtype = odt;
@@ -1193,7 +1039,7 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
             continue;
         }
         GemvArgs g{};
-        g.plan = pa.plan;
+        g.plan = pa.pl.plan;
         g.mat_packed = packed;
         g.mat_scales = scales;
         g.K = K;
@@ -1204,7 +1050,7 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
         g.bl = reinterpret_cast<__half*>(ws + L.xq_lo);
         g.bts = pa.xq_ts;
         g.part = reinterpret_cast<float*>(ws + L.part);
-        g.cnt = pa.cntB;
+        g.cnt = pa.pl.cntB;
         g.Pmax = Mc;
         g.y = static_cast<uint8_t*>(out) + size_t(m0) * N * osz;
         g.y_dtype = odt;
@@ -1288,8 +1134,8 @@ extern "C" K3_API int k3_moe_decode(const k3_moe_params* p, const void* x, int x
     float* logits = reinterpret_cast<float*>(ws + L.logits);
     int32_t* idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + L.route_idx);
     float* w = weight_out ? weight_out : reinterpret_cast<float*>(ws + L.route_w);
-    if (int rc = launch_router_logits(x, x_dtype, int(M), p->hidden, gate_w_bf16, p->num_experts, logits, s)) return rc;
-    return decode_impl(p, x, x_dtype, M, logits, bias, idx, w, y_out, y_dtype, ws, L, s);
+    (void)logits;
+    return decode_impl(p, x, x_dtype, M, gate_w_bf16, bias, idx, w, y_out, y_dtype, ws, L, s);
 }
 
 extern "C" K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* x, int x_dtype,

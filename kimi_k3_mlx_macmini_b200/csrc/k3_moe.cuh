@@ -58,7 +58,8 @@ struct DecodeLayout {
     int CA, CB;                    // k-chunks of the gate/up and down phases
     bool tma;                      // TMA-fed kernels over contiguous expert pools
     int64_t ppad, tspad;           // column strides of the blocked activation buffers
-    size_t plan, logits, route_idx, route_w, xq_hi, xq_lo, xq_ts, act_hi, act_lo, act_ts, partA, cntA, partB,
+    int KQ;                        // router k-slices (fused router)
+    size_t plan, logits, logit_part, route_done, route_idx, route_w, xq_hi, xq_lo, xq_ts, act_hi, act_lo, act_ts, partA, cntA, partB,
         cntB, total;
 };
 

@@ -1,0 +1,28 @@
+// Fused decode front end for the TMA path: router logits, x conversion, top-k + plan.
+#pragma once
+
+#include "k3_plan.cuh"
+
+namespace k3 {
+
+struct RouteArgs {
+    const void* x;
+    int x_dtype;
+    int M;
+    int64_t H;
+    const uint16_t* W;             // router weight, bf16 bits [E][H]
+    int64_t E;
+    float* logit_part;             // [KQ][M][E] slice partials
+    float* logits;                 // [M][E]
+    unsigned* done;                // arrival counters [1 + row blocks], zeroed before each launch
+    __half* xq_hi;                 // blocked x pieces [H/32][8][32]
+    __half* xq_lo;                 // null for bf16 x
+    float* xq_ts;                  // [8][H/512]
+    PlanArgs plan_args;
+    Plan* plan;
+};
+
+// Requirements: H % 512 == 0, H / kq % 512 == 0, M <= 8, E <= 1024.
+int launch_route_fused(const RouteArgs& a, int kq, cudaStream_t s);
+
+}  // namespace k3

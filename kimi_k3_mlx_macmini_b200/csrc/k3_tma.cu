@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 }
                 tma_3d(&st.bh[0][0][0], &maps.bh, 0, brow, kg, &full[si]);
                 if (HILO) tma_3d(&st.bl[0][0][0], &maps.bl, 0, brow, kg, &full[si]);
-                if (GROUP_TS) tma_2d(&st.ts[0][0], &maps.bts, kg, brow, &full[si]);
+                if (GROUP_TS) tma_2d(&st.ts[0][0], &maps.bts, brow, kg, &full[si]);
                 s_issued = gs + 1;
             }
         }
@@ -232,8 +232,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const int ctid = int(threadIdx.x);                // 0..255
     uint32_t gs = 0;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int64_t nkb = a.K / kTStageK;               // x scale blocks per token (!GROUP_TS)
     for (int64_t i = i0; i < i1; ++i) {
         const int64_t key = i / ipk, j = i % ipk;
+        const int64_t kst0 = (GATEUP ? j : j % a.C) * nst;     // first 512-k block of the item
         for (int s = 0; s < nst; ++s, ++gs) {
             const int si = int(gs % S);
             if (s_abort || !mbar_wait(&full[si], (gs / S) & 1, a.status)) {
@@ -241,6 +243,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 break;
             }
             const St& st = ring[si];
+            // !GROUP_TS: x has one scale per (token, stage); the stage's sums meet it once
+            float sacc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float* const dst = GROUP_TS ? acc : sacc;
             uint32_t sw0[4], sw8[4];                  // scale bytes of rows g, g+8 (16 groups)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -275,33 +280,34 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     const float rs0 = e8m0_to_f32((sw0[wi] >> sh) & 0xffu);
                     const float rs1 = e8m0_to_f32((sw8[wi] >> sh) & 0xffu);
                     if (GROUP_TS) {
-                        const float tv0 = st.ts[c0][G], tv1 = st.ts[c1][G];
-                        acc[0] = fmaf(rs0 * tv0, tmp[0], acc[0]);
-                        acc[1] = fmaf(rs0 * tv1, tmp[1], acc[1]);
-                        acc[2] = fmaf(rs1 * tv0, tmp[2], acc[2]);
-                        acc[3] = fmaf(rs1 * tv1, tmp[3], acc[3]);
+                        const float2 tv = *reinterpret_cast<const float2*>(&st.ts[G][c0]);
+                        dst[0] = fmaf(rs0 * tv.x, tmp[0], dst[0]);
+                        dst[1] = fmaf(rs0 * tv.y, tmp[1], dst[1]);
+                        dst[2] = fmaf(rs1 * tv.x, tmp[2], dst[2]);
+                        dst[3] = fmaf(rs1 * tv.y, tmp[3], dst[3]);
                     } else {
-                        acc[0] = fmaf(rs0, tmp[0], acc[0]);
-                        acc[1] = fmaf(rs0, tmp[1], acc[1]);
-                        acc[2] = fmaf(rs1, tmp[2], acc[2]);
-                        acc[3] = fmaf(rs1, tmp[3], acc[3]);
+                        dst[0] = fmaf(rs0, tmp[0], dst[0]);
+                        dst[1] = fmaf(rs0, tmp[1], dst[1]);
+                        dst[2] = fmaf(rs1, tmp[2], dst[2]);
+                        dst[3] = fmaf(rs1, tmp[3], dst[3]);
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[si]);
+            if (!GROUP_TS) {
+                // rows M..7 of x are zeros with a finite scale
+                const float t0 = __ldg(a.bts_tok + c0 * nkb + kst0 + s);
+                const float t1 = __ldg(a.bts_tok + c1 * nkb + kst0 + s);
+                acc[0] = fmaf(sacc[0], t0, acc[0]);
+                acc[1] = fmaf(sacc[1], t1, acc[1]);
+                acc[2] = fmaf(sacc[2], t0, acc[2]);
+                acc[3] = fmaf(sacc[3], t1, acc[3]);
+            }
         }
         if (!s_abort && i + 1 < i1 && (i + 1) / ipk == key) continue;   // key continues here
 
         // ---- flush the key
-        if (!GROUP_TS) {                                 // x carries one scale per token
-            const float t0 = c0 < M ? a.bts_tok[c0] : 0.0f;
-            const float t1 = c1 < M ? a.bts_tok[c1] : 0.0f;
-            acc[0] *= t0;
-            acc[1] *= t1;
-            acc[2] *= t0;
-            acc[3] *= t1;
-        }
         const int64_t ks = key * ipk;                                // first item of the key
         const bool local = cta_of(ks, n, grid) == cta_of(ks + ipk - 1, n, grid);
         float* kpart = a.part + key * a.maxseg * (kMaxTok * kTRows);
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 const int64_t o = (G * a.act_rows + arow) * 32 + lane;
                 a.act_hi[o] = hi;
                 a.act_lo[o] = lo;
-                if (lane == 0) a.act_ts[arow * a.act_groups + G] = ldexpf(1.0f, e);
+                if (lane == 0) a.act_ts[G * a.act_rows + arow] = ldexpf(1.0f, e);
             }
         } else if (!local) {
             const int rr = ctid & (kTRows - 1);

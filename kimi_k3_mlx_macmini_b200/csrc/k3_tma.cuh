@@ -26,7 +26,7 @@ struct alignas(1024) TStage {
     uint8_t s[kTRows][kTGroups];                           // E8M0 scales
     __half bh[kTGroups][kMaxTok][32];                      // B hi: [group][column][32 k]
     __half bl[HILO ? kTGroups : 1][kMaxTok][32];           // B lo
-    float ts[GROUP_TS ? kMaxTok : 1][kTGroups];            // B group scales [column][group]
+    float ts[GROUP_TS ? kTGroups : 1][kMaxTok];            // B group scales [group][column]
 };
 
 template <bool HILO>
@@ -44,9 +44,9 @@ static_assert(tsmem_bytes<false, false>() <= 227 * 1024 && tsmem_bytes<true, tru
 
 // Tensor maps of one launch: weights/scales of the first (gate, or the only) and second
 // (up) projection as 3-D [slot][row][k] views, the B pieces as 3-D [group][column][32]
-// views, and the B group scales as a 2-D [column][group] view. Every map's innermost
+// views, and the B group scales as a 2-D [group][column] view. Every map's innermost
 // coordinate is a multiple of 16 bytes (TMA requirement): byte offsets of 256, scale
-// groups of 16, element 0 of a 32-element block, group indices of 16 floats.
+// groups of 16, element 0 of a 32-element block, column indices of 8 floats.
 struct TMaps {
     CUtensorMap wA, sA, wB, sB, bh, bl, bts;
 };
@@ -70,7 +70,7 @@ struct TArgs {
     unsigned* cnt;           // arrival counter per key
     int maxseg;
     // gate/up epilogue: activation pieces per (active expert, token) in the blocked
-    // layout [group][expert * 8 + token][32] plus scales [expert * 8 + token][group]
+    // layout [group][expert * 8 + token][32] plus scales [group][expert * 8 + token]
     __half* act_hi;
     __half* act_lo;
     float* act_ts;
@@ -78,7 +78,7 @@ struct TArgs {
     int act_groups;          // I / 32
     int act_kind;
     float beta, lbeta;
-    const float* bts_tok;    // per-token scales of x (gate/up, matvec)
+    const float* bts_tok;    // scales of x per (token, 512-k block): [8][K/512] (gate/up, matvec)
     // projection epilogue
     void* y;
     int y_dtype;
