@@ -84,6 +84,23 @@ K3_API int k3_mxfp4_dequant(const uint8_t* packed, const uint8_t* scales, int64_
 /* minmax_out (device int32[2]) <- {min, max} of n scale bytes. The reduction half of
  * assert_scales_representable (air_llm/models/kimi_k3/mxfp4.py:58-65); the caller
  * applies the 2..252 rule. */
+/* Re-lays E8M0 scales [batch][rows][cols/32] (row-major, as stored) into the chunk
+ * layout the block-scaled tensor-core MMA reads: [batch][rows/128][cols/128][512], where
+ * the 512-byte chunk of (row block, 128-column block) holds the scale of row m and
+ * 32-column block j at byte (m % 32) * 16 + (m / 32) * 4 + j. rows and cols must be
+ * multiples of 128. No reference counterpart: a one-time preparation of an expert pool
+ * (the reference reads scales row-major inside its Metal kernel,
+ * air_llm/kernels/metal/mxfp4_matvec.py:29-63). */
+K3_API int k3_mxfp4_scales_tc(const uint8_t* scales, int64_t rows, int64_t cols, int64_t batch,
+                              uint8_t* out, void* stream);
+
+/* Re-lays packed E2M1 codes [batch][rows][cols/2] into tiles [batch][rows/128][cols/256]
+ * [128][128]: tile (row block, 256-column block) holds its 128 rows of 128 bytes
+ * contiguously. rows % 128 == 0, cols % 256 == 0. No reference counterpart (one-time pool
+ * preparation for the block-scaled decode kernels). */
+K3_API int k3_mxfp4_tiles(const uint8_t* packed, int64_t rows, int64_t cols, int64_t batch,
+                          uint8_t* out, void* stream);
+
 K3_API int k3_mxfp4_scale_minmax(const uint8_t* scales, int64_t n, int32_t* minmax_out,
                                  void* stream);
 
@@ -161,6 +178,18 @@ typedef struct k3_expert_pool {
     const uint8_t* w2_packed;
     const uint8_t* w2_scales;
     int64_t num_slots;
+    /* Optional: the same scales re-laid by k3_mxfp4_scales_tc for the block-scaled
+       tensor-core path ([slot][rows/128][cols/128][512]). All three non-NULL (and H, I
+       multiples of 256) select that path; otherwise the f16 tensor-core path runs. */
+    const uint8_t* w1_scales_tc;
+    const uint8_t* w3_scales_tc;
+    const uint8_t* w2_scales_tc;
+    /* Optional, block-scaled path only: the packed codes re-laid by k3_mxfp4_tiles into
+       contiguous 128-row x 128-byte tiles ([slot][rows/128][cols/256][128][128]) so every
+       TMA box is one sequential 16 KiB read; NULL streams the row-major pools. */
+    const uint8_t* w1_tiles;
+    const uint8_t* w3_tiles;
+    const uint8_t* w2_tiles;
 } k3_expert_pool;
 
 /* Static description of one MoE layer's expert set (host struct). */

@@ -29,8 +29,10 @@ class K3ExpertPtrs(ctypes.Structure):
 
 
 class K3ExpertPool(ctypes.Structure):
-    _fields_ = [(n, ctypes.c_void_p) for n in ("w1_packed", "w1_scales", "w3_packed", "w3_scales",
-                                               "w2_packed", "w2_scales")] + [("num_slots", ctypes.c_int64)]
+    _fields_ = ([(n, ctypes.c_void_p) for n in ("w1_packed", "w1_scales", "w3_packed", "w3_scales",
+                                                "w2_packed", "w2_scales")] + [("num_slots", ctypes.c_int64)]
+                + [(n, ctypes.c_void_p) for n in ("w1_scales_tc", "w3_scales_tc", "w2_scales_tc",
+                                                  "w1_tiles", "w3_tiles", "w2_tiles")])
 
 
 class K3MoEParams(ctypes.Structure):
@@ -51,6 +53,8 @@ SIGNATURES = {
     "k3_profile_collect": (_i32, [_vp, _vp, _i32]),
     "k3_mxfp4_dequant": (_i32, [_vp, _vp, _i64, _i64, _i32, _vp, _i32, _vp]),
     "k3_mxfp4_scale_minmax": (_i32, [_vp, _i64, _vp, _vp]),
+    "k3_mxfp4_scales_tc": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "k3_mxfp4_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
     "k3_mxfp4_matvec_workspace": (_sz, [_i64, _i64, _i64]),
     "k3_mxfp4_matvec": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp, _sz, _vp]),
     "k3_mxfp4_matvec_noalloc": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),

@@ -1,0 +1,479 @@
+// Block-scaled grouped MXFP4 matvec on tcgen05 (decode path, sm_100a).
+//
+// Roles per CTA (6 warps):
+//   warp 0  producer: one thread streams each stage -- weight tiles (TMA, 128-byte
+//           swizzle), their scale chunks and the B pieces' scale chunks (bulk copies),
+//           the B piece tile (TMA) -- into a ring of shared-memory stages (full/empty
+//           mbarriers, transaction-byte counted);
+//   warp 1  MMA issuer: owns the TMEM allocation; one thread copies each stage's scale
+//           chunks into TMEM (tcgen05.cp) and issues tcgen05.mma.kind::mxf4.block_scale
+//           (M=128 weight rows, N = 8 pieces x columns, K=64) into a double-buffered TMEM
+//           accumulator, then tcgen05.commit frees the stage and, at the end of an item,
+//           hands the accumulator to the epilogue;
+//   warps 2-5 epilogue: warp w reads TMEM lanes 32*(w%4).. (weight rows), sums the pieces
+//           of each column, accumulates the items of a key in registers and flushes it
+//           (gate/up: activation, weight, split into the next launch's E2M1 pieces; down:
+//           y rows), through per-segment partials when the key spans CTAs.
+//
+// Work items, keys and contiguous per-CTA item ranges are those of the f16 TMA kernels:
+// gate/up key = (active expert u, 128-row block of I), items = k-chunks of H; down key =
+// 128-row block of H, items = (u, k-chunk of I) with u ascending. Every wait is bounded.
+#include "k3_async.cuh"
+#include "k3_bs.cuh"
+#include "k3_tma.cuh"
+
+namespace k3 {
+
+namespace {
+
+__device__ __forceinline__ void epi_sync() {
+    asm volatile("bar.sync 1, %0;\n" ::"n"(kBEpiWarps * 32) : "memory");
+}
+
+__device__ __forceinline__ float act_value(int kind, float g, float u, float beta, float lbeta) {
+    if (kind == K3_ACT_SITU) {
+        const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
+        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
+        return a * v;
+    }
+    return g / (1.0f + expf(-g)) * u;
+}
+
+__device__ __forceinline__ int64_t owner_of(int64_t i, int64_t n, int64_t g) {
+    return ((i + 1) * g - 1) / n;
+}
+
+// sum of 8 consecutive values in a fixed order
+__device__ __forceinline__ float sum8(const float* v) {
+    return ((((((v[0] + v[1]) + v[2]) + v[3]) + v[4]) + v[5]) + v[6]) + v[7];
+}
+
+}  // namespace
+
+template <bool GATEUP>
+__global__ void __launch_bounds__(kBThreads, 1)
+    bs_gemv_kernel(const __grid_constant__ BMaps maps, const BArgs a) {
+    using St = BStage<GATEUP>;
+    constexpr int S = bstages<GATEUP>();
+    constexpr uint32_t kCols = btmem_cols<GATEUP>();
+    constexpr int kAccW = GATEUP ? 128 : 64;               // TMEM columns per accumulator
+    constexpr int kSf0 = 2 * kAccW;                        // first scale column
+    constexpr int kSfW = GATEUP ? 24 : 16;                 // scale columns per stage
+    constexpr int kPW = GATEUP ? 2 * kMaxTok : kMaxTok;    // partial values per row
+    static_assert(kSf0 + kSfW * S <= int(kCols), "TMEM plan exceeds the allocation");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    St* ring = reinterpret_cast<St*>(base);
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + sizeof(St) * S);
+    uint64_t* empty = full + S;
+    uint64_t* accf = empty + S;          // [2] accumulator ready (MMA -> epilogue)
+    uint64_t* acce = accf + 2;           // [2] accumulator drained (epilogue -> MMA)
+    uint64_t* drain = acce + 2;          // MMA teardown
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_last;
+    __shared__ int s_nseg;
+    __shared__ int s_seg[kTMaxSegments];
+    __shared__ volatile int s_abort;
+    __shared__ volatile unsigned s_issued;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        s_issued = 0;
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], kBEpiWarps);
+        }
+        mbar_init(drain, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(&s_tmem, kCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = s_tmem;
+
+    const Plan* P = a.plan;
+    const int n_active = P->n_active;
+    const int M = P->M;
+    const int64_t nRb = a.rows / kBRows;
+    const int64_t ipk = GATEUP ? a.C : int64_t(n_active) * a.C;      // items per key
+    const int64_t n_keys = GATEUP ? int64_t(n_active) * nRb : nRb;
+    const int64_t n = n_keys * ipk;
+    const int64_t grid = gridDim.x, bid = blockIdx.x;
+    const int64_t i0 = bid * n / grid, i1 = (bid + 1) * n / grid;
+    const int64_t kchunk = a.K / a.C;
+    const int nst = int(kchunk / kBStageK);
+    const int64_t kcks = a.K / 128;                                   // scale chunks per row block
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            uint32_t gs = 0;
+            for (int64_t i = i0; i < i1 && !s_abort; ++i) {
+                const int64_t key = i / ipk, j = i % ipk;
+                const int u = GATEUP ? int(key % n_active) : int(j / a.C);
+                const int rb = GATEUP ? int(key / n_active) : int(key);
+                const int kc = int(GATEUP ? j : j % a.C);
+                const int slot = P->expert[u];
+                const int ntok = GATEUP ? M : P->pair_start[u + 1] - P->pair_start[u];
+                const int64_t k0 = int64_t(kc) * kchunk;
+                const uint32_t bytes = uint32_t((GATEUP ? 2 : 1) * (kBRows * 128 + 2 * kBChunk) +
+                                                ntok * kBPieces * 128 + 2 * kBChunk);
+                for (int s = 0; s < nst; ++s, ++gs) {
+                    const int si = int(gs % S);
+                    if (!mbar_wait(&empty[si], ((gs / S) & 1) ^ 1, a.status, &s_abort)) {
+                        s_abort = 1;
+                        break;
+                    }
+                    St& st = ring[si];
+                    const int64_t k = k0 + int64_t(s) * kBStageK;
+                    mbar_expect_tx(&full[si], bytes);
+                    const int r0 = rb * kBRows;
+                    const int64_t sfo = int64_t(slot) * a.sf_slot + (int64_t(rb) * kcks + k / 128) * kBChunk;
+                    const int tb = slot * int(nRb) + rb;                 // tile row block
+                    if (a.tiled) tma_4d(&st.a[0][0][0], &maps.a0, 0, 0, int(k / kBStageK), tb, &full[si]);
+                    else tma_3d(&st.a[0][0][0], &maps.a0, int(k / 2), r0, slot, &full[si]);
+                    bulk_g2s(&st.sfa[0][0], a.sfa0 + sfo, 2 * kBChunk, &full[si]);
+                    if (GATEUP) {
+                        if (a.tiled) tma_4d(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), tb, &full[si]);
+                        else tma_3d(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), r0, slot, &full[si]);
+                        bulk_g2s(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si]);
+                        tma_2d(&st.b[0][0], &maps.b, int(k / 2), 0, &full[si]);
+                        bulk_g2s(&st.sfb[0], a.sfb + (k / 128) * kBChunk, 2 * kBChunk, &full[si]);
+                    } else {
+                        for (int it = 0; it < ntok; ++it)
+                            tma_3d(&st.b[kBPieces * it][0], &maps.b, int(k / 2), kBPieces * it, u, &full[si]);
+                        bulk_g2s(&st.sfb[0], a.sfb + (int64_t(u) * kcks + k / 128) * kBChunk, 2 * kBChunk,
+                                 &full[si]);
+                    }
+                    s_issued = gs + 1;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        // The whole warp runs the loop (warp-uniform descriptors); one elected lane issues.
+        uint32_t gs = 0, ib = 0;
+        for (int64_t i = i0; i < i1 && !s_abort; ++i, ++ib) {
+            const int64_t j = i % ipk;
+            const int u = GATEUP ? int((i / ipk) % n_active) : int(j / a.C);
+            const int ntok = GATEUP ? M : P->pair_start[u + 1] - P->pair_start[u];
+            const int nb = kBPieces * ntok;                              // MMA N
+            const uint32_t buf = ib & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&acce[buf], ((ib >> 1) & 1) ^ 1, a.status, &s_abort))) {
+                s_abort = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d0 = tm + buf * kAccW;                        // gate (or down)
+            const uint32_t d1 = d0 + 64;                                 // up
+            const uint32_t idesc0 = mxf4_idesc(nb, 0), idesc2 = mxf4_idesc(nb, 2);
+            for (int s = 0; s < nst; ++s, ++gs) {
+                const int si = int(gs % S);
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[si], (gs / S) & 1, a.status, &s_abort))) {
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const St& st = ring[si];
+                const uint32_t sf = tm + kSf0 + kSfW * si;
+                const uint32_t sfa0 = sf, sfa1 = sf + 8, sfb = sf + (GATEUP ? 16 : 8);
+                if (elect_one()) {
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        tc_cp_sf(sfa0 + 4 * c, sf_chunk_desc(&st.sfa[0][c * kBChunk]));
+                        if (GATEUP) tc_cp_sf(sfa1 + 4 * c, sf_chunk_desc(&st.sfa[GATEUP ? 1 : 0][c * kBChunk]));
+                        tc_cp_sf(sfb + 4 * c, sf_chunk_desc(&st.sfb[c * kBChunk]));
+                    }
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint32_t id = 2 * (kk & 1), ch = 4 * (kk >> 1);
+                        const uint32_t idesc = (kk & 1) ? idesc2 : idesc0;
+                        const uint32_t acc = (s > 0 || kk > 0) ? 1u : 0u;
+                        const uint64_t bd = sw128_desc(&st.b[0][0], 32 * kk);
+                        mma_mxf4(d0, sw128_desc(&st.a[0][0][0], 32 * kk), bd, idesc, (sfa0 + ch) | (id << 30),
+                                 (sfb + ch) | (id << 30), acc);
+                        if (GATEUP)
+                            mma_mxf4(d1, sw128_desc(&st.a[GATEUP ? 1 : 0][0][0], 32 * kk), bd, idesc,
+                                     (sfa1 + ch) | (id << 30), (sfb + ch) | (id << 30), acc);
+                    }
+                    tc_commit(&empty[si]);
+                }
+                __syncwarp();
+            }
+            if (s_abort) break;
+            if (elect_one()) tc_commit(&accf[buf]);
+            __syncwarp();
+        }
+        if (s_abort) {
+            // the producer's copies in flight land before the CTA leaves
+            const unsigned issued = s_issued;
+            for (unsigned k = gs; k < issued; ++k)
+                if (!mbar_wait(&full[k % S], (k / S) & 1, a.status)) break;
+        }
+        // every tcgen05 operation of this warp completes before TMEM is released
+        if (elect_one()) tc_commit(drain);
+        __syncwarp();
+        mbar_wait(drain, 0, a.status);
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;                               // TMEM lane quarter
+        const int r = 32 * q + lane;                          // weight row within the tile
+        const int et = int(threadIdx.x) - 64;                 // 0..127
+        const uint32_t lane_addr = uint32_t(32 * q) << 16;
+        float acc0[kMaxTok], acc1[kMaxTok];
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+        uint32_t ib = 0;
+        for (int64_t i = i0; i < i1; ++i, ++ib) {
+            const int64_t key = i / ipk, j = i % ipk;
+            const int u = GATEUP ? int(key % n_active) : int(j / a.C);
+            const int ps = P->pair_start[u];
+            const int ntok = GATEUP ? M : P->pair_start[u + 1] - ps;
+            const uint32_t buf = ib & 1;
+            const bool ok = mbar_wait(&accf[buf], (ib >> 1) & 1, a.status, &s_abort);
+            if (ok) {
+                tc_fence_after();
+                const uint32_t d0 = tm + lane_addr + buf * kAccW;
+#pragma unroll
+                for (int c = 0; c < kMaxTok / 2; ++c) {
+                    if (2 * c >= ntok) break;
+                    float v[16];
+                    tmem_ld16(d0 + 16 * c, v);
+                    const float s0 = sum8(v), s1 = sum8(v + 8);
+                    if (GATEUP) {
+                        float w[16];
+                        tmem_ld16(d0 + 64 + 16 * c, w);
+                        const float t0 = sum8(w), t1 = sum8(w + 8);
+#pragma unroll
+                        for (int t = 0; t < kMaxTok; ++t) {
+                            if (t == 2 * c) { acc0[t] += s0; acc1[t] += t0; }
+                            if (t == 2 * c + 1) { acc0[t] += s1; acc1[t] += t1; }
+                        }
+                    } else {
+                        const int tk0 = P->pair_tok[ps + 2 * c];
+                        const int tk1 = 2 * c + 1 < ntok ? P->pair_tok[ps + 2 * c + 1] : -1;
+#pragma unroll
+                        for (int t = 0; t < kMaxTok; ++t) {
+                            if (t == tk0) acc0[t] += s0;
+                            if (t == tk1) acc0[t] += s1;
+                        }
+                    }
+                }
+                tc_fence_before();
+            } else {
+                s_abort = 1;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[buf]);
+            // a timed-out wait reaches the other epilogue warps at the next named barrier
+            if (i + 1 < i1 && (i + 1) / ipk == key) {
+                epi_sync();
+                if (s_abort) break;
+                continue;
+            }
+
+            // ---- flush the key
+            const int64_t ks = key * ipk;
+            const bool local = owner_of(ks, n, grid) == owner_of(ks + ipk - 1, n, grid);
+            float* kpart = a.part + key * a.maxseg * (kPW * kBRows);
+            if (!local) {
+                const int64_t seg = (i0 > ks ? i0 : ks) - ks;
+                float* sp = kpart + seg * (kPW * kBRows);
+#pragma unroll
+                for (int t = 0; t < kMaxTok; ++t) {
+                    sp[t * kBRows + r] = acc0[t];
+                    if (GATEUP) sp[(kMaxTok + t) * kBRows + r] = acc1[t];
+                }
+                __threadfence();
+                if (et == 0) {
+                    int ns = 0;
+                    for (int64_t jj = 0; jj < ipk && ns < kTMaxSegments; ++jj)
+                        if (jj == 0 || owner_of(ks + jj, n, grid) != owner_of(ks + jj - 1, n, grid))
+                            s_seg[ns++] = int(jj);
+                    s_nseg = ns;
+                }
+            }
+            epi_sync();
+            if (et == 0) s_last = local || (!s_abort && atomicAdd(a.cnt + key, 1u) + 1 == unsigned(s_nseg));
+            epi_sync();
+            if (s_abort) break;
+            if (!s_last) {
+#pragma unroll
+                for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+                continue;
+            }
+            if (!local) {
+                __threadfence();
+#pragma unroll
+                for (int t = 0; t < kMaxTok; ++t) {
+                    float v0 = 0.0f, v1 = 0.0f;
+                    for (int sg = 0; sg < s_nseg; ++sg) {
+                        const float* sp = kpart + int64_t(s_seg[sg]) * (kPW * kBRows);
+                        v0 += __ldcg(sp + t * kBRows + r);
+                        if (GATEUP) v1 += __ldcg(sp + (kMaxTok + t) * kBRows + r);
+                    }
+                    acc0[t] = v0;
+                    acc1[t] = v1;
+                }
+            }
+            if (GATEUP) {
+                // activation of each (token, weight) pair of expert u, split into pieces,
+                // four pairs interleaved
+                const int rb = int(key / n_active);
+                const int pe = P->pair_start[u + 1];
+                const int64_t rowb = a.rows / 2;                            // bytes per act row (I/2)
+                uint8_t* sfc = a.act_sf + (int64_t(u) * (a.rows / 128) + rb) * kBChunk;
+                for (int p0 = ps; p0 < pe; p0 += 4) {
+                    float v[4];
+                    uint8_t* d[4];
+                    int ci[4];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        const int p = p0 + h < pe ? p0 + h : p0;
+                        const int t = P->pair_tok[p];
+                        float gv = 0.0f, uv = 0.0f;
+#pragma unroll
+                        for (int tt = 0; tt < kMaxTok; ++tt)
+                            if (tt == t) { gv = acc0[tt]; uv = acc1[tt]; }
+                        v[h] = act_value(a.act_kind, gv, uv, a.beta, a.lbeta) * P->pair_w[p];
+                        ci[h] = p0 + h < pe ? p - ps : -1;
+                        d[h] = a.act_p + (int64_t(u) * kBMaxN + kBPieces * (p - ps)) * rowb +
+                               (int64_t(rb) * kBRows + 32 * q) / 2;
+                    }
+                    split_pieces_n<4>(v, lane, d, rowb, sfc, ci, q);
+                }
+            } else {
+                const int64_t row = key * kBRows + r;
+                for (int t = 0; t < M; ++t) {
+                    float v = 0.0f;
+#pragma unroll
+                    for (int tt = 0; tt < kMaxTok; ++tt)
+                        if (tt == t) v = acc0[tt];
+                    store_from_f32(a.y, a.y_dtype, int64_t(t) * a.rows + row, v);
+                }
+            }
+            if (!local && et == 0) a.cnt[key] = 0u;        // ready for the next call
+            if (!local) epi_sync();                          // s_seg is rewritten by the next key
+#pragma unroll
+            for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tm, kCols);
+}
+
+// ---------------------------------------------------------------- scale layout
+
+__global__ void scales_tc_kernel(const uint8_t* __restrict__ in, int64_t rows, int64_t cols,
+                                 int64_t total_chunks, uint8_t* __restrict__ out) {
+    // one thread per (chunk, row): 4 scale bytes
+    const int64_t kc = cols / 128;                 // chunks per row block
+    const int64_t g = cols / 32;                   // scale bytes per row
+    for (int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total_chunks * 128;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t chunk = idx / 128;
+        const int m = int(idx % 128);
+        const int64_t c = chunk % kc;
+        const int64_t rbk = chunk / kc;            // (batch, row block)
+        const int64_t row = rbk * 128 + m;         // row in the flattened [batch*rows]
+        const uint8_t* src = in + row * g + c * 4;
+        uint8_t* dst = out + chunk * kBChunk;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) dst[sf_chunk_offset(m, j)] = src[j];
+    }
+    (void)rows;
+}
+
+__global__ void tiles_kernel(const uint4* __restrict__ in, int64_t rows, int64_t cols, int64_t total,
+                             uint4* __restrict__ out) {
+    // one thread per 16 bytes of the output, in output order (coalesced writes)
+    const int64_t rowb = cols / 32;                // 16-byte units per row
+    const int64_t kt_n = cols / 256;               // tiles per row block
+    for (int64_t o = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; o < total;
+         o += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t c16 = o & 7;                 // 16-byte unit within the tile row
+        const int64_t r = (o >> 3) & 127;          // row within the tile
+        const int64_t t = o >> 10;                 // tile index (batch, row block, k tile)
+        const int64_t kt = t % kt_n;
+        const int64_t rbk = t / kt_n;              // (batch, row block) in [batch * rows/128]
+        out[o] = in[(rbk * 128 + r) * rowb + kt * 8 + c16];
+    }
+    (void)rows;
+}
+
+int launch_tiles(const uint8_t* in, int64_t rows, int64_t cols, int64_t batch, uint8_t* out,
+                 cudaStream_t s) {
+    const int64_t total = batch * rows * cols / 32;          // 16-byte units
+    const int blocks = int(std::min<int64_t>((total + 255) / 256, int64_t(num_sms()) * 32));
+    tiles_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const uint4*>(in), rows, cols, total,
+                                        reinterpret_cast<uint4*>(out));
+    K3_CHECK_LAUNCH("tiles_kernel");
+    return K3_OK;
+}
+
+int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batch, uint8_t* out,
+                     cudaStream_t s) {
+    const int64_t chunks = batch * (rows / 128) * (cols / 128);
+    const int64_t threads = chunks * 128;
+    const int blocks = int(std::min<int64_t>((threads + 255) / 256, int64_t(num_sms()) * 16));
+    scales_tc_kernel<<<blocks, 256, 0, s>>>(in, rows, cols, chunks, out);
+    K3_CHECK_LAUNCH("scales_tc_kernel");
+    return K3_OK;
+}
+
+// ------------------------------------------------------------------ launches
+
+template <bool G>
+int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const char* what) {
+    static bool configured = false;
+    constexpr size_t smem = bsmem_bytes<G>();
+    if (!configured) {
+        if (int rc = cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                                what))
+            return rc;
+        configured = true;
+    }
+    bs_gemv_kernel<G><<<grid, kBThreads, smem, s>>>(maps, a);
+    K3_CHECK_LAUNCH(what);
+    return K3_OK;
+}
+
+int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
+    return launch_bs<true>(maps, a, grid, s, "bs_gemv<gate/up>");
+}
+int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
+    return launch_bs<false>(maps, a, grid, s, "bs_gemv<down>");
+}
+
+}  // namespace k3
+
+extern "C" K3_API int k3_mxfp4_scales_tc(const uint8_t* scales, int64_t rows, int64_t cols,
+                                         int64_t batch, uint8_t* out, void* stream) {
+    using namespace k3;
+    if (!scales || !out) return fail(K3_ERR_INVALID, "k3_mxfp4_scales_tc: NULL tensor");
+    if (rows < 128 || cols < 128 || batch < 1 || rows % 128 || cols % 128)
+        return fail(K3_ERR_UNSUPPORTED, "k3_mxfp4_scales_tc: rows and cols must be positive multiples of 128");
+    return launch_scales_tc(scales, rows, cols, batch, out, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" K3_API int k3_mxfp4_tiles(const uint8_t* packed, int64_t rows, int64_t cols, int64_t batch,
+                                     uint8_t* out, void* stream) {
+    using namespace k3;
+    if (!packed || !out) return fail(K3_ERR_INVALID, "k3_mxfp4_tiles: NULL tensor");
+    if (rows < 128 || cols < 256 || batch < 1 || rows % 128 || cols % 256)
+        return fail(K3_ERR_UNSUPPORTED, "k3_mxfp4_tiles: rows % 128 == 0 and cols % 256 == 0 required");
+    if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+        return fail(K3_ERR_INVALID, "k3_mxfp4_tiles: tensors must be 16-byte aligned");
+    return launch_tiles(packed, rows, cols, batch, out, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,161 @@
+// Block-scaled decode path on the 5th-generation tensor cores (tcgen05, sm_100a):
+// shared declarations.
+//
+// The MXFP4 weights are consumed as stored: E2M1 codes straight from HBM (TMA, 128-byte
+// swizzle) and their E8M0 scales, re-laid once into the tensor core's scale-chunk
+// layout. The activations enter as E2M1 too: each value is split into kBPieces E2M1
+// pieces with one E8M0 scale per (piece, 32-element block) -- piece p holds what pieces
+// 0..p-1 left over, so their sum reproduces the value to ~2^-25 relative (the split is
+// exact bookkeeping; only the final remainder is dropped). B row n = 8 * column + piece,
+// and the pieces of one column are summed after the MMA.
+#pragma once
+
+#include <cuda.h>
+
+#include "k3_moe.cuh"
+
+namespace k3 {
+
+constexpr int kBPieces = 8;                     // E2M1 pieces per activation value
+constexpr int kBStageK = 256;                   // k per pipeline stage: 128 packed bytes a row
+constexpr int kBRows = 128;                     // weight rows per MMA tile (M)
+constexpr int kBChunk = 512;                    // scale chunk: 128 rows x 4 k-blocks of 32
+constexpr int kBMaxN = kMaxTok * kBPieces;      // B rows of one MMA (64)
+constexpr int kBEpiWarps = 4;                   // epilogue warps (one per TMEM lane quarter)
+constexpr int kBThreads = (2 + kBEpiWarps) * 32;
+
+// Byte of the scale of (row n, k-block j) inside its 512-byte chunk: the chunk is the
+// 32 x 16-byte matrix tcgen05.cp replicates to the four TMEM lane quarters, row n in
+// lane n % 32, column n / 32, byte j.
+__host__ __device__ __forceinline__ int sf_chunk_offset(int n, int j) {
+    return (n & 31) * 16 + (n >> 5) * 4 + j;
+}
+
+// One pipeline stage. Gate/up: the 128-row gate tile and the 128-row up tile of one
+// expert block share the B tile; down: one 128-row tile.
+template <bool GATEUP>
+struct alignas(1024) BStage {
+    uint8_t a[GATEUP ? 2 : 1][kBRows][128];     // E2M1 weights, SW128
+    uint8_t b[kBMaxN][128];                     // E2M1 activation pieces, SW128
+    uint8_t sfa[GATEUP ? 2 : 1][2 * kBChunk];   // weight scales, two chunks (256 k)
+    uint8_t sfb[2 * kBChunk];                   // piece scales, two chunks
+};
+
+template <bool GATEUP>
+constexpr int bstages() { return GATEUP ? 5 : 8; }
+template <bool GATEUP>
+constexpr uint32_t btmem_cols() { return GATEUP ? 512 : 256; }
+template <bool GATEUP>
+constexpr size_t bsmem_bytes() {
+    return sizeof(BStage<GATEUP>) * bstages<GATEUP>() + 1024 /*align*/ + 256 /*barriers*/;
+}
+static_assert(bsmem_bytes<true>() + 4096 <= 227 * 1024 && bsmem_bytes<false>() + 4096 <= 227 * 1024,
+              "block-scaled ring exceeds shared memory");
+
+// Tensor maps: a0/a1 = packed weight pools, row-major [slot][rows][K/2] (box 128 B x 128
+// rows) or tiled [slot * rows/128][K/256][128][128] (box = one contiguous tile);
+// b = activation pieces, gate/up [8M][K/2] (box 128 B x 8M rows), down [u][64][K/2]
+// (box 128 B x 8 rows, one column's pieces).
+struct BMaps {
+    CUtensorMap a0, a1, b;
+};
+
+struct BArgs {
+    const Plan* plan;
+    int64_t K;              // reduction length
+    int64_t rows;           // rows of one projection (I for gate/up, H for down)
+    int C;                  // k-chunks per (expert, row block)
+    int* status;
+    float* part;            // segment partials [key][maxseg][PW][128], PW = 16 | 8
+    unsigned* cnt;          // arrival counter per key
+    int maxseg;
+    const uint8_t* sfa0;    // weight scale chunks of pool a0 [slot][rows/128][K/128][512]
+    const uint8_t* sfa1;    // of pool a1 (gate/up)
+    int tiled;              // a0/a1 are tile pools (4-D maps) rather than row-major pools
+    int64_t sf_slot;        // bytes per slot of a scale-chunk pool
+    const uint8_t* sfb;     // piece scale chunks: gate/up [K/128][512]; down [u][K/128][512]
+    // gate/up epilogue: act pieces of expert u, column i (its i-th pair), piece p at row
+    // u*64 + 8i + p of act_p [.][I/2]; their scale chunks act_sf [u][I/128][512]
+    uint8_t* act_p;
+    uint8_t* act_sf;
+    int act_kind;
+    float beta, lbeta;
+    // down epilogue
+    void* y;
+    int y_dtype;
+};
+
+int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
+int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
+// Scale re-layout [batch][rows][cols/32] -> [batch][rows/128][cols/128][512] chunks.
+int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batch, uint8_t* out,
+                     cudaStream_t s);
+// Packed-code re-layout [batch][rows][cols/2] -> [batch][rows/128][cols/256][128][128].
+int launch_tiles(const uint8_t* in, int64_t rows, int64_t cols, int64_t batch, uint8_t* out,
+                 cudaStream_t s);
+
+// Max of a non-negative float over the warp (bit patterns of non-negative floats order
+// like unsigned integers).
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+    uint32_t r;
+    asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;\n" : "=r"(r) : "r"(__float_as_uint(v)));
+    return __uint_as_float(r);
+}
+
+// Warp-wide: lane l holds element l of a 32-element block of NV values (independent
+// chains, interleaved); splits each into kBPieces E2M1 pieces. Piece p of value i: its
+// 16 packed bytes go to data[i] + p*row_stride (element 2j in the low nibble of byte j)
+// and its E8M0 scale to sf_chunk[sf_chunk_offset(8*col[i] + p, j)]. Values with
+// col[i] < 0 are skipped.
+template <int NV>
+__device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, uint8_t* const (&data)[NV],
+                                               int64_t row_stride, uint8_t* sf_chunk, const int (&col)[NV],
+                                               int j) {
+    float res[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) res[i] = v[i];
+#pragma unroll
+    for (int p = 0; p < kBPieces; ++p) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const float m = warp_max_nonneg(fabsf(res[i]));
+            // smallest power of two S with m <= 6 S, as E8M0 byte b (S = 2^(b-127))
+            int b = 1;
+            if (m > 0.0f) {
+                int E;
+                const float f = frexpf(m, &E);
+                b = E - 3 + (f > 0.75f ? 1 : 0) + 127;
+                b = b < 1 ? 1 : (b > 253 ? 253 : b);
+            }
+            const float S = __int_as_float(b << 23);
+            const float inv = __int_as_float((254 - b) << 23);
+            const float a = fabsf(res[i]) * inv;
+            // round to the E2M1 grid {0, .5, 1, 1.5, 2, 3, 4, 6}, ties to the even code
+            const int c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
+                          (a >= 3.5f) + (a > 5.0f);
+            const float q = c <= 4 ? 0.5f * float(c) : (c == 5 ? 3.0f : (c == 6 ? 4.0f : 6.0f));
+            const bool neg = res[i] < 0.0f;
+            res[i] -= (neg ? -q : q) * S;                // exact: q*S is on res's grid
+            uint32_t w = uint32_t(c | ((neg && c) ? 8 : 0)) << (4 * (lane & 7));
+            w |= __shfl_xor_sync(0xffffffffu, w, 1);
+            w |= __shfl_xor_sync(0xffffffffu, w, 2);
+            w |= __shfl_xor_sync(0xffffffffu, w, 4);
+            if (col[i] >= 0) {
+                if ((lane & 7) == 0)
+                    *reinterpret_cast<uint32_t*>(data[i] + p * row_stride + 4 * (lane >> 3)) = w;
+                if (lane == 0) sf_chunk[sf_chunk_offset(8 * col[i] + p, j)] = uint8_t(b);
+            }
+        }
+    }
+}
+
+// One value per lane (see split_pieces_n).
+__device__ __forceinline__ void split_pieces(float v, int lane, uint8_t* data, int64_t row_stride,
+                                             uint8_t* sf_chunk, int col, int j) {
+    const float vv[1] = {v};
+    uint8_t* const dd[1] = {data};
+    const int cc[1] = {col};
+    split_pieces_n<1>(vv, lane, dd, row_stride, sf_chunk, cc, j);
+}
+
+}  // namespace k3

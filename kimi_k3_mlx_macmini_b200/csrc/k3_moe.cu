@@ -18,6 +18,7 @@
 #include "k3_moe.cuh"
 #include "k3_plan.cuh"
 #include "k3_tma.cuh"
+#include "k3_bs.cuh"
 #include "k3_route.cuh"
 
 namespace k3 {
@@ -196,11 +197,23 @@ struct PrepArgs {
     int blocked;                   // blocked pieces with one exponent per (token, 512-k)
                                    // block, rows M..7 zeros (TMA kernels); else row-major
                                    // with one exponent per token (generic kernels)
+    uint8_t* xp;                   // block-scaled path: E2M1 pieces [8M][K/2] + scale
+    uint8_t* xsf;                  // chunks [K/128][512] instead of the f16 pieces
 };
 
 __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x > 0) {
+        if (a.xp) {                        // CTA 1+kb: 32-blocks 16kb.. of token `warp`
+            const int64_t g0 = int64_t(blockIdx.x - 1) * 16;
+            if (warp < a.M)
+                for (int64_t g = g0; g < g0 + 16 && g < a.K / 32; ++g) {
+                    const float v = load_as_f32(a.x, a.x_dtype, int64_t(warp) * a.K + 32 * g + lane);
+                    split_pieces(v, lane, a.xp + int64_t(kBPieces * warp) * (a.K / 2) + 16 * g, a.K / 2,
+                                 a.xsf + (g / 4) * kBChunk, warp, int(g % 4));
+                }
+            return;
+        }
         if (a.blocked) {                   // CTA 1+kb: block kb of every token (warp t)
             const int64_t kb = blockIdx.x - 1;
             if (kb < a.K / 512)
@@ -628,6 +641,30 @@ bool pool_usable(const k3_moe_params& p) {
            p.hidden % kTStageK == 0 && p.inter % kTStageK == 0;
 }
 
+bool pool_bs(const k3_moe_params& p) {
+    const k3_expert_pool* pl = p.pool;
+    return pool_usable(p) && pl->w1_scales_tc && pl->w3_scales_tc && pl->w2_scales_tc &&
+           p.hidden % kBStageK == 0 && p.inter % kBStageK == 0;
+}
+
+// k-split for the block-scaled kernels: as choose_split_tma, over 256-k stages.
+int choose_split_bs(int64_t n_base, int64_t K, int64_t grid) {
+    const int64_t nst = K / kBStageK;
+    int best = 1;
+    double best_eff = -1.0;
+    for (int64_t c = 1; c <= nst; ++c) {
+        if (nst % c) continue;
+        const int64_t n = n_base * c;
+        const double eff = double(n) / double(((n + grid - 1) / grid) * grid);
+        if (eff >= 0.95) return int(c);
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = int(c);
+        }
+    }
+    return best;
+}
+
 DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
     DecodeLayout L{};
     L.M = M;
@@ -637,7 +674,35 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
     L.U = std::min<int64_t>(p.num_experts, M * p.top_k) + (p.has_shared ? 1 : 0);
     L.P = M * p.top_k + (p.has_shared ? M : 0);
     L.tma = pool_usable(p);
+    L.bs = L.tma && pool_bs(p);
     size_t off = 0;
+    if (L.bs) {
+        // keys: gate/up = (active expert, 128-row block of I); down = 128-row block of y
+        L.CA = choose_split_bs(L.U * (L.I / kBRows), L.H, sms);
+        L.CB = choose_split_bs(L.U * (L.H / kBRows), L.I, sms);
+        L.plan = carve(off, sizeof(Plan));
+        L.logits = carve(off, sizeof(float) * M * L.E);
+        L.route_idx = carve(off, sizeof(int32_t) * M * p.top_k);
+        L.route_w = carve(off, sizeof(float) * M * p.top_k);
+        L.xq_hi = carve(off, size_t(kBMaxN) * (L.H / 2));              // x pieces
+        L.xq_ts = carve(off, size_t(L.H / 128) * kBChunk);              // their scale chunks
+        L.KQ = 1;
+        for (int64_t c = 1; c <= L.H / 512; ++c) {        // router k-slices: >= one CTA per SM
+            if ((L.H / 512) % c) continue;
+            L.KQ = int(c);
+            if (((L.E + 15) / 16) * c >= sms) break;
+        }
+        L.logit_part = carve(off, sizeof(float) * L.KQ * M * L.E);
+        L.route_done = carve(off, sizeof(unsigned) * (1 + (L.E + 15) / 16));
+        L.act_hi = carve(off, size_t(L.U) * kBMaxN * (L.I / 2));        // act pieces
+        L.act_ts = carve(off, size_t(L.U) * (L.I / 128) * kBChunk);
+        L.partA = carve(off, sizeof(float) * L.U * (L.I / kBRows) * L.CA * 2 * kMaxTok * kBRows);
+        L.cntA = carve(off, sizeof(unsigned) * L.U * (L.I / kBRows));
+        L.partB = carve(off, sizeof(float) * (L.H / kBRows) * L.U * L.CB * kMaxTok * kBRows);
+        L.cntB = carve(off, sizeof(unsigned) * (L.H / kBRows));
+        L.total = off;
+        return L;
+    }
     if (L.tma) {
         // keys: gate/up = (active expert, 64-row block); down = 128-row block of y
         L.CA = choose_split_tma(L.U * (L.I / 64), L.H, sms);
@@ -822,6 +887,104 @@ int decode_tma(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, bool 
     return rc;
 }
 
+// Map over a packed pool [slots][rows][cols/2]: 128-byte x 128-row boxes, 128-byte swizzle.
+int packed_map(CUtensorMap* m, const uint8_t* packed, int64_t rows, int64_t cols, int64_t slots) {
+    const uint64_t d[3] = {uint64_t(cols / 2), uint64_t(rows), uint64_t(slots)};
+    const uint64_t st[2] = {uint64_t(cols / 2), uint64_t(rows * cols / 2)};
+    const uint32_t b[3] = {128, uint32_t(kBRows), 1};
+    return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, packed, d, st, b, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Map over a tile pool [slots * rows/128][cols/256][128][128]: one box = one tile.
+int tiles_map(CUtensorMap* m, const uint8_t* tiles, int64_t rows, int64_t cols, int64_t slots) {
+    const uint64_t d[4] = {128, 128, uint64_t(cols / 256), uint64_t(slots * (rows / 128))};
+    const uint64_t st[3] = {128, 128 * 128, uint64_t(128 * 128) * uint64_t(cols / 256)};
+    const uint32_t b[4] = {128, 128, 1, 1};
+    return encode_map(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, tiles, d, st, b, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// Block-scaled gate/up + down launches (the plan and x pieces are already in `ws`).
+int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M, void* y, int ydt,
+              int sms, cudaStream_t s) {
+    const k3_expert_pool& pl = *p->pool;
+    Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
+    uint8_t* act_p = ws + L.act_hi;
+    uint8_t* act_sf = ws + L.act_ts;
+
+    const bool tiled = pl.w1_tiles && pl.w3_tiles && pl.w2_tiles;
+    BMaps ma{};
+    if (tiled) {
+        if (int rc = tiles_map(&ma.a0, pl.w1_tiles, L.I, L.H, pl.num_slots)) return rc;
+        if (int rc = tiles_map(&ma.a1, pl.w3_tiles, L.I, L.H, pl.num_slots)) return rc;
+    } else {
+        if (int rc = packed_map(&ma.a0, pl.w1_packed, L.I, L.H, pl.num_slots)) return rc;
+        if (int rc = packed_map(&ma.a1, pl.w3_packed, L.I, L.H, pl.num_slots)) return rc;
+    }
+    {
+        const uint64_t d[2] = {uint64_t(L.H / 2), uint64_t(kBPieces * M)};
+        const uint64_t st[1] = {uint64_t(L.H / 2)};
+        const uint32_t b[2] = {128, uint32_t(kBPieces * M)};
+        if (int rc = encode_map(&ma.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + L.xq_hi, d, st, b,
+                                CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+    }
+    BArgs ta{};
+    ta.plan = plan;
+    ta.K = L.H;
+    ta.rows = L.I;
+    ta.C = L.CA;
+    ta.status = &plan->status;
+    ta.part = reinterpret_cast<float*>(ws + L.partA);
+    ta.cnt = reinterpret_cast<unsigned*>(ws + L.cntA);
+    ta.maxseg = L.CA;
+    ta.sfa0 = pl.w1_scales_tc;
+    ta.sfa1 = pl.w3_scales_tc;
+    ta.tiled = tiled ? 1 : 0;
+    ta.sf_slot = (L.I / 128) * (L.H / 128) * kBChunk;
+    ta.sfb = ws + L.xq_ts;
+    ta.act_p = act_p;
+    ta.act_sf = act_sf;
+    ta.act_kind = p->activation;
+    ta.beta = p->situ_beta;
+    ta.lbeta = p->situ_linear_beta;
+    prof_begin(K3_PROF_GATEUP, s);
+    int rc = launch_bs_gateup(ma, ta, sms, s);
+    prof_end(K3_PROF_GATEUP, s);
+    if (rc) return rc;
+
+    BMaps mb{};
+    if (int rc2 = tiled ? tiles_map(&mb.a0, pl.w2_tiles, L.H, L.I, pl.num_slots)
+                        : packed_map(&mb.a0, pl.w2_packed, L.H, L.I, pl.num_slots))
+        return rc2;
+    {
+        const uint64_t d[3] = {uint64_t(L.I / 2), uint64_t(kBMaxN), uint64_t(L.U)};
+        const uint64_t st[2] = {uint64_t(L.I / 2), uint64_t(kBMaxN) * uint64_t(L.I / 2)};
+        const uint32_t b[3] = {128, uint32_t(kBPieces), 1};
+        if (int rc2 = encode_map(&mb.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, act_p, d, st, b,
+                                 CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc2;
+    }
+    BArgs tb{};
+    tb.plan = plan;
+    tb.K = L.I;
+    tb.rows = L.H;
+    tb.C = L.CB;
+    tb.status = &plan->status;
+    tb.part = reinterpret_cast<float*>(ws + L.partB);
+    tb.cnt = reinterpret_cast<unsigned*>(ws + L.cntB);
+    tb.maxseg = int(L.U * L.CB);
+    tb.sfa0 = pl.w2_scales_tc;
+    tb.tiled = tiled ? 1 : 0;
+    tb.sf_slot = (L.H / 128) * (L.I / 128) * kBChunk;
+    tb.sfb = act_sf;
+    tb.y = y;
+    tb.y_dtype = ydt;
+    prof_begin(K3_PROF_DOWN, s);
+    rc = launch_bs_down(mb, tb, sms, s);
+    prof_end(K3_PROF_DOWN, s);
+    return rc;
+}
+
 // Decode experts given routing; `logits` non-null also runs the top-k inside prep.
 int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
                 const uint16_t* gate_w, const float* bias, int32_t* idx, float* w, void* y,
@@ -846,7 +1009,7 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
     pl.plan = plan;
     pl.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
     pl.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
-    pl.n_cntA = L.tma ? L.U * (L.I / 64) : L.U * (L.I / 32);
+    pl.n_cntA = L.bs ? L.U * (L.I / kBRows) : L.tma ? L.U * (L.I / 64) : L.U * (L.I / 32);
     pl.n_cntB = L.tma ? L.H / kTRows : L.H / kItemRows;
     pl.M = int(M);
     const int sms = num_sms();
@@ -866,6 +1029,8 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
         ra.xq_hi = xq_hi;
         ra.xq_lo = x_hilo ? xq_lo : nullptr;
         ra.xq_ts = xq_ts;
+        ra.xp = L.bs ? ws + L.xq_hi : nullptr;
+        ra.xsf = L.bs ? ws + L.xq_ts : nullptr;
         ra.plan_args = pl;
         ra.plan = plan;
         if (int rc2 = cuda_check(cudaMemsetAsync(ra.done, 0, sizeof(unsigned) * (1 + (L.E + 15) / 16), s),
@@ -875,6 +1040,7 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
         rc = launch_route_fused(ra, L.KQ, s);
         prof_end(K3_PROF_ROUTER, s);
         if (rc) return rc;
+        if (L.bs) return decode_bs(p, L, ws, int(M), y, ydt, sms, s);
         return decode_tma(p, L, ws, x_hilo, y, ydt, sms, s);
     }
     if (gate_w) {
@@ -892,10 +1058,13 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
     pa.xq_lo = x_hilo ? xq_lo : nullptr;
     pa.xq_ts = xq_ts;
     pa.blocked = L.tma ? 1 : 0;
+    pa.xp = L.bs ? ws + L.xq_hi : nullptr;
+    pa.xsf = L.bs ? ws + L.xq_ts : nullptr;
     prof_begin(K3_PROF_TOPK, s);
-    prep_kernel<<<1 + (L.tma ? int(L.H / 512) : int(M)), 256, 0, s>>>(pa);
+    prep_kernel<<<1 + (L.tma ? int((L.H + 511) / 512) : int(M)), 256, 0, s>>>(pa);
     prof_end(K3_PROF_TOPK, s);
     K3_CHECK_LAUNCH("prep_kernel");
+    if (L.bs) return decode_bs(p, L, ws, int(M), y, ydt, sms, s);
 
     if (L.tma) return decode_tma(p, L, ws, x_hilo, y, ydt, sms, s);
     GemvArgs ga{};

@@ -57,6 +57,7 @@ struct DecodeLayout {
     int64_t M, H, I, E, U, P;      // tokens, hidden, inter, experts, max active, max pairs
     int CA, CB;                    // k-chunks of the gate/up and down phases
     bool tma;                      // TMA-fed kernels over contiguous expert pools
+    bool bs;                       // ... on the block-scaled (kind::mxf4) tensor-core path
     int64_t ppad, tspad;           // column strides of the blocked activation buffers
     int KQ;                        // router k-slices (fused router)
     size_t plan, logits, logit_part, route_done, route_idx, route_w, xq_hi, xq_lo, xq_ts, act_hi, act_lo, act_ts, partA, cntA, partB,

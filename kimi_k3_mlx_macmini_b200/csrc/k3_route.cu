@@ -81,8 +81,20 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     red[warp][g + 8][2 * q] = d[2];
     red[warp][g + 8][2 * q + 1] = d[3];
 
-    // ---- x -> f16 pieces: the CTAs of the first row blocks split the slice's 512-blocks
-    {
+    if (a.xp) {
+        // ---- x -> E2M1 pieces: (token, 32-block) tasks spread over every warp of the grid
+        const int64_t nw = int64_t(gridDim.x) * gridDim.y * 8;
+        const int64_t gw = (int64_t(kq) * gridDim.x + rb) * 8 + warp;
+        const int64_t ng = a.H / 32;
+        for (int64_t task = gw; task < a.M * ng; task += nw) {
+            const int t = int(task / ng);
+            const int64_t g = task % ng;
+            const float v = load_as_f32(a.x, a.x_dtype, int64_t(t) * a.H + 32 * g + lane);
+            split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (a.H / 2) + 16 * g, a.H / 2,
+                         a.xsf + (g / 4) * kBChunk, t, int(g % 4));
+        }
+    } else {
+        // ---- x -> f16 pieces: the CTAs of the first row blocks split the slice's 512-blocks
         const int64_t nb = slice / 512, b0 = int64_t(kq) * nb;
         for (int64_t j = rb; j < nb; j += gridDim.x)
             convert_block(a.x, a.x_dtype, a.M, a.H, warp, b0 + j, a.xq_hi, a.xq_lo, a.xq_ts, lane);

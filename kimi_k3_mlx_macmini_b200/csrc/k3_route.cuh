@@ -1,6 +1,7 @@
 // Fused decode front end for the TMA path: router logits, x conversion, top-k + plan.
 #pragma once
 
+#include "k3_bs.cuh"
 #include "k3_plan.cuh"
 
 namespace k3 {
@@ -18,6 +19,10 @@ struct RouteArgs {
     __half* xq_hi;                 // blocked x pieces [H/32][8][32]
     __half* xq_lo;                 // null for bf16 x
     float* xq_ts;                  // [8][H/512]
+    // block-scaled path: x as E2M1 pieces [8M][H/2] and their scale chunks [H/128][512]
+    // (replaces xq_* when non-null)
+    uint8_t* xp;
+    uint8_t* xsf;
     PlanArgs plan_args;
     Plan* plan;
 };

@@ -14,6 +14,7 @@
 #include <mutex>
 #include <string>
 
+#include "k3_async.cuh"
 #include "k3_tma.cuh"
 
 namespace k3 {
@@ -56,65 +57,6 @@ int encode_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* bas
 
 // --------------------------------------------------------------- device helpers
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;      // a bounded wait gives up after 2 s
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-// Waits for the phase of `bar` selected by `parity`; gives up after kWaitLimitNs and
-// records K3_ERR_TIMEOUT in *status.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    for (;;) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs) {
-            atomicExch(status, K3_ERR_TIMEOUT);
-            return false;
-        }
-    }
-}
-__device__ __forceinline__ void tma_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2,
-                                       uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void tma_2d(void* dst, const CUtensorMap* map, int c0, int c1,
-                                       uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-        : "memory");
-}
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;\n" ::"n"(kTWarps * 32) : "memory");
 }

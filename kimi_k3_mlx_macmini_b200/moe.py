@@ -28,7 +28,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
-from .mxfp4 import decode_mxfp4, mxfp4_matvec_fused, scale_minmax
+from .mxfp4 import decode_mxfp4, mxfp4_matvec_fused, packed_tiles, scale_minmax, scales_tc
 
 SHARED = "shared"
 WHICH = ("w1", "w3", "w2")
@@ -94,7 +94,7 @@ class ExpertPool:
     """
 
     def __init__(self, layer: int, num_experts: int, expert_source: Callable, device,
-                 with_shared: bool, check_scales: bool = True):
+                 with_shared: bool, check_scales: bool = True, block_scaled: bool = True):
         self.layer, self.E, self.device = layer, num_experts, torch.device(device)
         self.with_shared = with_shared
         ids = list(range(num_experts)) + ([SHARED] if with_shared else [])
@@ -124,10 +124,23 @@ class ExpertPool:
                              dtype=torch.int64)
         self.table = table.to(self.device)
         (w1p, w1s), (w3p, w3s), (w2p, w2s) = self.pools
+        # scales re-laid once for the block-scaled tensor-core path (when the shapes allow)
+        self.scales_tc = self.tiles = None
+        if block_scaled and all(sp.shape[1] % 128 == 0 and (sp.shape[2] * 32) % 256 == 0
+                                for _, sp in self.pools):
+            self.scales_tc = [scales_tc(sp) for _, sp in self.pools]
+            self.tiles = [packed_tiles(pp) for pp, _ in self.pools]
+        tc = [t.data_ptr() for t in self.scales_tc] if self.scales_tc is not None else [None] * 3
+        tl = [t.data_ptr() for t in self.tiles] if self.tiles is not None else [None] * 3
         self.desc = L.K3ExpertPool(w1_packed=w1p.data_ptr(), w1_scales=w1s.data_ptr(),
                                    w3_packed=w3p.data_ptr(), w3_scales=w3s.data_ptr(),
                                    w2_packed=w2p.data_ptr(), w2_scales=w2s.data_ptr(),
-                                   num_slots=self.slots)
+                                   num_slots=self.slots, w1_scales_tc=tc[0], w3_scales_tc=tc[1],
+                                   w2_scales_tc=tc[2], w1_tiles=tl[0], w3_tiles=tl[1], w2_tiles=tl[2])
+        self.desc_f16 = L.K3ExpertPool(w1_packed=w1p.data_ptr(), w1_scales=w1s.data_ptr(),
+                                       w3_packed=w3p.data_ptr(), w3_scales=w3s.data_ptr(),
+                                       w2_packed=w2p.data_ptr(), w2_scales=w2s.data_ptr(),
+                                       num_slots=self.slots)
         self.inter, self.hidden = w1p.shape[1], w1p.shape[2] * 2
 
     def get(self, e, which: str):
@@ -135,7 +148,8 @@ class ExpertPool:
         return self.tensors[i][WHICH.index(which)]
 
     def nbytes(self) -> int:
-        return sum(pp.numel() + sp.numel() for pp, sp in self.pools)
+        extra = [t for group in (self.scales_tc, self.tiles) if group is not None for t in group]
+        return sum(pp.numel() + sp.numel() for pp, sp in self.pools) + sum(t.numel() for t in extra)
 
 
 class LatentMoE:
@@ -168,6 +182,9 @@ class LatentMoE:
         self._pool: Optional[ExpertPool] = None
         # the contiguous pools feed the TMA kernels; False forces the pointer-table kernels
         self.use_pool = True
+        # block-scaled (kind::mxf4) tensor-core kernels when the pool carries re-laid
+        # scales; False runs the f16 tensor-core kernels over the same pool
+        self.block_scaled = True
 
     # ------------------------------------------------------------------ plumbing
     @property
@@ -200,7 +217,8 @@ class LatentMoE:
             situ_beta=float(getattr(c, "situ_beta", 4.0)),
             situ_linear_beta=-1.0 if lb is None else float(lb),
             experts=pool.table.data_ptr(),
-            pool=ctypes.pointer(pool.desc) if self.use_pool else None)
+            pool=(ctypes.pointer(pool.desc if self.block_scaled else pool.desc_f16)
+                  if self.use_pool else None))
 
     def _experts_decode(self, h: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
                         params: L.K3MoEParams) -> torch.Tensor:

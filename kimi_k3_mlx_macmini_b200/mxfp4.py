@@ -107,6 +107,37 @@ def scale_minmax(scales: torch.Tensor) -> tuple[int, int]:
     return int(lo), int(hi)
 
 
+def scales_tc(scales: torch.Tensor) -> torch.Tensor:
+    """E8M0 scales ``[..., rows, cols/32]`` re-laid for the block-scaled tensor-core path:
+    ``[batch, rows/128, cols/128, 512]`` chunks (``k3_mxfp4_scales_tc``)."""
+    scales = _u8(scales, "scales")
+    if scales.dim() < 2:
+        raise ValueError("scales must be at least 2-D [rows, cols/32]")
+    rows, g = scales.shape[-2], scales.shape[-1]
+    batch = scales.numel() // max(1, rows * g)
+    out = torch.empty((batch, rows // 128, (g * 32) // 128, 512), dtype=torch.uint8, device=scales.device)
+    lib = L.load_library()
+    L.check(lib.k3_mxfp4_scales_tc(scales.data_ptr(), rows, g * 32, batch, out.data_ptr(),
+                                   L.stream_of(scales)), "k3_mxfp4_scales_tc")
+    return out
+
+
+def packed_tiles(packed: torch.Tensor) -> torch.Tensor:
+    """Packed E2M1 codes ``[..., rows, cols/2]`` re-laid into contiguous 128-row x 128-byte
+    tiles ``[batch, rows/128, cols/256, 128, 128]`` (``k3_mxfp4_tiles``)."""
+    packed = _u8(packed, "packed")
+    if packed.dim() < 2:
+        raise ValueError("packed must be at least 2-D [rows, cols/2]")
+    rows, half = packed.shape[-2], packed.shape[-1]
+    batch = packed.numel() // max(1, rows * half)
+    out = torch.empty((batch, rows // 128, (half * 2) // 256, 128, 128), dtype=torch.uint8,
+                      device=packed.device)
+    lib = L.load_library()
+    L.check(lib.k3_mxfp4_tiles(packed.data_ptr(), rows, half * 2, batch, out.data_ptr(),
+                               L.stream_of(packed)), "k3_mxfp4_tiles")
+    return out
+
+
 def assert_scales_representable(scales: torch.Tensor) -> None:
     """``mxfp4.py:58-65``: scale bytes must lie in 2..252."""
     lo, hi = scale_minmax(scales)

@@ -305,3 +305,50 @@ def test_full_size_pool_and_table_paths_agree(k3, full_layer):
         b = moe(x)
         moe.use_pool = True
         assert O.rel_l2(host(a), host(b)) < 1e-6
+
+
+def test_full_size_block_scaled_and_f16_paths_agree(k3, full_layer):
+    """The block-scaled tensor-core kernels (E2M1 activation pieces, kind::mxf4) and the
+    f16 tensor-core kernels (f16 hi/lo activation pieces) compute the same layer."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    _, moe = full_layer
+    assert moe.pool.scales_tc is not None
+    for M in (1, 3, 8):
+        x = synthetic.tokens(5151 + M, M, 7168)
+        moe.block_scaled = True
+        a = moe(x)
+        moe.block_scaled = False
+        b = moe(x)
+        moe.block_scaled = True
+        assert O.rel_l2(host(a), host(b)) < 1e-6
+
+
+def test_scales_tc_layout(k3):
+    """k3_mxfp4_scales_tc places the scale of (row m, 32-block j) of each 128x128 tile at
+    byte (m % 32) * 16 + (m // 32) * 4 + j of its 512-byte chunk."""
+    from kimi_k3_mlx_macmini_b200.mxfp4 import scales_tc
+    rng = np.random.default_rng(3)
+    s = rng.integers(0, 256, size=(3, 256, 384 // 32), dtype=np.uint8)
+    out = scales_tc(torch.from_numpy(s).cuda()).cpu().numpy()
+    assert out.shape == (3, 2, 3, 512)
+    m = np.arange(128)[:, None]
+    j = np.arange(4)[None, :]
+    off = (m % 32) * 16 + (m // 32) * 4 + j
+    for b in range(3):
+        for rb in range(2):
+            for c in range(3):
+                want = s[b, rb * 128:(rb + 1) * 128, 4 * c:4 * c + 4]
+                assert np.array_equal(out[b, rb, c][off], want)
+
+
+def test_packed_tiles_layout(k3):
+    """k3_mxfp4_tiles stores tile (row block, 256-column block) as its 128 rows of 128 bytes."""
+    from kimi_k3_mlx_macmini_b200.mxfp4 import packed_tiles
+    rng = np.random.default_rng(4)
+    p = rng.integers(0, 256, size=(2, 256, 512 // 2), dtype=np.uint8)
+    out = packed_tiles(torch.from_numpy(p).cuda()).cpu().numpy()
+    assert out.shape == (2, 2, 2, 128, 128)
+    for b in range(2):
+        for rb in range(2):
+            for kt in range(2):
+                assert np.array_equal(out[b, rb, kt], p[b, rb * 128:(rb + 1) * 128, kt * 128:(kt + 1) * 128])
