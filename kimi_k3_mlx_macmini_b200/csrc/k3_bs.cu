@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
     uint64_t* acce = accf + 2;           // [2] accumulator drained (epilogue -> MMA)
     uint64_t* drain = acce + 2;          // MMA teardown
     __shared__ uint32_t s_tmem;
+    __shared__ Plan s_plan;                           // the routing plan, copied once
     __shared__ int s_last;
     __shared__ int s_nseg;
     __shared__ int s_seg[kTMaxSegments];
@@ -93,12 +94,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 1) tmem_alloc(&s_tmem, kCols);
+    for (int i = threadIdx.x; i < int(sizeof(Plan) / 4); i += blockDim.x)
+        reinterpret_cast<int*>(&s_plan)[i] = reinterpret_cast<const int*>(a.plan)[i];
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tm = s_tmem;
 
-    const Plan* P = a.plan;
+    const Plan* P = &s_plan;
     const int n_active = P->n_active;
     const int M = P->M;
     const int64_t nRb = a.rows / kBRows;
@@ -114,6 +117,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
+            const uint64_t stream_once = l2_evict_first();
             uint32_t gs = 0;
             for (int64_t i = i0; i < i1 && !s_abort; ++i) {
                 const int64_t key = i / ipk, j = i % ipk;
@@ -137,13 +141,19 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     const int r0 = rb * kBRows;
                     const int64_t sfo = int64_t(slot) * a.sf_slot + (int64_t(rb) * kcks + k / 128) * kBChunk;
                     const int tb = slot * int(nRb) + rb;                 // tile row block
-                    if (a.tiled) tma_4d(&st.a[0][0][0], &maps.a0, 0, 0, int(k / kBStageK), tb, &full[si]);
-                    else tma_3d(&st.a[0][0][0], &maps.a0, int(k / 2), r0, slot, &full[si]);
-                    bulk_g2s(&st.sfa[0][0], a.sfa0 + sfo, 2 * kBChunk, &full[si]);
+                    if (a.tiled)
+                        tma_4d_hint(&st.a[0][0][0], &maps.a0, 0, 0, int(k / kBStageK), tb, &full[si], stream_once);
+                    else
+                        tma_3d_hint(&st.a[0][0][0], &maps.a0, int(k / 2), r0, slot, &full[si], stream_once);
+                    bulk_g2s_hint(&st.sfa[0][0], a.sfa0 + sfo, 2 * kBChunk, &full[si], stream_once);
                     if (GATEUP) {
-                        if (a.tiled) tma_4d(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), tb, &full[si]);
-                        else tma_3d(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), r0, slot, &full[si]);
-                        bulk_g2s(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si]);
+                        if (a.tiled)
+                            tma_4d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), tb, &full[si],
+                                        stream_once);
+                        else
+                            tma_3d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), r0, slot, &full[si],
+                                        stream_once);
+                        bulk_g2s_hint(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si], stream_once);
                         tma_2d(&st.b[0][0], &maps.b, int(k / 2), 0, &full[si]);
                         bulk_g2s(&st.sfb[0], a.sfb + (k / 128) * kBChunk, 2 * kBChunk, &full[si]);
                     } else {
@@ -293,10 +303,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 }
                 __threadfence();
                 if (et == 0) {
+                    // the key's segments: one per CTA b owning items of it, starting at that
+                    // CTA's first item (CTAs with empty ranges own nothing)
                     int ns = 0;
-                    for (int64_t jj = 0; jj < ipk && ns < kTMaxSegments; ++jj)
-                        if (jj == 0 || owner_of(ks + jj, n, grid) != owner_of(ks + jj - 1, n, grid))
-                            s_seg[ns++] = int(jj);
+                    const int64_t b0 = owner_of(ks, n, grid), b1 = owner_of(ks + ipk - 1, n, grid);
+                    for (int64_t cb = b0; cb <= b1 && ns < kTMaxSegments; ++cb) {
+                        const int64_t f0 = cb * n / grid, f1 = (cb + 1) * n / grid;
+                        if (f1 > f0) s_seg[ns++] = int((f0 > ks ? f0 : ks) - ks);
+                    }
                     s_nseg = ns;
                 }
             }
@@ -312,15 +326,17 @@ __global__ void __launch_bounds__(kBThreads, 1)
             if (!local) {
                 __threadfence();
 #pragma unroll
-                for (int t = 0; t < kMaxTok; ++t) {
-                    float v0 = 0.0f, v1 = 0.0f;
-                    for (int sg = 0; sg < s_nseg; ++sg) {
-                        const float* sp = kpart + int64_t(s_seg[sg]) * (kPW * kBRows);
-                        v0 += __ldcg(sp + t * kBRows + r);
-                        if (GATEUP) v1 += __ldcg(sp + (kMaxTok + t) * kBRows + r);
+                for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+                for (int sg = 0; sg < s_nseg; ++sg) {       // segment order: deterministic sums
+                    const float* sp = kpart + int64_t(s_seg[sg]) * (kPW * kBRows);
+                    float v[kPW];
+#pragma unroll
+                    for (int c = 0; c < kPW; ++c) v[c] = __ldcg(sp + c * kBRows + r);
+#pragma unroll
+                    for (int t = 0; t < kMaxTok; ++t) {
+                        acc0[t] += v[t];
+                        if (GATEUP) acc1[t] += v[(GATEUP ? kMaxTok : 0) + t];
                     }
-                    acc0[t] = v0;
-                    acc1[t] = v1;
                 }
             }
             if (GATEUP) {

@@ -114,7 +114,7 @@ __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, u
     float res[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) res[i] = v[i];
-#pragma unroll
+#pragma unroll 1
     for (int p = 0; p < kBPieces; ++p) {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {

@@ -6,81 +6,150 @@
 
 namespace k3 {
 
+// Orderable 32-bit key of a float (unsigned order == float order; -0 keys as +0). NaN
+// keys as 0, below every number, so it is never selected.
+__device__ __forceinline__ uint32_t order_key(float f) {
+    if (f != f) return 0u;
+    const uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ uint32_t redux_max_u32(uint32_t v) {
+    uint32_t r;
+    asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;\n" : "=r"(r) : "r"(v));
+    return r;
+}
+__device__ __forceinline__ uint32_t redux_min_u32(uint32_t v) {
+    uint32_t r;
+    asm volatile("redux.sync.min.u32 %0, %1, 0xffffffff;\n" : "=r"(r) : "r"(v));
+    return r;
+}
+
 // Top-k of one token's row by one warp: raw = sigmoid(logit), corrected = raw + bias;
 // k rounds of a warp argmax on (corrected desc, index asc); weights gathered from raw.
+// Lane l holds entries l, l+32, ...; every load is issued up front (clamped index), and a
+// round is a lane-local scan plus two warp reductions (max key, then lowest index).
 __device__ inline void topk_row(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
-                         int k, int renorm, float scale, int32_t* __restrict__ idx_out,
-                         float* __restrict__ w_out, float* __restrict__ raw_out,
-                         float* __restrict__ cor_out, int lane, int* status) {
-    float raw[32], cor[32];
+                                int k, int renorm, float scale, int32_t* __restrict__ idx_out,
+                                float* __restrict__ w_out, float* __restrict__ raw_out,
+                                float* __restrict__ cor_out, int lane, int* status) {
+    const int ni = (E + 31) / 32;
+    float raw[32];
+    uint32_t key[32];
+    float lv[32], bv[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-        const int e = lane + 32 * i;
-        if (e < E) {
-            const float l = __ldcg(lrow + e);      // may come from other CTAs of this launch
-            const float r = 1.0f / (1.0f + expf(-l));
-            const float c = r + (bias ? bias[e] : 0.0f);
-            raw[i] = r;
-            cor[i] = c;
-            if (raw_out) raw_out[e] = r;
-            if (cor_out) cor_out[e] = c;
-        } else {
-            raw[i] = 0.0f;
-            cor[i] = -INFINITY;
+        const int e = min(lane + 32 * min(i, ni - 1), E - 1);
+        lv[i] = __ldcg(lrow + e);                          // may come from other CTAs
+        bv[i] = bias ? __ldg(bias + e) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        key[i] = 0u;
+        raw[i] = 0.0f;
+        if (i < ni) {
+            const int e = lane + 32 * i;
+            const float r = 1.0f / (1.0f + expf(-lv[i]));
+            const float c = r + bv[i];
+            if (e < E) {
+                raw[i] = r;
+                key[i] = order_key(c);
+                if (raw_out) raw_out[e] = r;
+                if (cor_out) cor_out[e] = c;
+            }
         }
     }
-    float wsel[kMaxTopK > 32 ? kMaxTopK : 32];
-    int isel[kMaxTopK > 32 ? kMaxTopK : 32];
-    for (int s = 0; s < 32; ++s) {
-        if (s >= k) break;
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
+    float wsum = 0.0f;
+    for (int s = 0; s < k; ++s) {
+        uint32_t best = 0u;
+        int bi = 0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int e = lane + 32 * i;
-            if (e < E && (cor[i] > bv || (cor[i] == bv && e < bi))) {
-                bv = cor[i];
-                bi = e;
+        for (int i = 0; i < 32; ++i)
+            if (i < ni && key[i] > best) {                // strict: the lowest index wins ties
+                best = key[i];
+                bi = i;
             }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (bi >= E) {            // only NaN rows get here: report, pick a valid index
+        const uint32_t kmax = redux_max_u32(best);
+        const uint32_t cand = (best == kmax) ? uint32_t(lane + 32 * bi) : 0xffffffffu;
+        uint32_t e = redux_min_u32(cand);
+        if (kmax == 0u) {                                  // only NaN / exhausted rows get here
             if (lane == 0) atomicExch(status, K3_ERR_INVALID);
-            bi = 0;
+            e = 0;
         }
-        // the owner lane reads the raw score and retires the entry: a NaN never compares
-        // greater or equal, so it cannot win again even when every other entry is -inf
         float mine = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            if (lane + 32 * i == bi) {
+        for (int i = 0; i < 32; ++i)
+            if (lane + 32 * i == int(e)) {
                 mine = raw[i];
-                cor[i] = __int_as_float(0x7fc00000u);
+                key[i] = 0u;                               // retired
             }
+        const float w = __shfl_sync(0xffffffffu, mine, int(e) & 31);
+        wsum += w;
+        if (lane == 0) {
+            idx_out[s] = int32_t(e);
+            w_out[s] = w;
         }
-        wsel[s] = __shfl_sync(0xffffffffu, mine, bi & 31);
-        isel[s] = bi;
     }
     // w / (sum + 1e-20) then * scale, as moe.py:74-76 / k3ref/layers.py:221-224
-    float sum = 0.0f;
-    for (int s = 0; s < k; ++s) sum += wsel[s];
-    const float den = sum + 1e-20f;
-    if (lane == 0) {
+    __syncwarp();
+    if (lane < k) {
+        const float w = w_out[lane];
+        w_out[lane] = ((k > 1 && renorm) ? w / (wsum + 1e-20f) : w) * scale;
+    }
+    __syncwarp();
+}
+
+// Whole-CTA top-k of M token rows with compact (rolled) loops: the code runs once per
+// call in one CTA, so its instruction footprint, not its arithmetic, sets its time.
+// s_key: shared scratch of M * E words. raw = sigmoid(logit), corrected = raw + bias;
+// per token (warp t) k rounds of argmax on (corrected desc, index asc); weights are the
+// raw scores of the winners, renormalised and scaled as topk_row does.
+__device__ inline void topk_cta(const float* __restrict__ logits, const float* __restrict__ bias, int M,
+                                int E, int k, int renorm, float scale, int32_t* __restrict__ idx_out,
+                                float* __restrict__ w_out, uint32_t* s_key, int warp, int lane, int* status) {
+#pragma unroll 1
+    for (int i = threadIdx.x; i < M * E; i += blockDim.x) {
+        const float l = __ldcg(logits + i);                   // may come from other CTAs
+        const float r = 1.0f / (1.0f + expf(-l));
+        s_key[i] = order_key(r + (bias ? __ldg(bias + i % E) : 0.0f));
+    }
+    __syncthreads();
+    if (warp < M) {
+        uint32_t* row = s_key + warp * E;
+        int mine = -1;                                        // lane s < k: index of round s
+#pragma unroll 1
         for (int s = 0; s < k; ++s) {
-            idx_out[s] = isel[s];
-            w_out[s] = ((k > 1 && renorm) ? wsel[s] / den : wsel[s]) * scale;
+            uint32_t best = 0u;
+            int bi = 0;
+#pragma unroll 1
+            for (int e = lane; e < E; e += 32) {
+                const uint32_t v = row[e];
+                if (v > best) {                               // strict: lowest index wins ties
+                    best = v;
+                    bi = e;
+                }
+            }
+            const uint32_t kmax = redux_max_u32(best);
+            uint32_t e = redux_min_u32(best == kmax ? uint32_t(bi) : 0xffffffffu);
+            if (kmax == 0u) {                                 // only NaN / exhausted rows
+                if (lane == 0) atomicExch(status, K3_ERR_INVALID);
+                e = 0;
+            }
+            if (lane == 0) row[e] = 0u;                       // retired
+            if (lane == s) mine = int(e);
+            __syncwarp();
+        }
+        // weights: raw scores of the winners, summed in selection order
+        float w = 0.0f;
+        if (lane < k) w = 1.0f / (1.0f + expf(-__ldcg(logits + int64_t(warp) * E + mine)));
+        float sum = 0.0f;
+#pragma unroll 1
+        for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, w, s);
+        if (lane < k) {
+            idx_out[warp * k + lane] = mine;
+            w_out[warp * k + lane] = ((k > 1 && renorm) ? w / (sum + 1e-20f) : w) * scale;
         }
     }
 }
-
 
 // The routing part of a decode call.
 struct PlanArgs {
@@ -100,107 +169,130 @@ struct PlanArgs {
 
 // Whole-CTA: zero the counters, run the top-k when `logits` is given (warp t: token t),
 // then build the plan: active experts in ascending id order (moe.py:120), per expert its
-// (token, weight) pairs in ascending token order, the shared expert last.
-__device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, int warp, int lane) {
+// (token, weight) pairs in ascending token order, the shared expert last. Every routing
+// entry finds its expert's slot and its rank among the same expert's earlier entries in
+// parallel.
+__device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, int warp, int lane,
+                                      uint32_t* s_key = nullptr) {
     Plan* P = a.plan;
     __shared__ uint32_t bitmap[kMaxExperts / 32];
+    __shared__ int16_t pos_e[kMaxExperts];          // active index of expert e
     __shared__ int cnt[kMaxActive];
+    __shared__ int start[kMaxActive + 1];
     __shared__ int n_routed;
     __shared__ int s_idx[kMaxTok * kMaxTopK];
     __shared__ float s_w[kMaxTok * kMaxTopK];
     if (threadIdx.x == 0) P->status = K3_OK;
     for (int64_t i = threadIdx.x; i < a.n_cntA; i += blockDim.x) a.cntA[i] = 0;
     for (int64_t i = threadIdx.x; i < a.n_cntB; i += blockDim.x) a.cntB[i] = 0;
+    for (int i = threadIdx.x; i < kMaxExperts / 32; i += blockDim.x) bitmap[i] = 0;
+    for (int i = threadIdx.x; i < kMaxActive; i += blockDim.x) cnt[i] = 0;
     __syncthreads();
-    if (logits && warp < a.M) {
+    if (logits && s_key) {
+        topk_cta(logits, a.bias, a.M, a.E, a.k, a.renorm, a.scale, a.idx, a.w, s_key, warp, lane,
+                 &P->status);
+    } else if (logits && warp < a.M) {
         topk_row(logits + int64_t(warp) * a.E, a.bias, a.E, a.k, a.renorm, a.scale,
                  a.idx + warp * a.k, a.w + warp * a.k, nullptr, nullptr, lane, &P->status);
     }
-    for (int i = threadIdx.x; i < kMaxExperts / 32; i += blockDim.x) bitmap[i] = 0;
-    __syncthreads();                               // top-k results and zeroed bitmap visible
+    __syncthreads();                               // top-k results visible
     const int nsel = a.M * a.k;
     for (int i = threadIdx.x; i < nsel; i += blockDim.x) {
-        s_idx[i] = a.idx[i];
+        const int e = a.idx[i];
+        s_idx[i] = e;
         s_w[i] = a.w[i];
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < nsel; i += blockDim.x) {
-        const int e = s_idx[i];
-        if (e < 0 || e >= a.E) {
+        if (e < 0 || e >= a.E)
             P->status = K3_ERR_INVALID;
-            continue;
-        }
-        atomicOr(&bitmap[e >> 5], 1u << (e & 31));
+        else
+            atomicOr(&bitmap[e >> 5], 1u << (e & 31));
     }
     __syncthreads();
     if (warp == 0) {                               // ascending unique expert list
-        const uint32_t word = bitmap[lane];
-        const int c = __popc(word);
-        int incl = c;
+        int base = 0;
+        for (int w0 = 0; w0 < kMaxExperts / 32; w0 += 32) {
+            const uint32_t word = bitmap[w0 + lane];
+            const int c = __popc(word);
+            int incl = c;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            int pos = base + incl - c;
+            uint32_t wv = word;
+            while (wv) {
+                const int b = __ffs(wv) - 1;
+                wv &= wv - 1;
+                const int e = (w0 + lane) * 32 + b;
+                P->expert[pos] = e;
+                pos_e[e] = int16_t(pos);
+                ++pos;
+            }
+            base += __shfl_sync(0xffffffffu, incl, 31);
         }
-        int pos = incl - c;
-        uint32_t wv = word;
-        while (wv) {
-            const int b = __ffs(wv) - 1;
-            wv &= wv - 1;
-            P->expert[pos++] = lane * 32 + b;
-        }
-        if (lane == 31) n_routed = incl;
+        if (lane == 0) n_routed = base;
     }
     __syncthreads();
     const int nr = n_routed;
     const int na = nr + (a.has_shared ? 1 : 0);
-    for (int u = threadIdx.x; u < na; u += blockDim.x) {
-        int c = 0;
-        if (u < nr) {
-            const int e = P->expert[u];
-            for (int i = 0; i < nsel; ++i) c += (s_idx[i] == e);
-            if (c > kMaxTok) {          // a token listed the same expert twice: invalid routing
-                P->status = K3_ERR_INVALID;
-                c = kMaxTok;
-            }
-        } else {
-            c = a.M;
-            P->expert[u] = a.E;                    // shared expert slot in the table
+    // rank of each entry among the earlier entries of its expert (token-major order)
+    int my_rank = 0, my_pos = 0;
+    const int i_me = threadIdx.x;
+    if (i_me < nsel) {
+        const int e = s_idx[i_me];
+        if (e >= 0 && e < a.E) {
+            for (int j = 0; j < i_me; ++j) my_rank += (s_idx[j] == e);
+            my_pos = pos_e[e];
+            atomicAdd(&cnt[my_pos], 1);
         }
-        cnt[u] = c;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int s = 0;
-        for (int u = 0; u < na; ++u) {
-            P->pair_start[u] = s;
-            s += cnt[u];
+    if (warp == 0) {                               // pair offsets: exclusive scan of counts
+        int base = 0;
+        for (int u0 = 0; u0 < na + 1; u0 += 32) {
+            const int u = u0 + lane;
+            int c = 0;
+            if (u < nr) {
+                c = cnt[u];
+                if (c > kMaxTok) {                 // a token listed the same expert twice
+                    P->status = K3_ERR_INVALID;
+                    c = kMaxTok;
+                }
+            } else if (u < na) {
+                c = a.M;                           // shared expert: every token
+            }
+            int incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (u <= na) {
+                start[u] = base + incl - c;
+                P->pair_start[u] = base + incl - c;
+            }
+            base += __shfl_sync(0xffffffffu, incl, 31);
         }
-        P->pair_start[na] = s;
-        P->n_active = na;
-        P->n_pairs = s;
-        P->M = a.M;
+        if (lane == 0) {
+            P->n_active = na;
+            P->n_pairs = start[na];
+            P->M = a.M;
+            if (a.has_shared) P->expert[nr] = a.E;     // shared expert slot in the table
+        }
     }
     __syncthreads();
-    for (int u = threadIdx.x; u < na; u += blockDim.x) {
-        int p = P->pair_start[u];
-        if (u < nr) {
-            const int e = P->expert[u];
-            const int pend = P->pair_start[u + 1];
-            for (int t = 0; t < a.M; ++t)
-                for (int s = 0; s < a.k; ++s)
-                    if (s_idx[t * a.k + s] == e && p < pend) {
-                        P->pair_tok[p] = t;
-                        P->pair_w[p] = s_w[t * a.k + s];
-                        ++p;
-                    }
-        } else {
-            for (int t = 0; t < a.M; ++t) {
-                P->pair_tok[p] = t;
-                P->pair_w[p] = 1.0f;
-                ++p;
-            }
+    if (i_me < nsel) {
+        const int e = s_idx[i_me];
+        if (e >= 0 && e < a.E && my_rank < kMaxTok) {
+            const int p = start[my_pos] + my_rank;
+            P->pair_tok[p] = i_me / a.k;
+            P->pair_w[p] = s_w[i_me];
         }
+    }
+    if (a.has_shared && int(threadIdx.x) < a.M) {
+        const int p = start[nr] + threadIdx.x;
+        P->pair_tok[p] = threadIdx.x;
+        P->pair_w[p] = 1.0f;
     }
 }
 

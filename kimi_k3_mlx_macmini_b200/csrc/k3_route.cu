@@ -133,15 +133,17 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    build_plan_cta(a.plan_args, a.logits, warp, lane);
+    extern __shared__ uint32_t s_key[];                      // M * E top-k keys
+    build_plan_cta(a.plan_args, a.logits, warp, lane, s_key);
 }
 
 int launch_route_fused(const RouteArgs& a, int kq, cudaStream_t s) {
     const dim3 grid(unsigned((a.E + 15) / 16), unsigned(kq));
+    const size_t keys = sizeof(uint32_t) * size_t(a.M) * size_t(a.E);     // <= 32 KiB
     if (a.x_dtype == K3_F32)
-        route_fused_kernel<true><<<grid, 256, 0, s>>>(a);
+        route_fused_kernel<true><<<grid, 256, keys, s>>>(a);
     else
-        route_fused_kernel<false><<<grid, 256, 0, s>>>(a);
+        route_fused_kernel<false><<<grid, 256, keys, s>>>(a);
     K3_CHECK_LAUNCH("route_fused_kernel");
     return K3_OK;
 }
