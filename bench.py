@@ -10,14 +10,16 @@ expert + weighted scatter-add).
 
     python bench.py [--gpus N --steps K --warmup W --tokens M] [--impl reference]
 
-Timing: ``value`` replays one CUDA graph per token batch with inputs resident in HBM,
-bracketed by CUDA events; every step uses a fresh token batch so it reads a fresh set of
-experts out of a 9 GB pool (inputs larger than L2). ``e2e`` times the public API call on
-pinned host tensors with the host->device copy of x and the device->host copy of y inside
-the timed region. ``roofline`` covers the dominant kernel (the grouped gate/up matvec),
-timed per launch with CUDA events on its launch stream in a second pass. Multi-GPU runs
-are weak-scaled replicas (each rank its own tokens and a full copy of the layer); the
-time is the max over ranks.
+Timing: ``value`` replays CUDA graphs (one per token batch, a ring of up to 64 distinct
+batches) with inputs resident in HBM, bracketed by CUDA events; consecutive steps use
+different token batches so each reads a different set of experts out of a 9 GB pool
+(inputs larger than L2). ``e2e`` times the public API call on pinned host tensors with
+the host->device copy of x and the device->host copy of y inside the timed region.
+``roofline`` covers the dominant kernel (the block-scaled gate/up grouped matvec), timed
+per launch with CUDA events on its launch stream in a second pass. SM clocks and
+throttle reasons are sampled during the timed region (NVML every ~2 ms, plus
+nvidia-smi). Multi-GPU runs are weak-scaled replicas (each rank its own tokens and a full
+copy of the layer); the time is the max over ranks.
 """
 from __future__ import annotations
 
@@ -46,8 +48,8 @@ ROUTER_BYTES = E * H * 2
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--tokens", type=int, default=8)
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
@@ -106,8 +108,33 @@ class ClockSampler:
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, local_rank: int):
+        import threading
+
         import torch
         self.proc = None
+        self.nv = []                                  # (sm MHz, max MHz, reasons bitmask)
+        self._stop = threading.Event()
+        self._thr = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+
+            def poll():
+                while not self._stop.is_set():
+                    try:
+                        self.nv.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                        pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                        pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                    except Exception:
+                        return
+                    time.sleep(0.002)
+            self._thr = threading.Thread(target=poll, daemon=True)
+            self._thr.start()
+        except Exception:
+            self._thr = None
         try:
             uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
             uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
@@ -117,9 +144,22 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    # NVML clocks-event reason bits (nvml.h): sw power cap 0x4, hw slowdown 0x8,
+    # sw thermal 0x20, hw thermal 0x40
+    NV_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
+
     def stop(self) -> dict:
-        if self.proc is None:
+        self._stop.set()
+        if self._thr is not None:
+            self._thr.join(timeout=2)
+        if self.proc is None and not self.nv:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        if self.proc is None:
+            reasons = sorted(n for n, b in self.NV_BITS.items() if any(r & b for _, _, r in self.nv))
+            return {"sm_mhz": statistics.median(c for c, _, _ in self.nv),
+                    "sm_max_mhz": max(m for _, m, _ in self.nv), "samples": len(self.nv),
+                    "source": "nvml", "reasons": reasons}
         time.sleep(0.25)
         self.proc.terminate()
         try:
@@ -141,8 +181,15 @@ class ClockSampler:
             for n, v in zip(names, f[4:8]):
                 if v.lower() == "active":
                     reasons.add(n)
+        for n, b in self.NV_BITS.items():
+            if any(r & b for _, _, r in self.nv):
+                reasons.add(n)
+        if self.nv:                                   # in-region NVML samples take precedence
+            sm = [c for c, _, _ in self.nv]
+            mx = mx + [m for _, m, _ in self.nv]
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
+                "source": "nvml+nvidia-smi" if self.nv else "nvidia-smi",
                 "reasons": sorted(reasons)}
 
 
@@ -222,12 +269,15 @@ def run_reference(args, rank, world):
 # ------------------------------------------------------------------ B200 arm
 
 def traffic_from_profiles():
-    """Per-launch DRAM bytes of the gate/up kernel from the committed ncu summary."""
-    f = ROOT / "profiles" / "gemv_gateup_config2.md"
+    """(DRAM bytes, algorithmic bytes) of one full-size gate/up launch from the committed
+    ncu summary (dram__bytes_read.sum + dram__bytes_write.sum)."""
+    f = ROOT / "profiles" / "bs_gemv_gateup_config2.md"
     if not f.exists():
-        return None
-    m = re.search(r"traffic_bytes_per_launch_full:\s*([0-9.eE+]+)", f.read_text())
-    return float(m.group(1)) if m else None
+        return None, None
+    txt = f.read_text()
+    m = re.search(r"traffic_bytes_per_launch_full:\s*([0-9.eE+]+)", txt)
+    a = re.search(r"traffic_launch_algorithmic_bytes:\s*([0-9.eE+]+)", txt)
+    return (float(m.group(1)) if m else None), (float(a.group(1)) if a else None)
 
 
 def run_b200(args, rank, world, local):
@@ -237,30 +287,31 @@ def run_b200(args, rank, world, local):
 
     torch.cuda.set_device(local)
     M, K, W = args.tokens, args.steps, args.warmup
-    nb = K + W
+    R = min(K + W, 64)                                      # distinct token batches
     lay = synthetic.baseline_layer(seed=args.seed, E=args.experts, H=H, I=I_, top_k=TOPK, scale=SCALE)
     moe = lay.moe()
     _ = moe.pool
-    xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, M, H) for i in range(nb)]
+    xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, M, H) for i in range(R)]
     U = []
     for x in xs:
         U.append(int(torch.unique(moe.route(x).expert_indices).numel()))
     torch.cuda.synchronize()
+    step_x = [(W + i) % R for i in range(K)]                # batch of timed step i
 
-    # ---- device-resident timing: one CUDA graph per token batch
+    # ---- device-resident timing: one CUDA graph per token batch, replayed as a ring
     cap = torch.cuda.Stream()
     with torch.cuda.stream(cap):
         for i in range(2):
             moe(xs[i])
     torch.cuda.synchronize()
     graphs, ys = [], []
-    for i in range(nb):
+    for i in range(R):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=cap):
             ys.append(moe(xs[i]))
         graphs.append(g)
     for i in range(W):
-        graphs[i].replay()
+        graphs[i % R].replay()
     torch.cuda.synchronize()
     barrier(world)
     clk = ClockSampler(local)
@@ -268,8 +319,8 @@ def run_b200(args, rank, world, local):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record()
-    for i in range(W, nb):
-        graphs[i].replay()
+    for i in range(K):
+        graphs[step_x[i]].replay()
     ev1.record()
     torch.cuda.synchronize()
     clocks = clk.stop()
@@ -277,20 +328,21 @@ def run_b200(args, rank, world, local):
     ms = dist_max(ev0.elapsed_time(ev1) / K, world)
     value = world * M / (ms / 1e3)
 
-    # ---- per-kernel timing of the same steps (eager launches, events per kernel)
+    # ---- per-kernel timing of the same batches (eager launches, events per kernel)
+    n_prof = min(K, 50)
     L.profile_enable(True)
     L.profile_collect()
     torch.cuda.synchronize()
     # keep the GPU busy while the host enqueues, so each event pair brackets device time
     torch.cuda._sleep(int(4e7))
-    for i in range(W, nb):
-        moe(xs[i])
+    for i in range(n_prof):
+        moe(xs[step_x[i]])
     torch.cuda.synchronize()
     prof = L.profile_collect()
     L.profile_enable(False)
     gu_ms, gu_n = prof["gateup"]
     dn_ms, dn_n = prof["down"]
-    U_t = U[W:]
+    U_t = [U[step_x[i]] for i in range(n_prof)]
     gu_bytes = np.mean([(u + 1) * 2 * PROJ_BYTES for u in U_t]) + M * H * 2
     dn_bytes = np.mean([(u + 1) * PROJ_BYTES for u in U_t])
     layer_bytes = np.mean([(u + 1) * EXPERT_BYTES for u in U_t]) + args.experts * H * 2
@@ -303,14 +355,14 @@ def run_b200(args, rank, world, local):
     yh = torch.empty((M, H), dtype=torch.float32).pin_memory()
     xd = torch.empty((M, H), dtype=torch.bfloat16, device="cuda")
     for i in range(W):
-        xd.copy_(xh[i], non_blocking=True)
+        xd.copy_(xh[i % R], non_blocking=True)
         yh.copy_(moe(xd), non_blocking=True)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(W, nb):
-        xd.copy_(xh[i], non_blocking=True)
+    for i in range(K):
+        xd.copy_(xh[step_x[i]], non_blocking=True)
         yh.copy_(moe(xd), non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
@@ -329,27 +381,31 @@ def run_b200(args, rank, world, local):
     line = {
         "metric": "moe_layer_decode_tokens_per_s", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "e2m1+f16 mma, f32 accumulate",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1 weights x e2m1 activation pieces, e8m0 block scales, f32 accumulate (tcgen05 kind::mxf4)",
         "data": "synthetic (seeded random-init weights of the BASELINE layer)",
         "config": {"workload": f"BASELINE configs[2]: one MoE layer decode, M={M} tokens per GPU, "
                                f"{args.experts} routed + 1 shared MXFP4 expert (7168/2048), bf16 router, "
                                "top-8, x2.5",
                    "tokens_per_gpu": M, "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2: 9.0 GB expert pool, fresh token batch per step",
-                   "timing": "CUDA graph per batch, events around K replays"},
+                   "timing": f"CUDA graph per batch ({R} distinct batches replayed as a ring), "
+                             "events around K replays"},
         "unique_experts_mean": float(np.mean(U_t)),
+        "unique_experts_per_batch": U[:8],
         "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<gate/up> (grouped MXFP4 matvec)",
+        "roofline": {"bound": "hbm", "kernel": "bs_gemv_kernel<gate/up> (block-scaled grouped MXFP4 matvec, tcgen05)",
                      "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
-                     "peak_kind": peak_kind, "traffic": traffic_from_profiles(),
+                     "peak_kind": peak_kind, "traffic": traffic_from_profiles()[0],
+                     "traffic_launch_algorithmic_bytes": traffic_from_profiles()[1],
                      "algorithmic_bytes_per_launch": gu_bytes,
                      "launch_ms": gu_ms / gu_n},
         "down_kernel": {"achieved": dn_gbs, "frac": dn_gbs / peak, "launch_ms": dn_ms / dn_n},
-        "kernel_ms_per_step": {k: v[0] / K for k, v in prof.items() if v[1]},
+        "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
         "e2e": {"value": world * M / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
                 "ms_per_step": e2e_ms, "api": "LatentMoE.__call__ (k3_moe_decode)"},
-        "gpu_launches": int(sum(c for _, c in prof.values())),
+        "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
