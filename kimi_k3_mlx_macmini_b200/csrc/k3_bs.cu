@@ -11,13 +11,16 @@
 //           accumulator, then tcgen05.commit frees the stage and, at the end of an item,
 //           hands the accumulator to the epilogue;
 //   warps 2-5 epilogue: warp w reads TMEM lanes 32*(w%4).. (weight rows), sums the pieces
-//           of each column, accumulates the items of a key in registers and flushes it
-//           (gate/up: activation, weight, split into the next launch's E2M1 pieces; down:
-//           y rows), through per-segment partials when the key spans CTAs.
+//           of each pair, accumulates the items of a key in registers and flushes it
+//           (gate/up: activation x routing weight, split into the next launch's E2M1
+//           pieces; down: one output row per pair), through per-segment partials when the
+//           key spans CTAs.
 //
-// Work items, keys and contiguous per-CTA item ranges are those of the f16 TMA kernels:
-// gate/up key = (active expert u, 128-row block of I), items = k-chunks of H; down key =
-// 128-row block of H, items = (u, k-chunk of I) with u ascending. Every wait is bounded.
+// Work: key = (128-row block, expert item) for both phases, items = its k-chunks; each
+// CTA owns a contiguous range of items. The B operand holds only the expert's (token,
+// weight) pairs (8 piece rows per pair), so a call may carry any number of tokens; the
+// down phase writes one output row per pair and the combine kernel sums a token's pairs.
+// Every wait is bounded.
 #include "k3_async.cuh"
 #include "k3_bs.cuh"
 #include "k3_tma.cuh"
@@ -59,7 +62,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
     constexpr int kAccW = GATEUP ? 128 : 64;               // TMEM columns per accumulator
     constexpr int kSf0 = 2 * kAccW;                        // first scale column
     constexpr int kSfW = GATEUP ? 24 : 16;                 // scale columns per stage
-    constexpr int kPW = GATEUP ? 2 * kMaxTok : kMaxTok;    // partial values per row
+    constexpr int kMaxPr = kBMaxN / kBPieces;              // pairs per expert item (8)
+    constexpr int kPW = GATEUP ? 2 * kMaxPr : kMaxPr;      // partial values per row
     static_assert(kSf0 + kSfW * S <= int(kCols), "TMEM plan exceeds the allocation");
 
     extern __shared__ uint8_t smem_raw[];
@@ -101,18 +105,19 @@ __global__ void __launch_bounds__(kBThreads, 1)
     tc_fence_after();
     const uint32_t tm = s_tmem;
 
+    // Keys: (128-row block rb, expert item v), key = rb * V + v (row-block major, so heavy
+    // experts spread over CTAs); items = the key's C k-chunks.
     const Plan* P = &s_plan;
-    const int n_active = P->n_active;
-    const int M = P->M;
+    const int V = P->n_active;
     const int64_t nRb = a.rows / kBRows;
-    const int64_t ipk = GATEUP ? a.C : int64_t(n_active) * a.C;      // items per key
-    const int64_t n_keys = GATEUP ? int64_t(n_active) * nRb : nRb;
-    const int64_t n = n_keys * ipk;
+    const int64_t ipk = a.C;
+    const int64_t n = int64_t(V) * nRb * ipk;
     const int64_t grid = gridDim.x, bid = blockIdx.x;
     const int64_t i0 = bid * n / grid, i1 = (bid + 1) * n / grid;
     const int64_t kchunk = a.K / a.C;
     const int nst = int(kchunk / kBStageK);
     const int64_t kcks = a.K / 128;                                   // scale chunks per row block
+    const int64_t G = a.K / 32;                                       // scale blocks per row
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -120,15 +125,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
             const uint64_t stream_once = l2_evict_first();
             uint32_t gs = 0;
             for (int64_t i = i0; i < i1 && !s_abort; ++i) {
-                const int64_t key = i / ipk, j = i % ipk;
-                const int u = GATEUP ? int(key % n_active) : int(j / a.C);
-                const int rb = GATEUP ? int(key / n_active) : int(key);
-                const int kc = int(GATEUP ? j : j % a.C);
-                const int slot = P->expert[u];
-                const int ntok = GATEUP ? M : P->pair_start[u + 1] - P->pair_start[u];
-                const int64_t k0 = int64_t(kc) * kchunk;
+                const int64_t key = i / ipk;
+                const int v = int(key % V), rb = int(key / V), kc = int(i % ipk);
+                const int slot = P->expert[v];
+                const int ps = P->pair_start[v], np = P->pair_start[v + 1] - ps;
                 const uint32_t bytes = uint32_t((GATEUP ? 2 : 1) * (kBRows * 128 + 2 * kBChunk) +
-                                                ntok * kBPieces * 128 + 2 * kBChunk);
+                                                np * kBPieces * 128 + 2 * kBChunk);
+                const int r0 = rb * kBRows;
+                const int tb = slot * int(nRb) + rb;                         // tile row block
                 for (int s = 0; s < nst; ++s, ++gs) {
                     const int si = int(gs % S);
                     if (!mbar_wait(&empty[si], ((gs / S) & 1) ^ 1, a.status, &s_abort)) {
@@ -136,11 +140,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
                         break;
                     }
                     St& st = ring[si];
-                    const int64_t k = k0 + int64_t(s) * kBStageK;
+                    const int64_t k = int64_t(kc) * kchunk + int64_t(s) * kBStageK;
                     mbar_expect_tx(&full[si], bytes);
-                    const int r0 = rb * kBRows;
                     const int64_t sfo = int64_t(slot) * a.sf_slot + (int64_t(rb) * kcks + k / 128) * kBChunk;
-                    const int tb = slot * int(nRb) + rb;                 // tile row block
                     if (a.tiled)
                         tma_4d_hint(&st.a[0][0][0], &maps.a0, 0, 0, int(k / kBStageK), tb, &full[si], stream_once);
                     else
@@ -148,20 +150,20 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     bulk_g2s_hint(&st.sfa[0][0], a.sfa0 + sfo, 2 * kBChunk, &full[si], stream_once);
                     if (GATEUP) {
                         if (a.tiled)
-                            tma_4d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), tb, &full[si],
-                                        stream_once);
+                            tma_4d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), tb,
+                                        &full[si], stream_once);
                         else
                             tma_3d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), r0, slot, &full[si],
                                         stream_once);
                         bulk_g2s_hint(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si], stream_once);
-                        tma_2d(&st.b[0][0], &maps.b, int(k / 2), 0, &full[si]);
-                        bulk_g2s(&st.sfb[0], a.sfb + (k / 128) * kBChunk, 2 * kBChunk, &full[si]);
+                        for (int pi = 0; pi < np; ++pi)      // one token's 8 piece rows per pair
+                            tma_2d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * P->pair_tok[ps + pi],
+                                   &full[si]);
                     } else {
-                        for (int it = 0; it < ntok; ++it)
-                            tma_3d(&st.b[kBPieces * it][0], &maps.b, int(k / 2), kBPieces * it, u, &full[si]);
-                        bulk_g2s(&st.sfb[0], a.sfb + (int64_t(u) * kcks + k / 128) * kBChunk, 2 * kBChunk,
-                                 &full[si]);
+                        for (int pi = 0; pi < np; ++pi)      // pair pi's 8 piece rows
+                            tma_3d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * pi, v, &full[si]);
                     }
+                    bulk_g2s(&st.sfb[0], a.sfb + (int64_t(v) * kcks + k / 128) * kBChunk, 2 * kBChunk, &full[si]);
                     s_issued = gs + 1;
                 }
             }
@@ -171,10 +173,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
         // The whole warp runs the loop (warp-uniform descriptors); one elected lane issues.
         uint32_t gs = 0, ib = 0;
         for (int64_t i = i0; i < i1 && !s_abort; ++i, ++ib) {
-            const int64_t j = i % ipk;
-            const int u = GATEUP ? int((i / ipk) % n_active) : int(j / a.C);
-            const int ntok = GATEUP ? M : P->pair_start[u + 1] - P->pair_start[u];
-            const int nb = kBPieces * ntok;                              // MMA N
+            const int v = int((i / ipk) % V);
+            const int np = P->pair_start[v + 1] - P->pair_start[v];
+            const int nb = kBPieces * np;                                // MMA N
             const uint32_t buf = ib & 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&acce[buf], ((ib >> 1) & 1) ^ 1, a.status, &s_abort))) {
                 s_abort = 1;
@@ -237,43 +238,30 @@ __global__ void __launch_bounds__(kBThreads, 1)
         const int r = 32 * q + lane;                          // weight row within the tile
         const int et = int(threadIdx.x) - 64;                 // 0..127
         const uint32_t lane_addr = uint32_t(32 * q) << 16;
-        float acc0[kMaxTok], acc1[kMaxTok];
+        float acc0[kMaxPr], acc1[kMaxPr];                     // per pair: gate (or down), up
 #pragma unroll
-        for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+        for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
         uint32_t ib = 0;
         for (int64_t i = i0; i < i1; ++i, ++ib) {
-            const int64_t key = i / ipk, j = i % ipk;
-            const int u = GATEUP ? int(key % n_active) : int(j / a.C);
-            const int ps = P->pair_start[u];
-            const int ntok = GATEUP ? M : P->pair_start[u + 1] - ps;
+            const int64_t key = i / ipk;
+            const int v = int(key % V), rb = int(key / V);
+            const int ps = P->pair_start[v], np = P->pair_start[v + 1] - ps;
             const uint32_t buf = ib & 1;
             const bool ok = mbar_wait(&accf[buf], (ib >> 1) & 1, a.status, &s_abort);
             if (ok) {
                 tc_fence_after();
                 const uint32_t d0 = tm + lane_addr + buf * kAccW;
 #pragma unroll
-                for (int c = 0; c < kMaxTok / 2; ++c) {
-                    if (2 * c >= ntok) break;
-                    float v[16];
-                    tmem_ld16(d0 + 16 * c, v);
-                    const float s0 = sum8(v), s1 = sum8(v + 8);
+                for (int c = 0; c < kMaxPr / 2; ++c) {
+                    if (2 * c >= np) break;
+                    float x[16];
+                    tmem_ld16(d0 + 16 * c, x);
+                    acc0[2 * c] += sum8(x);
+                    acc0[2 * c + 1] += sum8(x + 8);               // past np: unused garbage
                     if (GATEUP) {
-                        float w[16];
-                        tmem_ld16(d0 + 64 + 16 * c, w);
-                        const float t0 = sum8(w), t1 = sum8(w + 8);
-#pragma unroll
-                        for (int t = 0; t < kMaxTok; ++t) {
-                            if (t == 2 * c) { acc0[t] += s0; acc1[t] += t0; }
-                            if (t == 2 * c + 1) { acc0[t] += s1; acc1[t] += t1; }
-                        }
-                    } else {
-                        const int tk0 = P->pair_tok[ps + 2 * c];
-                        const int tk1 = 2 * c + 1 < ntok ? P->pair_tok[ps + 2 * c + 1] : -1;
-#pragma unroll
-                        for (int t = 0; t < kMaxTok; ++t) {
-                            if (t == tk0) acc0[t] += s0;
-                            if (t == tk1) acc0[t] += s1;
-                        }
+                        tmem_ld16(d0 + 64 + 16 * c, x);
+                        acc1[2 * c] += sum8(x);
+                        acc1[2 * c + 1] += sum8(x + 8);
                     }
                 }
                 tc_fence_before();
@@ -282,24 +270,23 @@ __global__ void __launch_bounds__(kBThreads, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[buf]);
-            // a timed-out wait reaches the other epilogue warps at the next named barrier
-            if (i + 1 < i1 && (i + 1) / ipk == key) {
-                epi_sync();
-                if (s_abort) break;
-                continue;
-            }
+            // every epilogue warp reads the abort flag after the same barrier, so all leave
+            // together when a wait gave up
+            epi_sync();
+            if (s_abort) break;
+            if (i + 1 < i1 && (i + 1) / ipk == key) continue;
 
             // ---- flush the key
             const int64_t ks = key * ipk;
-            const bool local = owner_of(ks, n, grid) == owner_of(ks + ipk - 1, n, grid);
+            const bool local = ipk == 1 || (ks >= i0 && ks + ipk <= i1);
             float* kpart = a.part + key * a.maxseg * (kPW * kBRows);
             if (!local) {
                 const int64_t seg = (i0 > ks ? i0 : ks) - ks;
                 float* sp = kpart + seg * (kPW * kBRows);
 #pragma unroll
-                for (int t = 0; t < kMaxTok; ++t) {
-                    sp[t * kBRows + r] = acc0[t];
-                    if (GATEUP) sp[(kMaxTok + t) * kBRows + r] = acc1[t];
+                for (int pi = 0; pi < kMaxPr; ++pi) {
+                    sp[pi * kBRows + r] = acc0[pi];
+                    if (GATEUP) sp[(kMaxPr + pi) * kBRows + r] = acc1[pi];
                 }
                 __threadfence();
                 if (et == 0) {
@@ -314,71 +301,67 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     s_nseg = ns;
                 }
             }
-            epi_sync();
-            if (et == 0) s_last = local || (!s_abort && atomicAdd(a.cnt + key, 1u) + 1 == unsigned(s_nseg));
-            epi_sync();
-            if (s_abort) break;
-            if (!s_last) {
+            if (!local) {
+                epi_sync();
+                if (et == 0) s_last = !s_abort && atomicAdd(a.cnt + key, 1u) + 1 == unsigned(s_nseg);
+                epi_sync();
+                if (s_abort) break;
+            }
+            if (!local && !s_last) {
 #pragma unroll
-                for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+                for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
                 continue;
             }
             if (!local) {
                 __threadfence();
 #pragma unroll
-                for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+                for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
                 for (int sg = 0; sg < s_nseg; ++sg) {       // segment order: deterministic sums
                     const float* sp = kpart + int64_t(s_seg[sg]) * (kPW * kBRows);
-                    float v[kPW];
+                    float x[kPW];
 #pragma unroll
-                    for (int c = 0; c < kPW; ++c) v[c] = __ldcg(sp + c * kBRows + r);
+                    for (int c = 0; c < kPW; ++c) x[c] = __ldcg(sp + c * kBRows + r);
 #pragma unroll
-                    for (int t = 0; t < kMaxTok; ++t) {
-                        acc0[t] += v[t];
-                        if (GATEUP) acc1[t] += v[(GATEUP ? kMaxTok : 0) + t];
+                    for (int pi = 0; pi < kMaxPr; ++pi) {
+                        acc0[pi] += x[pi];
+                        if (GATEUP) acc1[pi] += x[(GATEUP ? kMaxPr : 0) + pi];
                     }
                 }
             }
             if (GATEUP) {
-                // activation of each (token, weight) pair of expert u, split into pieces,
+                // activation x routing weight per pair, split into the down kernel's pieces,
                 // four pairs interleaved
-                const int rb = int(key / n_active);
-                const int pe = P->pair_start[u + 1];
                 const int64_t rowb = a.rows / 2;                            // bytes per act row (I/2)
-                uint8_t* sfc = a.act_sf + (int64_t(u) * (a.rows / 128) + rb) * kBChunk;
-                for (int p0 = ps; p0 < pe; p0 += 4) {
-                    float v[4];
+                uint8_t* sfc = a.act_sf + (int64_t(v) * (a.rows / 128) + rb) * kBChunk;
+#pragma unroll 1
+                for (int p0 = 0; p0 < np; p0 += 4) {
+                    float xv[4];
                     uint8_t* d[4];
-                    int ci[4];
+                    uint8_t* sf[4];
 #pragma unroll
                     for (int h = 0; h < 4; ++h) {
-                        const int p = p0 + h < pe ? p0 + h : p0;
-                        const int t = P->pair_tok[p];
+                        const int pi = p0 + h;
                         float gv = 0.0f, uv = 0.0f;
 #pragma unroll
-                        for (int tt = 0; tt < kMaxTok; ++tt)
-                            if (tt == t) { gv = acc0[tt]; uv = acc1[tt]; }
-                        v[h] = act_value(a.act_kind, gv, uv, a.beta, a.lbeta) * P->pair_w[p];
-                        ci[h] = p0 + h < pe ? p - ps : -1;
-                        d[h] = a.act_p + (int64_t(u) * kBMaxN + kBPieces * (p - ps)) * rowb +
-                               (int64_t(rb) * kBRows + 32 * q) / 2;
+                        for (int pp = 0; pp < kMaxPr; ++pp)
+                            if (pp == pi) { gv = acc0[pp]; uv = acc1[pp]; }
+                        xv[h] = pi < np ? act_value(a.act_kind, gv, uv, a.beta, a.lbeta) * P->pair_w[ps + pi] : 0.0f;
+                        d[h] = a.act_p + (int64_t(v) * kBMaxN + kBPieces * pi) * rowb + (int64_t(rb) * kBRows + 32 * q) / 2;
+                        sf[h] = pi < np ? sfc + sf_chunk_offset(kBPieces * pi, q) : nullptr;
                     }
-                    split_pieces_n<4>(v, lane, d, rowb, sfc, ci, q);
+                    split_pieces_n<4>(xv, lane, d, rowb, sf, 16);
                 }
             } else {
-                const int64_t row = key * kBRows + r;
-                for (int t = 0; t < M; ++t) {
-                    float v = 0.0f;
+                // one output row per pair (the combine kernel sums a token's pairs)
+                const int64_t row = int64_t(rb) * kBRows + r;
 #pragma unroll
-                    for (int tt = 0; tt < kMaxTok; ++tt)
-                        if (tt == t) v = acc0[tt];
-                    store_from_f32(a.y, a.y_dtype, int64_t(t) * a.rows + row, v);
-                }
+                for (int pi = 0; pi < kMaxPr; ++pi)
+                    if (pi < np) a.y_pair[int64_t(ps + pi) * a.rows + row] = acc0[pi];
             }
             if (!local && et == 0) a.cnt[key] = 0u;        // ready for the next call
             if (!local) epi_sync();                          // s_seg is rewritten by the next key
 #pragma unroll
-            for (int t = 0; t < kMaxTok; ++t) acc0[t] = acc1[t] = 0.0f;
+            for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
         }
     }
 
@@ -386,6 +369,94 @@ __global__ void __launch_bounds__(kBThreads, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tm, kCols);
+}
+
+// -------------------------------------------------------------- x scale gather
+
+// Scale chunks of each expert item's B operand: chunk c of item v holds, for its pair i
+// and piece p (row 8i + p), the E8M0 bytes of k-blocks 4c..4c+3 of token pair_tok's
+// piece row, gathered from the per-row scales xsf [8T][K/32]. One thread per 4-byte word.
+__global__ void gather_sfb_kernel(const Plan* __restrict__ plan, const uint8_t* __restrict__ xsf, int64_t K,
+                                  uint8_t* __restrict__ sfb) {
+    const int v = blockIdx.y;
+    if (v >= plan->n_active) return;
+    const int ps = plan->pair_start[v], np = plan->pair_start[v + 1] - ps;
+    const int64_t nc = K / 128, G = K / 32;
+    for (int64_t w = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; w < nc * np * kBPieces;
+         w += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t c = w / (np * kBPieces);
+        const int r = int(w % (np * kBPieces));                 // row 8i + p of the chunk
+        const int t = plan->pair_tok[ps + r / kBPieces];
+        const uint32_t word =
+            __ldg(reinterpret_cast<const uint32_t*>(xsf + (int64_t(kBPieces) * t + r % kBPieces) * G + 4 * c));
+        *reinterpret_cast<uint32_t*>(sfb + (int64_t(v) * nc + c) * kBChunk + sf_chunk_offset(r, 0)) = word;
+    }
+}
+
+int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
+                      cudaStream_t s) {
+    const dim3 grid(unsigned((K / 128 * kBMaxN + 255) / 256), unsigned(max_items));
+    gather_sfb_kernel<<<grid, 256, 0, s>>>(plan, xsf, K, sfb);
+    K3_CHECK_LAUNCH("gather_sfb_kernel");
+    return K3_OK;
+}
+
+// ------------------------------------------------------------------- combine
+
+// y[t][h] = sum of y_pair[p][h] over the pairs p of token t in plan order (experts
+// ascending, the shared expert last), like the reference's per-expert y.at[ti].add
+// loop (air_llm/models/kimi_k3/moe.py:120-131). Block (x, t): token t, 512 columns of h;
+// warp 0 lists the token's pairs in order with ballots, every thread sums 4 columns.
+__global__ void combine_kernel(const Plan* __restrict__ plan, const float* __restrict__ y_pair, int64_t H,
+                               void* y, int y_dtype) {
+    __shared__ int s_list[kMaxPairs];
+    __shared__ int s_n;
+    const int t = blockIdx.y;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int np = plan->n_pairs;
+        int cnt = 0;
+        for (int p0 = 0; p0 < np; p0 += 32) {
+            const int p = p0 + lane;
+            const bool mine = p < np && plan->pair_tok[p] == t;
+            const uint32_t bal = __ballot_sync(0xffffffffu, mine);
+            if (mine) s_list[cnt + __popc(bal & ((1u << lane) - 1u))] = p;
+            cnt += __popc(bal);
+        }
+        if (lane == 0) s_n = cnt;
+    }
+    __syncthreads();
+    const int64_t h4 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (h4 >= H) return;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int j0 = 0; j0 < s_n; j0 += 8) {            // eight rows in flight, summed in order
+        float4 v[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h)
+            v[h] = j0 + h < s_n ? __ldcg(reinterpret_cast<const float4*>(y_pair + int64_t(s_list[j0 + h]) * H + h4))
+                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            if (j0 + h >= s_n) break;
+            acc.x += v[h].x;
+            acc.y += v[h].y;
+            acc.z += v[h].z;
+            acc.w += v[h].w;
+        }
+    }
+    const int64_t o = int64_t(t) * H + h4;
+    store_from_f32(y, y_dtype, o, acc.x);
+    store_from_f32(y, y_dtype, o + 1, acc.y);
+    store_from_f32(y, y_dtype, o + 2, acc.z);
+    store_from_f32(y, y_dtype, o + 3, acc.w);
+}
+
+int launch_combine(const Plan* plan, const float* y_pair, int64_t H, int M, void* y, int y_dtype,
+                   cudaStream_t s) {
+    const dim3 grid(unsigned((H / 4 + 127) / 128), unsigned(M));
+    combine_kernel<<<grid, 128, 0, s>>>(plan, y_pair, H, y, y_dtype);
+    K3_CHECK_LAUNCH("combine_kernel");
+    return K3_OK;
 }
 
 // ---------------------------------------------------------------- scale layout

@@ -54,8 +54,8 @@ static_assert(bsmem_bytes<true>() + 4096 <= 227 * 1024 && bsmem_bytes<false>() +
 
 // Tensor maps: a0/a1 = packed weight pools, row-major [slot][rows][K/2] (box 128 B x 128
 // rows) or tiled [slot * rows/128][K/256][128][128] (box = one contiguous tile);
-// b = activation pieces, gate/up [8M][K/2] (box 128 B x 8M rows), down [u][64][K/2]
-// (box 128 B x 8 rows, one column's pieces).
+// b = activation pieces, gate/up x [8T][K/2] (box 128 B x 8 rows: one token's pieces),
+// down act [v][64][K/2] (box 128 B x 8 rows: one pair's pieces).
 struct BMaps {
     CUtensorMap a0, a1, b;
 };
@@ -73,20 +73,27 @@ struct BArgs {
     const uint8_t* sfa1;    // of pool a1 (gate/up)
     int tiled;              // a0/a1 are tile pools (4-D maps) rather than row-major pools
     int64_t sf_slot;        // bytes per slot of a scale-chunk pool
-    const uint8_t* sfb;     // piece scale chunks: gate/up [K/128][512]; down [u][K/128][512]
-    // gate/up epilogue: act pieces of expert u, column i (its i-th pair), piece p at row
-    // u*64 + 8i + p of act_p [.][I/2]; their scale chunks act_sf [u][I/128][512]
+    const uint8_t* sfb;     // B scale chunks per expert item [v][K/128][512] (gate/up: x
+                            // pieces gathered per pair; down: act pieces)
+    // gate/up epilogue: act pieces of expert v's pair i, piece p at row v*64 + 8i + p of
+    // act_p [.][I/2]; their scale chunks act_sf [v][I/128][512]
     uint8_t* act_p;
     uint8_t* act_sf;
     int act_kind;
     float beta, lbeta;
-    // down epilogue
-    void* y;
-    int y_dtype;
+    // down epilogue: one f32 output row per pair, y_pair [pairs][H]
+    float* y_pair;
 };
 
 int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
 int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
+// Per-item B scale chunks of the gate/up phase from the per-row x piece scales.
+int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
+                      cudaStream_t s);
+// y[t] = sum over the pairs of token t, in plan order, of y_pair[pair] (weights are
+// already applied); y [M][H] f32 or bf16.
+int launch_combine(const Plan* plan, const float* y_pair, int64_t H, int M, void* y, int y_dtype,
+                   cudaStream_t s);
 // Scale re-layout [batch][rows][cols/32] -> [batch][rows/128][cols/128][512] chunks.
 int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batch, uint8_t* out,
                      cudaStream_t s);
@@ -105,12 +112,13 @@ __device__ __forceinline__ float warp_max_nonneg(float v) {
 // Warp-wide: lane l holds element l of a 32-element block of NV values (independent
 // chains, interleaved); splits each into kBPieces E2M1 pieces. Piece p of value i: its
 // 16 packed bytes go to data[i] + p*row_stride (element 2j in the low nibble of byte j)
-// and its E8M0 scale to sf_chunk[sf_chunk_offset(8*col[i] + p, j)]. Values with
-// col[i] < 0 are skipped.
+// and its E8M0 scale to sf[i][p*sf_stride]. Values with sf[i] == nullptr are skipped.
+// Both scale layouts in use are affine in p: natural per-row scales ([row][block],
+// stride = blocks per row) and the tensor-core chunk (sf_chunk_offset(8*col + p, j),
+// stride 16 since the 8 rows of one column share a 32-row group).
 template <int NV>
 __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, uint8_t* const (&data)[NV],
-                                               int64_t row_stride, uint8_t* sf_chunk, const int (&col)[NV],
-                                               int j) {
+                                               int64_t row_stride, uint8_t* const (&sf)[NV], int64_t sf_stride) {
     float res[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) res[i] = v[i];
@@ -140,10 +148,10 @@ __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, u
             w |= __shfl_xor_sync(0xffffffffu, w, 1);
             w |= __shfl_xor_sync(0xffffffffu, w, 2);
             w |= __shfl_xor_sync(0xffffffffu, w, 4);
-            if (col[i] >= 0) {
+            if (sf[i]) {
                 if ((lane & 7) == 0)
                     *reinterpret_cast<uint32_t*>(data[i] + p * row_stride + 4 * (lane >> 3)) = w;
-                if (lane == 0) sf_chunk[sf_chunk_offset(8 * col[i] + p, j)] = uint8_t(b);
+                if (lane == 0) sf[i][p * sf_stride] = uint8_t(b);
             }
         }
     }
@@ -151,11 +159,11 @@ __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, u
 
 // One value per lane (see split_pieces_n).
 __device__ __forceinline__ void split_pieces(float v, int lane, uint8_t* data, int64_t row_stride,
-                                             uint8_t* sf_chunk, int col, int j) {
+                                             uint8_t* sf, int64_t sf_stride) {
     const float vv[1] = {v};
     uint8_t* const dd[1] = {data};
-    const int cc[1] = {col};
-    split_pieces_n<1>(vv, lane, dd, row_stride, sf_chunk, cc, j);
+    uint8_t* const ss[1] = {sf};
+    split_pieces_n<1>(vv, lane, dd, row_stride, ss, sf_stride);
 }
 
 }  // namespace k3

@@ -197,8 +197,8 @@ struct PrepArgs {
     int blocked;                   // blocked pieces with one exponent per (token, 512-k)
                                    // block, rows M..7 zeros (TMA kernels); else row-major
                                    // with one exponent per token (generic kernels)
-    uint8_t* xp;                   // block-scaled path: E2M1 pieces [8M][K/2] + scale
-    uint8_t* xsf;                  // chunks [K/128][512] instead of the f16 pieces
+    uint8_t* xp;                   // block-scaled path: E2M1 pieces [8M][K/2] + per-row
+    uint8_t* xsf;                  // scales [8M][K/32] instead of the f16 pieces
 };
 
 __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
@@ -210,7 +210,7 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
                 for (int64_t g = g0; g < g0 + 16 && g < a.K / 32; ++g) {
                     const float v = load_as_f32(a.x, a.x_dtype, int64_t(warp) * a.K + 32 * g + lane);
                     split_pieces(v, lane, a.xp + int64_t(kBPieces * warp) * (a.K / 2) + 16 * g, a.K / 2,
-                                 a.xsf + (g / 4) * kBChunk, warp, int(g % 4));
+                                 a.xsf + int64_t(kBPieces * warp) * (a.K / 32) + g, a.K / 32);
                 }
             return;
         }
@@ -677,7 +677,7 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
     L.bs = L.tma && pool_bs(p);
     size_t off = 0;
     if (L.bs) {
-        // keys: gate/up = (active expert, 128-row block of I); down = 128-row block of y
+        // keys: (128-row block, active expert) in both phases
         L.CA = choose_split_bs(L.U * (L.I / kBRows), L.H, sms);
         L.CB = choose_split_bs(L.U * (L.H / kBRows), L.I, sms);
         L.plan = carve(off, sizeof(Plan));
@@ -685,9 +685,10 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
         L.route_idx = carve(off, sizeof(int32_t) * M * p.top_k);
         L.route_w = carve(off, sizeof(float) * M * p.top_k);
         L.xq_hi = carve(off, size_t(kBMaxN) * (L.H / 2));              // x pieces
-        L.xq_ts = carve(off, size_t(L.H / 128) * kBChunk);              // their scale chunks
+        L.xq_ts = carve(off, size_t(kBMaxN) * (L.H / 32));              // their per-row scales
+        L.sfb_x = carve(off, size_t(L.U) * (L.H / 128) * kBChunk);      // per-item B scale chunks
         L.KQ = 1;
-        for (int64_t c = 1; c <= L.H / 512; ++c) {        // router k-slices: >= one CTA per SM
+        for (int64_t c = 1; c <= L.H / 512 && c <= 16; ++c) {  // router k-slices: >= one CTA per SM
             if ((L.H / 512) % c) continue;
             L.KQ = int(c);
             if (((L.E + 15) / 16) * c >= sms) break;
@@ -698,8 +699,9 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
         L.act_ts = carve(off, size_t(L.U) * (L.I / 128) * kBChunk);
         L.partA = carve(off, sizeof(float) * L.U * (L.I / kBRows) * L.CA * 2 * kMaxTok * kBRows);
         L.cntA = carve(off, sizeof(unsigned) * L.U * (L.I / kBRows));
-        L.partB = carve(off, sizeof(float) * (L.H / kBRows) * L.U * L.CB * kMaxTok * kBRows);
-        L.cntB = carve(off, sizeof(unsigned) * (L.H / kBRows));
+        L.partB = carve(off, sizeof(float) * L.U * (L.H / kBRows) * L.CB * kMaxTok * kBRows);
+        L.cntB = carve(off, sizeof(unsigned) * L.U * (L.H / kBRows));
+        L.y_pair = carve(off, sizeof(float) * L.P * L.H);              // one output row per pair
         L.total = off;
         return L;
     }
@@ -717,7 +719,7 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
         L.xq_lo = carve(off, sizeof(__half) * kMaxTok * L.H);
         L.xq_ts = carve(off, sizeof(float) * kMaxTok * (L.H / 512));
         L.KQ = 1;
-        for (int64_t c = 1; c <= L.H / 512; ++c) {        // router k-slices: >= one CTA per SM
+        for (int64_t c = 1; c <= L.H / 512 && c <= 16; ++c) {  // router k-slices: >= one CTA per SM
             if ((L.H / 512) % c) continue;
             L.KQ = int(c);
             if (((L.E + 15) / 16) * c >= sms) break;
@@ -923,7 +925,7 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     {
         const uint64_t d[2] = {uint64_t(L.H / 2), uint64_t(kBPieces * M)};
         const uint64_t st[1] = {uint64_t(L.H / 2)};
-        const uint32_t b[2] = {128, uint32_t(kBPieces * M)};
+        const uint32_t b[2] = {128, uint32_t(kBPieces)};                // one token's pieces
         if (int rc = encode_map(&ma.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + L.xq_hi, d, st, b,
                                 CU_TENSOR_MAP_SWIZZLE_128B))
             return rc;
@@ -941,14 +943,18 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     ta.sfa1 = pl.w3_scales_tc;
     ta.tiled = tiled ? 1 : 0;
     ta.sf_slot = (L.I / 128) * (L.H / 128) * kBChunk;
-    ta.sfb = ws + L.xq_ts;
+    ta.sfb = ws + L.sfb_x;
     ta.act_p = act_p;
     ta.act_sf = act_sf;
     ta.act_kind = p->activation;
     ta.beta = p->situ_beta;
     ta.lbeta = p->situ_linear_beta;
+    prof_begin(K3_PROF_TOPK, s);
+    int rc = launch_gather_sfb(plan, ws + L.xq_ts, L.H, int(L.U), ws + L.sfb_x, s);
+    prof_end(K3_PROF_TOPK, s);
+    if (rc) return rc;
     prof_begin(K3_PROF_GATEUP, s);
-    int rc = launch_bs_gateup(ma, ta, sms, s);
+    rc = launch_bs_gateup(ma, ta, sms, s);
     prof_end(K3_PROF_GATEUP, s);
     if (rc) return rc;
 
@@ -972,16 +978,19 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     tb.status = &plan->status;
     tb.part = reinterpret_cast<float*>(ws + L.partB);
     tb.cnt = reinterpret_cast<unsigned*>(ws + L.cntB);
-    tb.maxseg = int(L.U * L.CB);
+    tb.maxseg = L.CB;
     tb.sfa0 = pl.w2_scales_tc;
     tb.tiled = tiled ? 1 : 0;
     tb.sf_slot = (L.H / 128) * (L.I / 128) * kBChunk;
     tb.sfb = act_sf;
-    tb.y = y;
-    tb.y_dtype = ydt;
+    tb.y_pair = reinterpret_cast<float*>(ws + L.y_pair);
     prof_begin(K3_PROF_DOWN, s);
     rc = launch_bs_down(mb, tb, sms, s);
     prof_end(K3_PROF_DOWN, s);
+    if (rc) return rc;
+    prof_begin(K3_PROF_OTHER, s);
+    rc = launch_combine(plan, tb.y_pair, L.H, M, y, ydt, s);
+    prof_end(K3_PROF_OTHER, s);
     return rc;
 }
 
@@ -1010,7 +1019,7 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
     pl.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
     pl.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
     pl.n_cntA = L.bs ? L.U * (L.I / kBRows) : L.tma ? L.U * (L.I / 64) : L.U * (L.I / 32);
-    pl.n_cntB = L.tma ? L.H / kTRows : L.H / kItemRows;
+    pl.n_cntB = L.bs ? L.U * (L.H / kBRows) : L.tma ? L.H / kTRows : L.H / kItemRows;
     pl.M = int(M);
     const int sms = num_sms();
 

@@ -106,11 +106,21 @@ __device__ inline void topk_row(const float* __restrict__ lrow, const float* __r
 __device__ inline void topk_cta(const float* __restrict__ logits, const float* __restrict__ bias, int M,
                                 int E, int k, int renorm, float scale, int32_t* __restrict__ idx_out,
                                 float* __restrict__ w_out, uint32_t* s_key, int warp, int lane, int* status) {
+    // eight loads in flight per thread per pass (the logits come from other CTAs)
 #pragma unroll 1
-    for (int i = threadIdx.x; i < M * E; i += blockDim.x) {
-        const float l = __ldcg(logits + i);                   // may come from other CTAs
-        const float r = 1.0f / (1.0f + expf(-l));
-        s_key[i] = order_key(r + (bias ? __ldg(bias + i % E) : 0.0f));
+    for (int i0 = threadIdx.x; i0 < M * E; i0 += 8 * blockDim.x) {
+        float l[8], b[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int i = min(i0 + h * int(blockDim.x), M * E - 1);
+            l[h] = __ldcg(logits + i);
+            b[h] = bias ? __ldg(bias + i % E) : 0.0f;
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int i = i0 + h * int(blockDim.x);
+            if (i < M * E) s_key[i] = order_key(1.0f / (1.0f + expf(-l[h])) + b[h]);
+        }
     }
     __syncthreads();
     if (warp < M) {

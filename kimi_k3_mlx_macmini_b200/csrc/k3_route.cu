@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
             const int64_t g = task % ng;
             const float v = load_as_f32(a.x, a.x_dtype, int64_t(t) * a.H + 32 * g + lane);
             split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (a.H / 2) + 16 * g, a.H / 2,
-                         a.xsf + (g / 4) * kBChunk, t, int(g % 4));
+                         a.xsf + int64_t(kBPieces * t) * ng + g, ng);
         }
     } else {
         // ---- x -> f16 pieces: the CTAs of the first row blocks split the slice's 512-blocks
@@ -120,9 +120,16 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
         const int r = threadIdx.x / kMaxTok, t = threadIdx.x % kMaxTok;
         const int64_t e = int64_t(rb) * 16 + r;
         if (e < a.E && t < a.M) {
+            // every slice's partial in flight at once, summed in slice order
+            constexpr int kMaxSlices = 16;
+            float pv[kMaxSlices];
+#pragma unroll
+            for (int s = 0; s < kMaxSlices; ++s)
+                pv[s] = s < int(gridDim.y) ? __ldcg(a.logit_part + (int64_t(s) * a.M + t) * a.E + e) : 0.0f;
             float v = 0.0f;
-            for (int s = 0; s < int(gridDim.y); ++s)
-                v += __ldcg(a.logit_part + (int64_t(s) * a.M + t) * a.E + e);
+#pragma unroll
+            for (int s = 0; s < kMaxSlices; ++s)
+                if (s < int(gridDim.y)) v += pv[s];
             a.logits[int64_t(t) * a.E + e] = v;
         }
     }

@@ -19,7 +19,7 @@ struct RouteArgs {
     __half* xq_hi;                 // blocked x pieces [H/32][8][32]
     __half* xq_lo;                 // null for bf16 x
     float* xq_ts;                  // [8][H/512]
-    // block-scaled path: x as E2M1 pieces [8M][H/2] and their scale chunks [H/128][512]
+    // block-scaled path: x as E2M1 pieces [8M][H/2] and their per-row scales [8M][H/32]
     // (replaces xq_* when non-null)
     uint8_t* xp;
     uint8_t* xsf;
