@@ -209,6 +209,21 @@ typedef struct k3_moe_params {
     const k3_expert_pool* pool;   /* HOST pointer to pool descriptors, or NULL       */
 } k3_moe_params;
 
+/* Local expert computation of an expert-parallel MoE layer: T token rows x [T][H] and
+ * n_pairs candidate (slot, token row, weight) pairs; candidates with slot < 0 (or out of
+ * range) are skipped. y_out [T][H] (f32|bf16) receives, per token row, the sum over its
+ * pairs of weight * expert(slot)(x[token]) in ascending slot order (rows without pairs
+ * are zero). Needs the block-scaled pool (k3_expert_pool *_scales_tc and *_tiles).
+ * Limits: n_pairs <= 1024 candidates; at most 256 of them valid and 256 expert items
+ * (8 pairs each) per call, else the call's routing plan reports K3_ERR_UNSUPPORTED in
+ * its status word. Replaces the per-expert loop of LatentMoE.__call__
+ * (air_llm/models/kimi_k3/moe.py:110-132) for the experts one rank owns. */
+K3_API size_t k3_moe_pairs_workspace(const k3_moe_params* p, int64_t T, int64_t n_pairs);
+K3_API int k3_moe_pairs_decode(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                               const int32_t* pair_slot, const int32_t* pair_tok,
+                               const float* pair_w, int64_t n_pairs, void* y_out, int y_dtype,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* Decode (M <= 8 tokens) MoE block without the latent wrapper: route, then for every
  * routed expert y[t] += w[t,slot] * act(x W1^T, x W3^T) W2^T, summed in ascending
  * expert id, plus the shared expert. Replaces LatentMoE.__call__'s route + expert loop

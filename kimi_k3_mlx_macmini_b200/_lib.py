@@ -55,6 +55,9 @@ SIGNATURES = {
     "k3_mxfp4_scale_minmax": (_i32, [_vp, _i64, _vp, _vp]),
     "k3_mxfp4_scales_tc": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
     "k3_mxfp4_tiles": (_i32, [_vp, _i64, _i64, _i64, _vp, _vp]),
+    "k3_moe_pairs_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
+    "k3_moe_pairs_decode": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp, _i64, _vp,
+                                   _i32, _vp, _sz, _vp]),
     "k3_mxfp4_matvec_workspace": (_sz, [_i64, _i64, _i64]),
     "k3_mxfp4_matvec": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp, _sz, _vp]),
     "k3_mxfp4_matvec_noalloc": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _i64, _vp, _i32, _vp]),

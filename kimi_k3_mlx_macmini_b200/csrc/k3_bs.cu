@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
     __shared__ Plan s_plan;                           // the routing plan, copied once
     __shared__ int s_last;
     __shared__ int s_nseg;
-    __shared__ int s_seg[kTMaxSegments];
+    __shared__ int s_seg[kBMaxSegments];
     __shared__ volatile int s_abort;
     __shared__ volatile unsigned s_issued;
 
@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     // CTA's first item (CTAs with empty ranges own nothing)
                     int ns = 0;
                     const int64_t b0 = owner_of(ks, n, grid), b1 = owner_of(ks + ipk - 1, n, grid);
-                    for (int64_t cb = b0; cb <= b1 && ns < kTMaxSegments; ++cb) {
+                    for (int64_t cb = b0; cb <= b1 && ns < kBMaxSegments; ++cb) {
                         const int64_t f0 = cb * n / grid, f1 = (cb + 1) * n / grid;
                         if (f1 > f0) s_seg[ns++] = int((f0 > ks ? f0 : ks) - ks);
                     }
@@ -522,6 +522,7 @@ int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batc
 
 template <bool G>
 int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const char* what) {
+    if (grid > kBMaxSegments) return fail(K3_ERR_UNSUPPORTED, "block-scaled grid above 256 CTAs");
     static bool configured = false;
     constexpr size_t smem = bsmem_bytes<G>();
     if (!configured) {

@@ -23,6 +23,7 @@ constexpr int kBChunk = 512;                    // scale chunk: 128 rows x 4 k-b
 constexpr int kBMaxN = kMaxTok * kBPieces;      // B rows of one MMA (64)
 constexpr int kBEpiWarps = 4;                   // epilogue warps (one per TMEM lane quarter)
 constexpr int kBThreads = (2 + kBEpiWarps) * 32;
+constexpr int kBMaxSegments = 256;              // CTAs sharing one key (grid <= 256)
 
 // Byte of the scale of (row n, k-block j) inside its 512-byte chunk: the chunk is the
 // 32 x 16-byte matrix tcgen05.cp replicates to the four TMEM lane quarters, row n in

@@ -19,6 +19,7 @@
 #include "k3_plan.cuh"
 #include "k3_tma.cuh"
 #include "k3_bs.cuh"
+#include "k3_pairs.cuh"
 #include "k3_route.cuh"
 
 namespace k3 {
@@ -1329,4 +1330,85 @@ extern "C" K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* 
     return decode_impl(p, x, x_dtype, M, nullptr, nullptr, const_cast<int32_t*>(idx),
                        const_cast<float*>(w), y_out, y_dtype, static_cast<uint8_t*>(workspace), L,
                        static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------ pairs (expert parallel)
+
+namespace k3 {
+
+// Workspace of a pairs call: T token rows, up to n_in candidate pairs.
+DecodeLayout pairs_layout(const k3_moe_params& p, int64_t T, int64_t n_in, int sms) {
+    DecodeLayout L{};
+    L.M = T;
+    L.H = p.hidden;
+    L.I = p.inter;
+    L.E = p.num_experts;
+    L.U = std::min<int64_t>(n_in, kMaxActive);
+    L.P = std::min<int64_t>(n_in, kMaxPairs);
+    L.tma = L.bs = true;
+    L.CA = choose_split_bs(L.U * (L.I / kBRows), L.H, sms);
+    L.CB = choose_split_bs(L.U * (L.H / kBRows), L.I, sms);
+    size_t off = 0;
+    L.plan = carve(off, sizeof(Plan));
+    L.xq_hi = carve(off, size_t(kBPieces) * T * (L.H / 2));
+    L.xq_ts = carve(off, size_t(kBPieces) * T * (L.H / 32));
+    L.sfb_x = carve(off, size_t(L.U) * (L.H / 128) * kBChunk);
+    L.act_hi = carve(off, size_t(L.U) * kBMaxN * (L.I / 2));
+    L.act_ts = carve(off, size_t(L.U) * (L.I / 128) * kBChunk);
+    L.partA = carve(off, sizeof(float) * L.U * (L.I / kBRows) * L.CA * 2 * kMaxTok * kBRows);
+    L.cntA = carve(off, sizeof(unsigned) * L.U * (L.I / kBRows));
+    L.partB = carve(off, sizeof(float) * L.U * (L.H / kBRows) * L.CB * kMaxTok * kBRows);
+    L.cntB = carve(off, sizeof(unsigned) * L.U * (L.H / kBRows));
+    L.y_pair = carve(off, sizeof(float) * L.P * L.H);
+    L.total = off;
+    return L;
+}
+
+}  // namespace k3
+
+extern "C" K3_API size_t k3_moe_pairs_workspace(const k3_moe_params* p, int64_t T, int64_t n_pairs) {
+    using namespace k3;
+    if (!p || T < 1 || n_pairs < 1) return 0;
+    return pairs_layout(*p, T, n_pairs, num_sms()).total;
+}
+
+extern "C" K3_API int k3_moe_pairs_decode(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                                          const int32_t* pair_slot, const int32_t* pair_tok,
+                                          const float* pair_w, int64_t n_pairs, void* y_out, int y_dtype,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace k3;
+    if (!p) return fail(K3_ERR_INVALID, "k3_moe_pairs_decode: params is NULL");
+    if (!x || !pair_slot || !pair_tok || !pair_w || !y_out)
+        return fail(K3_ERR_INVALID, "k3_moe_pairs_decode: NULL tensor");
+    if (x_dtype != K3_F32 && x_dtype != K3_BF16) return fail(K3_ERR_INVALID, "x dtype must be f32 or bf16");
+    if (y_dtype != K3_F32 && y_dtype != K3_BF16) return fail(K3_ERR_INVALID, "y dtype must be f32 or bf16");
+    if (T < 1) return fail(K3_ERR_INVALID, "k3_moe_pairs_decode: T must be >= 1");
+    if (n_pairs < 1 || n_pairs > kMaxPairCandidates)
+        return fail(K3_ERR_UNSUPPORTED, "k3_moe_pairs_decode: 1..1024 candidate pairs");
+    if (!p->pool || !pool_bs(*p))
+        return fail(K3_ERR_UNSUPPORTED, "k3_moe_pairs_decode needs a block-scaled expert pool "
+                                        "(re-laid scales and tiles; H, I multiples of 512)");
+    const int sms = num_sms();
+    const DecodeLayout L = pairs_layout(*p, T, n_pairs, sms);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
+    if (int rc = configure_smem()) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    PairsArgs pa{};
+    pa.slot = pair_slot;
+    pa.tok = pair_tok;
+    pa.w = pair_w;
+    pa.n_in = int(n_pairs);
+    pa.num_slots = int(p->pool->num_slots);
+    pa.T = int(T);
+    pa.plan = reinterpret_cast<Plan*>(ws + L.plan);
+    pa.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
+    pa.n_cntA = L.U * (L.I / kBRows);
+    pa.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
+    pa.n_cntB = L.U * (L.H / kBRows);
+    prof_begin(K3_PROF_TOPK, s);
+    if (int rc = launch_plan_from_pairs(pa, s)) return rc;
+    if (int rc = launch_convert_tokens(x, x_dtype, T, L.H, ws + L.xq_hi, ws + L.xq_ts, s)) return rc;
+    prof_end(K3_PROF_TOPK, s);
+    return decode_bs(p, L, ws, int(T), y_out, y_dtype, sms, s);
 }

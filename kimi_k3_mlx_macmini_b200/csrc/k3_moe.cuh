@@ -8,8 +8,13 @@ namespace k3 {
 constexpr int kMaxTok = 8;                       // decode tokens = mma n8 columns
 constexpr int kMaxTopK = 16;
 constexpr int kMaxExperts = 1024;
-constexpr int kMaxActive = kMaxTok * kMaxTopK + 1;
-constexpr int kMaxPairs = kMaxTok * kMaxTopK + kMaxTok;
+// Routing plans hold at most this many expert items and (token, expert) pairs: a decode
+// call (8 tokens x top-16 + shared) and the expert-parallel local calls (pairs routed to
+// one rank's experts) both fit.
+constexpr int kMaxActive = 256;
+constexpr int kMaxPairs = 256;
+static_assert(kMaxActive >= kMaxTok * kMaxTopK + 1 && kMaxPairs >= kMaxTok * kMaxTopK + kMaxTok,
+              "plan capacity below one decode call");
 
 // Routing plan of one decode call: the active experts in ascending id order (the
 // reference's `for e in sorted(...)`, moe.py:120 / k3ref/layers.py:252) and, per

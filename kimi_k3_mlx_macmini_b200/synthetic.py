@@ -29,22 +29,41 @@ def bf16_normal(gen: torch.Generator, shape, std: float, device) -> torch.Tensor
 
 @dataclass
 class SyntheticLayer:
+    """Router weights plus lazily generated experts: expert e's three projections come
+    from a generator seeded with (seed, e), so any subset (one rank's share of an
+    expert-parallel layer) is generated alone and identically."""
     cfg: MoEConfig
     gate: torch.Tensor            # bf16 [E, H]
     bias: torch.Tensor            # f32 [E]
-    experts: list                 # [(w1, w3, w2)] with each (packed, scales)
-    shared: tuple                 # (w1, w3, w2) or None
+    seed: int
+    device: str
+    with_shared: bool
+
+    def expert(self, e):
+        """(w1, w3, w2), each (packed, scales), of routed expert e or SHARED."""
+        c = self.cfg
+        H, I = c.hidden_size, c.moe_intermediate_size
+        idx = c.num_experts if e == SHARED else int(e)
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(self.seed * 1_000_003 + 7 + idx)
+        return (random_mxfp4(gen, I, H, self.device), random_mxfp4(gen, I, H, self.device),
+                random_mxfp4(gen, H, I, self.device))
 
     def source(self, layer: int, e, which: str):
-        trip = self.shared if e == SHARED else self.experts[int(e)]
-        return trip[("w1", "w3", "w2").index(which)]
+        key = (e if e == SHARED else int(e))
+        if getattr(self, "_cached_key", None) != key:           # the pool asks w1, w3, w2 in turn
+            self._cached = self.expert(e)
+            self._cached_key = key
+        return self._cached[("w1", "w3", "w2").index(which)]
 
     def moe(self, device="cuda") -> LatentMoE:
         w = {"gate.weight": self.gate, "gate.e_score_correction_bias": self.bias}
         return LatentMoE(self.cfg, 0, w, self.source, fused=True, device=device)
 
     def nbytes_expert(self) -> int:
-        return sum(t.numel() for pair in self.experts[0] for t in pair)
+        c = self.cfg
+        H, I = c.hidden_size, c.moe_intermediate_size
+        return 3 * (I * H // 2 + I * H // 32)
 
 
 def baseline_layer(seed: int = 0, E: int = 384, H: int = 7168, I: int = 2048, top_k: int = 8,
@@ -59,11 +78,7 @@ def baseline_layer(seed: int = 0, E: int = 384, H: int = 7168, I: int = 2048, to
                     num_shared_experts=1 if shared else 0, activation="silu")
     gate = bf16_normal(gen, (E, H), 0.02, device)
     bias = torch.zeros(E, dtype=torch.float32, device=device)
-    experts = [(random_mxfp4(gen, I, H, device), random_mxfp4(gen, I, H, device),
-                random_mxfp4(gen, H, I, device)) for _ in range(E)]
-    sh = ((random_mxfp4(gen, I, H, device), random_mxfp4(gen, I, H, device),
-           random_mxfp4(gen, H, I, device)) if shared else None)
-    return SyntheticLayer(cfg, gate, bias, experts, sh)
+    return SyntheticLayer(cfg, gate, bias, seed, device, shared)
 
 
 def tokens(seed: int, M: int, H: int, device="cuda") -> torch.Tensor:

@@ -1,0 +1,97 @@
+"""Expert parallelism: the collective logic of ``kimi_k3_mlx_macmini_b200.ep`` on CPU
+``gloo`` ranks (world size 2), with the oracle as router and local expert computation.
+Each rank keeps its own tokens; the combined result must equal the single-process
+oracle of the whole layer (``moe_forward``, i.e. ``k3ref/layers.py:241-261`` with the
+BASELINE substitutions)."""
+import os
+import socket
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import mxfp4_oracle as O
+
+E, H, I, K, M, SCALE = 8, 64, 32, 2, 3, 2.5
+
+
+def _layer(seed=11):
+    rng = np.random.default_rng(seed)
+    gate = (rng.standard_normal((E, H)) * 0.2).astype(np.float32)
+    bias = (rng.standard_normal(E) * 0.01).astype(np.float32)
+    experts = {e: {w: O.random_mxfp4(rng, *((I, H) if w != "w2" else (H, I))) for w in ("w1", "w3", "w2")}
+               for e in list(range(E)) + ["shared"]}
+    return gate, bias, experts
+
+
+def _worker(rank, world, port, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from kimi_k3_mlx_macmini_b200.ep import ep_forward
+        gate, bias, experts = _layer()
+        rng = np.random.default_rng(100 + rank)
+        x = rng.standard_normal((M, H)).astype(np.float32)
+        E_loc = E // world
+        dec = {e: {w: O.decode_mxfp4(*experts[e][w]) for w in ("w1", "w3", "w2")} for e in experts}
+
+        def route_fn(xt):
+            r = O.route(xt.numpy(), gate, bias, K, True, SCALE)
+            return torch.from_numpy(r.expert_indices.astype(np.int32)), torch.from_numpy(r.expert_weights)
+
+        def local_fn(x_all, slot, tok, w):
+            y = np.zeros((x_all.shape[0], H), np.float32)
+            order = np.argsort(slot.numpy(), kind="stable")          # ascending slot, shared last
+            for i in order:
+                s = int(slot[i])
+                if s < 0:
+                    continue
+                e = "shared" if s == E_loc else rank * E_loc + s
+                t = int(tok[i])
+                out = O.expert_forward(x_all[t:t + 1].numpy(), dec[e]["w1"], dec[e]["w3"], dec[e]["w2"])
+                y[t] += (out[0] * float(w[i])).astype(np.float32)
+            return torch.from_numpy(y)
+
+        y = ep_forward(torch.from_numpy(x), route_fn, local_fn, num_experts=E, with_shared=True)
+        ref, _ = O.moe_forward(x, O.MoESpec(E, K, SCALE, True, "silu"), gate, bias,
+                               lambda e, w: experts[e][w],
+                               shared={"kind": "mxfp4", **{w: experts["shared"][w] for w in ("w1", "w3", "w2")}})
+        out_q.put((rank, O.rel_l2(y.numpy(), ref)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_ep_forward_gloo_two_ranks():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert set(res) == {0, 1}
+    for rank, err in res.items():
+        assert err < 1e-5, (rank, err)
+
+
+def test_pair_candidates_layout():
+    from kimi_k3_mlx_macmini_b200.ep import pair_candidates
+    idx = torch.tensor([[0, 5], [3, 4], [7, 1]], dtype=torch.int32)     # 3 gathered tokens, k = 2
+    w = torch.arange(6, dtype=torch.float32).reshape(3, 2)
+    slot, tok, wt = pair_candidates(idx, w, rank=1, world=2, num_experts=8, with_shared=True, M=1)
+    # rank 1 owns experts 4..7 (slots 0..3) and the shared expert at slot 4 for its own token 1
+    assert slot.tolist() == [-1, 1, -1, 0, 3, -1, 4]
+    assert tok.tolist() == [0, 0, 1, 1, 2, 2, 1]
+    assert wt.tolist() == [0, 1, 2, 3, 4, 5, 1]

@@ -1,0 +1,109 @@
+"""Expert-parallel local computation on the GPU: ``k3_moe_pairs_decode`` against the C
+oracle (more than 8 tokens in one call, an expert split into several 8-pair items,
+skipped candidates), and the full expert-parallel layer on 2 GPUs when the box has them."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mxfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+H, I, E = 1024, 512, 16
+
+
+def _small_layer(seed=5, top_k=4):
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    return synthetic.baseline_layer(seed=seed, E=E, H=H, I=I, top_k=top_k)
+
+
+def _params(pool, cfg, num_experts):
+    import ctypes
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    return L.K3MoEParams(hidden=pool.hidden, inter=pool.inter, num_experts=num_experts,
+                         top_k=cfg.num_experts_per_token, renormalize=1,
+                         routed_scaling_factor=float(cfg.routed_scaling_factor), has_shared=1,
+                         activation=L.K3_ACT_SILU, situ_beta=4.0, situ_linear_beta=-1.0,
+                         experts=pool.table.data_ptr(), pool=ctypes.pointer(pool.desc))
+
+
+def test_pairs_decode_matches_oracle(k3):
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    from kimi_k3_mlx_macmini_b200.moe import SHARED, ExpertPool
+    lay = _small_layer()
+    pool = ExpertPool(0, E, lay.source, "cuda", with_shared=True)
+    params = _params(pool, lay.cfg, E)
+    T = 12
+    x = synthetic.tokens(77, T, H)
+    rng = np.random.default_rng(3)
+    slot = rng.integers(-1, E + 1, size=40).astype(np.int32)     # E = the shared slot
+    slot[:10] = 3                                                # 10 pairs on one expert: 2 items
+    tok = rng.integers(0, T, size=40).astype(np.int32)
+    w = rng.uniform(0.1, 1.0, size=40).astype(np.float32)
+    lib = L.load_library()
+    y = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    ws = L.workspace(torch.device("cuda"), lib.k3_moe_pairs_workspace(params, T, 40))
+    ts = [torch.from_numpy(a).cuda() for a in (slot, tok, w)]
+    L.check(lib.k3_moe_pairs_decode(params, x.data_ptr(), L.K3_BF16, T, ts[0].data_ptr(), ts[1].data_ptr(),
+                                    ts[2].data_ptr(), 40, y.data_ptr(), L.K3_F32, ws.data_ptr(), ws.numel(),
+                                    L.stream_of(x)), "k3_moe_pairs_decode")
+    xf = x.float().cpu().numpy()
+    h = lambda t: t.cpu().numpy()  # noqa: E731
+    ref = np.zeros((T, H), np.float64)
+    for i in np.argsort(slot, kind="stable"):
+        if slot[i] < 0:
+            continue
+        e = SHARED if slot[i] == E else int(slot[i])
+        (p1, s1), (p3, s3), (p2, s2) = lay.expert(e)
+        xt = xf[tok[i]:tok[i] + 1]
+        g = O.matvec_fused(xt, h(p1), h(s1))
+        u = O.matvec_fused(xt, h(p3), h(s3))
+        ref[tok[i]] += O.matvec_fused(O.silu(g) * u, h(p2), h(s2))[0].astype(np.float64) * w[i]
+    got = y.cpu().numpy()
+    assert O.rel_l2(got, ref) < 1e-5
+    untouched = np.setdiff1d(np.arange(T), tok[slot >= 0])
+    assert np.all(got[untouched] == 0)
+
+
+def _ep_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        from kimi_k3_mlx_macmini_b200 import synthetic
+        from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
+        lay = _small_layer(seed=9, top_k=4)
+        w = {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias}
+        ep = ExpertParallelMoE(lay.cfg, 0, w, lay.source)
+        x = synthetic.tokens(500 + rank, 6, H)
+        y = ep(x)
+        ref = lay.moe()(x)                    # the whole layer on this GPU
+        q.put((rank, O.rel_l2(y.cpu().numpy(), ref.float().cpu().numpy())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_two_gpus():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err in res.items():
+        assert err < 1e-5, (rank, err)

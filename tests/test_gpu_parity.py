@@ -21,16 +21,6 @@ NORTH_STAR_REL_L2 = 1e-3       # expert outputs within rel-L2 1e-
 EXPECTED_REL_L2 = 1e-5         # fp32 accumulation with exact weights
 
 
-@pytest.fixture(scope="module")
-def k3():
-    if not torch.cuda.is_available():
-        pytest.fail("GPU tests need a CUDA device")
-    from kimi_k3_mlx_macmini_b200 import build
-    build.build()
-    import kimi_k3_mlx_macmini_b200 as k
-    return k
-
-
 def cu(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
 
@@ -246,18 +236,19 @@ def full_layer(k3):
 
 def _oracle_layer_output(lay, x_bits_host, idx, w):
     """C-oracle (reference fused-kernel order) for the selected experts + shared expert."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
     xf = O.bf16_bits_to_f32(x_bits_host)
     H = xf.shape[1]
     y = np.zeros((xf.shape[0], H), np.float64)
     h = lambda t: t.cpu().numpy()  # noqa: E731
     for e in sorted(set(idx.reshape(-1).tolist())):
         tok, slot = np.nonzero(idx == e)
-        (p1, s1), (p3, s3), (p2, s2) = lay.experts[e]
+        (p1, s1), (p3, s3), (p2, s2) = lay.expert(e)
         g = O.matvec_fused(xf[tok], h(p1), h(s1))
         u = O.matvec_fused(xf[tok], h(p3), h(s3))
         out = O.matvec_fused(O.silu(g) * u, h(p2), h(s2))
         np.add.at(y, tok, out.astype(np.float64) * w[tok, slot][:, None])
-    (p1, s1), (p3, s3), (p2, s2) = lay.shared
+    (p1, s1), (p3, s3), (p2, s2) = lay.expert(synthetic.SHARED)
     y += O.matvec_fused(O.silu(O.matvec_fused(xf, h(p1), h(s1))) * O.matvec_fused(xf, h(p3), h(s3)),
                         h(p2), h(s2))
     return y
