@@ -642,10 +642,15 @@ bool pool_usable(const k3_moe_params& p) {
            p.hidden % kTStageK == 0 && p.inter % kTStageK == 0;
 }
 
+// The block-scaled kernels read the re-laid scales and either the tiles or the row-major
+// packed codes; a pool may carry the re-laid copies alone (a streamed staging pool).
 bool pool_bs(const k3_moe_params& p) {
     const k3_expert_pool* pl = p.pool;
-    return pool_usable(p) && pl->w1_scales_tc && pl->w3_scales_tc && pl->w2_scales_tc &&
-           p.hidden % kBStageK == 0 && p.inter % kBStageK == 0;
+    if (!pl || !pl->w1_scales_tc || !pl->w3_scales_tc || !pl->w2_scales_tc) return false;
+    const bool tiles = pl->w1_tiles && pl->w3_tiles && pl->w2_tiles;
+    const bool packed = pl->w1_packed && pl->w3_packed && pl->w2_packed;
+    return (tiles || packed) && pl->num_slots >= p.num_experts + (p.has_shared ? 1 : 0) &&
+           p.hidden % kTStageK == 0 && p.inter % kTStageK == 0;
 }
 
 // k-split for the block-scaled kernels: as choose_split_tma, over 256-k stages.
@@ -674,8 +679,8 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
     L.E = p.num_experts;
     L.U = std::min<int64_t>(p.num_experts, M * p.top_k) + (p.has_shared ? 1 : 0);
     L.P = M * p.top_k + (p.has_shared ? M : 0);
-    L.tma = pool_usable(p);
-    L.bs = L.tma && pool_bs(p);
+    L.bs = pool_bs(p);
+    L.tma = L.bs || pool_usable(p);
     size_t off = 0;
     if (L.bs) {
         // keys: (128-row block, active expert) in both phases

@@ -1,0 +1,136 @@
+"""Streamed-expert decode: the routed experts live in pinned host
+memory and only the ones a token routes to are copied to HBM.
+
+The reference streams experts from SSD on every use (``air_llm/models/kimi_k3/
+loader.py:229-266``, one contiguous read of packed + scales per projection) and runs
+them through the Metal kernel. Here the host tier is pinned memory holding every expert
+already in the block-scaled kernels' layout (contiguous 128-row x 128-byte tiles of the
+E2M1 codes and the re-laid E8M0 scale chunks, ``k3_mxfp4_tiles`` /
+``k3_mxfp4_scales_tc``), so a copy lands ready to use. Per layer:
+
+1. the router (weights resident in HBM) picks the token's experts; their ids come back to
+   the host (one small device->host read: copies need host addresses);
+2. a side stream copies each routed expert's six arrays (tiles and scales of w1, w3, w2)
+   into a staging slot with ``cudaMemcpyAsync`` (one call per array) and records an event
+   per expert;
+3. meanwhile the compute stream runs the shared expert (resident, staging slot S);
+4. the compute stream waits for the copies and runs the routed experts
+   (``k3_moe_pairs_decode`` over the staging pool), then adds the shared output last,
+   like ``moe.py:131``.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Callable
+
+import torch
+
+from . import _lib as L
+from .moe import SHARED, LatentMoE
+from .mxfp4 import packed_tiles, scales_tc
+
+WHICH = ("w1", "w3", "w2")
+
+
+def _relaid(trip):
+    """((tiles, tc) for w1, w3, w2) of one expert given its device (packed, scales) pairs."""
+    return [(packed_tiles(p)[0], scales_tc(s)[0]) for p, s in trip]
+
+
+class HostExpertStore:
+    """Every routed expert of a layer in pinned host memory, in the block-scaled layout:
+    ``tiles[w]`` [E, rows/128, cols/256, 128, 128] and ``tc[w]`` [E, rows/128, cols/128,
+    512] per projection w (uint8)."""
+
+    def __init__(self, num_experts: int, expert: Callable, device="cuda"):
+        self.E = num_experts
+        self.tiles, self.tc = {}, {}
+        for e in range(num_experts):
+            for w, (t, s) in zip(WHICH, _relaid(expert(e))):
+                if e == 0:
+                    self.tiles[w] = torch.empty((num_experts, *t.shape), dtype=torch.uint8, pin_memory=True)
+                    self.tc[w] = torch.empty((num_experts, *s.shape), dtype=torch.uint8, pin_memory=True)
+                self.tiles[w][e].copy_(t)
+                self.tc[w][e].copy_(s)
+        torch.cuda.synchronize(device)
+
+    def nbytes_expert(self) -> int:
+        return sum(self.tiles[w][0].numel() + self.tc[w][0].numel() for w in WHICH)
+
+
+class StreamedMoE:
+    """One MoE layer (BASELINE semantics: MXFP4 routed experts in ``store``, resident
+    MXFP4 shared expert) whose routed experts are copied to HBM on demand."""
+
+    def __init__(self, cfg, layer: int, w: dict, store: HostExpertStore, shared: Callable, device="cuda"):
+        self.cfg, self.store = cfg, store
+        self.device = torch.device(device)
+        self.router = LatentMoE(cfg, layer, w, lambda *a: None, fused=True, device=self.device)
+        self.S = cfg.num_experts_per_token                   # staging slots (M = 1 decode)
+        sh = _relaid(shared())                               # the shared expert, resident
+        self.tiles, self.tc = {}, {}
+        for w_, (t, s) in zip(WHICH, sh):
+            self.tiles[w_] = torch.empty((self.S + 1, *t.shape), dtype=torch.uint8, device=self.device)
+            self.tc[w_] = torch.empty((self.S + 1, *s.shape), dtype=torch.uint8, device=self.device)
+            self.tiles[w_][self.S].copy_(t)
+            self.tc[w_][self.S].copy_(s)
+        H, I = cfg.hidden_size, cfg.moe_intermediate_size
+        self.desc = L.K3ExpertPool(num_slots=self.S + 1,
+                                   w1_scales_tc=self.tc["w1"].data_ptr(), w3_scales_tc=self.tc["w3"].data_ptr(),
+                                   w2_scales_tc=self.tc["w2"].data_ptr(), w1_tiles=self.tiles["w1"].data_ptr(),
+                                   w3_tiles=self.tiles["w3"].data_ptr(), w2_tiles=self.tiles["w2"].data_ptr())
+        self.params = L.K3MoEParams(
+            hidden=H, inter=I, num_experts=self.S, top_k=cfg.num_experts_per_token,
+            renormalize=int(bool(cfg.moe_renormalize)), routed_scaling_factor=float(cfg.routed_scaling_factor),
+            has_shared=1, activation=L.K3_ACT_SILU, situ_beta=4.0, situ_linear_beta=-1.0,
+            experts=None, pool=ctypes.pointer(self.desc))
+        self.copy_stream = torch.cuda.Stream(self.device)
+        self.events = [torch.cuda.Event() for _ in range(self.S)]
+
+    def _pairs(self, x, slot, tok, w):
+        lib = L.load_library()
+        T, H = x.shape
+        y = torch.empty((T, H), dtype=torch.float32, device=x.device)
+        ws = L.workspace(x.device, lib.k3_moe_pairs_workspace(self.params, T, slot.numel()))
+        L.check(lib.k3_moe_pairs_decode(self.params, x.data_ptr(), L.dtype_code(x), T, slot.data_ptr(),
+                                        tok.data_ptr(), w.data_ptr(), slot.numel(), y.data_ptr(), L.K3_F32,
+                                        ws.data_ptr(), ws.numel(), L.stream_of(x)), "k3_moe_pairs_decode")
+        return y
+
+    def stage(self, experts):
+        """Copy the given experts into staging slots 0.. on the side stream (one event each)."""
+        cur = torch.cuda.current_stream(self.device)
+        self.copy_stream.wait_stream(cur)                    # slots are free once earlier compute ran
+        with torch.cuda.stream(self.copy_stream):
+            for j, e in enumerate(experts):
+                for w_ in WHICH:
+                    self.tiles[w_][j].copy_(self.store.tiles[w_][e], non_blocking=True)
+                    self.tc[w_][j].copy_(self.store.tc[w_][e], non_blocking=True)
+                self.events[j].record(self.copy_stream)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """y = routed experts (streamed) + shared expert, for M tokens routing to at most
+        ``top_k`` distinct experts in total (M = 1 decode)."""
+        flat = x.reshape(-1, x.shape[-1])
+        M = flat.shape[0]
+        rr = self.router.route(flat)
+        ids = rr.expert_indices.cpu()                        # host addresses need the ids
+        experts = sorted(set(ids.reshape(-1).tolist()))
+        if len(experts) > self.S:
+            raise NotImplementedError(f"{len(experts)} distinct experts exceed the {self.S} staging slots")
+        self.stage(experts)
+        dev = flat.device
+        own = torch.arange(M, dtype=torch.int32, device=dev)
+        y_sh = self._pairs(flat, torch.full((M,), self.S, dtype=torch.int32, device=dev), own,
+                           torch.ones(M, dtype=torch.float32, device=dev))
+        slot_of = {e: j for j, e in enumerate(experts)}
+        slot = torch.tensor([slot_of[int(e)] for e in ids.reshape(-1).tolist()], dtype=torch.int32, device=dev)
+        tok = own.repeat_interleave(ids.shape[1])
+        cur = torch.cuda.current_stream(self.device)
+        for j in range(len(experts)):
+            cur.wait_event(self.events[j])
+        y = self._pairs(flat, slot, tok, rr.expert_weights.reshape(-1).contiguous())
+        return (y + y_sh).reshape(x.shape[:-1] + (y.shape[-1],))
+
+
+__all__ = ["HostExpertStore", "StreamedMoE", "SHARED"]
