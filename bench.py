@@ -18,8 +18,11 @@ the host->device copy of x and the device->host copy of y inside the timed regio
 ``roofline`` covers the dominant kernel (the block-scaled gate/up grouped matvec), timed
 per launch with CUDA events on its launch stream in a second pass. SM clocks and
 throttle reasons are sampled during the timed region (NVML every ~2 ms, plus
-nvidia-smi). Multi-GPU runs are weak-scaled replicas (each rank its own tokens and a full
-copy of the layer); the time is the max over ranks.
+nvidia-smi). Multi-GPU runs are expert parallel (configs[2] "expert-sharded across
+2/4/8 GPUs"): each rank brings its own M tokens (weak scaling) and holds E/N routed
+experts plus the shared one; tokens are all-gathered, each rank runs its experts over
+every pair routed to them, and a reduce-scatter returns each rank's rows; the time is the
+max over ranks.
 """
 from __future__ import annotations
 
@@ -55,6 +58,9 @@ def parse():
                     help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
+                    help="BASELINE config: 2 = MoE-layer decode (headline), 4 = streamed-expert decode")
+    ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -266,6 +272,118 @@ def run_reference(args, rank, world):
     print(json.dumps(line))
 
 
+# ------------------------------------------------------- config 4: streamed experts
+
+def run_stream(args, rank, world, local):
+    """one token (M=1) through ``--layers`` MoE layers whose 384
+    routed experts live in pinned host memory; per layer only the routed experts are
+    copied host->HBM on a side stream while the resident shared expert computes. Reports
+    s/token end to end and how much of the copy time is hidden behind compute."""
+    import torch
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    from kimi_k3_mlx_macmini_b200.moe import SHARED
+    from kimi_k3_mlx_macmini_b200.stream import HostExpertStore, StreamedMoE
+    if world != 1 or rank != 0:
+        return
+    torch.cuda.set_device(local)
+    K, W, NL = args.steps, args.warmup, args.layers
+    t0 = time.perf_counter()
+    layers, stores = [], []
+    for li in range(NL):                                     # each layer: its own router and pool
+        ll = synthetic.baseline_layer(seed=args.seed + 1 + li, E=args.experts, H=H, I=I_, top_k=TOPK, scale=SCALE)
+        stores.append(HostExpertStore(args.experts, ll.expert))
+        w = {"gate.weight": ll.gate, "gate.e_score_correction_bias": ll.bias}
+        layers.append(StreamedMoE(ll.cfg, li, w, stores[-1], lambda ll=ll: ll.expert(SHARED)))
+    build_s = time.perf_counter() - t0
+    store = stores[0]
+
+    def token(i):
+        x = synthetic.tokens(args.seed * 7919 + i, 1, H)
+        for m in layers:
+            x = (x.float() + m(x)).to(torch.bfloat16)        # residual stream between layers
+        return x
+
+    for i in range(W):
+        token(i)
+    torch.cuda.synchronize()
+    clk = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        token(W + i)
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    s_per_token = e0.elapsed_time(e1) / 1e3 / K
+    # copy-only: the same expert sets staged without compute; compute-only: staged first
+    sets = []
+    for i in range(K):
+        x = synthetic.tokens(args.seed * 7919 + W + i, 1, H)
+        per = []
+        for m in layers:
+            ids = sorted(set(m.router.route(x).expert_indices.reshape(-1).tolist()))
+            per.append(ids)
+            x = (x.float() + m(x)).to(torch.bfloat16)
+        sets.append(per)
+    torch.cuda.synchronize()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(layers[0].copy_stream)
+    for per in sets:
+        for m, ids in zip(layers, per):
+            m.stage(ids)
+    c1.record(layers[-1].copy_stream)
+    torch.cuda.synchronize()
+    copy_s = c0.elapsed_time(c1) / 1e3 / K
+    comp_ms = 0.0
+    for i, per in enumerate(sets):
+        x = synthetic.tokens(args.seed * 7919 + W + i, 1, H)
+        for m, ids in zip(layers, per):
+            m.stage(ids)
+            torch.cuda.synchronize()
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            d0.record()
+            y = m(x, stage=False)
+            d1.record()
+            torch.cuda.synchronize()
+            comp_ms += d0.elapsed_time(d1)
+            x = (x.float() + y).to(torch.bfloat16)
+    comp_s = comp_ms / 1e3 / K
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    L.profile_enable(True)
+    L.profile_collect()
+    token(W)                                                 # one token's launches, counted
+    torch.cuda.synchronize()
+    prof = L.profile_collect()
+    L.profile_enable(False)
+    launches = sum(c for _, c in prof.values())
+    overlap = max(0.0, copy_s + comp_s - s_per_token)
+    copied = float(np.mean([sum(len(ids) for ids in per) for per in sets])) * store.nbytes_expert()
+    line = {
+        "metric": "streamed_decode_s_per_token", "value": s_per_token, "unit": "s/token",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": s_per_token * 1e3, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1 weights x e2m1 activation pieces, e8m0 block scales, f32 accumulate (tcgen05 kind::mxf4)",
+        "data": "synthetic (seeded random-init weights of the BASELINE layer)",
+        "config": {"workload": f"BASELINE configs[4]: M=1 token through {NL} layers, each layer's "
+                               f"{args.experts} routed experts in pinned host memory, its top-{TOPK} "
+                               "copied host->HBM per token on a side stream, resident shared expert",
+                   "layers": NL, "host_store_gb": NL * args.experts * store.nbytes_expert() / 1e9,
+                   "store_build_s": build_s},
+        "copy_s_per_token": copy_s,
+        "compute_s_per_token": comp_s,
+        "overlap_s_per_token": overlap,
+        "copy_time_hidden_frac": overlap / copy_s if copy_s > 0 else None,
+        "compute_hidden_frac": overlap / comp_s if comp_s > 0 else None,
+        "h2d_gbs": copied / copy_s / 1e9,
+        "e2e": {"value": s_per_token, "unit": "s/token", "h2d_bytes_per_step": copied + 2 * H,
+                "d2h_bytes_per_step": NL * TOPK * 8},
+        "gpu_launches": int(launches * K),
+        "kernel_ms_per_token": {k: v[0] for k, v in prof.items() if v[1]},
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
 # ------------------------------------------------------------------ B200 arm
 
 def traffic_from_profiles():
@@ -289,12 +407,27 @@ def run_b200(args, rank, world, local):
     M, K, W = args.tokens, args.steps, args.warmup
     R = min(K + W, 64)                                      # distinct token batches
     lay = synthetic.baseline_layer(seed=args.seed, E=args.experts, H=H, I=I_, top_k=TOPK, scale=SCALE)
-    moe = lay.moe()
-    _ = moe.pool
-    xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, M, H) for i in range(R)]
+    router = lay.moe()                                      # whole layer (1 GPU) / router (EP)
+    if world > 1:
+        # expert parallel: this rank holds experts [rank*E/W, (rank+1)*E/W) + the shared one
+        from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
+        moe = ExpertParallelMoE(lay.cfg, 0, {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias},
+                                lay.source)
+    else:
+        moe = router
+        _ = moe.pool
+
+    def batch(rk, i):
+        return synthetic.tokens(args.seed * 7919 + rk * 100003 + i, M, H)
+
+    xs = [batch(rank, i) for i in range(R)]
+    # experts this rank streams per step: the local experts any rank's tokens route to
+    E_loc = args.experts // world
     U = []
-    for x in xs:
-        U.append(int(torch.unique(moe.route(x).expert_indices).numel()))
+    for i in range(R):
+        ids = torch.cat([router.route(batch(rk, i)).expert_indices.reshape(-1) for rk in range(world)])
+        ids = torch.unique(ids)
+        U.append(int(((ids >= rank * E_loc) & (ids < (rank + 1) * E_loc)).sum().item()))
     torch.cuda.synchronize()
     step_x = [(W + i) % R for i in range(K)]                # batch of timed step i
 
@@ -305,13 +438,22 @@ def run_b200(args, rank, world, local):
             moe(xs[i])
     torch.cuda.synchronize()
     graphs, ys = [], []
-    for i in range(R):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=cap):
-            ys.append(moe(xs[i]))
-        graphs.append(g)
+    try:
+        for i in range(R):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                ys.append(moe(xs[i]))
+            graphs.append(g)
+        run = [g.replay for g in graphs]
+        timing = f"CUDA graph per batch ({R} distinct batches replayed as a ring)"
+    except Exception as exc:                                # noqa: BLE001 -- report and time eagerly
+        torch.cuda.synchronize()
+        graphs = []
+        run = [(lambda x=x: moe(x)) for x in xs]
+        timing = f"eager launches ({R} distinct batches as a ring; graph capture failed: {type(exc).__name__})"
+    barrier(world)
     for i in range(W):
-        graphs[i % R].replay()
+        run[i % R]()
     torch.cuda.synchronize()
     barrier(world)
     clk = ClockSampler(local)
@@ -320,7 +462,7 @@ def run_b200(args, rank, world, local):
     torch.cuda.synchronize()
     ev0.record()
     for i in range(K):
-        graphs[step_x[i]].replay()
+        run[step_x[i]]()
     ev1.record()
     torch.cuda.synchronize()
     clocks = clk.stop()
@@ -387,10 +529,13 @@ def run_b200(args, rank, world, local):
         "config": {"workload": f"BASELINE configs[2]: one MoE layer decode, M={M} tokens per GPU, "
                                f"{args.experts} routed + 1 shared MXFP4 expert (7168/2048), bf16 router, "
                                "top-8, x2.5",
-                   "tokens_per_gpu": M, "parallelism": f"replicas x{world}",
-                   "l2": "inputs larger than L2: 9.0 GB expert pool, fresh token batch per step",
-                   "timing": f"CUDA graph per batch ({R} distinct batches replayed as a ring), "
-                             "events around K replays"},
+                   "tokens_per_gpu": M,
+                   "parallelism": "single GPU" if world == 1 else
+                                  f"ep{world}: {args.experts // world} routed experts per rank + replicated shared, "
+                                  "all_gather dispatch, reduce_scatter combine (NCCL)",
+                   "l2": f"inputs larger than L2: {9.0 / world:.2f} GB of expert weights per GPU, "
+                         "a different token batch every step",
+                   "timing": timing + ", events around K steps"},
         "unique_experts_mean": float(np.mean(U_t)),
         "unique_experts_per_batch": U[:8],
         "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
@@ -418,6 +563,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.config == 4:
+            run_stream(args, rank, world, local)
         else:
             run_b200(args, rank, world, local)
     finally:

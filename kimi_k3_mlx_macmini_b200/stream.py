@@ -14,9 +14,9 @@ E2M1 codes and the re-laid E8M0 scale chunks, ``k3_mxfp4_tiles`` /
    into a staging slot with ``cudaMemcpyAsync`` (one call per array) and records an event
    per expert;
 3. meanwhile the compute stream runs the shared expert (resident, staging slot S);
-4. the compute stream waits for the copies and runs the routed experts
-   (``k3_moe_pairs_decode`` over the staging pool), then adds the shared output last,
-   like ``moe.py:131``.
+4. the compute stream runs each routed expert (``k3_moe_pairs_decode`` over its staging
+   slot) once that expert's event fires, so the copies of later experts overlap the
+   compute of earlier ones, then adds the shared output last, like ``moe.py:131``.
 """
 from __future__ import annotations
 
@@ -108,28 +108,49 @@ class StreamedMoE:
                     self.tc[w_][j].copy_(self.store.tc[w_][e], non_blocking=True)
                 self.events[j].record(self.copy_stream)
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, stage: bool = True) -> torch.Tensor:
         """y = routed experts (streamed) + shared expert, for M tokens routing to at most
-        ``top_k`` distinct experts in total (M = 1 decode)."""
+        ``top_k`` distinct experts in total (M = 1 decode). ``stage=False`` skips the
+        copies (the routed experts must already sit in slots 0.. in ascending id order).
+
+        Each routed expert runs as soon as its own copy has landed (one pairs call per
+        expert, waiting on that expert's event), so only the last expert's compute trails
+        the copies; the outputs are summed in ascending expert order and the shared
+        expert's output is added last, the order of ``moe.py:120-131``."""
         flat = x.reshape(-1, x.shape[-1])
         M = flat.shape[0]
+        dev = flat.device
         rr = self.router.route(flat)
         ids = rr.expert_indices.cpu()                        # host addresses need the ids
         experts = sorted(set(ids.reshape(-1).tolist()))
         if len(experts) > self.S:
             raise NotImplementedError(f"{len(experts)} distinct experts exceed the {self.S} staging slots")
-        self.stage(experts)
-        dev = flat.device
+        if stage:
+            self.stage(experts)
+        else:
+            for j in range(len(experts)):
+                self.events[j].record(torch.cuda.current_stream(self.device))
+        # pairs grouped by expert (tokens ascending within an expert), uploaded once
+        k = ids.shape[1]
+        flat_ids = ids.reshape(-1).tolist()
+        order = sorted(range(len(flat_ids)), key=lambda p: (flat_ids[p], p))
+        slot_of = {e: j for j, e in enumerate(experts)}
+        host = torch.tensor([[slot_of[flat_ids[p]], p // k, p] for p in order], dtype=torch.int32)
+        dev_idx = host.to(dev, non_blocking=False)
+        slot = dev_idx[:, 0].contiguous()
+        tok = dev_idx[:, 1].contiguous()
+        wts = rr.expert_weights.reshape(-1).float()[dev_idx[:, 2].long()].contiguous()
         own = torch.arange(M, dtype=torch.int32, device=dev)
         y_sh = self._pairs(flat, torch.full((M,), self.S, dtype=torch.int32, device=dev), own,
                            torch.ones(M, dtype=torch.float32, device=dev))
-        slot_of = {e: j for j, e in enumerate(experts)}
-        slot = torch.tensor([slot_of[int(e)] for e in ids.reshape(-1).tolist()], dtype=torch.int32, device=dev)
-        tok = own.repeat_interleave(ids.shape[1])
         cur = torch.cuda.current_stream(self.device)
-        for j in range(len(experts)):
+        y, start = None, 0
+        counts = [sum(1 for e in flat_ids if e == ex) for ex in experts]
+        for j, n in enumerate(counts):
             cur.wait_event(self.events[j])
-        y = self._pairs(flat, slot, tok, rr.expert_weights.reshape(-1).contiguous())
+            y_j = self._pairs(flat, slot[start:start + n], tok[start:start + n], wts[start:start + n])
+            y = y_j if y is None else y + y_j
+            start += n
         return (y + y_sh).reshape(x.shape[:-1] + (y.shape[-1],))
 
 
