@@ -244,6 +244,48 @@ K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* x, int x_dt
                                  const int32_t* idx, const float* w, void* y_out, int y_dtype,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ prefill --- */
+
+/* Prefill (any number of tokens T, meant for T in the hundreds to thousands) MoE block
+ * without the latent wrapper: the same computation as k3_moe_decode -- route, every routed
+ * expert y[t] += w[t,slot] * act(x W1^T, x W3^T) W2^T, plus the shared expert -- for the
+ * BASELINE layer at prefill (replaces LatentMoE.__call__'s route + per-expert loop + shared
+ * expert, air_llm/models/kimi_k3/moe.py:110-132; oracle k3ref/layers.py:241-261). The
+ * pairs are grouped by expert and run as two block-scaled grouped GEMMs; the experts'
+ * contributions to a token are added in fp32 in an order that is not fixed (results agree
+ * with the ascending-expert sum to fp32 rounding). The activations enter the tensor cores
+ * as 4 E2M1 pieces per value (relative error ~4e-5 on x, ~2e-4 on the activation).
+ * Needs the block-scaled tile pool (k3_expert_pool *_scales_tc and *_tiles), H and I
+ * multiples of 256, E <= 1024, top_k <= 32. x [T][H] f32|bf16 (bf16 routes on the tensor
+ * cores); y [T][H] f32|bf16; idx_out/weight_out [T][top_k] may be NULL. */
+K3_API size_t k3_moe_prefill_workspace(const k3_moe_params* p, int64_t T);
+K3_API int k3_moe_prefill(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                          const uint16_t* gate_w_bf16, const float* bias, void* y_out, int y_dtype,
+                          int32_t* idx_out, float* weight_out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Same with the routing supplied (idx int32 [T][top_k], w f32 [T][top_k]; entries outside
+ * [0, E) are skipped): the expert loop of moe.py:115-127 + shared expert (:131). Uses the
+ * k3_moe_prefill_workspace size. */
+K3_API int k3_moe_experts_prefill(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                                  const int32_t* idx, const float* w, void* y_out, int y_dtype,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Prefill form of k3_moe_pairs_decode: n_pairs (slot, token row, weight) candidates, any
+ * number; slots index the pool (candidates outside [0, num_slots) or with a token outside
+ * [0, T) are skipped); y_out[t] = sum of weight * expert(slot)(x[t]) over t's candidates
+ * (rows without any are zero). The expert-parallel prefill runs its local experts (and its
+ * own tokens' shared expert) through this. */
+K3_API size_t k3_moe_pairs_prefill_workspace(const k3_moe_params* p, int64_t T, int64_t n_pairs);
+K3_API int k3_moe_pairs_prefill(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                                const int32_t* pair_slot, const int32_t* pair_tok,
+                                const float* pair_w, int64_t n_pairs, void* y_out, int y_dtype,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Device status word of the last prefill call on `workspace` (synchronises `stream`):
+ * K3_OK, or K3_ERR_TIMEOUT when a kernel's bounded wait gave up. */
+K3_API int k3_moe_prefill_status(const void* workspace, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

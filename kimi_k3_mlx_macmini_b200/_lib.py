@@ -69,6 +69,15 @@ SIGNATURES = {
                              _vp, _vp, _vp, _sz, _vp]),
     "k3_moe_experts_decode": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp,
                                      _i32, _vp, _sz, _vp]),
+    "k3_moe_prefill_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64]),
+    "k3_moe_prefill": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp, _i32,
+                              _vp, _vp, _vp, _sz, _vp]),
+    "k3_moe_experts_prefill": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp,
+                                      _i32, _vp, _sz, _vp]),
+    "k3_moe_pairs_prefill_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
+    "k3_moe_pairs_prefill": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp, _i64,
+                                    _vp, _i32, _vp, _sz, _vp]),
+    "k3_moe_prefill_status": (_i32, [_vp, _vp]),
 }
 
 _lib = None

@@ -111,20 +111,20 @@ __device__ __forceinline__ float warp_max_nonneg(float v) {
 }
 
 // Warp-wide: lane l holds element l of a 32-element block of NV values (independent
-// chains, interleaved); splits each into kBPieces E2M1 pieces. Piece p of value i: its
+// chains, interleaved); splits each into NP (default kBPieces) E2M1 pieces. Piece p of value i: its
 // 16 packed bytes go to data[i] + p*row_stride (element 2j in the low nibble of byte j)
 // and its E8M0 scale to sf[i][p*sf_stride]. Values with sf[i] == nullptr are skipped.
 // Both scale layouts in use are affine in p: natural per-row scales ([row][block],
 // stride = blocks per row) and the tensor-core chunk (sf_chunk_offset(8*col + p, j),
 // stride 16 since the 8 rows of one column share a 32-row group).
-template <int NV>
+template <int NV, int NP = kBPieces>
 __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, uint8_t* const (&data)[NV],
                                                int64_t row_stride, uint8_t* const (&sf)[NV], int64_t sf_stride) {
     float res[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) res[i] = v[i];
 #pragma unroll 1
-    for (int p = 0; p < kBPieces; ++p) {
+    for (int p = 0; p < NP; ++p) {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             const float m = warp_max_nonneg(fabsf(res[i]));

@@ -1341,6 +1341,29 @@ extern "C" K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* 
 
 namespace k3 {
 
+// Router logits of any number of tokens on the CUDA cores (fp32 fma, 8 tokens a launch):
+// the prefill path's route for f32 activations.
+int launch_router_logits_rows(const void* x, int xdt, int64_t M, int64_t H, const uint16_t* W,
+                              int64_t E, float* logits, cudaStream_t s) {
+    const size_t esz = xdt == K3_BF16 ? 2 : 4;
+    for (int64_t m0 = 0; m0 < M; m0 += kMaxTok) {
+        const int Mc = int(std::min<int64_t>(kMaxTok, M - m0));
+        if (int rc = launch_router_logits(static_cast<const uint8_t*>(x) + size_t(m0) * H * esz, xdt, Mc,
+                                          H, W, E, logits + m0 * E, s))
+            return rc;
+    }
+    return K3_OK;
+}
+
+// Sigmoid top-k of every row of logits [M][E] (one warp per row).
+int launch_topk_rows(const float* logits, int64_t M, int64_t E, const float* bias, int k, int renorm,
+                     float scale, int32_t* idx, float* w, int* status, cudaStream_t s) {
+    topk_kernel<<<int((M + 7) / 8), 256, 0, s>>>(logits, int(M), int(E), bias, k, renorm, scale, idx, w,
+                                                 nullptr, nullptr, status);
+    K3_CHECK_LAUNCH("topk_kernel");
+    return K3_OK;
+}
+
 // Workspace of a pairs call: T token rows, up to n_in candidate pairs.
 DecodeLayout pairs_layout(const k3_moe_params& p, int64_t T, int64_t n_in, int sms) {
     DecodeLayout L{};

@@ -1,0 +1,133 @@
+// Prefill path (many tokens per call) on the block-scaled tensor cores: shared
+// declarations.
+//
+// A call routes T tokens, groups the (token, expert) pairs by expert -- experts ascending,
+// tokens ascending within an expert, the shared expert last (the order of the reference's
+// `for e in sorted(...)` loop, air_llm/models/kimi_k3/moe.py:120) -- and cuts each
+// expert's pairs into chunks of at most kPN tokens. One grouped GEMM per phase then runs
+// over items = (chunk, weight row block):
+//
+//   gate/up: D_g, D_u [128 rows of I][chunk tokens] = W1/W3 rows x (x pieces)^T, then
+//            act = phi(D_g, D_u) * routing weight, split into E2M1 pieces for the down
+//            phase;
+//   down:    D [2 x 128 rows of H][chunk tokens] = W2 rows x (act pieces)^T, reduce-added
+//            into y[token] (fp32 adds in the L2; the order of the adds is not fixed).
+//
+// The activations enter the kind::mxf4 MMA as kPPieces E2M1 pieces with one E8M0 scale
+// per (piece, 32-block); the pieces of one value accumulate into the same TMEM column
+// (one MMA per piece, accumulate on), so a chunk of n tokens takes n TMEM columns.
+//
+// Token operands live in "images": for every (chunk, 256-k step, piece) one contiguous
+// block holding the two 512-byte scale chunks of the block's rows followed by its n8 rows
+// of 128 packed bytes, already in the 128-byte-swizzled order the tensor core reads
+// (16-byte unit u of row j at position u ^ (j & 7)). One bulk copy moves a block into a
+// shared-memory slot. The gate/up image is built from the token pieces by a permute
+// kernel; the down image is written directly by the gate/up epilogue.
+#pragma once
+
+#include <cuda.h>
+
+#include "k3_bs.cuh"
+
+namespace k3 {
+
+constexpr int kPPieces = 4;           // E2M1 pieces per activation value
+constexpr int kPN = 104;              // tokens per chunk (MMA N <= 104, a multiple of 8)
+constexpr int kPASlots = 3;           // weight ring: two 128-row tiles x 256 k per slot
+constexpr int kPBSlots = 6;           // token ring: one image block per slot
+constexpr int kPEpiWarps = 4;
+constexpr int kPThreads = (3 + kPEpiWarps) * 32;   // A producer, MMA, 4 epilogue, B producer
+constexpr int kPPlanBlock = 256;      // candidates per plan block
+constexpr int kPMaxSlots = kMaxExperts + 1;
+constexpr int kPImgSf = 2 * kBChunk;  // scale bytes at the head of an image block
+
+// TMEM columns: two accumulator buffers x two accumulators x kPN, then the scale slots.
+constexpr int kPAccCols = kPN;
+constexpr int kPSfaCol = 4 * kPAccCols;             // kPASlots x 16 columns
+constexpr int kPSfbCol = kPSfaCol + 16 * kPASlots;  // kPBSlots x 8 columns
+static_assert(kPSfbCol + 8 * kPBSlots <= 512, "prefill TMEM plan exceeds 512 columns");
+static_assert(kPN % 8 == 0 && kPN <= 128, "chunk width must be a multiple of 8, <= 128");
+
+struct alignas(1024) PASlot {
+    uint8_t a[2][kBRows][128];        // two weight tiles (gate + up, or two down row blocks), SW128
+    uint8_t sfa[2][2 * kBChunk];      // their scale chunks (256 k)
+};
+struct alignas(1024) PBSlot {
+    uint8_t sfb[kPImgSf];             // one image block: scale chunks, then
+    uint8_t b[kPN][128];              // the chunk's rows of one piece (256 k), SW128
+};
+// Gate/up epilogue: per warp a 32 x 32 fp32 transpose buffer (row stride 33).
+constexpr int kPEpiBuf = 32 * 33;
+constexpr size_t psmem_bytes() {
+    return sizeof(PASlot) * kPASlots + sizeof(PBSlot) * kPBSlots + sizeof(float) * kPEpiBuf * kPEpiWarps +
+           1024 /*align*/ + 256 /*barriers*/;
+}
+static_assert(psmem_bytes() + 2048 <= 227 * 1024, "prefill ring exceeds shared memory");
+
+// Byte offset of the image block (chunk c, k-step s, piece p): blocks are ordered
+// [chunk][step][piece], a block of a chunk with n8 rows holds kPImgSf + 128 n8 bytes, and
+// n8p[c] = sum of n8 over the chunks before c.
+__host__ __device__ __forceinline__ int64_t img_block(const int* n8p, int c, int nst, int s, int p, int n8) {
+    return int64_t(kPPieces) * nst * (int64_t(kPImgSf) * c + 128 * int64_t(n8p[c])) +
+           int64_t(s * kPPieces + p) * (kPImgSf + 128 * n8);
+}
+
+// Device-side routing plan of one prefill call (all arrays in the workspace).
+struct PrefillHeader {
+    int status;
+    int n_pairs;
+    int n_chunks;
+    int pad;
+};
+struct PrefillPlan {
+    PrefillHeader* hdr;
+    int* blk_cnt;        // [nblk][NS] per-block slot counts, then per-block bases
+    int* off;            // [NS + 1] first pair of each slot
+    int* ch_first;       // [NS + 1] first chunk of each slot
+    int* pair_tok;       // [NP] token row of each pair (grouped order)
+    float* pair_w;       // [NP] its routing weight
+    int* pair_cj;        // [NP] (chunk << 8) | row in the chunk
+    int* ch_slot;        // [NC] chunk -> slot
+    int* ch_p0;          // [NC] first pair of the chunk
+    int* ch_n;           // [NC] pairs in the chunk (1..kPN)
+    int* ch_n8p;         // [NC + 1] exclusive prefix of the chunks' rows rounded up to 8
+};
+
+// Where the (slot, token, weight) candidates come from: either a routing result
+// idx/w [T][k] (candidate i < T*k is (idx[i], i / k, w[i]); with shared_slot >= 0 the
+// next T candidates are (shared_slot, t, 1)), or explicit pair arrays.
+struct PrefillCand {
+    const int32_t* idx;
+    const float* w;
+    int T, k, shared_slot;
+    const int32_t* slot;
+    const int32_t* tok;
+    const float* pw;
+    int n;
+    int num_slots;
+};
+
+// Tensor maps: the two weight tile pools ([slot * rows/128][K/256][128][128] boxes).
+struct PMaps {
+    CUtensorMap a0, a1;
+};
+
+struct PArgs {
+    PrefillPlan P;
+    int64_t K;               // reduction length (H for gate/up, I for down)
+    int64_t rows;            // rows of one projection (I for gate/up, H for down)
+    int* status;
+    const uint8_t* sfa0;     // scale-chunk pools [slot][rows/128][K/128][512]
+    const uint8_t* sfa1;     // (gate/up: W3's; down: unused)
+    int64_t sf_slot;         // bytes per slot of a scale-chunk pool
+    int routed_slots;        // slots below this stream with an evict-first L2 policy
+    const uint8_t* img;      // B image of this phase
+    // gate/up epilogue -> the down phase's image
+    uint8_t* img_out;
+    int act_kind;
+    float beta, lbeta;
+    // down epilogue: y [T][H] fp32 (reduce-add)
+    float* y;
+};
+
+}  // namespace k3

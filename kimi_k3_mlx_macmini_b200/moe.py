@@ -220,11 +220,31 @@ class LatentMoE:
             pool=(ctypes.pointer(pool.desc if self.block_scaled else pool.desc_f16)
                   if self.use_pool else None))
 
+    @property
+    def prefill_ok(self) -> bool:
+        """True when calls of more than 8 tokens run on the block-scaled grouped GEMMs
+        (``k3_moe_prefill``): the pool carries tiles and re-laid scales, H and I are
+        multiples of 256."""
+        p = self.pool
+        return (self.use_pool and self.block_scaled and p.tiles is not None and p.scales_tc is not None
+                and p.hidden % 256 == 0 and p.inter % 256 == 0 and self.cfg.num_experts <= 1024
+                and self.cfg.num_experts_per_token <= 32)
+
     def _experts_decode(self, h: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
                         params: L.K3MoEParams) -> torch.Tensor:
         """y[t] = sum_slot w[t,slot] * expert_{idx[t,slot]}(h[t]) (+ MXFP4 shared), fp32."""
         lib = L.load_library()
         out = torch.empty((h.shape[0], self.pool.hidden), dtype=torch.float32, device=h.device)
+        if h.shape[0] > MAX_DECODE_TOKENS and self.prefill_ok:
+            hc = h.contiguous()
+            ic = idx.to(torch.int32).contiguous()
+            wc = w.to(torch.float32).contiguous()
+            ws = L.workspace(h.device, lib.k3_moe_prefill_workspace(params, hc.shape[0]))
+            L.check(lib.k3_moe_experts_prefill(params, hc.data_ptr(), L.dtype_code(hc), hc.shape[0],
+                                               ic.data_ptr(), wc.data_ptr(), out.data_ptr(), L.K3_F32,
+                                               ws.data_ptr(), ws.numel(), L.stream_of(hc)),
+                    "k3_moe_experts_prefill")
+            return out
         for m0 in range(0, h.shape[0], MAX_DECODE_TOKENS):
             hc = h[m0:m0 + MAX_DECODE_TOKENS].contiguous()
             ic = idx[m0:m0 + MAX_DECODE_TOKENS].to(torch.int32).contiguous()
@@ -340,6 +360,22 @@ class LatentMoE:
                                       L.stream_of(xc)), "k3_moe_decode")
         return y, idx, w
 
+    def _fused_prefill(self, flat: torch.Tensor):
+        """route + routed experts + MXFP4 shared expert for any number of tokens in one
+        library call (``k3_moe_prefill``: router GEMM, grouped block-scaled GEMMs)."""
+        lib = L.load_library()
+        params = self._params()
+        T, k = flat.shape[0], self.cfg.num_experts_per_token
+        y = torch.empty((T, self.pool.hidden), dtype=torch.float32, device=flat.device)
+        idx = torch.empty((T, k), dtype=torch.int32, device=flat.device)
+        w = torch.empty((T, k), dtype=torch.float32, device=flat.device)
+        ws = L.workspace(flat.device, lib.k3_moe_prefill_workspace(params, T))
+        L.check(lib.k3_moe_prefill(params, flat.data_ptr(), L.dtype_code(flat), T, self.gate_w.data_ptr(),
+                                   None if self.gate_b is None else self.gate_b.data_ptr(), y.data_ptr(),
+                                   L.K3_F32, idx.data_ptr(), w.data_ptr(), ws.data_ptr(), ws.numel(),
+                                   L.stream_of(flat)), "k3_moe_prefill")
+        return y, idx, w
+
     def __call__(self, x: torch.Tensor, return_router: bool = False):
         """``moe.py:110-132``: returns y shaped like x (fp32), and the RouterResult if asked."""
         L.require_cuda(x, "x")
@@ -350,6 +386,9 @@ class LatentMoE:
         flat = flat.contiguous()
         if (not self.latent and not self.dense_shared and not return_router and self.fused
                 and self.tiled):
+            if flat.shape[0] > MAX_DECODE_TOKENS and self.prefill_ok:
+                y, _, _ = self._fused_prefill(flat)
+                return y.reshape(*orig[:-1], y.shape[-1])
             y, _, _ = self._fused_decode(flat)
             return y.reshape(*orig[:-1], y.shape[-1])
         r = self.route(flat)

@@ -1,0 +1,192 @@
+"""Prefill path (BASELINE configs[3] semantics: many tokens per call) on the GPU, through
+the C ABI, against the CPU oracle.
+
+The routed-expert math is the reference's (``air_llm/models/kimi_k3/moe.py:110-132``,
+oracle ``k3ref/layers.py:241-261``); the activations enter the tensor cores as 4 E2M1
+pieces per value, whose dropped remainder bounds the error (about 4e-5 relative on x and
+2e-4 on the activation), inside the north-star bar of rel-L2 1e-3.
+"""
+import numpy as np
+import pytest
+import torch
+
+import goldens as G
+from oracle import mxfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+NORTH_STAR_REL_L2 = 1e-3       # expert outputs within rel-L2 1e-3
+EXPECTED_REL_L2 = 5e-4         # 4 E2M1 activation pieces (measured ~2e-4)
+
+
+def host(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _oracle(lay, xf, idx, w, shared=True):
+    """C oracle (reference fused-kernel order) for the routed experts + shared expert."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    h = lambda t: t.cpu().numpy()  # noqa: E731
+    y = np.zeros((xf.shape[0], xf.shape[1]), np.float64)
+    for e in sorted(set(idx.reshape(-1).tolist())):
+        if e < 0:
+            continue                                           # skipped candidates
+        tok, slot = np.nonzero(idx == e)
+        (p1, s1), (p3, s3), (p2, s2) = lay.expert(e)
+        g = O.matvec_fused(xf[tok], h(p1), h(s1))
+        u = O.matvec_fused(xf[tok], h(p3), h(s3))
+        out = O.matvec_fused(O.silu(g) * u, h(p2), h(s2))
+        np.add.at(y, tok, out.astype(np.float64) * w[tok, slot][:, None])
+    if shared:
+        (p1, s1), (p3, s3), (p2, s2) = lay.expert(synthetic.SHARED)
+        y += O.matvec_fused(O.silu(O.matvec_fused(xf, h(p1), h(s1))) * O.matvec_fused(xf, h(p3), h(s3)),
+                            h(p2), h(s2))
+    return y
+
+
+@pytest.fixture(scope="module")
+def small_layer(k3):
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay = synthetic.baseline_layer(seed=31, E=16, H=1024, I=512, top_k=4)
+    return lay, lay.moe()
+
+
+@pytest.mark.parametrize("T", [9, 37, 300, 520])
+def test_prefill_layer_matches_oracle(k3, small_layer, T):
+    """Route + experts + shared in one call; T=520 puts ~130 tokens on every expert, so
+    each expert splits into two chunks and the shared expert into five."""
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay, moe = small_layer
+    assert moe.prefill_ok
+    x = synthetic.tokens(900 + T, T, 1024)
+    y, idx, w = moe._fused_prefill(x)
+    torch.cuda.synchronize()
+    xf = x.float().cpu().numpy()
+    rr = O.route(xf, host(lay.gate), None if lay.bias is None else host(lay.bias), 4, True, 2.5)
+    bad, ties = G.index_sets_match(idx.cpu().numpy(), np.sort(rr.expert_indices, -1), rr.corrected_scores, 4)
+    assert bad == 0
+    if ties == 0:
+        assert np.allclose(G.canon_weights(idx.cpu().numpy(), host(w)),
+                           G.canon_weights(rr.expert_indices, rr.expert_weights), rtol=1e-5, atol=1e-6)
+    want = _oracle(lay, xf, idx.cpu().numpy(), host(w))
+    err = O.rel_l2(host(y), want)
+    assert err < NORTH_STAR_REL_L2
+    assert err < EXPECTED_REL_L2
+    # the public call dispatches here for T > 8
+    y2 = moe(x)
+    assert O.rel_l2(host(y2), host(y)) < 1e-6
+    ws = L.workspace(x.device, 1)
+    assert L.load_library().k3_moe_prefill_status(ws.data_ptr(), L.stream_of(x)) == 0
+
+
+def test_prefill_f32_input_and_bf16_output(k3, small_layer):
+    """f32 activations (CUDA-core router, pieces from f32) and a bf16 result."""
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay, moe = small_layer
+    T = 64
+    x = synthetic.tokens(4321, T, 1024).float() * 1.5
+    lib = L.load_library()
+    params = moe._params()
+    yb = torch.empty((T, 1024), dtype=torch.bfloat16, device="cuda")
+    idx = torch.empty((T, 4), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, 4), dtype=torch.float32, device="cuda")
+    ws = L.workspace(x.device, lib.k3_moe_prefill_workspace(params, T))
+    L.check(lib.k3_moe_prefill(params, x.data_ptr(), L.K3_F32, T, moe.gate_w.data_ptr(),
+                               None if moe.gate_b is None else moe.gate_b.data_ptr(),
+                               yb.data_ptr(), L.K3_BF16, idx.data_ptr(), w.data_ptr(), ws.data_ptr(), ws.numel(),
+                               L.stream_of(x)), "k3_moe_prefill")
+    torch.cuda.synchronize()
+    xf = x.cpu().numpy()
+    rr = O.route(xf, host(lay.gate), None if lay.bias is None else host(lay.bias), 4, True, 2.5)
+    bad, _ = G.index_sets_match(idx.cpu().numpy(), np.sort(rr.expert_indices, -1), rr.corrected_scores, 4)
+    assert bad == 0
+    want = _oracle(lay, xf, idx.cpu().numpy(), host(w))
+    assert O.rel_l2(host(yb), want) < 4e-3                         # bf16 output rounding (~1.1e-3 rms)
+    wb = torch.from_numpy(want.astype(np.float32)).to(torch.bfloat16).float().numpy()
+    assert O.rel_l2(host(yb), wb) < 2e-3                           # within about an ulp of bf16(exact)
+
+
+def test_experts_prefill_given_routing(k3, small_layer):
+    """Routing supplied by the caller, entries outside [0, E) skipped."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay, moe = small_layer
+    T = 150
+    x = synthetic.tokens(55, T, 1024)
+    rng = np.random.default_rng(7)
+    idx = np.stack([rng.choice(16, 4, replace=False) for _ in range(T)]).astype(np.int32)
+    idx[::7, 0] = -1                                           # skipped candidates
+    w = rng.uniform(0.1, 1.0, size=(T, 4)).astype(np.float32)
+    y = moe._experts_decode(x, torch.from_numpy(idx).cuda(), torch.from_numpy(w).cuda(), moe._params(has_shared=0))
+    want = _oracle(lay, x.float().cpu().numpy(), idx, w, shared=False)
+    assert O.rel_l2(host(y), want) < EXPECTED_REL_L2
+
+
+def test_pairs_prefill_matches_oracle(k3, small_layer):
+    """Explicit (slot, token, weight) candidates: skipped slots and tokens, the shared
+    slot, one expert with more pairs than a chunk holds."""
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    from kimi_k3_mlx_macmini_b200.moe import SHARED
+    lay, moe = small_layer
+    T, n = 40, 400
+    x = synthetic.tokens(66, T, 1024)
+    rng = np.random.default_rng(11)
+    slot = rng.integers(-1, 18, size=n).astype(np.int32)       # 16 = the shared slot, 17 out of range
+    slot[:150] = 5                                             # 150 pairs on one expert: two chunks
+    tok = rng.integers(-2, T, size=n).astype(np.int32)         # negative tokens are skipped
+    w = rng.uniform(0.1, 1.0, size=n).astype(np.float32)
+    lib = L.load_library()
+    params = moe._params()
+    y = torch.empty((T, 1024), dtype=torch.float32, device="cuda")
+    ws = L.workspace(x.device, lib.k3_moe_pairs_prefill_workspace(params, T, n))
+    ts = [torch.from_numpy(a).cuda() for a in (slot, tok, w)]
+    L.check(lib.k3_moe_pairs_prefill(params, x.data_ptr(), L.K3_BF16, T, ts[0].data_ptr(), ts[1].data_ptr(),
+                                     ts[2].data_ptr(), n, y.data_ptr(), L.K3_F32, ws.data_ptr(), ws.numel(),
+                                     L.stream_of(x)), "k3_moe_pairs_prefill")
+    xf = x.float().cpu().numpy()
+    h = lambda t: t.cpu().numpy()  # noqa: E731
+    ref = np.zeros((T, 1024), np.float64)
+    for i in range(n):
+        if slot[i] < 0 or slot[i] > 16 or tok[i] < 0:
+            continue
+        e = SHARED if slot[i] == 16 else int(slot[i])
+        (p1, s1), (p3, s3), (p2, s2) = lay.expert(e)
+        xt = xf[tok[i]:tok[i] + 1]
+        g = O.matvec_fused(xt, h(p1), h(s1))
+        u = O.matvec_fused(xt, h(p3), h(s3))
+        ref[tok[i]] += O.matvec_fused(O.silu(g) * u, h(p2), h(s2))[0].astype(np.float64) * w[i]
+    got = y.cpu().numpy()
+    assert O.rel_l2(got, ref) < EXPECTED_REL_L2
+    live = (slot >= 0) & (slot <= 16) & (tok >= 0)
+    untouched = np.setdiff1d(np.arange(T), tok[live])
+    assert np.all(got[untouched] == 0)
+
+
+def test_prefill_repeatable(k3, small_layer):
+    """Two calls agree to fp32 rounding (the fp32 adds into y are unordered)."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    _, moe = small_layer
+    x = synthetic.tokens(8, 200, 1024)
+    a, b = moe(x), moe(x)
+    assert O.rel_l2(host(a), host(b)) < 1e-6
+
+
+def test_full_size_prefill_agrees_with_decode(k3):
+    """BASELINE layer at full size (384 + 1 experts, 7168/2048, top-8, x2.5), 256 tokens:
+    the prefill call against the decode path (8 tokens a call, ~1e-7 from exact) on the
+    same tokens; router index sets must match (tensor-core bf16 products vs fp32 fma)."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay = synthetic.baseline_layer(seed=123)
+    moe = lay.moe()
+    T = 256
+    x = synthetic.tokens(2024, T, 7168)
+    y, idx, w = moe._fused_prefill(x)
+    yd = torch.cat([moe._fused_decode(x[m:m + 8])[0] for m in range(0, T, 8)])
+    torch.cuda.synchronize()
+    xf = x.float().cpu().numpy()
+    rr = O.route(xf, host(lay.gate), None, 8, True, 2.5)
+    bad, ties = G.index_sets_match(idx.cpu().numpy(), np.sort(rr.expert_indices, -1), rr.corrected_scores, 8)
+    assert bad == 0
+    assert O.rel_l2(host(y), host(yd)) < EXPECTED_REL_L2
