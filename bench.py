@@ -58,8 +58,9 @@ def parse():
                     help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
-                    help="BASELINE config: 2 = MoE-layer decode (headline), 4 = streamed-expert decode")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="BASELINE config: 2 = MoE-layer decode (headline), 3 = MoE-layer prefill "
+                         "(--tokens defaults to 4096), 4 = streamed-expert decode")
     ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -239,34 +240,48 @@ def cpu_baseline(M: int, seed: int, steps: int, budget_s: float = 20.0):
         if spent > budget_s:
             break
     per_step = t_route / n_steps + (U_tot / n_steps) * (t_exp / n_exp)
-    sample = (f"{n_steps} decode step(s) of M={M}: numpy fp32 router + C port of the reference "
+    sample = (f"{n_steps} step(s) of M={M}: numpy fp32 router + C port of the reference "
               f"fused-kernel loop over {n_exp} expert FFNs (of {U_tot} routed+shared); step time = "
               f"router + (U+1) x mean expert time")
     return M / per_step, O.oracle_threads(), sample
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU path (oracle port) on this box's host cores."""
+    """--impl reference: the reference's CPU path (oracle port) on this box's host cores, on
+    the same config and metric as the B200 arm. Each sample is one bounded slice of a step
+    (router + a subset of the step's expert FFNs, extrapolated to all of them); at most 8
+    samples after one warm-up, inside a ~150 s budget."""
     if rank != 0:
         return
-    M = args.tokens
+    cfg = args.config
+    M = 4096 if (cfg == 3 and args.tokens == 8) else (1 if cfg == 4 else args.tokens)
+    n_s, n_w = max(1, min(args.steps, 8)), min(args.warmup, 1)
+    budget = 150.0 / (n_s + n_w)
     t0 = time.perf_counter()
     vals = []
-    for i in range(args.warmup + args.steps):
-        v, cores, sample = cpu_baseline(M, args.seed + i, 1, budget_s=4.0)
-        if i >= args.warmup:
+    for i in range(n_w + n_s):
+        v, cores, sample = cpu_baseline(M, args.seed + i, 1, budget_s=budget)
+        if i >= n_w:
             vals.append(v)
-    value = statistics.median(vals) if vals else 0.0
+    tps = statistics.median(vals) if vals else 0.0
+    if cfg == 4:
+        metric, unit, value, hib = "streamed_decode_s_per_token", "s/token", args.layers / tps, False
+        workload = (f"BASELINE configs[4]: M=1 token through {args.layers} MoE layers (expert compute only; "
+                    "the reference's SSD reads are not timed)")
+    else:
+        metric = "moe_layer_prefill_tokens_per_s" if cfg == 3 else "moe_layer_decode_tokens_per_s"
+        unit, value, hib = "tokens/s", tps, True
+        workload = (f"BASELINE configs[{cfg}]: MoE layer {'prefill' if cfg == 3 else 'decode'}, M={M}, "
+                    "384+1 MXFP4 experts 7168/2048, top-8")
     line = {
-        "impl": "reference", "metric": "moe_layer_decode_tokens_per_s", "value": value,
-        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * M / value if value else None, "higher_is_better": True,
+        "impl": "reference", "metric": metric, "value": value,
+        "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * M / tps if tps else None, "higher_is_better": hib,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"BASELINE configs[2]: MoE layer decode, M={M}, 384+1 MXFP4 experts "
-                               "7168/2048, top-8", "tokens": M},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+        "config": {"workload": workload, "tokens": M, "samples": n_s},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
                          "sample": sample},
-        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t0,
     }
     print(json.dumps(line))
@@ -557,6 +572,154 @@ def run_b200(args, rank, world, local):
     print(json.dumps(line))
 
 
+def run_prefill(args, rank, world, local):
+    """one MoE layer at prefill, T = 4096 tokens per GPU (x bf16,
+    top-8 of 384 + shared), the whole layer in one library call (router GEMM, grouped
+    block-scaled GEMMs); at N > 1 the experts are sharded (all_gather dispatch,
+    reduce_scatter combine)."""
+    import torch
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+
+    torch.cuda.set_device(local)
+    T = args.tokens if args.tokens != 8 else 4096
+    K, W = args.steps, args.warmup
+    R = 4                                                   # distinct token batches (> L2 together)
+    lay = synthetic.baseline_layer(seed=args.seed, E=args.experts, H=H, I=I_, top_k=TOPK, scale=SCALE)
+    if world > 1:
+        from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
+        moe = ExpertParallelMoE(lay.cfg, 0, {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias},
+                                lay.source)
+    else:
+        moe = lay.moe()
+        _ = moe.pool
+    xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, T, H) for i in range(R)]
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        for i in range(2):
+            moe(xs[i])
+    torch.cuda.synchronize()
+    graphs = []
+    try:
+        for i in range(R):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                moe(xs[i])
+            graphs.append(g)
+        run = [g.replay for g in graphs]
+        timing = f"CUDA graph per batch ({R} distinct batches replayed as a ring)"
+    except Exception as exc:                                # noqa: BLE001 -- report and time eagerly
+        torch.cuda.synchronize()
+        graphs = []
+        run = [(lambda x=x: moe(x)) for x in xs]
+        timing = f"eager launches ({R} batches as a ring; graph capture failed: {type(exc).__name__})"
+    barrier(world)
+    for i in range(W):
+        run[i % R]()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = ClockSampler(local)
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(K):
+        run[(W + i) % R]()
+    ev1.record()
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    barrier(world)
+    ms = dist_max(ev0.elapsed_time(ev1) / K, world)
+    value = world * T / (ms / 1e3)
+
+    # per-kernel device time (profiling events, outside the timed region)
+    n_prof = min(K, 10)
+    L.profile_enable(True)
+    L.profile_collect()
+    for i in range(n_prof):
+        moe(xs[i % R])
+    torch.cuda.synchronize()
+    prof = L.profile_collect()
+    L.profile_enable(False)
+    gu_ms, gu_n = prof["gateup"]
+    dn_ms, dn_n = prof["down"]
+    peak_hbm, peak_kind = measured_peaks()
+    E_loc = args.experts // world
+    proj = 7168 * 2048 // 2 + 7168 * 2048 // 32                 # bytes of one MXFP4 projection
+    w_bytes = (E_loc + 1) * 3 * proj                           # every local expert is hit at T=4096
+    gu_bytes = (E_loc + 1) * 2 * proj
+    flops = 2.0 * world * T * (TOPK + 1) * 3 * H * I_ / world  # this rank's share (weak scaling)
+    gu_flops = flops * 2 / 3
+    gu_launch = gu_ms / max(gu_n, 1)
+    FP4_DENSE_NOMINAL = 9000.0                                  # TFLOP/s, B200 dense FP4 (datasheet)
+
+    # ---- end to end through the public API with host buffers
+    xh = torch.stack([x.cpu() for x in xs]).pin_memory()
+    yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
+    xd = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    for i in range(2):
+        xd.copy_(xh[i], non_blocking=True)
+        yh.copy_(moe(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = min(K, 20)
+    e0.record()
+    for i in range(n_e2e):
+        xd.copy_(xh[i % R], non_blocking=True)
+        yh.copy_(moe(xd), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = dist_max(e0.elapsed_time(e1) / n_e2e, world)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_baseline(T, args.seed, 1)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    for g in graphs:
+        g.reset()
+    if rank != 0:
+        return
+    line = {
+        "metric": "moe_layer_prefill_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1 weights x 4 e2m1 activation pieces, e8m0 block scales, f32 accumulate (tcgen05 kind::mxf4)",
+        "data": "synthetic (seeded random-init weights of the BASELINE layer)",
+        "config": {"workload": f"BASELINE configs[3]: one MoE layer prefill, T={T} tokens per GPU, "
+                               f"{args.experts} routed + 1 shared MXFP4 expert (7168/2048), bf16 router, top-8, x2.5",
+                   "tokens_per_gpu": T,
+                   "parallelism": "single GPU" if world == 1 else
+                                  f"ep{world}: {E_loc} routed experts per rank + replicated shared, "
+                                  "all_gather dispatch, reduce_scatter combine (NCCL)",
+                   "l2": f"inputs larger than L2: {w_bytes / 1e9:.2f} GB of expert weights per GPU and "
+                         f"{R} token batches of {T * H * 2 / 1e6:.0f} MB",
+                   "timing": timing + ", events around K steps"},
+        "layer_hbm_gbs": w_bytes / (ms / 1e3) / 1e9,
+        "layer_tflops_algorithmic": flops / (ms / 1e3) / 1e12,
+        "roofline": {"bound": "tensor", "kernel": "prefill_gemm_kernel<gate/up> (block-scaled grouped GEMM, tcgen05)",
+                     "achieved": gu_flops / (gu_launch / 1e3) / 1e12, "peak": FP4_DENSE_NOMINAL,
+                     "unit": "TFLOP/s", "frac": gu_flops / (gu_launch / 1e3) / 1e12 / FP4_DENSE_NOMINAL,
+                     "peak_kind": "nominal (dense FP4 datasheet; no measured FP4 peak on this pool)",
+                     "algorithmic_flops_per_launch": gu_flops,
+                     "tensor_instruction_flops_per_launch": 4 * gu_flops,
+                     "hbm_view": {"algorithmic_bytes_per_launch": gu_bytes,
+                                  "achieved_gbs": gu_bytes / (gu_launch / 1e3) / 1e9,
+                                  "peak_gbs": peak_hbm, "peak_kind": peak_kind},
+                     "traffic": None, "launch_ms": gu_launch},
+        "down_kernel": {"launch_ms": dn_ms / max(dn_n, 1),
+                        "achieved_tflops": flops / 3 / (dn_ms / max(dn_n, 1) / 1e3) / 1e12},
+        "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
+        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
+                "ms_per_step": e2e_ms, "api": "LatentMoE.__call__ (k3_moe_prefill)"},
+        "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args)
@@ -565,6 +728,8 @@ def main():
             run_reference(args, rank, world)
         elif args.config == 4:
             run_stream(args, rank, world, local)
+        elif args.config == 3:
+            run_prefill(args, rank, world, local)
         else:
             run_b200(args, rank, world, local)
     finally:

@@ -20,6 +20,7 @@
 #include "k3_tma.cuh"
 #include "k3_bs.cuh"
 #include "k3_pairs.cuh"
+#include "k3_prefill.cuh"
 #include "k3_route.cuh"
 
 namespace k3 {
@@ -1259,6 +1260,9 @@ using namespace k3;
 
 // ================================================================ C ABI
 
+// Above this many bf16 tokens the router logits run as a tensor-core GEMM.
+constexpr int64_t kRouteGemmMinTokens = 64;
+
 extern "C" K3_API size_t k3_moe_route_workspace(int64_t M, int64_t E) {
     return align_up(sizeof(float) * size_t(std::max<int64_t>(M, 1)) * size_t(std::max<int64_t>(E, 1)), 256) + 256;
 }
@@ -1282,11 +1286,18 @@ extern "C" K3_API int k3_moe_route(const void* x, int x_dtype, int64_t M, int64_
     int* status = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + need - 256);
     const size_t esz = x_dtype == K3_BF16 ? 2 : 4;
     if (int rc = cuda_check(cudaMemsetAsync(status, 0, sizeof(int), s), "cudaMemsetAsync")) return rc;
-    for (int64_t m0 = 0; m0 < M; m0 += kMaxTok) {
-        const int Mc = int(std::min<int64_t>(kMaxTok, M - m0));
-        if (int rc = launch_router_logits(static_cast<const uint8_t*>(x) + size_t(m0) * H * esz,
-                                          x_dtype, Mc, H, gate_w_bf16, E, logits + m0 * E, s))
-            return rc;
+    if (M > kRouteGemmMinTokens && router_gemm_ok(x_dtype, H, x, gate_w_bf16)) {
+        prof_begin(K3_PROF_ROUTER, s);
+        const int rc = launch_router_gemm(x, M, H, gate_w_bf16, E, logits, status, s);
+        prof_end(K3_PROF_ROUTER, s);
+        if (rc) return rc;
+    } else {
+        for (int64_t m0 = 0; m0 < M; m0 += kMaxTok) {
+            const int Mc = int(std::min<int64_t>(kMaxTok, M - m0));
+            if (int rc = launch_router_logits(static_cast<const uint8_t*>(x) + size_t(m0) * H * esz,
+                                              x_dtype, Mc, H, gate_w_bf16, E, logits + m0 * E, s))
+                return rc;
+        }
     }
     prof_begin(K3_PROF_TOPK, s);
     topk_kernel<<<int((M + 7) / 8), 256, 0, s>>>(logits, int(M), int(E), bias, top_k, renormalize,

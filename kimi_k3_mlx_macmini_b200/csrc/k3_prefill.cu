@@ -28,6 +28,9 @@ int launch_router_logits_rows(const void* x, int xdt, int64_t M, int64_t H, cons
                               int64_t E, float* logits, cudaStream_t s);
 int launch_topk_rows(const float* logits, int64_t M, int64_t E, const float* bias, int k, int renorm,
                      float scale, int32_t* idx, float* w, int* status, cudaStream_t s);
+bool router_gemm_ok(int xdt, int64_t H, const void* x, const void* gate_w);
+int launch_router_gemm(const void* x, int64_t T, int64_t H, const uint16_t* gate_w, int64_t E, float* logits,
+                       int* status, cudaStream_t s);
 
 namespace {
 
@@ -995,32 +998,11 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
 
 int prefill_route(const k3_moe_params* p, const void* x, int xdt, int64_t T, const uint16_t* gate_w,
                   const float* bias, int32_t* idx, float* w, uint8_t* ws, const PrefillLayout& L, cudaStream_t s) {
-    if (int rc = configure_prefill()) return rc;
     float* logits = reinterpret_cast<float*>(ws + L.logits);
     int* status = &reinterpret_cast<PrefillHeader*>(ws + L.hdr)->status;
     prof_begin(K3_PROF_ROUTER, s);
-    if (xdt == K3_BF16 && L.H % 64 == 0 && (reinterpret_cast<uintptr_t>(gate_w) & 15) == 0) {
-        CUtensorMap wmap, xmap;
-        {
-            const uint64_t d[2] = {uint64_t(L.H), uint64_t(L.E)};
-            const uint64_t st[1] = {uint64_t(L.H) * 2};
-            const uint32_t b[2] = {64, uint32_t(kBRows)};
-            if (int rc = encode_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gate_w, d, st, b,
-                                    CU_TENSOR_MAP_SWIZZLE_128B))
-                return rc;
-        }
-        {
-            const uint64_t d[2] = {uint64_t(L.H), uint64_t(T)};
-            const uint64_t st[1] = {uint64_t(L.H) * 2};
-            const uint32_t b[2] = {64, uint32_t(kRGN)};
-            if (int rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, d, st, b,
-                                    CU_TENSOR_MAP_SWIZZLE_128B))
-                return rc;
-        }
-        const dim3 grid(unsigned((L.E + kBRows - 1) / kBRows), unsigned((T + kRGN - 1) / kRGN));
-        router_gemm_kernel<<<grid, kRGThreads, rg_smem_bytes(), s>>>(wmap, xmap, int(T), int(L.E), L.H, logits,
-                                                                       status);
-        K3_CHECK_LAUNCH("router_gemm_kernel");
+    if (router_gemm_ok(xdt, L.H, x, gate_w)) {
+        if (int rc = launch_router_gemm(x, T, L.H, gate_w, L.E, logits, status, s)) return rc;
     } else {
         if (int rc = launch_router_logits_rows(x, xdt, T, L.H, gate_w, L.E, logits, s)) return rc;
     }
@@ -1037,6 +1019,37 @@ int64_t routed_candidates(const k3_moe_params& p, int64_t T) {
 }
 
 }  // namespace
+
+bool router_gemm_ok(int xdt, int64_t H, const void* x, const void* gate_w) {
+    return xdt == K3_BF16 && H % 64 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(gate_w) & 15) == 0;
+}
+
+int launch_router_gemm(const void* x, int64_t T, int64_t H, const uint16_t* gate_w, int64_t E, float* logits,
+                       int* status, cudaStream_t s) {
+    if (int rc = configure_prefill()) return rc;
+    CUtensorMap wmap, xmap;
+    {
+        const uint64_t d[2] = {uint64_t(H), uint64_t(E)};
+        const uint64_t st[1] = {uint64_t(H) * 2};
+        const uint32_t b[2] = {64, uint32_t(kBRows)};
+        if (int rc = encode_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gate_w, d, st, b,
+                                CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+    }
+    {
+        const uint64_t d[2] = {uint64_t(H), uint64_t(T)};
+        const uint64_t st[1] = {uint64_t(H) * 2};
+        const uint32_t b[2] = {64, uint32_t(kRGN)};
+        if (int rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, d, st, b, CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+    }
+    const dim3 grid(unsigned((E + kBRows - 1) / kBRows), unsigned((T + kRGN - 1) / kRGN));
+    router_gemm_kernel<<<grid, kRGThreads, rg_smem_bytes(), s>>>(wmap, xmap, int(T), int(E), H, logits, status);
+    K3_CHECK_LAUNCH("router_gemm_kernel");
+    return K3_OK;
+}
+
 }  // namespace k3
 
 using namespace k3;

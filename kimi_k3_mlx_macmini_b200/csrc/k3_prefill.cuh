@@ -130,4 +130,10 @@ struct PArgs {
     float* y;
 };
 
+// Router logits [T][E] of bf16 x on the tensor cores (tcgen05 kind::f16, fp32
+// accumulation of the exact bf16 products); router_gemm_ok tells whether it applies.
+bool router_gemm_ok(int xdt, int64_t H, const void* x, const void* gate_w);
+int launch_router_gemm(const void* x, int64_t T, int64_t H, const uint16_t* gate_w, int64_t E, float* logits,
+                       int* status, cudaStream_t s);
+
 }  // namespace k3

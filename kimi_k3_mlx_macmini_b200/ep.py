@@ -12,6 +12,9 @@ shared expert; the router is replicated. Every rank brings M tokens. A step:
    f32 partial row per gathered token (zero for tokens that touch none of its experts);
 4. combine: ``reduce_scatter`` (sum) returns to each rank the total of its own M rows.
 
+At prefill (thousands of tokens per rank) the same steps run with the local expert
+computation on the grouped-GEMM kernels (``k3_moe_pairs_prefill``).
+
 All transfers have fixed sizes, so a step captures into one CUDA graph with its NCCL
 collectives. Compared with W replicas of the whole layer, each rank streams only the
 experts its share is routed to by all W*M tokens, once.
@@ -30,6 +33,8 @@ import torch.distributed as dist
 
 from . import _lib as L
 from .moe import SHARED, ExpertPool, LatentMoE
+
+PAIRS_DECODE_MAX = 1024      # candidates one k3_moe_pairs_decode call takes
 
 RouteFn = Callable[[torch.Tensor], Tuple[torch.Tensor, torch.Tensor]]
 LocalFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
@@ -140,12 +145,22 @@ class ExpertParallelMoE:
 
     def _local(self, x_all: torch.Tensor, slot: torch.Tensor, tok: torch.Tensor,
                w: torch.Tensor) -> torch.Tensor:
+        """This rank's experts over the candidate pairs: the decode kernels for up to
+        ``PAIRS_DECODE_MAX`` candidates, the grouped-GEMM prefill kernels beyond."""
         lib = L.load_library()
         T, H = x_all.shape
+        n = slot.numel()
         y = torch.empty((T, H), dtype=torch.float32, device=x_all.device)
-        ws = L.workspace(x_all.device, lib.k3_moe_pairs_workspace(self.params, T, slot.numel()))
+        if n > PAIRS_DECODE_MAX:
+            ws = L.workspace(x_all.device, lib.k3_moe_pairs_prefill_workspace(self.params, T, n))
+            L.check(lib.k3_moe_pairs_prefill(self.params, x_all.data_ptr(), L.dtype_code(x_all), T,
+                                             slot.data_ptr(), tok.data_ptr(), w.data_ptr(), n,
+                                             y.data_ptr(), L.K3_F32, ws.data_ptr(), ws.numel(),
+                                             L.stream_of(x_all)), "k3_moe_pairs_prefill")
+            return y
+        ws = L.workspace(x_all.device, lib.k3_moe_pairs_workspace(self.params, T, n))
         L.check(lib.k3_moe_pairs_decode(self.params, x_all.data_ptr(), L.dtype_code(x_all), T,
-                                        slot.data_ptr(), tok.data_ptr(), w.data_ptr(), slot.numel(),
+                                        slot.data_ptr(), tok.data_ptr(), w.data_ptr(), n,
                                         y.data_ptr(), L.K3_F32, ws.data_ptr(), ws.numel(),
                                         L.stream_of(x_all)), "k3_moe_pairs_decode")
         return y
