@@ -33,14 +33,6 @@ __device__ __forceinline__ void epi_sync() {
     asm volatile("bar.sync 1, %0;\n" ::"n"(kBEpiWarps * 32) : "memory");
 }
 
-__device__ __forceinline__ float act_value(int kind, float g, float u, float beta, float lbeta) {
-    if (kind == K3_ACT_SITU) {
-        const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
-        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
-        return a * v;
-    }
-    return g / (1.0f + expf(-g)) * u;
-}
 
 __device__ __forceinline__ int64_t owner_of(int64_t i, int64_t n, int64_t g) {
     return ((i + 1) * g - 1) / n;

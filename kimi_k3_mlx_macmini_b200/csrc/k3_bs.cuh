@@ -102,6 +102,20 @@ int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batc
 int launch_tiles(const uint8_t* in, int64_t rows, int64_t cols, int64_t batch, uint8_t* out,
                  cudaStream_t s);
 
+// SwiGLU / situ activation of one (gate, up) pair (air_llm/models/kimi_k3/ops.py:17-28,
+// 42-43): sigmoid(g) = 1 / (1 + exp(-g)). exp's argument is clamped at 80 so the
+// denominator stays finite (below g = -80 sigmoid is under 2e-35 either way): a division
+// by infinity would send the whole warp down the division's slow path.
+__device__ __forceinline__ float act_value(int kind, float g, float u, float beta, float lbeta) {
+    const float den = 1.0f + expf(-fmaxf(g, -80.0f));
+    if (kind == K3_ACT_SITU) {
+        const float a = beta * tanhf(g / beta) / den;
+        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
+        return a * v;
+    }
+    return g / den * u;
+}
+
 // Max of a non-negative float over the warp (bit patterns of non-negative floats order
 // like unsigned integers).
 __device__ __forceinline__ float warp_max_nonneg(float v) {

@@ -282,12 +282,7 @@ struct GemvArgs {
 };
 
 __device__ __forceinline__ float apply_act(int kind, float g, float u, float beta, float lbeta) {
-    if (kind == K3_ACT_SITU) {
-        const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
-        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
-        return a * v;
-    }
-    return g / (1.0f + expf(-g)) * u;
+    return act_value(kind, g, u, beta, lbeta);
 }
 
 // GATEUP: gate+up items with the activation epilogue; otherwise plain projection items

@@ -36,20 +36,18 @@ namespace {
 
 // ------------------------------------------------------------------ primitives
 
-__device__ __forceinline__ void red_add_f32(float* p, float v) {
-    asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(p), "f"(v) : "memory");
+// Four consecutive floats reduce-added at once (16-byte aligned).
+__device__ __forceinline__ void red_add_v4(float* p, float4 v, uint64_t policy) {
+    asm volatile("red.global.add.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;\n" ::"l"(p), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w), "l"(policy)
+                 : "memory");
 }
-// Warp-wide: 8 consecutive 32-bit columns of this warp's 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
-    uint32_t r[8];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-        : "r"(taddr)
-        : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+// Barrier of the four epilogue warps (named barrier 1).
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, %0;\n" ::"n"(kPEpiWarps * 32) : "memory"); }
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
 }
 // Instruction descriptor of kind::f16: bf16 x bf16 -> fp32, M = 128, N = n, both K-major.
 __device__ __forceinline__ uint32_t bf16_idesc(int n) {
@@ -64,14 +62,6 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64
         : "memory");
 }
 
-__device__ __forceinline__ float act_value(int kind, float g, float u, float beta, float lbeta) {
-    if (kind == K3_ACT_SITU) {
-        const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
-        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
-        return a * v;
-    }
-    return g / (1.0f + expf(-g)) * u;
-}
 
 // ------------------------------------------------------------------ router GEMM
 
@@ -278,22 +268,35 @@ __device__ void block_exclusive_scan(const int* v, int n, int* out, int* s_warp)
     __syncthreads();
 }
 
-// One block: per-slot counts -> pair offsets, chunks (a slot's n pairs split into
-// ceil(n / kPN) chunks of near-equal size), the chunks' row prefix.
-__global__ void __launch_bounds__(1024) prefill_scan_kernel(const __grid_constant__ PrefillPlan P, int nblk, int NS,
+// One warp per slot: the per-block counts of the slot -> per-block bases (exclusive
+// scan over blocks); the slot's total count goes to cnt[s].
+__global__ void __launch_bounds__(256) prefill_blkscan_kernel(int* blk_cnt, int nblk, int NS, int* cnt) {
+    const int s = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (s >= NS) return;
+    int carry = 0;
+    for (int b0 = 0; b0 < nblk; b0 += 32) {
+        const int b = b0 + lane;
+        const int64_t o = int64_t(b) * NS + s;
+        const int v = b < nblk ? blk_cnt[o] : 0;
+        int x = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, d);
+            if (lane >= d) x += y;
+        }
+        if (b < nblk) blk_cnt[o] = carry + x - v;
+        carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+    if (lane == 0) cnt[s] = carry;
+}
+
+// One block: per-slot counts (in P.off) -> pair offsets, chunks (a slot's n pairs split
+// into ceil(n / kPN) chunks of near-equal size), the chunks' row prefix.
+__global__ void __launch_bounds__(1024) prefill_scan_kernel(const __grid_constant__ PrefillPlan P, int NS,
                                                             int nc_max) {
     __shared__ int s_cnt[kPMaxSlots + 1];
     __shared__ int s_warp[32];
-    for (int s = threadIdx.x; s < NS; s += blockDim.x) {
-        int run = 0;
-        for (int b = 0; b < nblk; ++b) {
-            const int64_t o = int64_t(b) * NS + s;
-            const int v = P.blk_cnt[o];
-            P.blk_cnt[o] = run;
-            run += v;
-        }
-        s_cnt[s] = run;
-    }
+    for (int s = threadIdx.x; s < NS; s += blockDim.x) s_cnt[s] = P.off[s];
     __syncthreads();
     block_exclusive_scan(s_cnt, NS, P.off, s_warp);              // P.off[s] = first pair of s
     for (int s = threadIdx.x; s < NS; s += blockDim.x) s_cnt[s] = (s_cnt[s] + kPN - 1) / kPN;
@@ -475,9 +478,10 @@ __global__ void __launch_bounds__(256) prefill_permute_kernel(const __grid_const
     for (int p = 0; p < kPPieces; ++p) {
         const int64_t row = int64_t(p) * T + tok;
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(xp + row * (K / 2) + 16 * u));
-        uint8_t* blk = img + img_block(P.ch_n8p, c, nst, s, p, n8);
-        *reinterpret_cast<uint4*>(blk + kPImgSf + j * 128 + ((q ^ (j & 7)) << 4)) = v;
-        blk[(q >> 2) * kBChunk + sf_chunk_offset(j, q & 3)] = __ldg(xsf + row * U + u);
+        uint8_t* blk = img + img_block(P.ch_n8p, c, nst, s, p / kPStack, n8);
+        const int r = (p % kPStack) * n8 + j;                      // row in the stacked block
+        *reinterpret_cast<uint4*>(blk + kPImgSf + r * 128 + ((q ^ (r & 7)) << 4)) = v;
+        blk[img_sf(r, q)] = __ldg(xsf + row * U + u);
     }
 }
 
@@ -513,25 +517,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 template <bool GATEUP>
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ PMaps maps, const __grid_constant__ PArgs a) {
+    constexpr int kPairs = kPPieces / kPStack;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     PASlot* aring = reinterpret_cast<PASlot*>(base);
     PBSlot* bring = reinterpret_cast<PBSlot*>(base + sizeof(PASlot) * kPASlots);
-    float* ebuf = reinterpret_cast<float*>(base + sizeof(PASlot) * kPASlots + sizeof(PBSlot) * kPBSlots);
-    uint64_t* afull = reinterpret_cast<uint64_t*>(ebuf + kPEpiBuf * kPEpiWarps);
+    uint64_t* afull = reinterpret_cast<uint64_t*>(base + sizeof(PASlot) * kPASlots + sizeof(PBSlot) * kPBSlots);
     uint64_t* aempty = afull + kPASlots;
     uint64_t* bfull = aempty + kPASlots;
     uint64_t* bempty = bfull + kPBSlots;
-    uint64_t* accf = bempty + kPBSlots;   // [2] accumulator ready (MMA -> epilogue)
-    uint64_t* acce = accf + 2;            // [2] accumulator drained (epilogue -> MMA)
-    uint64_t* drain = acce + 2;
+    uint64_t* accf = bempty + kPBSlots;   // accumulator ready (MMA -> epilogue)
+    uint64_t* acce = accf + 1;            // accumulator drained (epilogue -> MMA)
+    uint64_t* drain = acce + 1;
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_abort;
+    __shared__ volatile int s_efail;      // written by epilogue warps only, read after epi_bar()
     __shared__ volatile unsigned s_aiss, s_biss;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         s_abort = 0;
+        s_efail = 0;
         s_aiss = 0;
         s_biss = 0;
         for (int s = 0; s < kPASlots; ++s) {
@@ -542,10 +548,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
             mbar_init(&bfull[s], 1);
             mbar_init(&bempty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], kPEpiWarps);
-        }
+        mbar_init(accf, 1);
+        mbar_init(acce, kPEpiWarps);
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -614,17 +618,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
             for (int i = i0; i < n_items && ok && !s_abort; i += di) {
                 const int c = i / nrb;
                 const int n8 = (P.ch_n[c] + 7) & ~7;
-                const uint32_t bytes = uint32_t(kPImgSf + 128 * n8);
+                const uint32_t bytes = uint32_t(kPImgSf + 128 * kPStack * n8);
                 const uint8_t* cimg = a.img + img_block(P.ch_n8p, c, nst, 0, 0, n8);
                 for (int s = 0; s < nst && ok; ++s) {
-                    for (int p = 0; p < kPPieces; ++p, ++gb) {
+                    for (int pp = 0; pp < kPairs; ++pp, ++gb) {
                         const int si = int(gb % kPBSlots);
                         if (!mbar_wait(&bempty[si], ((gb / kPBSlots) & 1) ^ 1, a.status, &s_abort)) {
                             ok = false;
                             break;
                         }
                         mbar_expect_tx(&bfull[si], bytes);
-                        bulk_g2s(&bring[si].sfb[0], cimg + int64_t(s * kPPieces + p) * bytes, bytes, &bfull[si]);
+                        bulk_g2s(&bring[si].sfb[0], cimg + int64_t(s * kPairs + pp) * bytes, bytes, &bfull[si]);
                         s_biss = gb + 1;
                     }
                 }
@@ -635,17 +639,16 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // ------------------------------------------------------------ MMA issuer
         uint32_t ga = 0, gb = 0, ib = 0;
         bool ok = true;
+        const uint32_t d0 = tm, d1 = tm + kPAccCols;
         for (int i = i0; i < n_items && ok && !s_abort; i += di, ++ib) {
             const int c = i / nrb;
             const int n8 = (P.ch_n[c] + 7) & ~7;
-            const uint32_t buf = ib & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&acce[buf], ((ib >> 1) & 1) ^ 1, a.status, &s_abort))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(acce, (ib & 1) ^ 1, a.status, &s_abort))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t d0 = tm + 2 * buf * kPAccCols, d1 = d0 + kPAccCols;
-            const uint32_t idesc0 = mxf4_idesc(n8, 0), idesc2 = mxf4_idesc(n8, 2);
+            const uint32_t idesc0 = mxf4_idesc(kPStack * n8, 0), idesc2 = mxf4_idesc(kPStack * n8, 2);
             for (int s = 0; s < nst && ok; ++s, ++ga) {
                 const int sa = int(ga % kPASlots);
                 if (!__all_sync(0xffffffffu, mbar_wait(&afull[sa], (ga / kPASlots) & 1, a.status, &s_abort))) {
@@ -662,7 +665,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     tc_cp_sf(sfa + 12, sf_chunk_desc(&as.sfa[1][kBChunk]));
                 }
                 __syncwarp();
-                for (int p = 0; p < kPPieces; ++p, ++gb) {
+                for (int pp = 0; pp < kPairs; ++pp, ++gb) {
                     const int sb = int(gb % kPBSlots);
                     if (!__all_sync(0xffffffffu, mbar_wait(&bfull[sb], (gb / kPBSlots) & 1, a.status, &s_abort))) {
                         ok = false;
@@ -670,20 +673,23 @@ __global__ void __launch_bounds__(kPThreads, 1)
                     }
                     tc_fence_after();
                     const PBSlot& bs = bring[sb];
-                    const uint32_t sfb = tm + kPSfbCol + 8 * sb;
+                    const uint32_t sfb = tm + kPSfbCol + 16 * sb;   // [k-half][row set] x 4 columns
                     if (elect_one()) {
-                        tc_cp_sf(sfb + 0, sf_chunk_desc(&bs.sfb[0]));
-                        tc_cp_sf(sfb + 4, sf_chunk_desc(&bs.sfb[kBChunk]));
+#pragma unroll
+                        for (int h = 0; h < 2; ++h)
+#pragma unroll
+                            for (int rs = 0; rs < 2; ++rs)
+                                tc_cp_sf(sfb + 8 * h + 4 * rs, sf_chunk_desc(&bs.sfb[(2 * h + rs) * kBChunk]));
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
-                            const uint32_t id = 2 * (kk & 1), ch = 4 * (kk >> 1);
+                            const uint32_t id = 2 * (kk & 1), h = kk >> 1;
                             const uint32_t idesc = (kk & 1) ? idesc2 : idesc0;
-                            const uint32_t acc = (s > 0 || p > 0 || kk > 0) ? 1u : 0u;
+                            const uint32_t acc = (s > 0 || pp > 0 || kk > 0) ? 1u : 0u;
                             const uint64_t bd = sw128_desc(&bs.b[0][0], 32 * kk);
-                            mma_mxf4(d0, sw128_desc(&as.a[0][0][0], 32 * kk), bd, idesc, (sfa + ch) | (id << 30),
-                                     (sfb + ch) | (id << 30), acc);
+                            mma_mxf4(d0, sw128_desc(&as.a[0][0][0], 32 * kk), bd, idesc, (sfa + 4 * h) | (id << 30),
+                                     (sfb + 8 * h) | (id << 30), acc);
                             mma_mxf4(d1, sw128_desc(&as.a[1][0][0], 32 * kk), bd, idesc,
-                                     (sfa + 8 + ch) | (id << 30), (sfb + ch) | (id << 30), acc);
+                                     (sfa + 8 + 4 * h) | (id << 30), (sfb + 8 * h) | (id << 30), acc);
                         }
                         tc_commit(&bempty[sb]);
                     }
@@ -694,7 +700,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 __syncwarp();
             }
             if (!ok) break;
-            if (elect_one()) tc_commit(&accf[buf]);
+            if (elect_one()) tc_commit(accf);
             __syncwarp();
         }
         if (!ok || s_abort) {
@@ -714,78 +720,113 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // -------------------------------------------------------------- epilogue
         const int q = warp & 3;                               // TMEM lane quarter
         const uint32_t lane_addr = uint32_t(32 * q) << 16;
-        float* tb = ebuf + q * kPEpiBuf;
+        const uint32_t d0 = tm + lane_addr, d1 = d0 + kPAccCols;
+        const uint64_t keep = l2_evict_last();
+        float* const slab = a.slab + int64_t(blockIdx.x) * (kPN * 2 * kBRows);
         uint32_t ib = 0;
         for (int i = i0; i < n_items; i += di, ++ib) {
-            const uint32_t buf = ib & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&accf[buf], (ib >> 1) & 1, a.status, &s_abort))) {
-                s_abort = 1;
-                break;
+            const bool okw = __all_sync(0xffffffffu, mbar_wait(accf, ib & 1, a.status, &s_abort));
+            if (GATEUP) {
+                if (!okw) {
+                    s_abort = 1;
+                    break;
+                }
+            } else {
+                // the four warps share the slab: they agree on failing, and none drains
+                // into it before all have finished reading the previous item
+                if (!okw && lane == 0) s_efail = 1;
+                epi_bar();
+                if (s_efail) {
+                    s_abort = 1;
+                    break;
+                }
             }
             tc_fence_after();
             const int c = i / nrb, rb = i - (i / nrb) * nrb;
             const int n = P.ch_n[c], n8 = (n + 7) & ~7, p0 = P.ch_p0[c];
-            const uint32_t d0 = tm + lane_addr + 2 * buf * kPAccCols, d1 = d0 + kPAccCols;
             if (GATEUP) {
-                // act = phi(gate, up) * w for rows rb*128 + 32q + lane (one 32-block of the
-                // down phase's k) and 32 columns at a time; transposed through shared memory
-                // so that each thread splits one column's block into pieces
-                const int nst_dn = int(a.rows / kBStageK);
-                uint8_t* const blk0 = a.img_out + img_block(P.ch_n8p, c, nst_dn, rb >> 1, 0, n8);
-                const int64_t pstep = kPImgSf + 128 * n8;                 // next piece's block
-                const int unit = ((rb & 1) << 2) + q;                     // 16-byte unit of the row
+                // drain: gate and up of rows rb*128 + 32q + lane (the two stacked piece
+                // columns of a token added) -> the CTA's slab [token][gate|up][128 rows]
 #pragma unroll 1
                 for (int j0 = 0; j0 < n; j0 += 32) {
-                    float g[32], u[32];
-                    tmem_ld32(d0 + j0, g);
-                    tmem_ld32(d1 + j0, u);
+                    float va[32], vb[32];
+                    tmem_ld32(d0 + j0, va);
+                    tmem_ld32(d0 + n8 + j0, vb);
 #pragma unroll
-                    for (int cc = 0; cc < 32; ++cc) {
-                        const int j = j0 + cc;
-                        float v = 0.0f;
-                        if (j < n) v = act_value(a.act_kind, g[cc], u[cc], a.beta, a.lbeta) * P.pair_w[p0 + j];
-                        tb[cc * 33 + lane] = v;
-                    }
-                    __syncwarp();
+                    for (int cc = 0; cc < 32; ++cc)
+                        if (j0 + cc < n) slab[(j0 + cc) * 2 * kBRows + 32 * q + lane] = va[cc] + vb[cc];
+                    tmem_ld32(d1 + j0, va);
+                    tmem_ld32(d1 + n8 + j0, vb);
+#pragma unroll
+                    for (int cc = 0; cc < 32; ++cc)
+                        if (j0 + cc < n) slab[(j0 + cc) * 2 * kBRows + kBRows + 32 * q + lane] = va[cc] + vb[cc];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acce);             // the MMA may run the next item
+                // act = phi(gate, up) * w, one token per lane: its 32 rows (one 32-block of
+                // the down phase's k) split into pieces and written to the down image
+                const int nst_dn = int(a.rows / kBStageK);
+                const int unit = ((rb & 1) << 2) + q;                     // 16-byte unit of a row
+#pragma unroll 1
+                for (int j0 = 0; j0 < n; j0 += 32) {
                     const int j = j0 + lane;
                     if (j < n) {
+                        const float4* gp = reinterpret_cast<const float4*>(slab + j * 2 * kBRows + 32 * q);
+                        const float wt = P.pair_w[p0 + j];
                         float r[32];
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) r[e] = tb[lane * 33 + e];
+                        for (int e4 = 0; e4 < 8; ++e4) {
+                            const float4 g4 = gp[e4], u4 = gp[e4 + kBRows / 4];
+                            r[4 * e4 + 0] = act_value(a.act_kind, g4.x, u4.x, a.beta, a.lbeta) * wt;
+                            r[4 * e4 + 1] = act_value(a.act_kind, g4.y, u4.y, a.beta, a.lbeta) * wt;
+                            r[4 * e4 + 2] = act_value(a.act_kind, g4.z, u4.z, a.beta, a.lbeta) * wt;
+                            r[4 * e4 + 3] = act_value(a.act_kind, g4.w, u4.w, a.beta, a.lbeta) * wt;
+                        }
                         uint4 dv[kPPieces];
                         uint32_t sv[kPPieces];
                         split_block32<kPPieces>(r, dv, sv);
-                        uint8_t* row = blk0 + kPImgSf + j * 128 + ((unit ^ (j & 7)) << 4);
-                        uint8_t* sfp = blk0 + (rb & 1) * kBChunk + sf_chunk_offset(j, q);
 #pragma unroll
                         for (int p = 0; p < kPPieces; ++p) {
-                            *reinterpret_cast<uint4*>(row + p * pstep) = dv[p];
-                            sfp[p * pstep] = uint8_t(sv[p]);
+                            uint8_t* blk = a.img_out + img_block(P.ch_n8p, c, nst_dn, rb >> 1, p / kPStack, n8);
+                            const int row = (p % kPStack) * n8 + j;
+                            *reinterpret_cast<uint4*>(blk + kPImgSf + row * 128 + ((unit ^ (row & 7)) << 4)) = dv[p];
+                            blk[img_sf(row, unit)] = uint8_t(sv[p]);
                         }
                     }
-                    __syncwarp();
                 }
+                __syncwarp();
             } else {
+                // drain: both row blocks (stacked piece columns added) -> the slab
+                // [token][row block][128 rows]; then the reduce-adds into y run from the
+                // slab while the MMA computes the next item
+#pragma unroll 1
+                for (int j0 = 0; j0 < n; j0 += 32) {
+                    float va[32], vb[32];
+                    tmem_ld32(d0 + j0, va);
+                    tmem_ld32(d0 + n8 + j0, vb);
+#pragma unroll
+                    for (int cc = 0; cc < 32; ++cc)
+                        if (j0 + cc < n) slab[(j0 + cc) * 2 * kBRows + 32 * q + lane] = va[cc] + vb[cc];
+                    tmem_ld32(d1 + j0, va);
+                    tmem_ld32(d1 + n8 + j0, vb);
+#pragma unroll
+                    for (int cc = 0; cc < 32; ++cc)
+                        if (j0 + cc < n) slab[(j0 + cc) * 2 * kBRows + kBRows + 32 * q + lane] = va[cc] + vb[cc];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(acce);             // the MMA may run the next item
+                epi_bar();                                    // every warp's rows are in the slab
                 const int64_t H = a.rows;
 #pragma unroll 1
-                for (int j0 = 0; j0 < n8; j0 += 8) {
-                    float v0[8], v1[8];
-                    tmem_ld8(d0 + j0, v0);
-                    tmem_ld8(d1 + j0, v1);
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj) {
-                        const int j = j0 + jj;
-                        if (j < n) {
-                            float* yr = a.y + int64_t(P.pair_tok[p0 + j]) * H + rb * 2 * kBRows + 32 * q + lane;
-                            red_add_f32(yr, v0[jj]);
-                            red_add_f32(yr + kBRows, v1[jj]);
-                        }
-                    }
+                for (int j = q; j < n; j += kPEpiWarps) {     // token j: 256 rows, 8 per lane
+                    float* yr = a.y + int64_t(P.pair_tok[p0 + j]) * H + rb * 2 * kBRows + 4 * lane;
+                    const float4* sp = reinterpret_cast<const float4*>(slab + j * 2 * kBRows) + lane;
+                    red_add_v4(yr, sp[0], keep);
+                    red_add_v4(yr + kBRows, sp[kBRows / 4], keep);
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acce[buf]);
         }
     }
     tc_fence_before();
@@ -827,12 +868,14 @@ struct PrefillLayout {
     int64_t T, H, I, E, NS, n_cand, nc_max, nblk;
     int G;
     size_t hdr, logits, idx, w, blk, off, ch_first, pair_tok, pair_w, pair_cj, ch_slot, ch_p0, ch_n, ch_n8p;
-    size_t xp, xsf, img_gu, img_dn, y32, total;
+    size_t xp, xsf, img_gu, img_dn, slab, y32, total;
 };
 
-// Bytes of an image over nst k-steps: at most nc_max chunks and n_cand + 7 nc_max rows.
+// Bytes of an image over nst k-steps: at most nc_max chunks and n_cand + 7 nc_max rows
+// per piece.
 size_t img_bytes(int64_t nst, int64_t n_cand, int64_t nc_max) {
-    return size_t(kPPieces) * size_t(nst) * (size_t(kPImgSf) * nc_max + 128 * size_t(n_cand + 7 * nc_max));
+    return size_t(kPPieces / kPStack) * size_t(nst) *
+           (size_t(kPImgSf) * nc_max + 128 * kPStack * size_t(n_cand + 7 * nc_max));
 }
 
 PrefillLayout prefill_layout(const k3_moe_params& p, int64_t T, int64_t n_cand, int64_t num_slots, bool route) {
@@ -867,6 +910,7 @@ PrefillLayout prefill_layout(const k3_moe_params& p, int64_t T, int64_t n_cand, 
     L.xsf = carve_p(off, size_t(kPPieces) * T * (L.H / 32));
     L.img_gu = carve_p(off, img_bytes(L.H / kBStageK, n_cand, L.nc_max));
     L.img_dn = carve_p(off, img_bytes(L.I / kBStageK, n_cand, L.nc_max));
+    L.slab = carve_p(off, kPSlabBytes * size_t(L.G));
     L.y32 = carve_p(off, sizeof(float) * T * L.H);
     L.total = off;
     return L;
@@ -932,7 +976,9 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
     prof_begin(K3_PROF_TOPK, s);
     prefill_count_kernel<<<int(L.nblk), kPPlanBlock, mask_bytes, s>>>(cand, n_cand, P.blk_cnt);
     K3_CHECK_LAUNCH("prefill_count_kernel");
-    prefill_scan_kernel<<<1, 1024, 0, s>>>(P, int(L.nblk), NS, int(L.nc_max));
+    prefill_blkscan_kernel<<<(NS + 7) / 8, 256, 0, s>>>(P.blk_cnt, int(L.nblk), NS, P.off);
+    K3_CHECK_LAUNCH("prefill_blkscan_kernel");
+    prefill_scan_kernel<<<1, 1024, 0, s>>>(P, NS, int(L.nc_max));
     K3_CHECK_LAUNCH("prefill_scan_kernel");
     prefill_place_kernel<<<int(L.nblk), kPPlanBlock, mask_bytes, s>>>(cand, n_cand, P);
     K3_CHECK_LAUNCH("prefill_place_kernel");
@@ -960,6 +1006,7 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
     ga.routed_slots = int(p->num_experts);
     ga.img = ws + L.img_gu;
     ga.img_out = ws + L.img_dn;
+    ga.slab = reinterpret_cast<float*>(ws + L.slab);
     ga.act_kind = p->activation;
     ga.beta = p->situ_beta;
     ga.lbeta = p->situ_linear_beta;
@@ -979,6 +1026,7 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
     da.sf_slot = (L.H / 128) * (L.I / 128) * kBChunk;
     da.img = ws + L.img_dn;
     da.img_out = nullptr;
+    da.slab = ga.slab;                   // the gate/up launch is done with it (same stream)
     da.y = y32;
     PMaps mb{};
     if (int rc = tile_pool_map(&mb.a0, pl.w2_tiles, L.H, L.I, pl.num_slots)) return rc;

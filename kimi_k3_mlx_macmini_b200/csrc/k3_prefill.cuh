@@ -17,12 +17,17 @@
 // per (piece, 32-block); the pieces of one value accumulate into the same TMEM column
 // (one MMA per piece, accumulate on), so a chunk of n tokens takes n TMEM columns.
 //
-// Token operands live in "images": for every (chunk, 256-k step, piece) one contiguous
-// block holding the two 512-byte scale chunks of the block's rows followed by its n8 rows
+// Two pieces are stacked along N in one MMA (B rows [piece][token]); the two TMEM columns
+// of a token are added in the epilogue. A tcgen05 MMA costs about the same per
+// instruction for any N up to 256, so the stacking halves the tensor time; the price is
+// a single-buffered accumulator (2 x 208 columns), drained quickly by the epilogue.
+//
+// Token operands live in "images": for every (chunk, 256-k step, piece pair) one
+// contiguous block holding the scale chunks of the block's rows followed by its 2 n8 rows
 // of 128 packed bytes, already in the 128-byte-swizzled order the tensor core reads
-// (16-byte unit u of row j at position u ^ (j & 7)). One bulk copy moves a block into a
+// (16-byte unit u of row r at position u ^ (r & 7)). One bulk copy moves a block into a
 // shared-memory slot. The gate/up image is built from the token pieces by a permute
-// kernel; the down image is written directly by the gate/up epilogue.
+// kernel; the down image is written by the gate/up epilogue.
 #pragma once
 
 #include <cuda.h>
@@ -32,21 +37,24 @@
 namespace k3 {
 
 constexpr int kPPieces = 4;           // E2M1 pieces per activation value
-constexpr int kPN = 104;              // tokens per chunk (MMA N <= 104, a multiple of 8)
+constexpr int kPStack = 2;            // pieces stacked along N in one MMA (B rows = piece-major)
+constexpr int kPN = 104;              // tokens per chunk (MMA N = kPStack x rows <= 208)
 constexpr int kPASlots = 3;           // weight ring: two 128-row tiles x 256 k per slot
-constexpr int kPBSlots = 6;           // token ring: one image block per slot
+constexpr int kPBSlots = 3;           // token ring: one image block (two pieces) per slot
 constexpr int kPEpiWarps = 4;
 constexpr int kPThreads = (3 + kPEpiWarps) * 32;   // A producer, MMA, 4 epilogue, B producer
 constexpr int kPPlanBlock = 256;      // candidates per plan block
 constexpr int kPMaxSlots = kMaxExperts + 1;
-constexpr int kPImgSf = 2 * kBChunk;  // scale bytes at the head of an image block
+constexpr int kPImgSf = 4 * kBChunk;  // scale bytes at the head of an image block:
+                                      // [k-half h][row set (rows 0-127, 128-255)][512]
 
-// TMEM columns: two accumulator buffers x two accumulators x kPN, then the scale slots.
-constexpr int kPAccCols = kPN;
-constexpr int kPSfaCol = 4 * kPAccCols;             // kPASlots x 16 columns
-constexpr int kPSfbCol = kPSfaCol + 16 * kPASlots;  // kPBSlots x 8 columns
-static_assert(kPSfbCol + 8 * kPBSlots <= 512, "prefill TMEM plan exceeds 512 columns");
-static_assert(kPN % 8 == 0 && kPN <= 128, "chunk width must be a multiple of 8, <= 128");
+// TMEM columns: two accumulators of kPStack * kPN columns (single buffer), then the scale
+// slots (A: two tiles x two k-halves x 4 columns; B: two k-halves x two row sets x 4).
+constexpr int kPAccCols = kPStack * kPN;
+constexpr int kPSfaCol = 2 * kPAccCols;             // kPASlots x 16 columns
+constexpr int kPSfbCol = kPSfaCol + 16 * kPASlots;  // kPBSlots x 16 columns
+static_assert(kPSfbCol + 16 * kPBSlots <= 512, "prefill TMEM plan exceeds 512 columns");
+static_assert(kPN % 8 == 0 && kPStack * kPN <= 256, "MMA N must be a multiple of 8, <= 256");
 
 struct alignas(1024) PASlot {
     uint8_t a[2][kBRows][128];        // two weight tiles (gate + up, or two down row blocks), SW128
@@ -54,22 +62,27 @@ struct alignas(1024) PASlot {
 };
 struct alignas(1024) PBSlot {
     uint8_t sfb[kPImgSf];             // one image block: scale chunks, then
-    uint8_t b[kPN][128];              // the chunk's rows of one piece (256 k), SW128
+    uint8_t b[kPStack * kPN][128];    // rows [piece][token] of two pieces (256 k), SW128
 };
-// Gate/up epilogue: per warp a 32 x 32 fp32 transpose buffer (row stride 33).
-constexpr int kPEpiBuf = 32 * 33;
 constexpr size_t psmem_bytes() {
-    return sizeof(PASlot) * kPASlots + sizeof(PBSlot) * kPBSlots + sizeof(float) * kPEpiBuf * kPEpiWarps +
-           1024 /*align*/ + 256 /*barriers*/;
+    return sizeof(PASlot) * kPASlots + sizeof(PBSlot) * kPBSlots + 1024 /*align*/ + 256 /*barriers*/;
 }
 static_assert(psmem_bytes() + 2048 <= 227 * 1024, "prefill ring exceeds shared memory");
+// Gate/up epilogue staging per CTA: [token][gate | up][128 rows] fp32.
+constexpr size_t kPSlabBytes = sizeof(float) * kPN * 2 * kBRows;
 
-// Byte offset of the image block (chunk c, k-step s, piece p): blocks are ordered
-// [chunk][step][piece], a block of a chunk with n8 rows holds kPImgSf + 128 n8 bytes, and
-// n8p[c] = sum of n8 over the chunks before c.
-__host__ __device__ __forceinline__ int64_t img_block(const int* n8p, int c, int nst, int s, int p, int n8) {
-    return int64_t(kPPieces) * nst * (int64_t(kPImgSf) * c + 128 * int64_t(n8p[c])) +
-           int64_t(s * kPPieces + p) * (kPImgSf + 128 * n8);
+// Byte offset of the image block (chunk c, k-step s, piece pair pp): blocks are ordered
+// [chunk][step][pair], a block of a chunk with n8 rows per piece holds kPImgSf +
+// 128 * kPStack * n8 bytes, and n8p[c] = sum of n8 over the chunks before c. Row r of a
+// block is (piece pp*kPStack + r / n8, token r % n8).
+__host__ __device__ __forceinline__ int64_t img_block(const int* n8p, int c, int nst, int s, int pp, int n8) {
+    constexpr int kPairs = kPPieces / kPStack;
+    return int64_t(kPairs) * nst * (int64_t(kPImgSf) * c + 128 * kPStack * int64_t(n8p[c])) +
+           int64_t(s * kPairs + pp) * (kPImgSf + 128 * kPStack * n8);
+}
+// Offset inside a block of the scale byte of (row r, k-block j of the block's 256 k).
+__host__ __device__ __forceinline__ int img_sf(int r, int j) {
+    return (j >> 2) * 2 * kBChunk + (r >> 7) * kBChunk + sf_chunk_offset(r & 127, j & 3);
 }
 
 // Device-side routing plan of one prefill call (all arrays in the workspace).
@@ -122,8 +135,9 @@ struct PArgs {
     int64_t sf_slot;         // bytes per slot of a scale-chunk pool
     int routed_slots;        // slots below this stream with an evict-first L2 policy
     const uint8_t* img;      // B image of this phase
-    // gate/up epilogue -> the down phase's image
+    // gate/up epilogue -> the down phase's image, through a per-CTA staging slab
     uint8_t* img_out;
+    float* slab;
     int act_kind;
     float beta, lbeta;
     // down epilogue: y [T][H] fp32 (reduce-add)

@@ -15,6 +15,7 @@
 #include <string>
 
 #include "k3_async.cuh"
+#include "k3_bs.cuh"
 #include "k3_tma.cuh"
 
 namespace k3 {
@@ -62,12 +63,7 @@ __device__ __forceinline__ void consumer_sync() {
 }
 
 __device__ __forceinline__ float act_fn(int kind, float g, float u, float beta, float lbeta) {
-    if (kind == K3_ACT_SITU) {
-        const float a = beta * tanhf(g / beta) * (1.0f / (1.0f + expf(-g)));
-        const float v = lbeta > 0.0f ? lbeta * tanhf(u / lbeta) : u;
-        return a * v;
-    }
-    return g / (1.0f + expf(-g)) * u;
+    return act_value(kind, g, u, beta, lbeta);
 }
 
 // ---------------------------------------------------------------------- kernel
