@@ -10,10 +10,15 @@ expert + weighted scatter-add).
 
     python bench.py [--gpus N --steps K --warmup W --tokens M] [--impl reference]
 
+    python bench.py --config 3 ...      # configs[3]: prefill, T = 4096 tokens per GPU
+    python bench.py --config 4 ...      # configs[4]: experts streamed from pinned host memory
+
 Timing: ``value`` replays CUDA graphs (one per token batch, a ring of up to 64 distinct
 batches) with inputs resident in HBM, bracketed by CUDA events; consecutive steps use
 different token batches so each reads a different set of experts out of a 9 GB pool
-(inputs larger than L2). ``e2e`` times the public API call on pinned host tensors with
+(inputs larger than L2). With several GPUs the step holds NCCL collectives: an eager ring
+and one graph over a static input buffer are both timed and the faster is reported
+(``config.timing`` names it). ``e2e`` times the public API call on pinned host tensors with
 the host->device copy of x and the device->host copy of y inside the timed region.
 ``roofline`` covers the dominant kernel (the block-scaled gate/up grouped matvec), timed
 per launch with CUDA events on its launch stream in a second pass. SM clocks and
@@ -446,43 +451,10 @@ def run_b200(args, rank, world, local):
     torch.cuda.synchronize()
     step_x = [(W + i) % R for i in range(K)]                # batch of timed step i
 
-    # ---- device-resident timing: one CUDA graph per token batch, replayed as a ring
-    cap = torch.cuda.Stream()
-    with torch.cuda.stream(cap):
-        for i in range(2):
-            moe(xs[i])
-    torch.cuda.synchronize()
-    graphs, ys = [], []
-    try:
-        for i in range(R):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
-                ys.append(moe(xs[i]))
-            graphs.append(g)
-        run = [g.replay for g in graphs]
-        timing = f"CUDA graph per batch ({R} distinct batches replayed as a ring)"
-    except Exception as exc:                                # noqa: BLE001 -- report and time eagerly
-        torch.cuda.synchronize()
-        graphs = []
-        run = [(lambda x=x: moe(x)) for x in xs]
-        timing = f"eager launches ({R} distinct batches as a ring; graph capture failed: {type(exc).__name__})"
+    # ---- device-resident timing
+    graphs, modes = step_modes(moe, xs, R, world)
     barrier(world)
-    for i in range(W):
-        run[i % R]()
-    torch.cuda.synchronize()
-    barrier(world)
-    clk = ClockSampler(local)
-    time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    ev0.record()
-    for i in range(K):
-        run[step_x[i]]()
-    ev1.record()
-    torch.cuda.synchronize()
-    clocks = clk.stop()
-    barrier(world)
-    ms = dist_max(ev0.elapsed_time(ev1) / K, world)
+    ms, timing, clocks = time_modes(modes, step_x, K, W, R, world, local)
     value = world * M / (ms / 1e3)
 
     # ---- per-kernel timing of the same batches (eager launches, events per kernel)
@@ -572,6 +544,75 @@ def run_b200(args, rank, world, local):
     print(json.dumps(line))
 
 
+def step_modes(moe, xs, R, world):
+    """Callables per token batch to time. One GPU: one CUDA graph per batch (a ring of R
+    graphs). Several GPUs (NCCL collectives in the step): an eager ring and one graph
+    over a static input buffer refilled by a device copy before each replay -- replaying
+    many graphs that each hold collectives is slower than launching eagerly."""
+    import torch
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        for i in range(min(2, R)):
+            moe(xs[i])
+    torch.cuda.synchronize()
+    graphs, modes = [], []
+    if world == 1:
+        try:
+            for i in range(R):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    moe(xs[i])
+                graphs.append(g)
+            modes.append((f"CUDA graph per batch ({R} distinct batches replayed as a ring)",
+                          [g.replay for g in graphs]))
+        except Exception as exc:                            # noqa: BLE001 -- report and time eagerly
+            torch.cuda.synchronize()
+            graphs = []
+            modes.append((f"eager launches ({R} distinct batches as a ring; graph capture failed: "
+                          f"{type(exc).__name__})", [(lambda x=x: moe(x)) for x in xs]))
+    else:
+        modes.append((f"eager launches ({R} distinct batches as a ring)", [(lambda x=x: moe(x)) for x in xs]))
+        xin = xs[0].clone()
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                moe(xin)
+            graphs.append(g)
+            modes.append((f"one CUDA graph over a static input ({R} distinct batches copied in as a ring)",
+                          [(lambda x=x: (xin.copy_(x, non_blocking=True), g.replay())) for x in xs]))
+        except Exception:                                   # noqa: BLE001 -- the eager mode stands
+            torch.cuda.synchronize()
+    return graphs, modes
+
+
+def time_modes(modes, steps, K, W, R, world, local):
+    """Times K steps of every mode (W warm-up steps each; events bracketed by barriers and
+    synchronisation; max over ranks); returns (ms per step, mode name, clocks) of the
+    fastest."""
+    import torch
+    best = None
+    for name, run in modes:
+        for i in range(W):
+            run[i % R]()
+        torch.cuda.synchronize()
+        barrier(world)
+        clk = ClockSampler(local)
+        time.sleep(0.3)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record()
+        for i in range(K):
+            run[steps[i]]()
+        ev1.record()
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        barrier(world)
+        ms = dist_max(ev0.elapsed_time(ev1) / K, world)
+        if best is None or ms < best[0]:
+            best = (ms, name, clocks)
+    return best
+
+
 def run_prefill(args, rank, world, local):
     """one MoE layer at prefill, T = 4096 tokens per GPU (x bf16,
     top-8 of 384 + shared), the whole layer in one library call (router GEMM, grouped
@@ -594,41 +635,9 @@ def run_prefill(args, rank, world, local):
         moe = lay.moe()
         _ = moe.pool
     xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, T, H) for i in range(R)]
-    cap = torch.cuda.Stream()
-    with torch.cuda.stream(cap):
-        for i in range(2):
-            moe(xs[i])
-    torch.cuda.synchronize()
-    graphs = []
-    try:
-        for i in range(R):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
-                moe(xs[i])
-            graphs.append(g)
-        run = [g.replay for g in graphs]
-        timing = f"CUDA graph per batch ({R} distinct batches replayed as a ring)"
-    except Exception as exc:                                # noqa: BLE001 -- report and time eagerly
-        torch.cuda.synchronize()
-        graphs = []
-        run = [(lambda x=x: moe(x)) for x in xs]
-        timing = f"eager launches ({R} batches as a ring; graph capture failed: {type(exc).__name__})"
+    graphs, modes = step_modes(moe, xs, R, world)
     barrier(world)
-    for i in range(W):
-        run[i % R]()
-    torch.cuda.synchronize()
-    barrier(world)
-    clk = ClockSampler(local)
-    time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for i in range(K):
-        run[(W + i) % R]()
-    ev1.record()
-    torch.cuda.synchronize()
-    clocks = clk.stop()
-    barrier(world)
-    ms = dist_max(ev0.elapsed_time(ev1) / K, world)
+    ms, timing, clocks = time_modes(modes, [(W + i) % R for i in range(K)], K, W, R, world, local)
     value = world * T / (ms / 1e3)
 
     # per-kernel device time (profiling events, outside the timed region)

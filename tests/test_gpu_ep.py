@@ -1,6 +1,7 @@
 """Expert-parallel local computation on the GPU: ``k3_moe_pairs_decode`` against the C
 oracle (more than 8 tokens in one call, an expert split into several 8-pair items,
-skipped candidates), and the full expert-parallel layer on 2 GPUs when the box has them."""
+skipped candidates), and the full expert-parallel layer (decode and prefill) on up to 4
+GPUs when the box has them."""
 import os
 import socket
 
@@ -69,7 +70,7 @@ def test_pairs_decode_matches_oracle(k3):
     assert np.all(got[untouched] == 0)
 
 
-def _ep_worker(rank, world, port, q):
+def _ep_worker(rank, world, port, q, T=6):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -82,7 +83,7 @@ def _ep_worker(rank, world, port, q):
         lay = _small_layer(seed=9, top_k=4)
         w = {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias}
         ep = ExpertParallelMoE(lay.cfg, 0, w, lay.source)
-        x = synthetic.tokens(500 + rank, 6, H)
+        x = synthetic.tokens(500 + rank, T, H)
         y = ep(x)
         ref = lay.moe()(x)                    # the whole layer on this GPU
         q.put((rank, O.rel_l2(y.cpu().numpy(), ref.float().cpu().numpy())))
@@ -90,20 +91,36 @@ def _ep_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_expert_parallel_two_gpus():
+def _run_ep(world, T):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, q, T)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, err in res.items():
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_decode():
+    """Every GPU of the box (up to 4) as one expert-parallel layer, 6 tokens per rank."""
+    world = min(4, torch.cuda.device_count())
+    for rank, err in _run_ep(world, 6).items():
+        assert err < 1e-5, (rank, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_expert_parallel_prefill():
+    """300 tokens per rank: the local experts run on the prefill kernels
+    (k3_moe_pairs_prefill); the single-GPU reference runs the prefill path too, so the
+    two agree to the unordered fp32 adds into y."""
+    world = min(4, torch.cuda.device_count())
+    for rank, err in _run_ep(world, 300).items():
         assert err < 1e-5, (rank, err)
