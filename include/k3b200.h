@@ -282,6 +282,20 @@ K3_API int k3_moe_pairs_prefill(const k3_moe_params* p, const void* x, int x_dty
                                 const float* pair_w, int64_t n_pairs, void* y_out, int y_dtype,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Local expert computation of one expert-parallel rank, straight from the gathered
+ * routing (no candidate arrays): x [T][H] holds every rank's tokens, idx/w the routing of
+ * each token row (top_k entries per row, rows route_stride elements apart). This rank's
+ * pool holds routed experts [expert_lo, expert_lo + num_experts) in slots 0.. and, with
+ * has_shared, the shared expert in slot num_experts, applied to token rows
+ * [shared_t0, shared_t0 + shared_n) with weight 1. y_out[t] = sum over t's local experts
+ * of w * expert(x[t]) (+ shared), rows with none are zero. Up to 1024 candidates
+ * (T * top_k + shared_n) run on the decode kernels, more on the prefill kernels. */
+K3_API size_t k3_moe_ep_local_workspace(const k3_moe_params* p, int64_t T, int64_t shared_n);
+K3_API int k3_moe_ep_local(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                           const int32_t* idx, const float* w, int64_t route_stride, int32_t expert_lo,
+                           int32_t shared_t0, int32_t shared_n, void* y_out, int y_dtype,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* Device status word of the last prefill call on `workspace` (synchronises `stream`):
  * K3_OK, or K3_ERR_TIMEOUT when a kernel's bounded wait gave up. */
 K3_API int k3_moe_prefill_status(const void* workspace, void* stream);

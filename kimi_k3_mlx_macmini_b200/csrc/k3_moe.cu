@@ -1400,10 +1400,47 @@ DecodeLayout pairs_layout(const k3_moe_params& p, int64_t T, int64_t n_in, int s
 
 }  // namespace k3
 
+namespace k3 {
+
+size_t pairs_decode_workspace(const k3_moe_params& p, int64_t T, int64_t n_in) {
+    return pairs_layout(p, T, n_in, num_sms()).total;
+}
+
+// The decode kernels over the candidates of `cand` (explicit pairs or a routing result,
+// cand.n_in of them): plan, x pieces, gate/up, down, ordered combine.
+int pairs_decode_run(const k3_moe_params* p, const void* x, int x_dtype, int64_t T, const PairsArgs& cand,
+                     void* y_out, int y_dtype, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+    if (cand.n_in < 1 || cand.n_in > kMaxPairCandidates)
+        return fail(K3_ERR_UNSUPPORTED, "pairs decode: 1..1024 candidate pairs");
+    if (!p->pool || !pool_bs(*p))
+        return fail(K3_ERR_UNSUPPORTED, "pairs decode needs a block-scaled expert pool "
+                                        "(re-laid scales and tiles; H, I multiples of 512)");
+    const int sms = num_sms();
+    const DecodeLayout L = pairs_layout(*p, T, cand.n_in, sms);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
+    if (int rc = configure_smem()) return rc;
+    PairsArgs pa = cand;
+    pa.num_slots = int(p->pool->num_slots);
+    pa.T = int(T);
+    pa.plan = reinterpret_cast<Plan*>(ws + L.plan);
+    pa.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
+    pa.n_cntA = L.U * (L.I / kBRows);
+    pa.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
+    pa.n_cntB = L.U * (L.H / kBRows);
+    prof_begin(K3_PROF_TOPK, s);
+    if (int rc = launch_plan_from_pairs(pa, s)) return rc;
+    if (int rc = launch_convert_tokens(x, x_dtype, T, L.H, ws + L.xq_hi, ws + L.xq_ts, s)) return rc;
+    prof_end(K3_PROF_TOPK, s);
+    return decode_bs(p, L, ws, int(T), y_out, y_dtype, sms, s);
+}
+
+}  // namespace k3
+
 extern "C" K3_API size_t k3_moe_pairs_workspace(const k3_moe_params* p, int64_t T, int64_t n_pairs) {
     using namespace k3;
     if (!p || T < 1 || n_pairs < 1) return 0;
-    return pairs_layout(*p, T, n_pairs, num_sms()).total;
+    return pairs_decode_workspace(*p, T, n_pairs);
 }
 
 extern "C" K3_API int k3_moe_pairs_decode(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
@@ -1419,30 +1456,11 @@ extern "C" K3_API int k3_moe_pairs_decode(const k3_moe_params* p, const void* x,
     if (T < 1) return fail(K3_ERR_INVALID, "k3_moe_pairs_decode: T must be >= 1");
     if (n_pairs < 1 || n_pairs > kMaxPairCandidates)
         return fail(K3_ERR_UNSUPPORTED, "k3_moe_pairs_decode: 1..1024 candidate pairs");
-    if (!p->pool || !pool_bs(*p))
-        return fail(K3_ERR_UNSUPPORTED, "k3_moe_pairs_decode needs a block-scaled expert pool "
-                                        "(re-laid scales and tiles; H, I multiples of 512)");
-    const int sms = num_sms();
-    const DecodeLayout L = pairs_layout(*p, T, n_pairs, sms);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
-    if (int rc = configure_smem()) return rc;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    PairsArgs pa{};
-    pa.slot = pair_slot;
-    pa.tok = pair_tok;
-    pa.w = pair_w;
-    pa.n_in = int(n_pairs);
-    pa.num_slots = int(p->pool->num_slots);
-    pa.T = int(T);
-    pa.plan = reinterpret_cast<Plan*>(ws + L.plan);
-    pa.cntA = reinterpret_cast<unsigned*>(ws + L.cntA);
-    pa.n_cntA = L.U * (L.I / kBRows);
-    pa.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
-    pa.n_cntB = L.U * (L.H / kBRows);
-    prof_begin(K3_PROF_TOPK, s);
-    if (int rc = launch_plan_from_pairs(pa, s)) return rc;
-    if (int rc = launch_convert_tokens(x, x_dtype, T, L.H, ws + L.xq_hi, ws + L.xq_ts, s)) return rc;
-    prof_end(K3_PROF_TOPK, s);
-    return decode_bs(p, L, ws, int(T), y_out, y_dtype, sms, s);
+    PairsArgs cand{};
+    cand.slot = pair_slot;
+    cand.tok = pair_tok;
+    cand.w = pair_w;
+    cand.n_in = int(n_pairs);
+    return pairs_decode_run(p, x, x_dtype, T, cand, y_out, y_dtype, workspace, workspace_bytes,
+                            static_cast<cudaStream_t>(stream));
 }

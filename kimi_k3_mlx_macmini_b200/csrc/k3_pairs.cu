@@ -36,9 +36,11 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
     for (int h = 0; h < kMaxPairCandidates / 256; ++h) {
         const int i = h * 256 + threadIdx.x;
         bool ok = false;
+        int sl = -1, t = 0;
+        float wv = 0.0f;
         if (i < nin) {
-            const int sl = a.slot[i], t = a.tok[i];
-            ok = sl >= 0 && sl < a.num_slots && t >= 0 && t < a.T;
+            pair_candidate(a, i, sl, t, wv);
+            ok = sl >= 0;
         }
         vk[h] = ok;
         const uint32_t bal = __ballot_sync(0xffffffffu, ok);
@@ -62,11 +64,14 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
         const int i = h * 256 + threadIdx.x;
         const uint32_t bal = __ballot_sync(0xffffffffu, vk[h]);
         if (vk[h]) {
+            int sl, t;
+            float wv;
+            pair_candidate(a, i, sl, t, wv);
             const int pos = chunk_cnt[h * 8 + warp] + __popc(bal & ((1u << lane) - 1u));
             vidx[pos] = i;
-            vslot[pos] = a.slot[i];
-            atomicOr(&bitmap[a.slot[i] >> 5], 1u << (a.slot[i] & 31));
-            atomicAdd(&cnt_s[a.slot[i]], 1);
+            vslot[pos] = sl;
+            atomicOr(&bitmap[sl >> 5], 1u << (sl & 31));
+            atomicAdd(&cnt_s[sl], 1);
         }
     }
     __syncthreads();
@@ -142,8 +147,11 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
         for (int u = 0; u < v; ++u) rank += (vslot[u] == sl);
         const int p = pbase[pos_s[sl]] + rank;
         if (p < npairs) {
-            P->pair_tok[p] = a.tok[vidx[v]];
-            P->pair_w[p] = a.w[vidx[v]];
+            int s2, t;
+            float wv;
+            pair_candidate(a, vidx[v], s2, t, wv);
+            P->pair_tok[p] = t;
+            P->pair_w[p] = wv;
         }
     }
     if (threadIdx.x == 0) {

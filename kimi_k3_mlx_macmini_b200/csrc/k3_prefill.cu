@@ -19,6 +19,7 @@
 //                         double-buffered TMEM accumulators, epilogue warps draining the
 //                         other buffer.
 #include "k3_async.cuh"
+#include "k3_pairs.cuh"
 #include "k3_prefill.cuh"
 #include "k3_tma.cuh"
 
@@ -189,15 +190,17 @@ __device__ __forceinline__ void prefill_cand(const PrefillCand& c, int i, int& s
         w = c.pw[i];
         if (tok < 0 || tok >= c.T) slot = -1;
     } else if (i < c.T * c.k) {
-        slot = c.idx[i];
-        tok = i / c.k;
-        w = c.w[i];
+        const int t = i / c.k, j = i - t * c.k;
+        const int e = c.idx[int64_t(t) * c.rstride + j] - c.expert_lo;
+        slot = (e >= 0 && e < c.n_local) ? e : -1;
+        tok = t;
+        w = c.w[int64_t(t) * c.rstride + j];
     } else {
         slot = c.shared_slot;
-        tok = i - c.T * c.k;
+        tok = c.shared_t0 + (i - c.T * c.k);
         w = 1.0f;
     }
-    if (slot < 0 || slot >= c.num_slots) slot = -1;
+    if (slot < 0 || slot >= c.num_slots || tok < 0 || tok >= c.T) slot = -1;
 }
 
 // Candidates of this block as per-slot bit masks (bit = candidate index in the block).
@@ -1066,6 +1069,24 @@ int64_t routed_candidates(const k3_moe_params& p, int64_t T) {
     return T * p.top_k + (p.has_shared ? T : 0);
 }
 
+// Candidates of a whole layer's routing: every expert local, the shared expert (slot E)
+// for every token.
+PrefillCand routed_cand(const k3_moe_params& p, const int32_t* idx, const float* w, int64_t T, int ns) {
+    PrefillCand c{};
+    c.idx = idx;
+    c.w = w;
+    c.T = int(T);
+    c.k = p.top_k;
+    c.rstride = p.top_k;
+    c.expert_lo = 0;
+    c.n_local = int(p.num_experts);
+    c.shared_slot = p.has_shared ? int(p.num_experts) : -1;
+    c.shared_t0 = 0;
+    c.shared_n = p.has_shared ? int(T) : 0;
+    c.num_slots = ns;
+    return c;
+}
+
 }  // namespace
 
 bool router_gemm_ok(int xdt, int64_t H, const void* x, const void* gate_w) {
@@ -1129,14 +1150,7 @@ extern "C" K3_API int k3_moe_prefill(const k3_moe_params* p, const void* x, int 
     int32_t* idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + L.idx);
     float* w = weight_out ? weight_out : reinterpret_cast<float*>(ws + L.w);
     if (int rc = prefill_route(p, x, x_dtype, T, gate_w_bf16, bias, idx, w, ws, L, s)) return rc;
-    PrefillCand c{};
-    c.idx = idx;
-    c.w = w;
-    c.T = int(T);
-    c.k = p->top_k;
-    c.shared_slot = p->has_shared ? int(p->num_experts) : -1;
-    c.num_slots = int(ns);
-    return prefill_run(p, x, x_dtype, T, c, y_out, y_dtype, ws, L, s);
+    return prefill_run(p, x, x_dtype, T, routed_cand(*p, idx, w, T, int(ns)), y_out, y_dtype, ws, L, s);
 }
 
 extern "C" K3_API int k3_moe_experts_prefill(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
@@ -1156,14 +1170,7 @@ extern "C" K3_API int k3_moe_experts_prefill(const k3_moe_params* p, const void*
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (int rc = cuda_check(cudaMemsetAsync(ws + L.hdr, 0, sizeof(PrefillHeader), s), "cudaMemsetAsync(header)"))
         return rc;
-    PrefillCand c{};
-    c.idx = idx;
-    c.w = w;
-    c.T = int(T);
-    c.k = p->top_k;
-    c.shared_slot = p->has_shared ? int(p->num_experts) : -1;
-    c.num_slots = int(ns);
-    return prefill_run(p, x, x_dtype, T, c, y_out, y_dtype, ws, L, s);
+    return prefill_run(p, x, x_dtype, T, routed_cand(*p, idx, w, T, int(ns)), y_out, y_dtype, ws, L, s);
 }
 
 extern "C" K3_API size_t k3_moe_pairs_prefill_workspace(const k3_moe_params* p, int64_t T, int64_t n_pairs) {
@@ -1198,6 +1205,74 @@ extern "C" K3_API int k3_moe_pairs_prefill(const k3_moe_params* p, const void* x
     c.n = int(n_pairs);
     c.T = int(T);
     c.shared_slot = -1;
+    c.num_slots = int(p->pool->num_slots);
+    return prefill_run(p, x, x_dtype, T, c, y_out, y_dtype, ws, L, s);
+}
+
+namespace k3 {
+size_t pairs_decode_workspace(const k3_moe_params& p, int64_t T, int64_t n_in);
+int pairs_decode_run(const k3_moe_params* p, const void* x, int x_dtype, int64_t T, const PairsArgs& cand,
+                     void* y_out, int y_dtype, void* workspace, size_t workspace_bytes, cudaStream_t s);
+}  // namespace k3
+
+extern "C" K3_API size_t k3_moe_ep_local_workspace(const k3_moe_params* p, int64_t T, int64_t shared_n) {
+    if (!p || !p->pool || T < 1 || shared_n < 0) return 0;
+    const int64_t n = T * p->top_k + shared_n;
+    if (n <= kMaxPairCandidates) return pairs_decode_workspace(*p, T, n);
+    return prefill_layout(*p, T, n, p->pool->num_slots, false).total;
+}
+
+extern "C" K3_API int k3_moe_ep_local(const k3_moe_params* p, const void* x, int x_dtype, int64_t T,
+                                      const int32_t* idx, const float* w, int64_t route_stride, int32_t expert_lo,
+                                      int32_t shared_t0, int32_t shared_n, void* y_out, int y_dtype,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+    if (!p || !p->pool) return fail(K3_ERR_INVALID, "k3_moe_ep_local: params or pool is NULL");
+    if (!x || !idx || !w || !y_out) return fail(K3_ERR_INVALID, "k3_moe_ep_local: NULL tensor");
+    if (x_dtype != K3_F32 && x_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_ep_local: x must be f32 or bf16");
+    if (y_dtype != K3_F32 && y_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_ep_local: y must be f32 or bf16");
+    if (T < 1 || T > (int64_t(1) << 24)) return fail(K3_ERR_INVALID, "k3_moe_ep_local: T must be 1..2^24");
+    if (p->top_k < 1 || route_stride < p->top_k) return fail(K3_ERR_INVALID, "k3_moe_ep_local: route_stride < top_k");
+    if (shared_n < 0 || shared_t0 < 0 || int64_t(shared_t0) + shared_n > T)
+        return fail(K3_ERR_INVALID, "k3_moe_ep_local: shared token range outside [0, T)");
+    const int64_t n = T * p->top_k + shared_n;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int shared_slot = p->has_shared ? int(p->num_experts) : -1;
+    if (n <= kMaxPairCandidates) {
+        PairsArgs c{};
+        c.ridx = idx;
+        c.rw = w;
+        c.rk = p->top_k;
+        c.rstride = int(route_stride);
+        c.expert_lo = expert_lo;
+        c.n_local = int(p->num_experts);
+        c.shared_slot = shared_slot;
+        c.shared_t0 = shared_t0;
+        c.shared_n = shared_n;
+        c.n_in = int(n);
+        return pairs_decode_run(p, x, x_dtype, T, c, y_out, y_dtype, workspace, workspace_bytes, s);
+    }
+    if (int rc = check_prefill(p, x, x_dtype, T, y_out, y_dtype, "k3_moe_ep_local")) return rc;
+    if (p->pool->num_slots < 1 || p->pool->num_slots > kPMaxSlots)
+        return fail(K3_ERR_UNSUPPORTED, "k3_moe_ep_local: the pool must have 1..1025 slots");
+    const PrefillLayout L = prefill_layout(*p, T, n, p->pool->num_slots, false);
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(K3_ERR_WORKSPACE, "k3_moe_ep_local: workspace must be non-NULL and 256-byte aligned");
+    if (workspace_bytes < L.total)
+        return fail(K3_ERR_WORKSPACE, "k3_moe_ep_local: workspace too small: need " + std::to_string(L.total) + " bytes");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    if (int rc = cuda_check(cudaMemsetAsync(ws + L.hdr, 0, sizeof(PrefillHeader), s), "cudaMemsetAsync(header)"))
+        return rc;
+    PrefillCand c{};
+    c.idx = idx;
+    c.w = w;
+    c.T = int(T);
+    c.k = p->top_k;
+    c.rstride = int(route_stride);
+    c.expert_lo = expert_lo;
+    c.n_local = int(p->num_experts);
+    c.shared_slot = shared_slot;
+    c.shared_t0 = shared_t0;
+    c.shared_n = shared_n;
     c.num_slots = int(p->pool->num_slots);
     return prefill_run(p, x, x_dtype, T, c, y_out, y_dtype, ws, L, s);
 }

@@ -107,12 +107,14 @@ struct PrefillPlan {
 };
 
 // Where the (slot, token, weight) candidates come from: either a routing result
-// idx/w [T][k] (candidate i < T*k is (idx[i], i / k, w[i]); with shared_slot >= 0 the
-// next T candidates are (shared_slot, t, 1)), or explicit pair arrays.
+// idx/w (rows rstride elements apart; candidate i < T*k, i = t*k + j, is (idx[t][j] -
+// expert_lo when in [0, n_local), t, w[t][j]); the next shared_n candidates are
+// (shared_slot, shared_t0 + j, 1)), or explicit pair arrays.
 struct PrefillCand {
     const int32_t* idx;
     const float* w;
     int T, k, shared_slot;
+    int rstride, expert_lo, n_local, shared_t0, shared_n;
     const int32_t* slot;
     const int32_t* tok;
     const float* pw;

@@ -4,12 +4,14 @@ One process per GPU. Rank r owns routed experts [r*E/W, (r+1)*E/W) and a copy of
 shared expert; the router is replicated. Every rank brings M tokens. A step:
 
 1. route: each rank runs the router on its own M tokens (top-k ids and weights);
-2. dispatch: ``all_gather`` of the tokens (bf16 [W*M, H]) and of their routing -- at
-   decode M is at most 8, so broadcasting every token to every rank is smaller than a
-   counted all-to-all and needs no host synchronisation;
-3. local experts: every rank runs ``k3_moe_pairs_decode`` over the (token, expert) pairs
-   that route to its experts, plus the shared expert for its own tokens, producing one
-   f32 partial row per gathered token (zero for tokens that touch none of its experts);
+2. dispatch: ``all_gather`` of the tokens (bf16 [W*M, H]) and of their routing (one
+   [M, 2k] int32 block: expert ids, then the weights' bits) -- at decode M is at most 8,
+   so broadcasting every token to every rank is smaller than a counted all-to-all and
+   needs no host synchronisation;
+3. local experts: every rank runs its experts over the (token, expert) pairs that route
+   to them, plus the shared expert for its own tokens (``k3_moe_ep_local``: the pairs
+   are taken from the gathered routing on the device), producing one f32 partial row per
+   gathered token (zero for tokens that touch none of its experts);
 4. combine: ``reduce_scatter`` (sum) returns to each rank the total of its own M rows.
 
 At prefill (thousands of tokens per rank) the same steps run with the local expert
@@ -165,12 +167,49 @@ class ExpertParallelMoE:
                                         L.stream_of(x_all)), "k3_moe_pairs_decode")
         return y
 
+    def _forward_nccl(self, flat: torch.Tensor) -> torch.Tensor:
+        """One step with two all_gathers (tokens; routing packed as [M][2k] int32: expert
+        ids, then the weights' bits) and the local experts taken straight from the
+        gathered routing on the device (``k3_moe_ep_local``)."""
+        lib = L.load_library()
+        c = self.cfg
+        M, H = flat.shape
+        k, E, W = c.num_experts_per_token, c.num_experts, self.W
+        dev = flat.device
+        idx = torch.empty((M, k), dtype=torch.int32, device=dev)
+        w = torch.empty((M, k), dtype=torch.float32, device=dev)
+        r = self.router
+        ws = L.workspace(dev, lib.k3_moe_route_workspace(M, E))
+        L.check(lib.k3_moe_route(flat.data_ptr(), L.dtype_code(flat), M, H, r.gate_w.data_ptr(),
+                                 None if r.gate_b is None else r.gate_b.data_ptr(), E, k,
+                                 int(bool(c.moe_renormalize)), float(c.routed_scaling_factor),
+                                 idx.data_ptr(), w.data_ptr(), None, None, ws.data_ptr(), ws.numel(),
+                                 L.stream_of(flat)), "k3_moe_route")
+        routing = torch.cat([idx, w.view(torch.int32)], dim=1)
+        x_all = torch.empty((W * M, H), dtype=flat.dtype, device=dev)
+        r_all = torch.empty((W * M, 2 * k), dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(x_all, flat, group=self.group)
+        dist.all_gather_into_tensor(r_all, routing, group=self.group)
+        y_part = torch.empty((W * M, H), dtype=torch.float32, device=dev)
+        w_all = r_all[:, k:].view(torch.float32)
+        shared_n = M if self.with_shared else 0
+        ws2 = L.workspace(dev, lib.k3_moe_ep_local_workspace(self.params, W * M, shared_n))
+        L.check(lib.k3_moe_ep_local(self.params, x_all.data_ptr(), L.dtype_code(x_all), W * M, r_all.data_ptr(),
+                                    w_all.data_ptr(), 2 * k, self.lo, self.r * M, shared_n, y_part.data_ptr(),
+                                    L.K3_F32, ws2.data_ptr(), ws2.numel(), L.stream_of(x_all)), "k3_moe_ep_local")
+        y = torch.empty((M, H), dtype=torch.float32, device=dev)
+        dist.reduce_scatter_tensor(y, y_part, group=self.group)
+        return y
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         L.require_cuda(x, "x")
         shape = x.shape
         flat = x.reshape(-1, shape[-1])
         if flat.dtype not in (torch.float32, torch.bfloat16):
             flat = flat.float()
+        flat = flat.contiguous()
+        if _is_nccl(self.group):
+            return self._forward_nccl(flat).reshape(shape)
         y = ep_forward(flat, self._route, self._local, group=self.group,
                        num_experts=self.cfg.num_experts, with_shared=self.with_shared)
         return y.reshape(shape)

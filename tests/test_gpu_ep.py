@@ -70,6 +70,54 @@ def test_pairs_decode_matches_oracle(k3):
     assert np.all(got[untouched] == 0)
 
 
+@pytest.mark.parametrize("T", [12, 300])
+def test_ep_local_matches_explicit_pairs(k3, T):
+    """k3_moe_ep_local (pairs taken on the device from the gathered routing, experts
+    offset by expert_lo, the shared expert on a token range) equals the explicit-pair
+    calls on the same candidates: the decode kernels at T=12, the prefill kernels at
+    T=300 (more than 1024 candidates)."""
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    from kimi_k3_mlx_macmini_b200.moe import SHARED, ExpertPool
+    lay = _small_layer(seed=13)
+    lo, E_loc, k = 4, 8, 4
+    pool = ExpertPool(0, E_loc, lambda la, e, which: lay.source(la, e if e == SHARED else lo + int(e), which),
+                      "cuda", with_shared=True)
+    params = _params(pool, lay.cfg, E_loc)
+    x = synthetic.tokens(31 + T, T, H)
+    rng = np.random.default_rng(T)
+    idx = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.uniform(0.1, 1.0, size=(T, k)).astype(np.float32)
+    routing = np.concatenate([idx, w.view(np.int32)], axis=1)
+    t0, ns = 2, T - 5
+    lib = L.load_library()
+    dev = torch.device("cuda")
+    r_all = torch.from_numpy(routing).cuda()
+    y1 = torch.empty((T, H), dtype=torch.float32, device=dev)
+    ws = L.workspace(dev, lib.k3_moe_ep_local_workspace(params, T, ns))
+    L.check(lib.k3_moe_ep_local(params, x.data_ptr(), L.K3_BF16, T, r_all.data_ptr(),
+                                r_all[:, k:].view(torch.float32).data_ptr(), 2 * k, lo, t0, ns, y1.data_ptr(),
+                                L.K3_F32, ws.data_ptr(), ws.numel(), L.stream_of(x)), "k3_moe_ep_local")
+    e_loc = idx.reshape(-1) - lo
+    slot = np.where((e_loc >= 0) & (e_loc < E_loc), e_loc, -1).astype(np.int32)
+    tok = np.repeat(np.arange(T, dtype=np.int32), k)
+    wv = w.reshape(-1)
+    slot = np.concatenate([slot, np.full(ns, E_loc, np.int32)])
+    tok = np.concatenate([tok, np.arange(t0, t0 + ns, dtype=np.int32)])
+    wv = np.concatenate([wv, np.ones(ns, np.float32)])
+    ts = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (slot, tok, wv)]
+    y2 = torch.empty((T, H), dtype=torch.float32, device=dev)
+    n = slot.size
+    fn, wsfn = ((lib.k3_moe_pairs_decode, lib.k3_moe_pairs_workspace) if n <= 1024 else
+                (lib.k3_moe_pairs_prefill, lib.k3_moe_pairs_prefill_workspace))
+    ws2 = L.workspace(dev, wsfn(params, T, n))
+    L.check(fn(params, x.data_ptr(), L.K3_BF16, T, ts[0].data_ptr(), ts[1].data_ptr(), ts[2].data_ptr(), n,
+               y2.data_ptr(), L.K3_F32, ws2.data_ptr(), ws2.numel(), L.stream_of(x)), "explicit pairs")
+    a, b = y1.cpu().numpy(), y2.cpu().numpy()
+    assert O.rel_l2(a, b) < 1e-6
+    assert np.abs(b).sum() > 0
+
+
 def _ep_worker(rank, world, port, q, T=6):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
