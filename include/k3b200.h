@@ -65,7 +65,8 @@ enum {
     K3_PROF_DOWN = 3,        /* grouped MXFP4 matvec: down projection + combine   */
     K3_PROF_MATVEC = 4,      /* single-matrix MXFP4 matvec                        */
     K3_PROF_OTHER = 5,       /* codec and generic kernels                         */
-    K3_PROF_KINDS = 6
+    K3_PROF_DENSE = 6,       /* dense bf16 matvecs (latent, shared expert, lm_head) */
+    K3_PROF_KINDS = 7
 };
 K3_API int k3_profile_enable(int on);
 K3_API int k3_profile_collect(double* ms_out, int64_t* launches_out, int n);
@@ -295,6 +296,58 @@ K3_API int k3_moe_ep_local(const k3_moe_params* p, const void* x, int x_dtype, i
                            const int32_t* idx, const float* w, int64_t route_stride, int32_t expert_lo,
                            int32_t shared_t0, int32_t shared_n, void* y_out, int y_dtype,
                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------- dense bf16 matvecs ----- */
+
+/* The Kimi-K3 layer's dense bf16 parts around the MXFP4 experts, at decode (M <= 8
+ * tokens): the latent projections `flat @ down.T` and `rmsnorm(y) @ up.T`
+ * (air_llm/models/kimi_k3/moe.py:116, 128-129), the bf16 shared expert
+ * `shared_forward` (moe.py:105-107) and the lm_head logits (model.py:111-133). fp32
+ * products and sums over bf16 weights, as the reference computes them.
+ *
+ * One segment is out += X W^T with W bf16 [N][K] (row stride ldw elements, 16-byte
+ * aligned, K and ldw multiples of 8) and X [M][K] f32 or bf16 (row stride ldx). With
+ * norm_w set, X is first replaced by norm_w * X * rsqrt(mean(X^2) + eps) per row
+ * (ops.rmsnorm, ops.py:11-14). */
+typedef struct k3_dense_seg {
+    const uint16_t* w;
+    int64_t ldw;
+    int64_t K;
+    const void* x;
+    int32_t x_dtype;
+    int64_t ldx;
+    const float* norm_w;
+    float eps;
+} k3_dense_seg;
+
+enum {
+    K3_DENSE_SUM = 0,   /* out = sum over the segments of X_s W_s^T                        */
+    K3_DENSE_ACT = 1    /* two segments (gate, up) over segment 0's X: out = act(X Wg^T, X Wu^T) */
+};
+
+/* Workspace bytes for k3_dense_matvec with M tokens, N output rows and nseg segments of
+ * K0 (and K1) columns. */
+K3_API size_t k3_dense_workspace(int64_t M, int64_t N, int nseg, int64_t K0, int64_t K1);
+/* out [M][N] (row stride ldo, f32 or bf16). `activation` (K3_ACT_SILU / K3_ACT_SITU,
+ * situ_linear_beta <= 0 for none) is read for K3_DENSE_ACT only. The result does not
+ * depend on timing: the split-k partial sums are added in a fixed order. */
+K3_API int k3_dense_matvec(const k3_dense_seg* segs, int nseg, int64_t M, int64_t N, int combine,
+                           int activation, float situ_beta, float situ_linear_beta, void* out,
+                           int out_dtype, int64_t ldo, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Streamed lm_head argmax (`KimiK3.logits`, air_llm/models/kimi_k3/model.py:111-133): for
+ * one hidden row h [H] (f32 or bf16) and W bf16 [V][H], idx_out = argmax_n h . W[n]
+ * (lowest n on ties, as the reference's first-occurrence argmax over ascending chunks)
+ * and val_out = that logit, both device scalars; logits_out (optional, [V] f32) receives
+ * every logit. The reference's byte count is V * H * 2 by construction. */
+K3_API size_t k3_lm_head_workspace(int64_t H, int64_t V);
+/* Status of the last dense call on `workspace` (synchronises `stream`): K3_OK, or
+ * K3_ERR_TIMEOUT when a kernel's bounded wait gave up. */
+K3_API int k3_dense_status(const void* workspace, void* stream);
+K3_API int k3_lm_head_argmax(const void* h, int h_dtype, int64_t H, const uint16_t* w, int64_t V,
+                             int32_t* idx_out, float* val_out, float* logits_out, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* Device status word of the last prefill call on `workspace` (synchronises `stream`):
  * K3_OK, or K3_ERR_TIMEOUT when a kernel's bounded wait gave up. */

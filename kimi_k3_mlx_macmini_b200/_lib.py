@@ -16,7 +16,8 @@ LIB_PATH = Path(__file__).resolve().with_name("libk3b200.so")
 K3_OK, K3_ERR_INVALID, K3_ERR_UNSUPPORTED, K3_ERR_CUDA, K3_ERR_WORKSPACE, K3_ERR_TIMEOUT = range(6)
 K3_F32, K3_BF16, K3_F16 = 0, 1, 2
 K3_ACT_SILU, K3_ACT_SITU = 0, 1
-PROF_KINDS = ("router", "topk", "gateup", "down", "matvec", "other")
+K3_DENSE_SUM, K3_DENSE_ACT = 0, 1
+PROF_KINDS = ("router", "topk", "gateup", "down", "matvec", "other", "dense")
 
 _DTYPE = {torch.float32: K3_F32, torch.bfloat16: K3_BF16, torch.float16: K3_F16}
 
@@ -42,6 +43,12 @@ class K3MoEParams(ctypes.Structure):
                 ("has_shared", ctypes.c_int32), ("activation", ctypes.c_int32),
                 ("situ_beta", ctypes.c_float), ("situ_linear_beta", ctypes.c_float),
                 ("experts", ctypes.c_void_p), ("pool", ctypes.POINTER(K3ExpertPool))]
+
+
+class K3DenseSeg(ctypes.Structure):
+    _fields_ = [("w", ctypes.c_void_p), ("ldw", ctypes.c_int64), ("K", ctypes.c_int64),
+                ("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int32), ("ldx", ctypes.c_int64),
+                ("norm_w", ctypes.c_void_p), ("eps", ctypes.c_float)]
 
 
 # name -> (restype, argtypes); mirrors include/k3b200.h
@@ -78,6 +85,12 @@ SIGNATURES = {
     "k3_moe_pairs_prefill": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp, _i64,
                                     _vp, _i32, _vp, _sz, _vp]),
     "k3_moe_prefill_status": (_i32, [_vp, _vp]),
+    "k3_dense_workspace": (_sz, [_i64, _i64, _i32, _i64, _i64]),
+    "k3_dense_matvec": (_i32, [ctypes.POINTER(K3DenseSeg), _i32, _i64, _i64, _i32, _i32, _f32, _f32, _vp, _i32,
+                               _i64, _vp, _sz, _vp]),
+    "k3_lm_head_workspace": (_sz, [_i64, _i64]),
+    "k3_dense_status": (_i32, [_vp, _vp]),
+    "k3_lm_head_argmax": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "k3_moe_ep_local_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
     "k3_moe_ep_local": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                _vp, _i32, _vp, _sz, _vp]),

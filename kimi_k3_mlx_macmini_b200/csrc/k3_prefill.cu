@@ -420,6 +420,7 @@ __device__ __forceinline__ void split_block32(float (&r)[32], uint4 (&data)[NP],
 
 // One thread per (token t, 32-block g): x[t][32g..32g+32) -> pieces at
 // xp[(p*T + t)*(K/2) + 16g] and scales xsf[(p*T + t)*(K/32) + g].
+template <int NP>
 __global__ void __launch_bounds__(256) prefill_pieces_kernel(const void* __restrict__ x, int xdt, int T, int64_t K,
                                                              uint8_t* __restrict__ xp, uint8_t* __restrict__ xsf) {
     const int64_t G = K / 32;
@@ -450,11 +451,11 @@ __global__ void __launch_bounds__(256) prefill_pieces_kernel(const void* __restr
             r[4 * q + 3] = v.w;
         }
     }
-    uint4 d[kPPieces];
-    uint32_t sf[kPPieces];
-    split_block32<kPPieces>(r, d, sf);
+    uint4 d[NP];
+    uint32_t sf[NP];
+    split_block32<NP>(r, d, sf);
 #pragma unroll
-    for (int p = 0; p < kPPieces; ++p) {
+    for (int p = 0; p < NP; ++p) {
         const int64_t row = int64_t(p) * T + t;
         *reinterpret_cast<uint4*>(xp + row * (K / 2) + 16 * g) = d[p];
         xsf[row * G + g] = uint8_t(sf[p]);
@@ -466,7 +467,7 @@ __global__ void __launch_bounds__(256) prefill_pieces_kernel(const void* __restr
 __global__ void __launch_bounds__(256) prefill_permute_kernel(const __grid_constant__ PrefillPlan P,
                                                               const uint8_t* __restrict__ xp,
                                                               const uint8_t* __restrict__ xsf, int T, int64_t K,
-                                                              uint8_t* __restrict__ img) {
+                                                              int np, uint8_t* __restrict__ img) {
     const int64_t U = K / 32;
     const int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (id >= int64_t(P.hdr->n_pairs) * U) return;
@@ -477,11 +478,10 @@ __global__ void __launch_bounds__(256) prefill_permute_kernel(const __grid_const
     const int tok = P.pair_tok[pos];
     const int s = u >> 3, q = u & 7;
     const int nst = int(K / kBStageK);
-#pragma unroll
-    for (int p = 0; p < kPPieces; ++p) {
+    for (int p = 0; p < np; ++p) {
         const int64_t row = int64_t(p) * T + tok;
         const uint4 v = __ldg(reinterpret_cast<const uint4*>(xp + row * (K / 2) + 16 * u));
-        uint8_t* blk = img + img_block(P.ch_n8p, c, nst, s, p / kPStack, n8);
+        uint8_t* blk = img + img_block(P.ch_n8p, c, nst, s, p / kPStack, n8, np / kPStack);
         const int r = (p % kPStack) * n8 + j;                      // row in the stacked block
         *reinterpret_cast<uint4*>(blk + kPImgSf + r * 128 + ((q ^ (r & 7)) << 4)) = v;
         blk[img_sf(r, q)] = __ldg(xsf + row * U + u);
@@ -516,11 +516,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 // Items = (chunk c, row block r), r fastest; CTA b takes items b, b + grid, ... so the
 // CTAs running at one time cover a few consecutive chunks and share their image blocks
-// in the L2.
-template <bool GATEUP>
+// in the L2. PAIRS = piece pairs of this phase's token image (the down phase always has
+// kPPieces / kPStack; the gate/up phase more for fp32 tokens).
+template <bool GATEUP, int PAIRS>
 __global__ void __launch_bounds__(kPThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ PMaps maps, const __grid_constant__ PArgs a) {
-    constexpr int kPairs = kPPieces / kPStack;
+    constexpr int kPairs = PAIRS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     PASlot* aring = reinterpret_cast<PASlot*>(base);
@@ -622,7 +623,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
                 const int c = i / nrb;
                 const int n8 = (P.ch_n[c] + 7) & ~7;
                 const uint32_t bytes = uint32_t(kPImgSf + 128 * kPStack * n8);
-                const uint8_t* cimg = a.img + img_block(P.ch_n8p, c, nst, 0, 0, n8);
+                const uint8_t* cimg = a.img + img_block(P.ch_n8p, c, nst, 0, 0, n8, kPairs);
                 for (int s = 0; s < nst && ok; ++s) {
                     for (int pp = 0; pp < kPairs; ++pp, ++gb) {
                         const int si = int(gb % kPBSlots);
@@ -791,7 +792,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
                         split_block32<kPPieces>(r, dv, sv);
 #pragma unroll
                         for (int p = 0; p < kPPieces; ++p) {
-                            uint8_t* blk = a.img_out + img_block(P.ch_n8p, c, nst_dn, rb >> 1, p / kPStack, n8);
+                            uint8_t* blk = a.img_out + img_block(P.ch_n8p, c, nst_dn, rb >> 1, p / kPStack, n8,
+                                                                 kPPieces / kPStack);
                             const int row = (p % kPStack) * n8 + j;
                             *reinterpret_cast<uint4*>(blk + kPImgSf + row * 128 + ((unit ^ (row & 7)) << 4)) = dv[p];
                             blk[img_sf(row, unit)] = uint8_t(sv[p]);
@@ -845,12 +847,16 @@ __global__ void __launch_bounds__(kPThreads, 1)
 bool g_attr_done = false;
 int configure_prefill() {
     if (g_attr_done) return K3_OK;
-    if (int rc = cuda_check(cudaFuncSetAttribute(prefill_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 int(psmem_bytes())),
+    if (int rc = cuda_check(cudaFuncSetAttribute(prefill_gemm_kernel<true, kPPieces / kPStack>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, int(psmem_bytes())),
                             "cudaFuncSetAttribute(prefill gate/up)"))
         return rc;
-    if (int rc = cuda_check(cudaFuncSetAttribute(prefill_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 int(psmem_bytes())),
+    if (int rc = cuda_check(cudaFuncSetAttribute(prefill_gemm_kernel<true, kPPiecesF32 / kPStack>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, int(psmem_bytes())),
+                            "cudaFuncSetAttribute(prefill gate/up, fp32 tokens)"))
+        return rc;
+    if (int rc = cuda_check(cudaFuncSetAttribute(prefill_gemm_kernel<false, kPPieces / kPStack>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, int(psmem_bytes())),
                             "cudaFuncSetAttribute(prefill down)"))
         return rc;
     if (int rc = cuda_check(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -874,11 +880,10 @@ struct PrefillLayout {
     size_t xp, xsf, img_gu, img_dn, slab, y32, total;
 };
 
-// Bytes of an image over nst k-steps: at most nc_max chunks and n_cand + 7 nc_max rows
-// per piece.
-size_t img_bytes(int64_t nst, int64_t n_cand, int64_t nc_max) {
-    return size_t(kPPieces / kPStack) * size_t(nst) *
-           (size_t(kPImgSf) * nc_max + 128 * kPStack * size_t(n_cand + 7 * nc_max));
+// Bytes of an image of `pairs` piece pairs over nst k-steps: at most nc_max chunks and
+// n_cand + 7 nc_max rows per piece.
+size_t img_bytes(int pairs, int64_t nst, int64_t n_cand, int64_t nc_max) {
+    return size_t(pairs) * size_t(nst) * (size_t(kPImgSf) * nc_max + 128 * kPStack * size_t(n_cand + 7 * nc_max));
 }
 
 PrefillLayout prefill_layout(const k3_moe_params& p, int64_t T, int64_t n_cand, int64_t num_slots, bool route) {
@@ -909,10 +914,11 @@ PrefillLayout prefill_layout(const k3_moe_params& p, int64_t T, int64_t n_cand, 
     L.ch_p0 = carve_p(off, sizeof(int) * L.nc_max);
     L.ch_n = carve_p(off, sizeof(int) * L.nc_max);
     L.ch_n8p = carve_p(off, sizeof(int) * (L.nc_max + 1));
-    L.xp = carve_p(off, size_t(kPPieces) * T * (L.H / 2));
-    L.xsf = carve_p(off, size_t(kPPieces) * T * (L.H / 32));
-    L.img_gu = carve_p(off, img_bytes(L.H / kBStageK, n_cand, L.nc_max));
-    L.img_dn = carve_p(off, img_bytes(L.I / kBStageK, n_cand, L.nc_max));
+    // token pieces and the gate/up image are sized for fp32 tokens (the larger case)
+    L.xp = carve_p(off, size_t(kPPiecesF32) * T * (L.H / 2));
+    L.xsf = carve_p(off, size_t(kPPiecesF32) * T * (L.H / 32));
+    L.img_gu = carve_p(off, img_bytes(kPPiecesF32 / kPStack, L.H / kBStageK, n_cand, L.nc_max));
+    L.img_dn = carve_p(off, img_bytes(kPPieces / kPStack, L.I / kBStageK, n_cand, L.nc_max));
     L.slab = carve_p(off, kPSlabBytes * size_t(L.G));
     L.y32 = carve_p(off, sizeof(float) * T * L.H);
     L.total = off;
@@ -987,11 +993,16 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
     K3_CHECK_LAUNCH("prefill_place_kernel");
     {
         const int64_t n = T * (L.H / 32);
-        prefill_pieces_kernel<<<int((n + 255) / 256), 256, 0, s>>>(x, xdt, int(T), L.H, ws + L.xp, ws + L.xsf);
+        if (xdt == K3_F32)
+            prefill_pieces_kernel<kPPiecesF32>
+                <<<int((n + 255) / 256), 256, 0, s>>>(x, xdt, int(T), L.H, ws + L.xp, ws + L.xsf);
+        else
+            prefill_pieces_kernel<kPPieces>
+                <<<int((n + 255) / 256), 256, 0, s>>>(x, xdt, int(T), L.H, ws + L.xp, ws + L.xsf);
         K3_CHECK_LAUNCH("prefill_pieces_kernel");
         const int64_t m = int64_t(n_cand) * (L.H / 32);
-        prefill_permute_kernel<<<int((m + 255) / 256), 256, 0, s>>>(P, ws + L.xp, ws + L.xsf, int(T), L.H,
-                                                                    ws + L.img_gu);
+        prefill_permute_kernel<<<int((m + 255) / 256), 256, 0, s>>>(
+            P, ws + L.xp, ws + L.xsf, int(T), L.H, xdt == K3_F32 ? kPPiecesF32 : kPPieces, ws + L.img_gu);
         K3_CHECK_LAUNCH("prefill_permute_kernel");
     }
     prof_end(K3_PROF_TOPK, s);
@@ -1017,7 +1028,10 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
     if (int rc = tile_pool_map(&ma.a0, pl.w1_tiles, L.I, L.H, pl.num_slots)) return rc;
     if (int rc = tile_pool_map(&ma.a1, pl.w3_tiles, L.I, L.H, pl.num_slots)) return rc;
     prof_begin(K3_PROF_GATEUP, s);
-    prefill_gemm_kernel<true><<<G, kPThreads, psmem_bytes(), s>>>(ma, ga);
+    if (xdt == K3_F32)
+        prefill_gemm_kernel<true, kPPiecesF32 / kPStack><<<G, kPThreads, psmem_bytes(), s>>>(ma, ga);
+    else
+        prefill_gemm_kernel<true, kPPieces / kPStack><<<G, kPThreads, psmem_bytes(), s>>>(ma, ga);
     prof_end(K3_PROF_GATEUP, s);
     K3_CHECK_LAUNCH("prefill_gemm_kernel<gate/up>");
 
@@ -1035,7 +1049,7 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
     if (int rc = tile_pool_map(&mb.a0, pl.w2_tiles, L.H, L.I, pl.num_slots)) return rc;
     mb.a1 = mb.a0;
     prof_begin(K3_PROF_DOWN, s);
-    prefill_gemm_kernel<false><<<G, kPThreads, psmem_bytes(), s>>>(mb, da);
+    prefill_gemm_kernel<false, kPPieces / kPStack><<<G, kPThreads, psmem_bytes(), s>>>(mb, da);
     prof_end(K3_PROF_DOWN, s);
     K3_CHECK_LAUNCH("prefill_gemm_kernel<down>");
     if (ydt != K3_F32) {

@@ -13,9 +13,11 @@
 //   down:    D [2 x 128 rows of H][chunk tokens] = W2 rows x (act pieces)^T, reduce-added
 //            into y[token] (fp32 adds in the L2; the order of the adds is not fixed).
 //
-// The activations enter the kind::mxf4 MMA as kPPieces E2M1 pieces with one E8M0 scale
-// per (piece, 32-block); the pieces of one value accumulate into the same TMEM column
-// (one MMA per piece, accumulate on), so a chunk of n tokens takes n TMEM columns.
+// The activations enter the kind::mxf4 MMA as E2M1 pieces with one E8M0 scale per (piece,
+// 32-block); the pieces of one value accumulate into the same TMEM column (one MMA per
+// piece, accumulate on), so a chunk of n tokens takes n TMEM columns. bf16 tokens and the
+// activations take kPPieces pieces (bf16's 8 significant bits fit in them); fp32 tokens
+// take kPPiecesF32, which keeps the split error near 2e-6 of the value.
 //
 // Two pieces are stacked along N in one MMA (B rows [piece][token]); the two TMEM columns
 // of a token are added in the epilogue. A tcgen05 MMA costs about the same per
@@ -36,7 +38,8 @@
 
 namespace k3 {
 
-constexpr int kPPieces = 4;           // E2M1 pieces per activation value
+constexpr int kPPieces = 4;           // E2M1 pieces per activation value (bf16 tokens, act)
+constexpr int kPPiecesF32 = 6;        // pieces per fp32 token value (gate/up input)
 constexpr int kPStack = 2;            // pieces stacked along N in one MMA (B rows = piece-major)
 constexpr int kPN = 104;              // tokens per chunk (MMA N = kPStack x rows <= 208)
 constexpr int kPASlots = 3;           // weight ring: two 128-row tiles x 256 k per slot
@@ -71,14 +74,14 @@ static_assert(psmem_bytes() + 2048 <= 227 * 1024, "prefill ring exceeds shared m
 // Gate/up epilogue staging per CTA: [token][gate | up][128 rows] fp32.
 constexpr size_t kPSlabBytes = sizeof(float) * kPN * 2 * kBRows;
 
-// Byte offset of the image block (chunk c, k-step s, piece pair pp): blocks are ordered
-// [chunk][step][pair], a block of a chunk with n8 rows per piece holds kPImgSf +
-// 128 * kPStack * n8 bytes, and n8p[c] = sum of n8 over the chunks before c. Row r of a
-// block is (piece pp*kPStack + r / n8, token r % n8).
-__host__ __device__ __forceinline__ int64_t img_block(const int* n8p, int c, int nst, int s, int pp, int n8) {
-    constexpr int kPairs = kPPieces / kPStack;
-    return int64_t(kPairs) * nst * (int64_t(kPImgSf) * c + 128 * kPStack * int64_t(n8p[c])) +
-           int64_t(s * kPairs + pp) * (kPImgSf + 128 * kPStack * n8);
+// Byte offset of the image block (chunk c, k-step s, piece pair pp) of an image with
+// `pairs` piece pairs: blocks are ordered [chunk][step][pair], a block of a chunk with n8
+// rows per piece holds kPImgSf + 128 * kPStack * n8 bytes, and n8p[c] = sum of n8 over the
+// chunks before c. Row r of a block is (piece pp*kPStack + r / n8, token r % n8).
+__host__ __device__ __forceinline__ int64_t img_block(const int* n8p, int c, int nst, int s, int pp, int n8,
+                                                      int pairs) {
+    return int64_t(pairs) * nst * (int64_t(kPImgSf) * c + 128 * kPStack * int64_t(n8p[c])) +
+           int64_t(s * pairs + pp) * (kPImgSf + 128 * kPStack * n8);
 }
 // Offset inside a block of the scale byte of (row r, k-block j of the block's 256 k).
 __host__ __device__ __forceinline__ int img_sf(int r, int j) {

@@ -28,6 +28,7 @@ import numpy as np
 import torch
 
 from . import _lib as L
+from . import dense as D
 from .mxfp4 import decode_mxfp4, mxfp4_matvec_fused, packed_tiles, scale_minmax, scales_tc
 
 SHARED = "shared"
@@ -168,16 +169,17 @@ class LatentMoE:
             raise ValueError("gate.weight is not bf16-representable; the router reads bf16 weights")
         b = w.get("gate.e_score_correction_bias")
         self.gate_b = None if b is None else _as_device(b, self.device, torch.float32)
+        # dense weights stay bf16 (the checkpoint dtype) for the streaming matvecs
         self.latent = "routed_expert_down_proj.weight" in w
         if self.latent:
-            self.down = _as_device(w["routed_expert_down_proj.weight"], self.device, torch.float32)
-            self.up = _as_device(w["routed_expert_up_proj.weight"], self.device, torch.float32)
+            self.down = D.device_weight(w["routed_expert_down_proj.weight"], self.device)
+            self.up = D.device_weight(w["routed_expert_up_proj.weight"], self.device)
             self.norm_w = _as_device(w["routed_expert_norm.weight"], self.device, torch.float32)
         self.dense_shared = "shared_experts.gate_proj.weight" in w
         if self.dense_shared:
-            self.sh_gate = _as_device(w["shared_experts.gate_proj.weight"], self.device, torch.float32)
-            self.sh_up = _as_device(w["shared_experts.up_proj.weight"], self.device, torch.float32)
-            self.sh_down = _as_device(w["shared_experts.down_proj.weight"], self.device, torch.float32)
+            self.sh_gate = D.device_weight(w["shared_experts.gate_proj.weight"], self.device)
+            self.sh_up = D.device_weight(w["shared_experts.up_proj.weight"], self.device)
+            self.sh_down = D.device_weight(w["shared_experts.down_proj.weight"], self.device)
         self.mxfp4_shared = (not self.dense_shared) and getattr(cfg, "num_shared_experts", 0) > 0
         self._pool: Optional[ExpertPool] = None
         # the contiguous pools feed the TMA kernels; False forces the pointer-table kernels
@@ -317,11 +319,25 @@ class LatentMoE:
         y = self._experts_decode(h2, idx, w, self._params(top_k=1, has_shared=0))
         return y.reshape(*h.shape[:-1], y.shape[-1])
 
+    def _act_args(self):
+        c = self.cfg
+        lb = getattr(c, "situ_linear_beta", None)
+        return dict(activation=L.K3_ACT_SITU if self.act == "situ" else L.K3_ACT_SILU,
+                    situ_beta=float(getattr(c, "situ_beta", 4.0)),
+                    situ_linear_beta=-1.0 if lb is None else float(lb))
+
+    def _dense_shared_act(self, flat: torch.Tensor) -> torch.Tensor:
+        """act(x W_gate^T, x W_up^T) of the bf16 shared expert, fp32 [M][I_shared]."""
+        return D.matvec([(self.sh_gate, flat, None, 0.0), (self.sh_up, flat, None, 0.0)],
+                        self.sh_gate.shape[0], combine=L.K3_DENSE_ACT, **self._act_args())
+
     def shared_forward(self, x: torch.Tensor) -> torch.Tensor:
         """Shared experts on the original hidden (``moe.py:105-107``)."""
         if self.dense_shared:
-            xf = x.float()
-            return self._activation(xf @ self.sh_gate.T, xf @ self.sh_up.T) @ self.sh_down.T
+            flat = x.reshape(-1, x.shape[-1])
+            a = self._dense_shared_act(flat)
+            y = D.matvec([(self.sh_down, a, None, 0.0)], self.sh_down.shape[0])
+            return y.reshape(*x.shape[:-1], y.shape[-1])
         if not self.mxfp4_shared:
             return torch.zeros((*x.shape[:-1], self.cfg.hidden_size), dtype=torch.float32,
                                device=x.device)
@@ -392,7 +408,7 @@ class LatentMoE:
             y, _, _ = self._fused_decode(flat)
             return y.reshape(*orig[:-1], y.shape[-1])
         r = self.route(flat)
-        h = flat if not self.latent else flat.float() @ self.down.T
+        h = flat if not self.latent else D.matvec([(self.down, flat, None, 0.0)], self.down.shape[0])
         if self.fused and self.tiled:
             y = self._experts_decode(h.contiguous(), r.expert_indices, r.expert_weights,
                                      self._params(has_shared=0))
@@ -403,9 +419,14 @@ class LatentMoE:
                 y.index_add_(0, tok, self.expert_forward(h[tok].float(), e)
                              * r.expert_weights[tok, slot, None])
         if self.latent:
-            yf = y.float()
-            y = self.norm_w * (yf * torch.rsqrt(yf.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps))
-            y = y @ self.up.T
-        y = y + self.shared_forward(flat)
+            # rmsnorm(y) @ up.T (+ the bf16 shared expert's down projection) in one matvec
+            segs = [(self.up, y, self.norm_w, float(self.cfg.rms_norm_eps))]
+            if self.dense_shared:
+                segs.append((self.sh_down, self._dense_shared_act(flat), None, 0.0))
+            y = D.matvec(segs, self.up.shape[0])
+            if not self.dense_shared:
+                y = y + self.shared_forward(flat)
+        else:
+            y = y + self.shared_forward(flat)
         y = y.reshape(*orig[:-1], y.shape[-1])
         return (y, r) if return_router else y
