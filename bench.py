@@ -12,6 +12,9 @@ expert + weighted scatter-add).
 
     python bench.py --config 3 ...      # configs[3]: prefill, T = 4096 tokens per GPU
     python bench.py --config 4 ...      # configs[4]: experts streamed from pinned host memory
+    python bench.py --config 5 ...      # a Kimi-K3 layer at decode (896 experts, top-16, latent
+                                        # 3584/3072, bf16 shared expert); supplementary, not a
+                                        # BASELINE config
 
 Timing: ``value`` replays CUDA graphs (one per token batch, a ring of up to 64 distinct
 batches) with inputs resident in HBM, bracketed by CUDA events; consecutive steps use
@@ -63,9 +66,10 @@ def parse():
                     help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
                     help="BASELINE config: 2 = MoE-layer decode (headline), 3 = MoE-layer prefill "
-                         "(--tokens defaults to 4096), 4 = streamed-expert decode")
+                         "(--tokens defaults to 4096), 4 = streamed-expert decode; 5 = Kimi-K3 "
+                         "layer decode (supplementary)")
     ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -729,12 +733,89 @@ def run_prefill(args, rank, world, local):
     print(json.dumps(line))
 
 
+def run_k3(args, rank, world, local):
+    """A Kimi-K3 MoE layer at decode (``air_llm/models/kimi_k3/moe.py:1-12,110-131``): 896
+    routed MXFP4 experts, top-16, in a 3584-wide latent space (experts 3584 -> 3072 ->
+    3584) between bf16 latent projections, plus a bf16 shared expert [2 x 3072, 7168];
+    situ activation. One GPU; synthetic seeded weights. Supplementary to the BASELINE
+    configs (the reference's own model shapes)."""
+    import torch
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": "k3_layer_decode_tokens_per_s", "unavailable": "config 5 runs on one GPU"}))
+        return
+    torch.cuda.set_device(local)
+    M = args.tokens if args.tokens != 8 else 1
+    K, W = args.steps, args.warmup
+    R = min(K + W, 32)
+    lay = synthetic.k3_layer(seed=args.seed)
+    moe = lay.moe()
+    Hk, Lk, Ik, Ek = 7168, 3584, 3072, 896
+    xs = [synthetic.tokens(args.seed * 7919 + i, M, Hk) for i in range(R)]
+    U = [int(torch.unique(moe.route(x).expert_indices).numel()) for x in xs]
+    step_x = [(W + i) % R for i in range(K)]
+    graphs, modes = step_modes(moe, xs, R, world)
+    ms, timing, clocks = time_modes(modes, step_x, K, W, R, world, local)
+
+    n_prof = min(K, 50)
+    L.profile_enable(True)
+    L.profile_collect()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(4e7))
+    for i in range(n_prof):
+        moe(xs[step_x[i]])
+    torch.cuda.synchronize()
+    prof = L.profile_collect()
+    L.profile_enable(False)
+    proj = Ik * Lk // 2 + Ik * Lk // 32
+    dense_bytes = 2 * (Lk * Hk + Hk * Lk + 2 * Ik * Hk + Hk * Ik)       # latent down/up, shared gate/up/down
+    router_bytes = Ek * Hk * 2
+    u_mean = float(np.mean([U[step_x[i]] for i in range(n_prof)]))
+    layer_bytes = u_mean * 3 * proj + dense_bytes + router_bytes
+    peak, peak_kind = measured_peaks()
+    d_ms, d_n = prof["dense"]
+    d_gbs = dense_bytes / (d_ms / n_prof / 1e3) / 1e9           # the step's three dense matvecs together
+    for g in graphs:
+        g.reset()
+    line = {
+        "metric": "k3_layer_decode_tokens_per_s", "value": M / (ms / 1e3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "MXFP4 experts (e2m1 x e2m1 pieces, tcgen05 kind::mxf4); bf16 dense weights x fp32 (f32x2 FMA)",
+        "data": "synthetic (seeded random-init weights of the Kimi-K3 layer shapes)",
+        "config": {"workload": f"Kimi-K3 MoE layer decode, M={M}: 896 routed MXFP4 experts top-16 (latent 3584, "
+                               "intermediate 3072), bf16 latent projections 7168<->3584, bf16 shared expert "
+                               "2x3072x7168, situ, x2.5",
+                   "tokens_per_gpu": M, "parallelism": "single GPU",
+                   "l2": f"inputs larger than L2: {Ek * 3 * proj / 1e9:.1f} GB expert pool + "
+                         f"{dense_bytes / 1e6:.0f} MB dense weights per step, a different token batch every step",
+                   "timing": timing + ", events around K steps"},
+        "unique_experts_mean": u_mean,
+        "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "dense_matvec_kernel (latent down, shared gate/up + act, "
+                                                "rmsnorm.up + shared down; prep kernels included)",
+                     "achieved": d_gbs, "peak": peak, "unit": "GB/s", "frac": d_gbs / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_step": dense_bytes, "ms_per_step": d_ms / n_prof},
+        "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
+        # profiled spans per step; a dense span is two kernels (input prep + matvec)
+        "gpu_launches": int(round((sum(c for _, c in prof.values()) + d_n) / n_prof * K)),
+        "clocks": clocks,
+    }
+    print(json.dumps(line))
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args)
     try:
         if args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.config == 5:
+            run_k3(args, rank, world, local)
         elif args.config == 4:
             run_stream(args, rank, world, local)
         elif args.config == 3:

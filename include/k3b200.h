@@ -297,6 +297,20 @@ K3_API int k3_moe_ep_local(const k3_moe_params* p, const void* x, int x_dtype, i
                            int32_t shared_t0, int32_t shared_n, void* y_out, int y_dtype,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* Latent MoE decode (Kimi-K3, air_llm/models/kimi_k3/moe.py:110-127): the router reads
+ * x_router [M][H_router] (the hidden state), the routed experts read x_expert [M][hidden]
+ * (the latent state, p->hidden wide); y_out [M][hidden] = the weighted sum of the routed
+ * experts (+ an MXFP4 shared expert when p->has_shared). One fused router launch (logits,
+ * expert-input E2M1 pieces, top-k, plan) and the block-scaled expert kernels; needs the
+ * block-scaled pool and H_router % 512 == 0. logits_out (optional, [M][E] fp32) receives
+ * the router logits, from which RouterResult's raw / corrected scores follow. */
+K3_API size_t k3_moe_decode_latent_workspace(const k3_moe_params* p, int64_t M, int64_t H_router);
+K3_API int k3_moe_decode_latent(const k3_moe_params* p, const void* x_router, int xr_dtype, int64_t H_router,
+                                const void* x_expert, int xe_dtype, int64_t M, const uint16_t* gate_w_bf16,
+                                const float* bias, void* y_out, int y_dtype, int32_t* idx_out,
+                                float* weight_out, float* logits_out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------- dense bf16 matvecs ----- */
 
 /* The Kimi-K3 layer's dense bf16 parts around the MXFP4 experts, at decode (M <= 8

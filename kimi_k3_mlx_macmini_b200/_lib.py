@@ -85,6 +85,9 @@ SIGNATURES = {
     "k3_moe_pairs_prefill": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp, _i64,
                                     _vp, _i32, _vp, _sz, _vp]),
     "k3_moe_prefill_status": (_i32, [_vp, _vp]),
+    "k3_moe_decode_latent_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
+    "k3_moe_decode_latent": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _i32, _i64, _vp, _vp, _vp,
+                                    _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
     "k3_dense_workspace": (_sz, [_i64, _i64, _i32, _i64, _i64]),
     "k3_dense_matvec": (_i32, [ctypes.POINTER(K3DenseSeg), _i32, _i64, _i64, _i32, _i32, _f32, _f32, _vp, _i32,
                                _i64, _vp, _sz, _vp]),

@@ -667,7 +667,10 @@ int choose_split_bs(int64_t n_base, int64_t K, int64_t grid) {
     return best;
 }
 
-DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
+// H_router: width of the router input (the expert input's, p.hidden, unless the MoE is
+// latent); it sets the router's k-slices.
+DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms, int64_t H_router = 0) {
+    if (H_router <= 0) H_router = p.hidden;
     DecodeLayout L{};
     L.M = M;
     L.H = p.hidden;
@@ -690,8 +693,8 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms) {
         L.xq_ts = carve(off, size_t(kBMaxN) * (L.H / 32));              // their per-row scales
         L.sfb_x = carve(off, size_t(L.U) * (L.H / 128) * kBChunk);      // per-item B scale chunks
         L.KQ = 1;
-        for (int64_t c = 1; c <= L.H / 512 && c <= 16; ++c) {  // router k-slices: >= one CTA per SM
-            if ((L.H / 512) % c) continue;
+        for (int64_t c = 1; c <= H_router / 512 && c <= 16; ++c) {  // router k-slices: >= one CTA per SM
+            if ((H_router / 512) % c) continue;
             L.KQ = int(c);
             if (((L.E + 15) / 16) * c >= sms) break;
         }
@@ -997,9 +1000,11 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
 }
 
 // Decode experts given routing; `logits` non-null also runs the top-k inside prep.
+// xr (width Hr, dtype xrdt): a separate router input (latent MoE); null routes on x.
 int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
                 const uint16_t* gate_w, const float* bias, int32_t* idx, float* w, void* y,
-                int ydt, uint8_t* ws, const DecodeLayout& L, cudaStream_t s) {
+                int ydt, uint8_t* ws, const DecodeLayout& L, cudaStream_t s, const void* xr = nullptr,
+                int xrdt = K3_F32, int64_t Hr = 0) {
     int rc = configure_smem();
     if (rc) return rc;
     Plan* plan = reinterpret_cast<Plan*>(ws + L.plan);
@@ -1028,10 +1033,13 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
     if (L.tma && gate_w) {
         // one launch: router logits + x conversion + (last CTA) top-k and plan
         RouteArgs ra{};
-        ra.x = x;
-        ra.x_dtype = xdt;
+        ra.x = xr ? xr : x;
+        ra.x_dtype = xr ? xrdt : xdt;
         ra.M = int(M);
-        ra.H = L.H;
+        ra.H = xr ? Hr : L.H;
+        ra.xe = xr ? x : nullptr;
+        ra.xe_dtype = xdt;
+        ra.He = L.H;
         ra.W = gate_w;
         ra.E = L.E;
         ra.logit_part = reinterpret_cast<float*>(ws + L.logit_part);
@@ -1326,6 +1334,44 @@ extern "C" K3_API int k3_moe_decode(const k3_moe_params* p, const void* x, int x
     float* w = weight_out ? weight_out : reinterpret_cast<float*>(ws + L.route_w);
     (void)logits;
     return decode_impl(p, x, x_dtype, M, gate_w_bf16, bias, idx, w, y_out, y_dtype, ws, L, s);
+}
+
+extern "C" K3_API size_t k3_moe_decode_latent_workspace(const k3_moe_params* p, int64_t M, int64_t H_router) {
+    if (check_moe_params(p, M) != K3_OK || H_router < 512) return 0;
+    return decode_layout(*p, M, num_sms(), H_router).total;
+}
+
+extern "C" K3_API int k3_moe_decode_latent(const k3_moe_params* p, const void* x_router, int xr_dtype,
+                                           int64_t H_router, const void* x_expert, int xe_dtype, int64_t M,
+                                           const uint16_t* gate_w_bf16, const float* bias, void* y_out,
+                                           int y_dtype, int32_t* idx_out, float* weight_out, float* logits_out,
+                                           void* workspace, size_t workspace_bytes, void* stream) {
+    if (int rc = check_moe_params(p, M)) return rc;
+    if (!x_router || !x_expert || !gate_w_bf16 || !y_out)
+        return fail(K3_ERR_INVALID, "k3_moe_decode_latent: NULL tensor");
+    if (xr_dtype != K3_F32 && xr_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_decode_latent: x_router must be f32 or bf16");
+    if (xe_dtype != K3_F32 && xe_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_decode_latent: x_expert must be f32 or bf16");
+    if (y_dtype != K3_F32 && y_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_decode_latent: y must be f32 or bf16");
+    if (H_router < 512 || H_router % 512)
+        return fail(K3_ERR_UNSUPPORTED, "k3_moe_decode_latent: the router width must be a multiple of 512");
+    if (!pool_bs(*p))
+        return fail(K3_ERR_UNSUPPORTED, "k3_moe_decode_latent needs the block-scaled expert pool (re-laid scales)");
+    if (!aligned16(x_router) || !aligned16(gate_w_bf16))
+        return fail(K3_ERR_INVALID, "k3_moe_decode_latent: x_router and gate_w must be 16-byte aligned");
+    const DecodeLayout L = decode_layout(*p, M, num_sms(), H_router);
+    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int32_t* idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + L.route_idx);
+    float* w = weight_out ? weight_out : reinterpret_cast<float*>(ws + L.route_w);
+    if (int rc = decode_impl(p, x_expert, xe_dtype, M, gate_w_bf16, bias, idx, w, y_out, y_dtype, ws, L, s, x_router,
+                             xr_dtype, H_router))
+        return rc;
+    if (logits_out)
+        return cuda_check(cudaMemcpyAsync(logits_out, ws + L.logits, sizeof(float) * M * p->num_experts,
+                                          cudaMemcpyDeviceToDevice, s),
+                          "cudaMemcpyAsync(logits)");
+    return K3_OK;
 }
 
 extern "C" K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* x, int x_dtype,

@@ -82,15 +82,18 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     red[warp][g + 8][2 * q + 1] = d[3];
 
     if (a.xp) {
-        // ---- x -> E2M1 pieces: (token, 32-block) tasks spread over every warp of the grid
+        // ---- expert input -> E2M1 pieces: (token, 32-block) tasks over every warp of the grid
+        const void* xe = a.xe ? a.xe : a.x;
+        const int xedt = a.xe ? a.xe_dtype : a.x_dtype;
+        const int64_t He = a.xe ? a.He : a.H;
         const int64_t nw = int64_t(gridDim.x) * gridDim.y * 8;
         const int64_t gw = (int64_t(kq) * gridDim.x + rb) * 8 + warp;
-        const int64_t ng = a.H / 32;
+        const int64_t ng = He / 32;
         for (int64_t task = gw; task < a.M * ng; task += nw) {
             const int t = int(task / ng);
             const int64_t g = task % ng;
-            const float v = load_as_f32(a.x, a.x_dtype, int64_t(t) * a.H + 32 * g + lane);
-            split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (a.H / 2) + 16 * g, a.H / 2,
+            const float v = load_as_f32(xe, xedt, int64_t(t) * He + 32 * g + lane);
+            split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (He / 2) + 16 * g, He / 2,
                          a.xsf + int64_t(kBPieces * t) * ng + g, ng);
         }
     } else {

@@ -7,10 +7,15 @@
 namespace k3 {
 
 struct RouteArgs {
-    const void* x;
+    const void* x;                 // router input [M][H]
     int x_dtype;
     int M;
     int64_t H;
+    // expert input [M][He] for the E2M1 pieces (block-scaled path); null: x itself. A
+    // latent MoE routes on the hidden state and runs its experts on the latent one.
+    const void* xe;
+    int xe_dtype;
+    int64_t He;
     const uint16_t* W;             // router weight, bf16 bits [E][H]
     int64_t E;
     float* logit_part;             // [KQ][M][E] slice partials

@@ -392,6 +392,38 @@ class LatentMoE:
                                    L.stream_of(flat)), "k3_moe_prefill")
         return y, idx, w
 
+    def _latent_fused_ok(self, flat: torch.Tensor) -> bool:
+        return (self.latent and self.fused and self.tiled and self.use_pool and self.block_scaled
+                and flat.shape[0] <= MAX_DECODE_TOKENS and self.pool.scales_tc is not None
+                and flat.shape[1] % 512 == 0)
+
+    def _fused_latent_decode(self, flat: torch.Tensor, h: torch.Tensor, return_router: bool):
+        """Routed experts of a latent MoE for <= 8 tokens in one library call
+        (``k3_moe_decode_latent``): route on the hidden state ``flat``, experts on the
+        latent ``h``. Returns (y_latent fp32, RouterResult or None)."""
+        lib = L.load_library()
+        params = self._params(has_shared=0)       # a shared expert acts on the hidden state
+        M, k, E = flat.shape[0], self.cfg.num_experts_per_token, self.cfg.num_experts
+        dev = flat.device
+        y = torch.empty((M, self.pool.hidden), dtype=torch.float32, device=dev)
+        idx = torch.empty((M, k), dtype=torch.int32, device=dev)
+        w = torch.empty((M, k), dtype=torch.float32, device=dev)
+        logits = torch.empty((M, E), dtype=torch.float32, device=dev) if return_router else None
+        hc = h.contiguous()
+        ws = L.workspace(dev, lib.k3_moe_decode_latent_workspace(params, M, flat.shape[1]))
+        L.check(lib.k3_moe_decode_latent(params, flat.data_ptr(), L.dtype_code(flat), flat.shape[1],
+                                         hc.data_ptr(), L.dtype_code(hc), M, self.gate_w.data_ptr(),
+                                         None if self.gate_b is None else self.gate_b.data_ptr(),
+                                         y.data_ptr(), L.K3_F32, idx.data_ptr(), w.data_ptr(),
+                                         None if logits is None else logits.data_ptr(), ws.data_ptr(),
+                                         ws.numel(), L.stream_of(flat)), "k3_moe_decode_latent")
+        r = None
+        if return_router:
+            raw = torch.sigmoid(logits)
+            cor = raw if self.gate_b is None else raw + self.gate_b
+            r = RouterResult(idx.long(), w, raw, cor)
+        return y, r
+
     def __call__(self, x: torch.Tensor, return_router: bool = False):
         """``moe.py:110-132``: returns y shaped like x (fp32), and the RouterResult if asked."""
         L.require_cuda(x, "x")
@@ -407,17 +439,23 @@ class LatentMoE:
                 return y.reshape(*orig[:-1], y.shape[-1])
             y, _, _ = self._fused_decode(flat)
             return y.reshape(*orig[:-1], y.shape[-1])
-        r = self.route(flat)
-        h = flat if not self.latent else D.matvec([(self.down, flat, None, 0.0)], self.down.shape[0])
-        if self.fused and self.tiled:
-            y = self._experts_decode(h.contiguous(), r.expert_indices, r.expert_weights,
-                                     self._params(has_shared=0))
+        if self._latent_fused_ok(flat):
+            # latent decode: hidden -> latent matvec, then one fused router launch (routing on
+            # the hidden state, E2M1 pieces of the latent) and the block-scaled experts
+            h = D.matvec([(self.down, flat, None, 0.0)], self.down.shape[0])
+            y, r = self._fused_latent_decode(flat, h, return_router)
         else:
-            y = torch.zeros((flat.shape[0], h.shape[1]), dtype=torch.float32, device=x.device)
-            for e in sorted(set(r.expert_indices.reshape(-1).tolist())):
-                tok, slot = (r.expert_indices == e).nonzero(as_tuple=True)
-                y.index_add_(0, tok, self.expert_forward(h[tok].float(), e)
-                             * r.expert_weights[tok, slot, None])
+            r = self.route(flat)
+            h = flat if not self.latent else D.matvec([(self.down, flat, None, 0.0)], self.down.shape[0])
+            if self.fused and self.tiled:
+                y = self._experts_decode(h.contiguous(), r.expert_indices, r.expert_weights,
+                                         self._params(has_shared=0))
+            else:
+                y = torch.zeros((flat.shape[0], h.shape[1]), dtype=torch.float32, device=x.device)
+                for e in sorted(set(r.expert_indices.reshape(-1).tolist())):
+                    tok, slot = (r.expert_indices == e).nonzero(as_tuple=True)
+                    y.index_add_(0, tok, self.expert_forward(h[tok].float(), e)
+                                 * r.expert_weights[tok, slot, None])
         if self.latent:
             # rmsnorm(y) @ up.T (+ the bf16 shared expert's down projection) in one matvec
             segs = [(self.up, y, self.norm_w, float(self.cfg.rms_norm_eps))]
