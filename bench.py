@@ -61,7 +61,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--tokens", type=int, default=8)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per GPU (default: 8 for config 2, 4096 for 3, 1 for 4 and 5)")
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
@@ -72,7 +73,10 @@ def parse():
                          "layer decode (supplementary)")
     ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    if args.tokens is None:
+        args.tokens = {2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
+    return args
 
 
 def measured_peaks():
@@ -263,7 +267,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     cfg = args.config
-    M = 4096 if (cfg == 3 and args.tokens == 8) else (1 if cfg == 4 else args.tokens)
+    M = 1 if cfg == 4 else args.tokens
     n_s, n_w = max(1, min(args.steps, 8)), min(args.warmup, 1)
     budget = 150.0 / (n_s + n_w)
     t0 = time.perf_counter()
@@ -627,7 +631,7 @@ def run_prefill(args, rank, world, local):
     from kimi_k3_mlx_macmini_b200 import synthetic
 
     torch.cuda.set_device(local)
-    T = args.tokens if args.tokens != 8 else 4096
+    T = args.tokens
     K, W = args.steps, args.warmup
     R = 4                                                   # distinct token batches (> L2 together)
     lay = synthetic.baseline_layer(seed=args.seed, E=args.experts, H=H, I=I_, top_k=TOPK, scale=SCALE)
@@ -748,7 +752,7 @@ def run_k3(args, rank, world, local):
             print(json.dumps({"metric": "k3_layer_decode_tokens_per_s", "unavailable": "config 5 runs on one GPU"}))
         return
     torch.cuda.set_device(local)
-    M = args.tokens if args.tokens != 8 else 1
+    M = args.tokens
     K, W = args.steps, args.warmup
     R = min(K + W, 32)
     lay = synthetic.k3_layer(seed=args.seed)
