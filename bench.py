@@ -63,8 +63,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default: 8 for config 2, 4096 for 3, 1 for 4 and 5)")
-    ap.add_argument("--experts", type=int, default=E,
-                    help="routed experts in the layer (384 = BASELINE; fewer only for small ncu captures)")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="routed experts in the layer (default 384 = BASELINE, 896 for config 5; fewer "
+                         "only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
@@ -76,6 +77,8 @@ def parse():
     args = ap.parse_args()
     if args.tokens is None:
         args.tokens = {2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
+    if args.experts is None:
+        args.experts = 896 if args.config == 5 else E
     return args
 
 
@@ -755,9 +758,9 @@ def run_k3(args, rank, world, local):
     M = args.tokens
     K, W = args.steps, args.warmup
     R = min(K + W, 32)
-    lay = synthetic.k3_layer(seed=args.seed)
+    Hk, Lk, Ik, Ek = 7168, 3584, 3072, args.experts
+    lay = synthetic.k3_layer(seed=args.seed, E=Ek)
     moe = lay.moe()
-    Hk, Lk, Ik, Ek = 7168, 3584, 3072, 896
     xs = [synthetic.tokens(args.seed * 7919 + i, M, Hk) for i in range(R)]
     U = [int(torch.unique(moe.route(x).expert_indices).numel()) for x in xs]
     step_x = [(W + i) % R for i in range(K)]
@@ -790,7 +793,7 @@ def run_k3(args, rank, world, local):
         "scaling": "weak", "vs_baseline": None,
         "dtype": "MXFP4 experts (e2m1 x e2m1 pieces, tcgen05 kind::mxf4); bf16 dense weights x fp32 (f32x2 FMA)",
         "data": "synthetic (seeded random-init weights of the Kimi-K3 layer shapes)",
-        "config": {"workload": f"Kimi-K3 MoE layer decode, M={M}: 896 routed MXFP4 experts top-16 (latent 3584, "
+        "config": {"workload": f"Kimi-K3 MoE layer decode, M={M}: {Ek} routed MXFP4 experts top-16 (latent 3584, "
                                "intermediate 3072), bf16 latent projections 7168<->3584, bf16 shared expert "
                                "2x3072x7168, situ, x2.5",
                    "tokens_per_gpu": M, "parallelism": "single GPU",
