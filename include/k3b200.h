@@ -42,7 +42,8 @@ enum {
     K3_ERR_UNSUPPORTED = 2,  /* valid request outside what this build implements */
     K3_ERR_CUDA = 3,         /* a CUDA runtime call failed */
     K3_ERR_WORKSPACE = 4,    /* workspace missing, too small or misaligned */
-    K3_ERR_TIMEOUT = 5       /* a bounded device-side wait gave up */
+    K3_ERR_TIMEOUT = 5,      /* a bounded device-side wait gave up */
+    K3_ERR_IO = 6            /* a file could not be opened or read (reference: OSError) */
 };
 
 enum { K3_F32 = 0, K3_BF16 = 1, K3_F16 = 2 };             /* element types */
@@ -362,6 +363,23 @@ K3_API int k3_dense_status(const void* workspace, void* stream);
 K3_API int k3_lm_head_argmax(const void* h, int h_dtype, int64_t H, const uint16_t* w, int64_t V,
                              int32_t* idx_out, float* val_out, float* logits_out, void* workspace,
                              size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------ checkpoint reads ----- */
+
+/* Byte ranges of one checkpoint file (manifest records: offset, nbytes —
+ * tools/k3_manifest.py:97-156) into host memory with pread on `threads` threads.
+ * Ranges adjacent in the file and in memory are read as one (the reference's one-read
+ * packed + scale pair, air_llm/models/kimi_k3/loader.py:229-266). *bytes_read_out
+ * (optional) = the bytes delivered. K3_ERR_IO on open/read failures, K3_ERR_INVALID for
+ * ranges outside the file. */
+K3_API int k3_file_read_ranges(const char* path, const int64_t* offsets, const int64_t* nbytes, int n,
+                               void* const* dst, int threads, int64_t* bytes_read_out);
+/* The same ranges into device memory through a caller-owned pinned staging buffer
+ * (>= 8 KiB, used as two halves: the read of one half overlaps the host->device copy of
+ * the other on `stream`). Returns after every copy has finished. */
+K3_API int k3_file_read_to_device(const char* path, const int64_t* offsets, const int64_t* nbytes, int n,
+                                  void* const* device_dst, void* pinned_staging, size_t staging_bytes,
+                                  int threads, void* stream);
 
 /* Device status word of the last prefill call on `workspace` (synchronises `stream`):
  * K3_OK, or K3_ERR_TIMEOUT when a kernel's bounded wait gave up. */

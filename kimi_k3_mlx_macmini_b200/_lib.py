@@ -13,7 +13,7 @@ import torch
 
 LIB_PATH = Path(__file__).resolve().with_name("libk3b200.so")
 
-K3_OK, K3_ERR_INVALID, K3_ERR_UNSUPPORTED, K3_ERR_CUDA, K3_ERR_WORKSPACE, K3_ERR_TIMEOUT = range(6)
+K3_OK, K3_ERR_INVALID, K3_ERR_UNSUPPORTED, K3_ERR_CUDA, K3_ERR_WORKSPACE, K3_ERR_TIMEOUT, K3_ERR_IO = range(7)
 K3_F32, K3_BF16, K3_F16 = 0, 1, 2
 K3_ACT_SILU, K3_ACT_SITU = 0, 1
 K3_DENSE_SUM, K3_DENSE_ACT = 0, 1
@@ -93,6 +93,8 @@ SIGNATURES = {
                                _i64, _vp, _sz, _vp]),
     "k3_lm_head_workspace": (_sz, [_i64, _i64]),
     "k3_dense_status": (_i32, [_vp, _vp]),
+    "k3_file_read_ranges": (_i32, [ctypes.c_char_p, _vp, _vp, _i32, _vp, _i32, _vp]),
+    "k3_file_read_to_device": (_i32, [ctypes.c_char_p, _vp, _vp, _i32, _vp, _vp, _sz, _i32, _vp]),
     "k3_lm_head_argmax": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "k3_moe_ep_local_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
     "k3_moe_ep_local": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
@@ -132,6 +134,8 @@ def check(rc: int, what: str) -> None:
         raise ValueError(f"{what}: {msg}")
     if rc == K3_ERR_UNSUPPORTED:
         raise NotImplementedError(f"{what}: {msg}")
+    if rc == K3_ERR_IO:
+        raise OSError(f"{what}: {msg}")
     raise K3Error(f"{what} failed ({rc}): {msg}")
 
 
