@@ -58,11 +58,90 @@ class HostExpertStore:
         return sum(self.tiles[w][0].numel() + self.tc[w][0].numel() for w in WHICH)
 
 
+class DiskExpertStore:
+    """The routed experts of one layer read from the checkpoint on every use: the
+    reference's SSD tier (``air_llm/models/kimi_k3/loader.py:229-266``). An expert's six
+    tensors (packed + scale of w1, w3, w2) are read with as few ``pread`` calls as their
+    manifest records allow (one per run of contiguous tensors: one for the whole expert
+    when the shard stores them back to back) into a pinned host slot, copied to a device
+    slot, and re-laid there into the block-scaled layout (``k3_mxfp4_tiles`` /
+    ``k3_mxfp4_scales_tc``) straight into the streaming slot the kernels read."""
+
+    def __init__(self, src, layer: int, num_experts: int, device="cuda"):
+        self.src, self.layer, self.E = src, layer, num_experts
+        self.device = torch.device(device)
+        self.plan = [self._expert_plan(e) for e in range(num_experts)]
+        self.bytes_read = 0
+        self.host = self.dev = None
+        self.host_free = []
+
+    def _expert_plan(self, e: int):
+        """(reads [(path, file offset, nbytes, host offset)], host bytes, device bytes,
+        parts {(which, kind): (host offset, device offset, nbytes, shape)}) of expert e:
+        the host slot mirrors the file runs, the device slot puts every tensor at a
+        256-byte boundary for the re-layout kernels."""
+        recs = []
+        for w in WHICH:
+            for name in self.src.expert_names(self.layer, e, w):
+                path, off, r = self.src._locate(name)
+                recs.append((path, off, r, w, name.rsplit(".", 1)[1]))
+        recs.sort(key=lambda t: (str(t[0]), t[1]))
+        reads, parts, pos, dpos = [], {}, 0, 0
+        for path, off, r, w, kind in recs:
+            n = r["nbytes"]
+            if reads and reads[-1][0] == path and reads[-1][1] + reads[-1][2] == off:
+                reads[-1] = (path, reads[-1][1], reads[-1][2] + n, reads[-1][3])
+            else:
+                reads.append((path, off, n, pos))
+            parts[(w, kind)] = (pos, dpos, n, tuple(r["shape"]))
+            pos += n
+            dpos += (n + 255) // 256 * 256
+        return reads, pos, dpos, parts
+
+    def nbytes_expert(self) -> int:
+        return max(p[1] for p in self.plan)
+
+    def bind(self, slots: int) -> None:
+        if self.host is None or self.host.shape[0] < slots:
+            self.host = torch.empty((slots, max(p[1] for p in self.plan)), dtype=torch.uint8, pin_memory=True)
+            self.dev = torch.empty((slots, max(p[2] for p in self.plan)), dtype=torch.uint8, device=self.device)
+            self.host_free = [None] * slots
+
+    def stage_one(self, moe: "StreamedMoE", j: int, e: int, stream: torch.cuda.Stream) -> None:
+        """Reads expert e (blocking pread on this thread) and queues its copy and re-layout
+        into streaming slot j on ``stream``; moe.events[j] fires when it is ready."""
+        from .loader import read_ranges
+        self.bind(moe.S)
+        if self.host_free[j] is not None:
+            self.host_free[j].synchronize()                  # the slot's previous copies are done
+        reads, _, _, parts = self.plan[e]
+        base = self.host[j].data_ptr()
+        by_file = {}
+        for path, off, n, pos in reads:
+            by_file.setdefault(path, []).append((off, n, base + pos))
+        for path, rr in by_file.items():
+            self.bytes_read += read_ranges(path, rr, self.src.threads)
+        lib = L.load_library()
+        with torch.cuda.stream(stream):
+            for hp, dp, n, _ in parts.values():
+                self.dev[j, dp:dp + n].copy_(self.host[j, hp:hp + n], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            self.host_free[j] = ev
+            for w in WHICH:
+                (_, dpk, _, (rows, half)), (_, dsc, _, _) = parts[(w, "weight_packed")], parts[(w, "weight_scale")]
+                L.check(lib.k3_mxfp4_tiles(self.dev[j].data_ptr() + dpk, rows, 2 * half, 1,
+                                           moe.tiles[w][j].data_ptr(), stream.cuda_stream), "k3_mxfp4_tiles")
+                L.check(lib.k3_mxfp4_scales_tc(self.dev[j].data_ptr() + dsc, rows, 2 * half, 1,
+                                               moe.tc[w][j].data_ptr(), stream.cuda_stream), "k3_mxfp4_scales_tc")
+            moe.events[j].record(stream)
+
+
 class StreamedMoE:
     """One MoE layer (BASELINE semantics: MXFP4 routed experts in ``store``, resident
     MXFP4 shared expert) whose routed experts are copied to HBM on demand."""
 
-    def __init__(self, cfg, layer: int, w: dict, store: HostExpertStore, shared: Callable, device="cuda"):
+    def __init__(self, cfg, layer: int, w: dict, store, shared: Callable, device="cuda"):
         self.cfg, self.store = cfg, store
         self.device = torch.device(device)
         self.router = LatentMoE(cfg, layer, w, lambda *a: None, fused=True, device=self.device)
@@ -125,7 +204,11 @@ class StreamedMoE:
         experts = sorted(set(ids.reshape(-1).tolist()))
         if len(experts) > self.S:
             raise NotImplementedError(f"{len(experts)} distinct experts exceed the {self.S} staging slots")
-        if stage:
+        # a disk store reads expert j+1 on the host while the GPU runs expert j
+        lazy = stage and hasattr(self.store, "stage_one")
+        if lazy:
+            self.copy_stream.wait_stream(torch.cuda.current_stream(self.device))
+        elif stage:
             self.stage(experts)
         else:
             for j in range(len(experts)):
@@ -147,6 +230,8 @@ class StreamedMoE:
         y, start = None, 0
         counts = [sum(1 for e in flat_ids if e == ex) for ex in experts]
         for j, n in enumerate(counts):
+            if lazy:
+                self.store.stage_one(self, j, experts[j], self.copy_stream)
             cur.wait_event(self.events[j])
             y_j = self._pairs(flat, slot[start:start + n], tok[start:start + n], wts[start:start + n])
             y = y_j if y is None else y + y_j
@@ -154,4 +239,4 @@ class StreamedMoE:
         return (y + y_sh).reshape(x.shape[:-1] + (y.shape[-1],))
 
 
-__all__ = ["HostExpertStore", "StreamedMoE", "SHARED"]
+__all__ = ["HostExpertStore", "DiskExpertStore", "StreamedMoE", "SHARED"]

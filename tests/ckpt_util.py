@@ -45,12 +45,13 @@ def save_safetensors(path: Path, tensors: list) -> None:
             fh.write(b)
 
 
-def make_tiny_k3(out: Path, seed: int = 0, scale_first: bool = False) -> dict:
-    """Writes the checkpoint; returns {name: (array, dtype)} of every tensor written."""
+def make_tiny_k3(out: Path, seed: int = 0, scale_first: bool = False, **dims) -> dict:
+    """Writes the checkpoint; returns {name: (array, dtype)} of every tensor written.
+    ``dims`` overrides TINY's sizes (e.g. 256-wide experts for the tiled kernels)."""
     out = Path(out)
     out.mkdir(parents=True, exist_ok=True)
     rng = np.random.default_rng(seed)
-    c = TINY
+    c = {**TINY, **dims}
     H, Lt, I, E = c["hidden_size"], c["routed_expert_hidden_size"], c["moe_intermediate_size"], c["num_experts"]
 
     def bf(*shape, s=0.05):
