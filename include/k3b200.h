@@ -364,6 +364,17 @@ K3_API int k3_lm_head_argmax(const void* h, int h_dtype, int64_t H, const uint16
                              int32_t* idx_out, float* val_out, float* logits_out, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------ caller step ----- */
+
+/* The MoE input of a Kimi-K3 decoder layer (air_llm/models/kimi_k3/layer.py:120-121):
+ * out [N][H] = post_norm * rmsnorm(apply_attn_res(prefix_sum, block_residual, res_proj,
+ * res_norm)) — a softmax over the n_blocks checkpoints block_residual [N][n_blocks][H]
+ * plus prefix_sum [N][H], each scored by its RMS-normalised dot with res_norm * res_proj
+ * (ops.py:61-74). fp32 inputs and weights; out f32 or bf16; n_blocks <= 16. */
+K3_API int k3_attn_res_norm(const float* prefix_sum, const float* block_residual, int64_t n_blocks, int64_t N,
+                            int64_t H, const float* res_proj, const float* res_norm, const float* post_norm,
+                            float eps, void* out, int out_dtype, void* stream);
+
 /* ------------------------------------------------------ checkpoint reads ----- */
 
 /* Byte ranges of one checkpoint file (manifest records: offset, nbytes —

@@ -93,6 +93,7 @@ SIGNATURES = {
                                _i64, _vp, _sz, _vp]),
     "k3_lm_head_workspace": (_sz, [_i64, _i64]),
     "k3_dense_status": (_i32, [_vp, _vp]),
+    "k3_attn_res_norm": (_i32, [_vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp, _f32, _vp, _i32, _vp]),
     "k3_file_read_ranges": (_i32, [ctypes.c_char_p, _vp, _vp, _i32, _vp, _i32, _vp]),
     "k3_file_read_to_device": (_i32, [ctypes.c_char_p, _vp, _vp, _i32, _vp, _vp, _sz, _i32, _vp]),
     "k3_lm_head_argmax": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),

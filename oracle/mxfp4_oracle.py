@@ -198,6 +198,27 @@ def rmsnorm(x, w, eps: float):
     return (np.asarray(w, dtype=np.float32) * (xf * r.astype(np.float32))).astype(np.float32)
 
 
+def attn_res(prefix_sum, block_residual, proj_w, norm_w, eps: float):
+    """``apply_attn_res`` (``air_llm/models/kimi_k3/ops.py:61-74``, ``k3ref/layers.py:83-96``):
+    a softmax over the block checkpoints plus the running sum, each scored by its
+    RMS-normalised dot with norm_w * proj_w; returns the probability-weighted sum.
+    prefix_sum [N, H], block_residual [N, B, H], proj_w [1, H] or [H], norm_w [H]."""
+    v = np.concatenate([np.asarray(block_residual, np.float32).reshape(len(prefix_sum), -1, prefix_sum.shape[-1]),
+                        np.asarray(prefix_sum, np.float32)[:, None, :]], axis=1)
+    k = v / np.sqrt((v * v).mean(-1, keepdims=True) + eps)
+    sw = np.asarray(norm_w, np.float32) * np.asarray(proj_w, np.float32).reshape(-1)
+    s = (k * sw).sum(-1)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    return (p[..., None] * v).sum(1).astype(np.float32)
+
+
+def moe_input(prefix_sum, block_residual, res_proj, res_norm, post_norm, eps: float):
+    """The MoE input of a decoder layer: rmsnorm(attn_res(...), post_attention_layernorm)
+    (``air_llm/models/kimi_k3/layer.py:120-121``)."""
+    return rmsnorm(attn_res(prefix_sum, block_residual, res_proj, res_norm, eps), post_norm, eps)
+
+
 def activation(g, u, act: str, situ_beta: float = 4.0, situ_linear_beta: Optional[float] = 25.0):
     if act == "silu":
         return silu(g) * u

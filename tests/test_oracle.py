@@ -91,3 +91,20 @@ def test_mini_k3_layer_matches_reference():
     bad, ties = G.index_sets_match(r.expert_indices, g["idx_sorted"], g["corrected"], spec.top_k)
     assert bad == 0 and ties == 0
     assert O.rel_l2(y, g["y"]) < 1e-5
+
+
+@pytest.mark.parametrize("case", ["small", "none", "k3"])
+def test_attn_res_moe_input_matches_reference(case):
+    """The decoder layer's MoE input, rmsnorm(apply_attn_res(...)), against the reference's
+    own torch oracle (``k3ref/layers.py:83-96``) on regenerated inputs (digest-checked)."""
+    g = G.load("attn_res")
+    c = {k: int(g[f"{case}_{k}"]) for k in ("seed", "N", "B", "H")}
+    d = I.attnres_inputs(**c)
+    assert I.digest(d["prefix_sum"], d["block_residual"], d["proj_bf16"], d["res_norm_bf16"],
+                    d["post_norm_bf16"]) == str(g[f"{case}_digest"]), "input regen drift"
+    x = O.attn_res(d["prefix_sum"], d["block_residual"], I.as_f32(d["proj_bf16"]), I.as_f32(d["res_norm_bf16"]),
+                   d["eps"])
+    y = O.moe_input(d["prefix_sum"], d["block_residual"], I.as_f32(d["proj_bf16"]), I.as_f32(d["res_norm_bf16"]),
+                    I.as_f32(d["post_norm_bf16"]), d["eps"])
+    assert O.rel_l2(x, g[f"{case}_attn"]) < 1e-6
+    assert O.rel_l2(y, g[f"{case}_y"]) < 1e-6
