@@ -462,29 +462,41 @@ __global__ void __launch_bounds__(256) prefill_pieces_kernel(const void* __restr
     }
 }
 
-// The gate/up image: one thread per (pair, 16-byte unit u of a row) copies the pair's
-// token pieces of unit u (and their scales) into the image block of its chunk.
+// The gate/up image: one CTA per pair (grid = the candidate bound; CTAs past the plan's
+// pair count leave at once), thread u per 16-byte unit of a row. For each of the np
+// pieces a thread copies its unit into the pair's row of the image block (swizzled
+// position); the lane owning unit 8s of a 256-k step also moves that step's 8 scale bytes
+// as two 4-byte words (their chunk positions for k-blocks 0-3 and 4-7 are contiguous).
+// Every thread of a CTA reads the same plan entries (one broadcast load each).
 __global__ void __launch_bounds__(256) prefill_permute_kernel(const __grid_constant__ PrefillPlan P,
                                                               const uint8_t* __restrict__ xp,
                                                               const uint8_t* __restrict__ xsf, int T, int64_t K,
                                                               int np, uint8_t* __restrict__ img) {
-    const int64_t U = K / 32;
-    const int64_t id = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (id >= int64_t(P.hdr->n_pairs) * U) return;
-    const int pos = int(id / U), u = int(id - int64_t(pos) * U);
+    const int pos = blockIdx.x;
+    if (pos >= P.hdr->n_pairs) return;
+    const int U = int(K / 32);
     const int cj = P.pair_cj[pos];
     const int c = cj >> 8, j = cj & 255;
     const int n8 = (P.ch_n[c] + 7) & ~7;
     const int tok = P.pair_tok[pos];
-    const int s = u >> 3, q = u & 7;
     const int nst = int(K / kBStageK);
-    for (int p = 0; p < np; ++p) {
-        const int64_t row = int64_t(p) * T + tok;
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(xp + row * (K / 2) + 16 * u));
-        uint8_t* blk = img + img_block(P.ch_n8p, c, nst, s, p / kPStack, n8, np / kPStack);
-        const int r = (p % kPStack) * n8 + j;                      // row in the stacked block
-        *reinterpret_cast<uint4*>(blk + kPImgSf + r * 128 + ((q ^ (r & 7)) << 4)) = v;
-        blk[img_sf(r, q)] = __ldg(xsf + row * U + u);
+    const int pairs = np / kPStack;
+    const int64_t cbase = img_block(P.ch_n8p, c, nst, 0, 0, n8, pairs);
+    const int64_t bstride = kPImgSf + 128 * kPStack * int64_t(n8);
+    for (int u = threadIdx.x; u < U; u += blockDim.x) {
+        const int s = u >> 3, q = u & 7;
+        for (int p = 0; p < np; ++p) {
+            const int64_t row = int64_t(p) * T + tok;
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(xp + row * (K / 2) + 16 * u));
+            uint8_t* blk = img + cbase + int64_t(s * pairs + p / kPStack) * bstride;
+            const int r = (p % kPStack) * n8 + j;                  // row in the stacked block
+            *reinterpret_cast<uint4*>(blk + kPImgSf + r * 128 + ((q ^ (r & 7)) << 4)) = v;
+            if (q == 0) {
+                const uint2 sc = __ldg(reinterpret_cast<const uint2*>(xsf + row * U + 8 * s));
+                *reinterpret_cast<uint32_t*>(blk + img_sf(r, 0)) = sc.x;
+                *reinterpret_cast<uint32_t*>(blk + img_sf(r, 4)) = sc.y;
+            }
+        }
     }
 }
 
@@ -1000,8 +1012,8 @@ int prefill_run(const k3_moe_params* p, const void* x, int xdt, int64_t T, const
             prefill_pieces_kernel<kPPieces>
                 <<<int((n + 255) / 256), 256, 0, s>>>(x, xdt, int(T), L.H, ws + L.xp, ws + L.xsf);
         K3_CHECK_LAUNCH("prefill_pieces_kernel");
-        const int64_t m = int64_t(n_cand) * (L.H / 32);
-        prefill_permute_kernel<<<int((m + 255) / 256), 256, 0, s>>>(
+        const int U = int(L.H / 32);                      // a multiple of 8 (H % 256 == 0)
+        prefill_permute_kernel<<<n_cand, std::min(U, 256), 0, s>>>(
             P, ws + L.xp, ws + L.xsf, int(T), L.H, xdt == K3_F32 ? kPPiecesF32 : kPPieces, ws + L.img_gu);
         K3_CHECK_LAUNCH("prefill_permute_kernel");
     }
