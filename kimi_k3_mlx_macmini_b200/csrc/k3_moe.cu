@@ -699,7 +699,7 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms, int64_t H
             if (((L.E + 15) / 16) * c >= sms) break;
         }
         L.logit_part = carve(off, sizeof(float) * L.KQ * M * L.E);
-        L.route_done = carve(off, sizeof(unsigned) * (1 + (L.E + 15) / 16));
+        L.route_done = carve(off, sizeof(unsigned) * (2 + (L.E + 15) / 16));   // + piece-task counter
         L.act_hi = carve(off, size_t(L.U) * kBMaxN * (L.I / 2));        // act pieces
         L.act_ts = carve(off, size_t(L.U) * (L.I / 128) * kBChunk);
         L.partA = carve(off, sizeof(float) * L.U * (L.I / kBRows) * L.CA * 2 * kMaxTok * kBRows);
@@ -730,7 +730,7 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms, int64_t H
             if (((L.E + 15) / 16) * c >= sms) break;
         }
         L.logit_part = carve(off, sizeof(float) * L.KQ * M * L.E);
-        L.route_done = carve(off, sizeof(unsigned) * (1 + (L.E + 15) / 16));
+        L.route_done = carve(off, sizeof(unsigned) * (2 + (L.E + 15) / 16));   // + piece-task counter
         L.act_hi = carve(off, sizeof(__half) * L.ppad * L.I);
         L.act_lo = carve(off, sizeof(__half) * L.ppad * L.I);
         L.act_ts = carve(off, sizeof(float) * L.ppad * L.tspad);
@@ -1052,7 +1052,7 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
         ra.xsf = L.bs ? ws + L.xq_ts : nullptr;
         ra.plan_args = pl;
         ra.plan = plan;
-        if (int rc2 = cuda_check(cudaMemsetAsync(ra.done, 0, sizeof(unsigned) * (1 + (L.E + 15) / 16), s),
+        if (int rc2 = cuda_check(cudaMemsetAsync(ra.done, 0, sizeof(unsigned) * (2 + (L.E + 15) / 16), s),
                                  "route counters"))
             return rc2;
         prof_begin(K3_PROF_ROUTER, s);

@@ -98,67 +98,88 @@ __device__ inline void topk_row(const float* __restrict__ lrow, const float* __r
     __syncwarp();
 }
 
-// Whole-CTA top-k of M token rows with compact (rolled) loops: the code runs once per
-// call in one CTA, so its instruction footprint, not its arithmetic, sets its time.
-// s_key: shared scratch of M * E words. raw = sigmoid(logit), corrected = raw + bias;
-// per token (warp t) k rounds of argmax on (corrected desc, index asc); weights are the
-// raw scores of the winners, renormalised and scaled as topk_row does.
+// One warp per token row: the row's scores live in registers (lane l holds experts
+// l, l+32, ...; NE = ceil(E/32) slots), loaded with one round trip; k rounds of argmax on
+// (corrected desc, index asc) retire the winners and pick up their raw scores from the
+// owning lane; the weights are those raw scores, renormalised (sum in selection order)
+// and scaled as topk_row does.
+template <int NE>
+__device__ __noinline__ void topk_warp_regs(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
+                                            int k, int renorm, float scale, int32_t* __restrict__ idx_out,
+                                            float* __restrict__ w_out, int lane, int* status) {
+    float raw[NE];
+    uint32_t key[NE];
+#pragma unroll
+    for (int i = 0; i < NE; ++i) {
+        const int e = lane + 32 * i;
+        raw[i] = e < E ? __ldcg(lrow + e) : 0.0f;             // logits from other CTAs
+        key[i] = (bias && e < E) ? __float_as_uint(__ldg(bias + e)) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < NE; ++i) {
+        const int e = lane + 32 * i;
+        const float r = 1.0f / (1.0f + expf(-raw[i]));
+        const float c = r + __uint_as_float(key[i]);
+        raw[i] = r;
+        key[i] = e < E ? order_key(c) : 0u;
+    }
+    int mine = -1;
+    float wmine = 0.0f;
+#pragma unroll 1
+    for (int s = 0; s < k; ++s) {
+        uint32_t best = 0u;
+        int bi = 0;
+#pragma unroll
+        for (int i = 0; i < NE; ++i)
+            if (key[i] > best) {                              // strict: lowest index wins ties
+                best = key[i];
+                bi = i;
+            }
+        const uint32_t kmax = redux_max_u32(best);
+        uint32_t e = redux_min_u32(best == kmax ? uint32_t(lane + 32 * bi) : 0xffffffffu);
+        if (kmax == 0u) {                                     // only NaN / exhausted rows
+            if (lane == 0) atomicExch(status, K3_ERR_INVALID);
+            e = 0;
+        }
+        float rw = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NE; ++i)
+            if (lane + 32 * i == int(e)) {
+                key[i] = 0u;                                  // retired
+                rw = raw[i];
+            }
+        const float w = __shfl_sync(0xffffffffu, rw, int(e) & 31);
+        if (lane == s) {
+            mine = int(e);
+            wmine = w;
+        }
+    }
+    float sum = 0.0f;
+#pragma unroll 1
+    for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, wmine, s);
+    if (lane < k) {
+        idx_out[lane] = mine;
+        w_out[lane] = ((k > 1 && renorm) ? wmine / (sum + 1e-20f) : wmine) * scale;
+    }
+}
+
+// Whole-CTA top-k of M token rows: warp t handles token t (M <= 8 warps of the CTA).
+// s_key (shared scratch of M * E words) is unused; kept for the launch's shared-memory
+// contract.
 __device__ inline void topk_cta(const float* __restrict__ logits, const float* __restrict__ bias, int M,
                                 int E, int k, int renorm, float scale, int32_t* __restrict__ idx_out,
                                 float* __restrict__ w_out, uint32_t* s_key, int warp, int lane, int* status) {
-    // eight loads in flight per thread per pass (the logits come from other CTAs)
-#pragma unroll 1
-    for (int i0 = threadIdx.x; i0 < M * E; i0 += 8 * blockDim.x) {
-        float l[8], b[8];
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-            const int i = min(i0 + h * int(blockDim.x), M * E - 1);
-            l[h] = __ldcg(logits + i);
-            b[h] = bias ? __ldg(bias + i % E) : 0.0f;
-        }
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-            const int i = i0 + h * int(blockDim.x);
-            if (i < M * E) s_key[i] = order_key(1.0f / (1.0f + expf(-l[h])) + b[h]);
-        }
-    }
-    __syncthreads();
-    if (warp < M) {
-        uint32_t* row = s_key + warp * E;
-        int mine = -1;                                        // lane s < k: index of round s
-#pragma unroll 1
-        for (int s = 0; s < k; ++s) {
-            uint32_t best = 0u;
-            int bi = 0;
-#pragma unroll 1
-            for (int e = lane; e < E; e += 32) {
-                const uint32_t v = row[e];
-                if (v > best) {                               // strict: lowest index wins ties
-                    best = v;
-                    bi = e;
-                }
-            }
-            const uint32_t kmax = redux_max_u32(best);
-            uint32_t e = redux_min_u32(best == kmax ? uint32_t(bi) : 0xffffffffu);
-            if (kmax == 0u) {                                 // only NaN / exhausted rows
-                if (lane == 0) atomicExch(status, K3_ERR_INVALID);
-                e = 0;
-            }
-            if (lane == 0) row[e] = 0u;                       // retired
-            if (lane == s) mine = int(e);
-            __syncwarp();
-        }
-        // weights: raw scores of the winners, summed in selection order
-        float w = 0.0f;
-        if (lane < k) w = 1.0f / (1.0f + expf(-__ldcg(logits + int64_t(warp) * E + mine)));
-        float sum = 0.0f;
-#pragma unroll 1
-        for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, w, s);
-        if (lane < k) {
-            idx_out[warp * k + lane] = mine;
-            w_out[warp * k + lane] = ((k > 1 && renorm) ? w / (sum + 1e-20f) : w) * scale;
-        }
-    }
+    (void)s_key;
+    if (warp >= M) return;
+    const float* lrow = logits + int64_t(warp) * E;
+    int32_t* io = idx_out + warp * k;
+    float* wo = w_out + warp * k;
+    if (E <= 128) topk_warp_regs<4>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+    else if (E <= 256) topk_warp_regs<8>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+    else if (E <= 384) topk_warp_regs<12>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+    else if (E <= 512) topk_warp_regs<16>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+    else if (E <= 768) topk_warp_regs<24>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+    else topk_warp_regs<32>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
 }
 
 // The routing part of a decode call.

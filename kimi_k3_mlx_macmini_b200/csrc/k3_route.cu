@@ -81,27 +81,38 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     red[warp][g + 8][2 * q] = d[2];
     red[warp][g + 8][2 * q + 1] = d[3];
 
-    if (a.xp) {
-        // ---- expert input -> E2M1 pieces: (token, 32-block) tasks over every warp of the grid
-        const void* xe = a.xe ? a.xe : a.x;
-        const int xedt = a.xe ? a.xe_dtype : a.x_dtype;
-        const int64_t He = a.xe ? a.He : a.H;
-        const int64_t nw = int64_t(gridDim.x) * gridDim.y * 8;
-        const int64_t gw = (int64_t(kq) * gridDim.x + rb) * 8 + warp;
-        const int64_t ng = He / 32;
-        for (int64_t task = gw; task < a.M * ng; task += nw) {
-            const int t = int(task / ng);
-            const int64_t g = task % ng;
-            const float v = load_as_f32(xe, xedt, int64_t(t) * He + 32 * g + lane);
-            split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (He / 2) + 16 * g, He / 2,
-                         a.xsf + int64_t(kBPieces * t) * ng + g, ng);
+    // ---- expert input -> pieces, off the router's critical path: every CTA but the one that
+    // ends up running the top-k and plan claims (token, 32-block) tasks in batches of 4 from
+    // a counter after its last duty in the logits -> top-k chain (the next kernels read the
+    // pieces only after this launch completes)
+    auto do_pieces = [&]() {
+        if (a.xp) {
+            const void* xe = a.xe ? a.xe : a.x;
+            const int xedt = a.xe ? a.xe_dtype : a.x_dtype;
+            const int64_t He = a.xe ? a.He : a.H;
+            const int64_t ng = He / 32;
+            const int64_t ntask = a.M * ng;
+            unsigned* claim = a.done + 1 + gridDim.x;
+            for (;;) {
+                unsigned t0 = 0;
+                if (lane == 0) t0 = atomicAdd(claim, 4u);
+                t0 = __shfl_sync(0xffffffffu, t0, 0);
+                if (int64_t(t0) >= ntask) break;
+                for (int64_t task = t0; task < int64_t(t0) + 4 && task < ntask; ++task) {
+                    const int t = int(task / ng);
+                    const int64_t g = task % ng;
+                    const float v = load_as_f32(xe, xedt, int64_t(t) * He + 32 * g + lane);
+                    split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (He / 2) + 16 * g, He / 2,
+                                 a.xsf + int64_t(kBPieces * t) * ng + g, ng);
+                }
+            }
+        } else {
+            // ---- x -> f16 pieces: the CTAs of the first row blocks split the slice's 512-blocks
+            const int64_t nb = slice / 512, b0 = int64_t(kq) * nb;
+            for (int64_t j = rb; j < nb; j += gridDim.x)
+                convert_block(a.x, a.x_dtype, a.M, a.H, warp, b0 + j, a.xq_hi, a.xq_lo, a.xq_ts, lane);
         }
-    } else {
-        // ---- x -> f16 pieces: the CTAs of the first row blocks split the slice's 512-blocks
-        const int64_t nb = slice / 512, b0 = int64_t(kq) * nb;
-        for (int64_t j = rb; j < nb; j += gridDim.x)
-            convert_block(a.x, a.x_dtype, a.M, a.H, warp, b0 + j, a.xq_hi, a.xq_lo, a.xq_ts, lane);
-    }
+    };
     __syncthreads();
     const int64_t n_rb = gridDim.x;
     if (threadIdx.x < 16 * kMaxTok) {
@@ -117,7 +128,10 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     // ---- the last slice CTA of this row block sums the slices (in slice order)
     if (threadIdx.x == 0) s_last = (atomicAdd(a.done + 1 + rb, 1u) + 1 == gridDim.y);
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        do_pieces();
+        return;
+    }
     __threadfence();
     if (threadIdx.x < 16 * kMaxTok) {
         const int r = threadIdx.x / kMaxTok, t = threadIdx.x % kMaxTok;
@@ -141,10 +155,14 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     // ---- the last row block: top-k and plan
     if (threadIdx.x == 0) s_last = (atomicAdd(a.done, 1u) + 1 == unsigned(n_rb));
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        do_pieces();
+        return;
+    }
     __threadfence();
     extern __shared__ uint32_t s_key[];                      // M * E top-k keys
     build_plan_cta(a.plan_args, a.logits, warp, lane, s_key);
+    do_pieces();                                             // whatever the others left
 }
 
 int launch_route_fused(const RouteArgs& a, int kq, cudaStream_t s) {

@@ -20,7 +20,8 @@ struct RouteArgs {
     int64_t E;
     float* logit_part;             // [KQ][M][E] slice partials
     float* logits;                 // [M][E]
-    unsigned* done;                // arrival counters [1 + row blocks], zeroed before each launch
+    unsigned* done;                // arrival counters [1 + row blocks] and the piece-task counter,
+                                   // zeroed before each launch
     __half* xq_hi;                 // blocked x pieces [H/32][8][32]
     __half* xq_lo;                 // null for bf16 x
     float* xq_ts;                  // [8][H/512]
