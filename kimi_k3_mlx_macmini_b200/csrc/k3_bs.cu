@@ -89,7 +89,12 @@ __global__ void __launch_bounds__(kBThreads, 1)
         mbar_init(drain, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    // the next launch (down, or the combine) may start its prologue (barriers, TMEM, plan
+    // copy) now; it waits for this launch before reading anything it writes
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     if (warp == 1) tmem_alloc(&s_tmem, kCols);
+    // the plan was written two launches back (router / plan kernel, then the scale-chunk
+    // gather), which had completed when the previous launch started
     for (int i = threadIdx.x; i < int(sizeof(Plan) / 4); i += blockDim.x)
         reinterpret_cast<int*>(&s_plan)[i] = reinterpret_cast<const int*>(a.plan)[i];
     tc_fence_before();
@@ -115,6 +120,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint64_t stream_once = l2_evict_first();
+            // The B operand (token or activation pieces and their scale chunks) comes from
+            // the previous launch, which may still be running (programmatic dependent
+            // launch): wait for it before the first request.
+            asm volatile("griddepcontrol.wait;\n" ::: "memory");
             uint32_t gs = 0;
             for (int64_t i = i0; i < i1 && !s_abort; ++i) {
                 const int64_t key = i / ipk;
@@ -148,6 +157,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
                             tma_3d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), r0, slot, &full[si],
                                         stream_once);
                         bulk_g2s_hint(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si], stream_once);
+                    }
+                    if (GATEUP) {
                         for (int pi = 0; pi < np; ++pi)      // one token's 8 piece rows per pair
                             tma_2d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * P->pair_tok[ps + pi],
                                    &full[si]);
@@ -370,6 +381,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
 // piece row, gathered from the per-row scales xsf [8T][K/32]. One thread per 4-byte word.
 __global__ void gather_sfb_kernel(const Plan* __restrict__ plan, const uint8_t* __restrict__ xsf, int64_t K,
                                   uint8_t* __restrict__ sfb) {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");   // the gate/up launch may start
     const int v = blockIdx.y;
     if (v >= plan->n_active) return;
     const int ps = plan->pair_start[v], np = plan->pair_start[v + 1] - ps;
@@ -418,6 +430,7 @@ __global__ void combine_kernel(const Plan* __restrict__ plan, const float* __res
         if (lane == 0) s_n = cnt;
     }
     __syncthreads();
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");     // y_pair comes from the down launch
     const int64_t h4 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
     if (h4 >= H) return;
     float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -446,9 +459,7 @@ __global__ void combine_kernel(const Plan* __restrict__ plan, const float* __res
 int launch_combine(const Plan* plan, const float* y_pair, int64_t H, int M, void* y, int y_dtype,
                    cudaStream_t s) {
     const dim3 grid(unsigned((H / 4 + 127) / 128), unsigned(M));
-    combine_kernel<<<grid, 128, 0, s>>>(plan, y_pair, H, y, y_dtype);
-    K3_CHECK_LAUNCH("combine_kernel");
-    return K3_OK;
+    return cuda_check(launch_pdl(combine_kernel, grid, dim3(128), 0, s, plan, y_pair, H, y, y_dtype), "combine_kernel");
 }
 
 // ---------------------------------------------------------------- scale layout
@@ -524,8 +535,9 @@ int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const
             return rc;
         configured = true;
     }
-    bs_gemv_kernel<G><<<grid, kBThreads, smem, s>>>(maps, a);
-    K3_CHECK_LAUNCH(what);
+    if (int rc = cuda_check(launch_pdl(bs_gemv_kernel<G>, dim3(unsigned(grid)), dim3(kBThreads), smem, s, maps, a),
+                            what))
+        return rc;
     return K3_OK;
 }
 
