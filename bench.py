@@ -270,6 +270,11 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     cfg = args.config
+    if cfg == 5:
+        print(json.dumps({"impl": "reference", "metric": "k3_layer_decode_tokens_per_s",
+                          "unavailable": "config 5 is supplementary (not a BASELINE config); the CPU reference "
+                                         "arm is timed on configs 2-4"}))
+        return
     M = 1 if cfg == 4 else args.tokens
     n_s, n_w = max(1, min(args.steps, 8)), min(args.warmup, 1)
     budget = 150.0 / (n_s + n_w)
