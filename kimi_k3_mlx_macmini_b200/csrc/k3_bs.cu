@@ -381,7 +381,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
 // piece row, gathered from the per-row scales xsf [8T][K/32]. One thread per 4-byte word.
 __global__ void gather_sfb_kernel(const Plan* __restrict__ plan, const uint8_t* __restrict__ xsf, int64_t K,
                                   uint8_t* __restrict__ sfb) {
-    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");   // the gate/up launch may start
+    // launched as a programmatic dependent of the route launch: wait for its plan and scales,
+    // then let the gate/up launch start (it copies the plan before its own wait)
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int v = blockIdx.y;
     if (v >= plan->n_active) return;
     const int ps = plan->pair_start[v], np = plan->pair_start[v + 1] - ps;
@@ -400,8 +403,9 @@ __global__ void gather_sfb_kernel(const Plan* __restrict__ plan, const uint8_t* 
 int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
                       cudaStream_t s) {
     const dim3 grid(unsigned((K / 128 * kBMaxN + 255) / 256), unsigned(max_items));
-    gather_sfb_kernel<<<grid, 256, 0, s>>>(plan, xsf, K, sfb);
-    K3_CHECK_LAUNCH("gather_sfb_kernel");
+    if (int rc = cuda_check(launch_pdl(gather_sfb_kernel, grid, dim3(256), 0, s, plan, xsf, K, sfb),
+                            "gather_sfb_kernel"))
+        return rc;
     return K3_OK;
 }
 

@@ -7,9 +7,11 @@
 namespace k3 {
 
 // Orderable 32-bit key of a float (unsigned order == float order; -0 keys as +0). NaN
-// keys as 0, below every number, so it is never selected.
+// keys as 1, below every number (-inf keys as 0x007fffff), so a row is taken from its
+// NaN entries (lowest index first, the call flagged invalid) only when it has fewer than
+// k numbers; 0 marks retired and padding slots.
 __device__ __forceinline__ uint32_t order_key(float f) {
-    if (f != f) return 0u;
+    if (f != f) return 1u;
     const uint32_t b = __float_as_uint(f == 0.0f ? 0.0f : f);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
@@ -71,9 +73,9 @@ __device__ inline void topk_row(const float* __restrict__ lrow, const float* __r
         const uint32_t kmax = redux_max_u32(best);
         const uint32_t cand = (best == kmax) ? uint32_t(lane + 32 * bi) : 0xffffffffu;
         uint32_t e = redux_min_u32(cand);
-        if (kmax == 0u) {                                  // only NaN / exhausted rows get here
+        if (kmax <= 1u) {                                  // only NaN (1) / exhausted (0) rows
             if (lane == 0) atomicExch(status, K3_ERR_INVALID);
-            e = 0;
+            if (kmax == 0u) e = 0;
         }
         float mine = 0.0f;
 #pragma unroll
@@ -137,9 +139,9 @@ __device__ __noinline__ void topk_warp_regs(const float* __restrict__ lrow, cons
             }
         const uint32_t kmax = redux_max_u32(best);
         uint32_t e = redux_min_u32(best == kmax ? uint32_t(lane + 32 * bi) : 0xffffffffu);
-        if (kmax == 0u) {                                     // only NaN / exhausted rows
+        if (kmax <= 1u) {                                     // only NaN (1) / exhausted (0) rows
             if (lane == 0) atomicExch(status, K3_ERR_INVALID);
-            e = 0;
+            if (kmax == 0u) e = 0;
         }
         float rw = 0.0f;
 #pragma unroll
@@ -163,23 +165,144 @@ __device__ __noinline__ void topk_warp_regs(const float* __restrict__ lrow, cons
     }
 }
 
-// Whole-CTA top-k of M token rows: warp t handles token t (M <= 8 warps of the CTA).
-// s_key (shared scratch of M * E words) is unused; kept for the launch's shared-memory
-// contract.
+// Top-k of one token row by one warp, from keys the CTA staged in shared memory (row[e] =
+// order_key(sigmoid(logit) + bias), 1 for NaN). The selection is that of k rounds of argmax
+// on (key desc, index asc), found without the rounds' serial chains: T, the k-th largest
+// key, by a bitwise search on counts (keys >= candidate; lane l holds keys l, l+32, ... in
+// NE registers, so each step is NE independent compares and one warp reduction, over only
+// the bits below the common prefix of the row's largest and smallest key); then one pass in
+// index order takes the keys above T and the lowest-index keys equal to T; then each winner's
+// rank by counting. Weights are the winners' raw scores, renormalised (sum in rank order) and
+// scaled as topk_row does. For wide routers (E > 512) this beats k argmax rounds over 24-32
+// registers per lane; up to 512 experts the rounds are faster.
+template <int NE>
+__device__ __noinline__ void topk_warp_count(const uint32_t* row, const float* __restrict__ lrow, int E, int k,
+                                             int renorm, float scale, int32_t* __restrict__ idx_out,
+                                             float* __restrict__ w_out, int* cand_e, uint32_t* cand_k,
+                                             int lane, int* status) {
+    uint32_t key[NE];
+    uint32_t hi = 0u, lo = 0xffffffffu;
+#pragma unroll
+    for (int s = 0; s < NE; ++s) {
+        const int e = lane + 32 * s;
+        key[s] = e < E ? row[e] : 0u;
+        hi = max(hi, key[s]);
+        lo = e < E ? min(lo, key[s]) : lo;
+    }
+    hi = redux_max_u32(hi);
+    lo = redux_min_u32(lo);
+    // every key shares hi's bits above the highest bit where hi and lo differ
+    const uint32_t diff = hi ^ lo;
+    const int nbits = diff ? 32 - __clz(int(diff)) : 0;
+    uint32_t T = nbits == 32 ? 0u : (hi & ~((1u << nbits) - 1u));
+    int n_gt = 0;
+#pragma unroll 1
+    for (int it = 0; it <= nbits; ++it) {
+        // steps 0..nbits-1 try the next bit of T; the last counts the keys above T
+        const uint32_t cand = it < nbits ? (T | (1u << (nbits - 1 - it))) : T + 1u;
+        uint32_t c = 0;
+#pragma unroll
+        for (int s = 0; s < NE; ++s) c += key[s] >= cand ? 1u : 0u;
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (it < nbits) {
+            if (c >= uint32_t(k)) T = cand;
+        } else {
+            n_gt = int(c);
+        }
+    }
+    if (T <= 1u && lane == 0) atomicExch(status, K3_ERR_INVALID);   // fewer than k non-NaN scores
+    // the winners in index order: every key above T, then keys equal to T up to k
+    const uint32_t lt = (1u << lane) - 1u;
+    int taken = 0, quota = k - n_gt;
+    uint32_t v = lane < E ? row[lane] : 0u;
+#pragma unroll 1
+    for (int e0 = 0; e0 < E && taken < k; e0 += 32) {
+        const int e = e0 + lane;
+        const uint32_t cur = v;
+        v = e + 32 < E ? row[e + 32] : 0u;                       // next chunk in flight
+        const bool eq = e < E && cur == T;
+        const uint32_t be = __ballot_sync(0xffffffffu, eq);
+        const bool take = (e < E && cur > T) || (eq && __popc(be & lt) < quota);
+        const uint32_t bt = __ballot_sync(0xffffffffu, take);
+        if (take) {
+            const int at = taken + __popc(bt & lt);
+            cand_e[at] = e;
+            cand_k[at] = cur;
+        }
+        taken += __popc(bt);
+        quota -= min(__popc(be), quota);
+    }
+    __syncwarp();
+    // rank of each winner on (key desc, index asc), then the outputs in rank order
+    const int ej = lane < k ? cand_e[lane] : 0;
+    const uint32_t kj = lane < k ? cand_k[lane] : 0u;
+    int rank = 0;
+#pragma unroll 1
+    for (int i = 0; i < k; ++i) {
+        const uint32_t ki = __shfl_sync(0xffffffffu, kj, i);
+        const int ei = __shfl_sync(0xffffffffu, ej, i);
+        rank += (ki > kj || (ki == kj && ei < ej)) ? 1 : 0;
+    }
+    __syncwarp();
+    if (lane < k) cand_e[rank] = ej;
+    __syncwarp();
+    const int mine = lane < k ? cand_e[lane] : 0;
+    const float w = lane < k ? 1.0f / (1.0f + expf(-__ldcg(lrow + mine))) : 0.0f;
+    float sum = 0.0f;
+#pragma unroll 1
+    for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, w, s);
+    if (lane < k) {
+        idx_out[lane] = mine;
+        w_out[lane] = ((k > 1 && renorm) ? w / (sum + 1e-20f) : w) * scale;
+    }
+}
+
+// Whole-CTA top-k of M token rows (M <= 8), warp t selecting token t's k experts. Up to
+// E = 512 the warp holds its row in registers and runs k argmax rounds; wider rows are
+// first staged as keys in s_key by every thread (M * E words of shared scratch; eight
+// logit loads in flight per thread per pass, the logits coming from other CTAs) for the
+// counting search.
 __device__ inline void topk_cta(const float* __restrict__ logits, const float* __restrict__ bias, int M,
                                 int E, int k, int renorm, float scale, int32_t* __restrict__ idx_out,
                                 float* __restrict__ w_out, uint32_t* s_key, int warp, int lane, int* status) {
-    (void)s_key;
+    __shared__ int cand_e[kMaxTok][kMaxTopK];
+    __shared__ uint32_t cand_k[kMaxTok][kMaxTopK];
+    if (E <= 512) {
+        if (warp >= M) return;
+        const float* lrow = logits + int64_t(warp) * E;
+        int32_t* io = idx_out + warp * k;
+        float* wo = w_out + warp * k;
+        if (E <= 128) topk_warp_regs<4>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+        else if (E <= 256) topk_warp_regs<8>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+        else if (E <= 384) topk_warp_regs<12>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+        else topk_warp_regs<16>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+        return;
+    }
+#pragma unroll 1
+    for (int i0 = threadIdx.x; i0 < M * E; i0 += 8 * blockDim.x) {
+        float l[8], b[8];
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int i = min(i0 + h * int(blockDim.x), M * E - 1);
+            l[h] = __ldcg(logits + i);
+            b[h] = bias ? __ldg(bias + i % E) : 0.0f;
+        }
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int i = i0 + h * int(blockDim.x);
+            if (i < M * E) s_key[i] = order_key(1.0f / (1.0f + expf(-l[h])) + b[h]);
+        }
+    }
+    __syncthreads();
     if (warp >= M) return;
+    const uint32_t* row = s_key + warp * E;
     const float* lrow = logits + int64_t(warp) * E;
     int32_t* io = idx_out + warp * k;
     float* wo = w_out + warp * k;
-    if (E <= 128) topk_warp_regs<4>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-    else if (E <= 256) topk_warp_regs<8>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-    else if (E <= 384) topk_warp_regs<12>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-    else if (E <= 512) topk_warp_regs<16>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-    else if (E <= 768) topk_warp_regs<24>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-    else topk_warp_regs<32>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+    int* ce = cand_e[warp];
+    uint32_t* ck = cand_k[warp];
+    if (E <= 768) topk_warp_count<24>(row, lrow, E, k, renorm, scale, io, wo, ce, ck, lane, status);
+    else topk_warp_count<32>(row, lrow, E, k, renorm, scale, io, wo, ce, ck, lane, status);
 }
 
 // The routing part of a decode call.
@@ -203,6 +326,10 @@ struct PlanArgs {
 // (token, weight) pairs in ascending token order, the shared expert last. Every routing
 // entry finds its expert's slot and its rank among the same expert's earlier entries in
 // parallel.
+// kSharedKeys: the top-k stages its keys in s_key (M * E words of shared scratch) and runs
+// topk_cta; otherwise warp t runs topk_row on token t. A compile-time choice, so a kernel
+// carries the registers of only the form it uses.
+template <bool kSharedKeys = false>
 __device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, int warp, int lane,
                                       uint32_t* s_key = nullptr) {
     Plan* P = a.plan;
@@ -219,12 +346,14 @@ __device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, in
     for (int i = threadIdx.x; i < kMaxExperts / 32; i += blockDim.x) bitmap[i] = 0;
     for (int i = threadIdx.x; i < kMaxActive; i += blockDim.x) cnt[i] = 0;
     __syncthreads();
-    if (logits && s_key) {
-        topk_cta(logits, a.bias, a.M, a.E, a.k, a.renorm, a.scale, a.idx, a.w, s_key, warp, lane,
-                 &P->status);
-    } else if (logits && warp < a.M) {
-        topk_row(logits + int64_t(warp) * a.E, a.bias, a.E, a.k, a.renorm, a.scale,
-                 a.idx + warp * a.k, a.w + warp * a.k, nullptr, nullptr, lane, &P->status);
+    if constexpr (kSharedKeys) {
+        if (logits)
+            topk_cta(logits, a.bias, a.M, a.E, a.k, a.renorm, a.scale, a.idx, a.w, s_key, warp, lane,
+                     &P->status);
+    } else {
+        if (logits && warp < a.M)
+            topk_row(logits + int64_t(warp) * a.E, a.bias, a.E, a.k, a.renorm, a.scale,
+                     a.idx + warp * a.k, a.w + warp * a.k, nullptr, nullptr, lane, &P->status);
     }
     __syncthreads();                               // top-k results visible
     const int nsel = a.M * a.k;

@@ -34,6 +34,9 @@ template <bool XF32>
 __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     __shared__ float red[8][16][kMaxTok];
     __shared__ int s_last;
+    // the next launch (the scale gather, a programmatic dependent that waits for this grid
+    // before reading anything) may be scheduled as soon as every CTA here is resident
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
     const int rb = blockIdx.x, kq = blockIdx.y;
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     }
     __threadfence();
     extern __shared__ uint32_t s_key[];                      // M * E top-k keys
-    build_plan_cta(a.plan_args, a.logits, warp, lane, s_key);
+    build_plan_cta<true>(a.plan_args, a.logits, warp, lane, s_key);
     do_pieces();                                             // whatever the others left
 }
 
