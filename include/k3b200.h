@@ -49,6 +49,7 @@ enum {
 enum { K3_F32 = 0, K3_BF16 = 1, K3_F16 = 2 };             /* element types */
 enum { K3_ACT_SILU = 0, K3_ACT_SITU = 1 };                 /* expert activation */
 
+/* 3: k3_dense_seg gained act_input. */
 K3_API int k3_abi_version(void);
 K3_API const char* k3_last_error(void);
 /* Number of streaming multiprocessors of the current device (grid sizing / tests). */
@@ -323,7 +324,10 @@ K3_API int k3_moe_decode_latent(const k3_moe_params* p, const void* x_router, in
  * One segment is out += X W^T with W bf16 [N][K] (row stride ldw elements, 16-byte
  * aligned, K and ldw multiples of 8) and X [M][K] f32 or bf16 (row stride ldx). With
  * norm_w set, X is first replaced by norm_w * X * rsqrt(mean(X^2) + eps) per row
- * (ops.rmsnorm, ops.py:11-14). */
+ * (ops.rmsnorm, ops.py:11-14). With act_input set, each input row holds [gate | up]
+ * (2K values, ldx >= 2K) and X = act(gate, up) with the call's activation, formed as the
+ * input is staged (the bf16 shared expert's act(x Wg^T, x Wu^T), moe.py:105-107, fed to
+ * its down projection); act_input excludes norm_w and K3_DENSE_ACT. */
 typedef struct k3_dense_seg {
     const uint16_t* w;
     int64_t ldw;
@@ -333,6 +337,7 @@ typedef struct k3_dense_seg {
     int64_t ldx;
     const float* norm_w;
     float eps;
+    int32_t act_input;
 } k3_dense_seg;
 
 enum {
@@ -344,8 +349,9 @@ enum {
  * K0 (and K1) columns. */
 K3_API size_t k3_dense_workspace(int64_t M, int64_t N, int nseg, int64_t K0, int64_t K1);
 /* out [M][N] (row stride ldo, f32 or bf16). `activation` (K3_ACT_SILU / K3_ACT_SITU,
- * situ_linear_beta <= 0 for none) is read for K3_DENSE_ACT only. The result does not
- * depend on timing: the split-k partial sums are added in a fixed order. */
+ * situ_linear_beta <= 0 for none) is read for K3_DENSE_ACT and act_input segments only.
+ * The result does not depend on timing: the split-k partial sums are added in a fixed
+ * order. */
 K3_API int k3_dense_matvec(const k3_dense_seg* segs, int nseg, int64_t M, int64_t N, int combine,
                            int activation, float situ_beta, float situ_linear_beta, void* out,
                            int out_dtype, int64_t ldo, void* workspace, size_t workspace_bytes,

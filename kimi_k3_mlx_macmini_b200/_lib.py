@@ -48,7 +48,7 @@ class K3MoEParams(ctypes.Structure):
 class K3DenseSeg(ctypes.Structure):
     _fields_ = [("w", ctypes.c_void_p), ("ldw", ctypes.c_int64), ("K", ctypes.c_int64),
                 ("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int32), ("ldx", ctypes.c_int64),
-                ("norm_w", ctypes.c_void_p), ("eps", ctypes.c_float)]
+                ("norm_w", ctypes.c_void_p), ("eps", ctypes.c_float), ("act_input", ctypes.c_int32)]
 
 
 # name -> (restype, argtypes); mirrors include/k3b200.h

@@ -93,7 +93,7 @@ int launch_matvec_simple(const void* x, int xdt, int64_t M, int64_t K, const uin
 
 using namespace k3;
 
-extern "C" K3_API int k3_abi_version(void) { return 2; }
+extern "C" K3_API int k3_abi_version(void) { return 3; }
 
 extern "C" K3_API const char* k3_last_error(void) { return g_last_error.c_str(); }
 

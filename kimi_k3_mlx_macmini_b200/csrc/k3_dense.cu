@@ -432,8 +432,8 @@ __global__ void __launch_bounds__(kDThreads, 1) dense_matvec_kernel(const __grid
 }
 
 // Stages every segment's input (blockIdx.y = segment, blockIdx.x = token slot < MT) in
-// the unit layout of xslot(), RMS-normalised when the segment asks for it; zeroes the
-// row-block counters, the argmax key and the status word.
+// the unit layout of xslot(), RMS-normalised or formed as act(gate, up) when the segment
+// asks for it; zeroes the row-block counters, the argmax key and the status word.
 struct PrepArgs {
     const void* x[kDMaxSeg];
     int xdt[kDMaxSeg];
@@ -442,6 +442,9 @@ struct PrepArgs {
     int64_t Kp[kDMaxSeg];
     const float* norm_w[kDMaxSeg];
     float eps[kDMaxSeg];
+    int act_in[kDMaxSeg];   // input row = [gate | up]; staged value act(gate, up)
+    int act_kind;
+    float beta, lbeta;
     float* xt[kDMaxSeg];
     int M, MT;
     int* cnt;
@@ -503,7 +506,11 @@ __global__ void __launch_bounds__(256) dense_prep_kernel(const __grid_constant__
         v[i] = 0.0f;
         if (live && k < K) {
             v[i] = load_as_f32(p.x[s], p.xdt[s], m * p.ldx[s] + k);
-            if (p.norm_w[s]) v[i] = p.norm_w[s][k] * (v[i] * scale);
+            if (p.act_in[s])
+                v[i] = act_value(p.act_kind, v[i], load_as_f32(p.x[s], p.xdt[s], m * p.ldx[s] + K + k), p.beta,
+                                 p.lbeta);
+            else if (p.norm_w[s])
+                v[i] = p.norm_w[s][k] * (v[i] * scale);
         }
     }
 #pragma unroll
@@ -603,6 +610,10 @@ int check_seg(const k3_dense_seg& g, const char* who) {
     if (g.ldw < g.K || g.ldw % 8) return fail(K3_ERR_INVALID, w + ": ldw must be >= K and a multiple of 8");
     if (g.ldx < g.K) return fail(K3_ERR_INVALID, w + ": ldx must be >= K");
     if (!aligned16(g.w)) return fail(K3_ERR_INVALID, w + ": weights must be 16-byte aligned");
+    if (g.act_input) {
+        if (g.ldx < 2 * g.K) return fail(K3_ERR_INVALID, w + ": an act_input row holds [gate | up]: ldx must be >= 2K");
+        if (g.norm_w) return fail(K3_ERR_INVALID, w + ": act_input and norm_w exclude each other");
+    }
     return K3_OK;
 }
 
@@ -633,8 +644,12 @@ int dense_run(const k3_dense_seg* segs, int nseg, int64_t M, int64_t N, int comb
         p.Kp[i] = units_of(segs[i].K) * kDUnitK;
         p.norm_w[i] = segs[i].norm_w;
         p.eps[i] = segs[i].eps;
+        p.act_in[i] = segs[i].act_input ? 1 : 0;
         p.xt[i] = reinterpret_cast<float*>(w8 + L.xt[i]);
     }
+    p.act_kind = act;
+    p.beta = beta;
+    p.lbeta = lbeta;
     p.M = int(M);
     p.MT = MT;
     p.cnt = reinterpret_cast<int*>(w8 + L.cnt);
@@ -709,8 +724,15 @@ extern "C" K3_API int k3_dense_matvec(const k3_dense_seg* segs, int nseg, int64_
         return fail(K3_ERR_INVALID, "k3_dense_matvec: combine must be K3_DENSE_SUM or K3_DENSE_ACT");
     if (out_dtype != K3_F32 && out_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_dense_matvec: out must be f32 or bf16");
     if (ldo < N) return fail(K3_ERR_INVALID, "k3_dense_matvec: ldo must be >= N");
-    for (int i = 0; i < nseg; ++i)
+    bool act_in = false;
+    for (int i = 0; i < nseg; ++i) {
         if (int rc = check_seg(segs[i], "k3_dense_matvec")) return rc;
+        act_in = act_in || segs[i].act_input;
+    }
+    if (act_in && combine != K3_DENSE_SUM)
+        return fail(K3_ERR_INVALID, "k3_dense_matvec: act_input segments need K3_DENSE_SUM");
+    if (act_in && activation != K3_ACT_SILU && activation != K3_ACT_SITU)
+        return fail(K3_ERR_INVALID, "k3_dense_matvec: unknown activation");
     if (combine == K3_DENSE_ACT) {
         if (nseg != 2) return fail(K3_ERR_INVALID, "k3_dense_matvec: ACT needs two segments (gate, up)");
         if (segs[1].K != segs[0].K) return fail(K3_ERR_INVALID, "k3_dense_matvec: ACT segments need the same K");

@@ -24,8 +24,9 @@ from . import _lib as L
 
 MAX_DENSE_TOKENS = 8
 
-# (weight bf16 [N][K], input [M][K], rmsnorm weight or None, eps)
-Seg = Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor], float]
+# (weight bf16 [N][K], input [M][K], rmsnorm weight or None, eps[, act_input]); with
+# act_input true the input is [M][2K] = [gate | up] and the segment reads act(gate, up)
+Seg = Tuple
 
 
 def device_weight(t, device) -> torch.Tensor:
@@ -42,7 +43,7 @@ def device_weight(t, device) -> torch.Tensor:
 
 
 def _native_ok(segs: Sequence[Seg]) -> bool:
-    for w, x, _, _ in segs:
+    for w, x, *_ in segs:
         if (w.dtype != torch.bfloat16 or w.dim() != 2 or w.stride(1) != 1 or w.shape[1] % 8
                 or w.stride(0) % 8 or w.data_ptr() % 16 or x.shape[0] > MAX_DENSE_TOKENS):
             return False
@@ -88,7 +89,7 @@ def matvec(segs: Sequence[Seg], N: int, combine: int = L.K3_DENSE_SUM, activatio
            out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """out [M][N] = sum_s X_s W_s^T (``K3_DENSE_SUM``) or act(X W_0^T, X W_1^T)
     (``K3_DENSE_ACT``: two segments over the first segment's X). A segment with a norm
-    weight uses rmsnorm(X) instead of X."""
+    weight uses rmsnorm(X) instead of X; one marked act_input uses act(X[:, :K], X[:, K:2K])."""
     x0 = segs[0][1]
     L.require_cuda(x0, "x")
     M = x0.shape[0]
@@ -97,13 +98,16 @@ def matvec(segs: Sequence[Seg], N: int, combine: int = L.K3_DENSE_SUM, activatio
         lib = L.load_library()
         arr = (L.K3DenseSeg * len(segs))()
         keep = []
-        for i, (w, x, nw, eps) in enumerate(segs):
+        for i, sg in enumerate(segs):
+            w, x, nw, eps = sg[:4]
+            act_in = bool(sg[4]) if len(sg) > 4 else False
             xc = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
             xc = xc if xc.stride(-1) == 1 and xc.stride(0) >= xc.shape[1] else xc.contiguous()
             nwc = None if nw is None else nw.float().contiguous()
             keep += [xc, nwc]
             arr[i] = L.K3DenseSeg(w.data_ptr(), w.stride(0), w.shape[1], xc.data_ptr(), L.dtype_code(xc),
-                                  xc.stride(0), None if nwc is None else nwc.data_ptr(), float(eps))
+                                  xc.stride(0), None if nwc is None else nwc.data_ptr(), float(eps),
+                                  int(act_in))
         out = torch.empty((M, N), dtype=out_dtype, device=dev)
         K1 = segs[1][0].shape[1] if len(segs) > 1 else 0
         ws = L.workspace(dev, lib.k3_dense_workspace(M, N, len(segs), segs[0][0].shape[1], K1))
@@ -112,7 +116,13 @@ def matvec(segs: Sequence[Seg], N: int, combine: int = L.K3_DENSE_SUM, activatio
                                     ws.data_ptr(), ws.numel(), L.stream_of(x0)), "k3_dense_matvec")
         return out
     # more than 8 tokens (or weights that are not bf16): cuBLAS GEMMs
-    parts = [_mm_f32(x if nw is None else _rmsnorm(x, nw, eps), w) for w, x, nw, eps in segs]
+    parts = []
+    for sg in segs:
+        w, x, nw, eps = sg[:4]
+        if len(sg) > 4 and sg[4]:
+            K = w.shape[1]
+            x = _activation(activation, x[:, :K].float(), x[:, K:2 * K].float(), situ_beta, situ_linear_beta)
+        parts.append(_mm_f32(x if nw is None else _rmsnorm(x, nw, eps), w))
     if combine == L.K3_DENSE_ACT:
         y = _activation(activation, parts[0], parts[1], situ_beta, situ_linear_beta)
     else:

@@ -180,6 +180,16 @@ class LatentMoE:
             self.sh_gate = D.device_weight(w["shared_experts.gate_proj.weight"], self.device)
             self.sh_up = D.device_weight(w["shared_experts.up_proj.weight"], self.device)
             self.sh_down = D.device_weight(w["shared_experts.down_proj.weight"], self.device)
+        # the three bf16 projections of the hidden state -- latent down, shared gate, shared
+        # up -- in one [L + 2 I_shared][H] matrix (the old names are row views of it), so a
+        # decode step streams them in one launch
+        self.front = None
+        if self.latent and self.dense_shared:
+            parts = [self.down, self.sh_gate, self.sh_up]
+            if all(t.dtype == torch.bfloat16 for t in parts) and len({t.shape[1] for t in parts}) == 1:
+                self.front = torch.cat(parts, 0).contiguous()
+                n0, n1 = self.down.shape[0], self.down.shape[0] + self.sh_gate.shape[0]
+                self.down, self.sh_gate, self.sh_up = self.front[:n0], self.front[n0:n1], self.front[n1:]
         self.mxfp4_shared = (not self.dense_shared) and getattr(cfg, "num_shared_experts", 0) > 0
         self._pool: Optional[ExpertPool] = None
         # the contiguous pools feed the TMA kernels; False forces the pointer-table kernels
@@ -439,10 +449,16 @@ class LatentMoE:
                 return y.reshape(*orig[:-1], y.shape[-1])
             y, _, _ = self._fused_decode(flat)
             return y.reshape(*orig[:-1], y.shape[-1])
+        gu = None                        # [gate | up] of the bf16 shared expert, when fused
         if self._latent_fused_ok(flat):
-            # latent decode: hidden -> latent matvec, then one fused router launch (routing on
+            # latent decode: hidden -> latent matvec (with the shared expert's gate and up
+            # rows when they share its matrix), then one fused router launch (routing on
             # the hidden state, E2M1 pieces of the latent) and the block-scaled experts
-            h = D.matvec([(self.down, flat, None, 0.0)], self.down.shape[0])
+            if self.front is not None:
+                hf = D.matvec([(self.front, flat, None, 0.0)], self.front.shape[0])
+                h, gu = hf[:, :self.down.shape[0]], hf[:, self.down.shape[0]:]
+            else:
+                h = D.matvec([(self.down, flat, None, 0.0)], self.down.shape[0])
             y, r = self._fused_latent_decode(flat, h, return_router)
         else:
             r = self.route(flat)
@@ -459,9 +475,11 @@ class LatentMoE:
         if self.latent:
             # rmsnorm(y) @ up.T (+ the bf16 shared expert's down projection) in one matvec
             segs = [(self.up, y, self.norm_w, float(self.cfg.rms_norm_eps))]
-            if self.dense_shared:
+            if self.dense_shared and gu is not None:
+                segs.append((self.sh_down, gu, None, 0.0, True))         # act(gate, up) staged in
+            elif self.dense_shared:
                 segs.append((self.sh_down, self._dense_shared_act(flat), None, 0.0))
-            y = D.matvec(segs, self.up.shape[0])
+            y = D.matvec(segs, self.up.shape[0], **self._act_args())
             if not self.dense_shared:
                 y = y + self.shared_forward(flat)
         else:

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version_and_error_string(lib):
-    assert lib.k3_abi_version() == 2
+    assert lib.k3_abi_version() == 3
     assert isinstance(lib.k3_last_error(), bytes)
 
 

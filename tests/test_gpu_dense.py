@@ -60,6 +60,38 @@ def test_dense_bf16_input_and_output(k3):
     assert O.rel_l2(_h64(yb), want) < 4e-3                        # bf16 output rounding
 
 
+@pytest.mark.parametrize("M,xdt", [(1, torch.float32), (5, torch.bfloat16), (8, torch.float32)])
+def test_dense_act_input_segment(k3, M, xdt):
+    """A segment marked act_input reads act(gate, up) from [gate | up] rows (row stride
+    above 2K): the bf16 shared expert's down projection fed straight from the front
+    matvec's output, next to a plain segment. The activation is fp32 on the device, so
+    the bound is twice the plain fp32 one."""
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import dense as D
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(40 + M)
+    K, N, ld = 3072, 1536, 2 * 3072 + 512
+    base = (torch.randn((M, ld), generator=gen, device="cuda") * 2.0).to(xdt)
+    gu = base[:, 512:512 + 2 * K]
+    w, w2, x2 = _w(gen, N, K), _w(gen, N, 640), _x(gen, M, 640)
+    for act, name, lb in ((L.K3_ACT_SITU, "situ", 25.0), (L.K3_ACT_SITU, "situ", None), (L.K3_ACT_SILU, "silu", None)):
+        y = D.matvec([(w2, x2, None, 0.0), (w, gu, None, 0.0, True)], N, activation=act, situ_beta=4.0,
+                     situ_linear_beta=-1.0 if lb is None else lb)
+        a = O.activation(_h64(gu[:, :K]), _h64(gu[:, K:]), name, 4.0, lb)
+        want = _h64(x2) @ _h64(w2).T + a @ _h64(w).T
+        assert O.rel_l2(_h64(y), want) < 2 * F32_REL_L2, name
+
+
+def test_dense_act_input_checks(k3):
+    from kimi_k3_mlx_macmini_b200 import dense as D
+    w = torch.zeros((64, 256), dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros((1, 400), device="cuda")                      # row shorter than 2K
+    with pytest.raises(ValueError, match="ldx must be >= 2K"):
+        D.matvec([(w, x, None, 0.0, True)], 64)
+    with pytest.raises(ValueError, match="exclude each other"):
+        D.matvec([(w, torch.zeros((1, 512), device="cuda"), torch.ones(256, device="cuda"), 1e-5, True)], 64)
+
+
 def test_dense_two_segments_with_rmsnorm(k3):
     """rmsnorm(y) @ up.T + a @ sh_down.T in one call (the K3 layer's last matvec)."""
     from kimi_k3_mlx_macmini_b200 import dense as D
