@@ -789,7 +789,7 @@ def run_k3(args, rank, world, local):
     layer_bytes = u_mean * 3 * proj + dense_bytes + router_bytes
     peak, peak_kind = measured_peaks()
     d_ms, d_n = prof["dense"]
-    d_gbs = dense_bytes / (d_ms / n_prof / 1e3) / 1e9           # the step's three dense matvecs together
+    d_gbs = dense_bytes / (d_ms / n_prof / 1e3) / 1e9           # the step's two dense matvecs together
     for g in graphs:
         g.reset()
     line = {
@@ -807,8 +807,9 @@ def run_k3(args, rank, world, local):
                    "timing": timing + ", events around K steps"},
         "unique_experts_mean": u_mean,
         "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
-        "roofline": {"bound": "hbm", "kernel": "dense_matvec_kernel (latent down, shared gate/up + act, "
-                                                "rmsnorm.up + shared down; prep kernels included)",
+        "roofline": {"bound": "hbm", "kernel": "dense_matvec_kernel (front: latent down + shared gate/up; "
+                                                "back: rmsnorm.up + shared down on act(gate, up); "
+                                                "prep kernels included)",
                      "achieved": d_gbs, "peak": peak, "unit": "GB/s", "frac": d_gbs / peak,
                      "peak_kind": peak_kind, "traffic": None,
                      "algorithmic_bytes_per_step": dense_bytes, "ms_per_step": d_ms / n_prof},
