@@ -33,3 +33,17 @@ def test_device_weight_and_dispatch():
     assert not D._native_ok([(wb, torch.zeros((9, 32)), None, 0.0)])             # > 8 tokens: GEMM path
     assert not D._native_ok([(wb[:, :20], torch.zeros((2, 20)), None, 0.0)])      # K % 8 != 0
     assert not D._native_ok([(wb.float(), torch.zeros((2, 32)), None, 0.0)])      # fp32 weights
+    assert D._native_ok([(wb, torch.zeros((2, 64)), None, 0.0, True)])            # act_input segment
+
+
+def test_dense_seg_struct_matches_header():
+    """The ctypes mirror of k3_dense_seg carries every field of the header's struct, in
+    order, ending with act_input (ABI 3)."""
+    import re
+    from pathlib import Path
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    hdr = (Path(__file__).resolve().parents[1] / "include" / "k3b200.h").read_text()
+    body = re.search(r"typedef struct k3_dense_seg \{(.*?)\} k3_dense_seg;", hdr, re.S).group(1)
+    names = re.findall(r"(\w+);", body)
+    assert names == [f[0] for f in L.K3DenseSeg._fields_]
+    assert names[-1] == "act_input"
