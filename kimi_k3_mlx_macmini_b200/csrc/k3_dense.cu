@@ -8,7 +8,9 @@
 //
 // W is bf16 [N][K] row-major (the checkpoint layout), X is f32 or bf16. A segment may
 // RMS-normalise its input first (x -> norm_w * x * rsqrt(mean(x^2) + eps), the
-// reference's `ops.rmsnorm`, air_llm/models/kimi_k3/ops.py:11-14). Products and sums are
+// reference's `ops.rmsnorm`, air_llm/models/kimi_k3/ops.py:11-14), or read it as
+// act(gate, up) from a [gate | up] row (the bf16 shared expert's activation feeding its
+// down projection, moe.py:105-107). Products and sums are
 // fp32, as in the reference, which computes these in fp32 on bf16 weights
 // (air_llm/models/kimi_k3/moe.py:105-107, 116, 128-130; model.py:111-133).
 //
@@ -16,7 +18,7 @@
 //
 //   * a prep kernel stages each segment's input as fp32 in the order the matvec's lanes
 //     read it (MT = M rounded up to 1, 2, 4 or 8; padded tokens and k beyond K are zero),
-//     normalised when the segment asks for it;
+//     normalised or activated when the segment asks for it;
 //   * the matvec kernel runs one CTA per SM. Units are (row block of 64 weight rows,
 //     256-k step); a row block's units run over its segments' k in order. CTA b takes
 //     the contiguous unit range [U b / G, U (b+1) / G), so every CTA streams the same
@@ -477,14 +479,17 @@ __global__ void __launch_bounds__(256) dense_prep_kernel(const __grid_constant__
     const bool live = m < p.M;
     float scale = 1.0f;
     if (live && p.norm_w[s]) {
+        // sixteen loads in flight per thread: one round trip for rows up to 4096 wide
         float ss[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int64_t k = threadIdx.x; k < K; k += 4 * blockDim.x) {
+        for (int64_t k = threadIdx.x; k < K; k += 16 * blockDim.x) {
+            float q[16];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
+            for (int i = 0; i < 16; ++i) {
                 const int64_t kk = k + i * blockDim.x;
-                const float v = kk < K ? load_as_f32(p.x[s], p.xdt[s], m * p.ldx[s] + kk) : 0.0f;
-                ss[i] = fmaf(v, v, ss[i]);
+                q[i] = kk < K ? load_as_f32(p.x[s], p.xdt[s], m * p.ldx[s] + kk) : 0.0f;
             }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss[i & 3] = fmaf(q[i], q[i], ss[i & 3]);
         }
         float t = (ss[0] + ss[1]) + (ss[2] + ss[3]);
 #pragma unroll
