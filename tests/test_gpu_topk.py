@@ -45,7 +45,7 @@ def _expected(cor, raw, k, scale, tol=1e-5):
             out.append(None)
             continue
         sel = order[:k]
-        w = r[sel] / (r[sel].sum() + 1e-20) * scale
+        w = (r[sel] / (r[sel].sum() + 1e-20) if k > 1 else r[sel]) * scale    # no renorm at k = 1
         out.append((sel, w))
     return out
 
@@ -56,6 +56,8 @@ def _expected(cor, raw, k, scale, tol=1e-5):
     (640, 16, 5, 41),
     (896, 16, 1, 53),    # the Kimi-K3 router width
     (896, 16, 8, 29),
+    (1024, 16, 4, 61),   # the widest router the kernels take
+    (520, 1, 2, 19),     # k = 1 in the counting form
 ])
 def test_fused_topk_lowest_index_on_ties(k3, E, k, M, D):
     moe = _tied_moe(E, k, D, seed=E + M)
