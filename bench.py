@@ -10,6 +10,7 @@ expert + weighted scatter-add).
 
     python bench.py [--gpus N --steps K --warmup W --tokens M] [--impl reference]
 
+    python bench.py --config 1 ...      # configs[1]: single-expert MXFP4 matvec GB/s (--tokens 1 or 8)
     python bench.py --config 3 ...      # configs[3]: prefill, T = 4096 tokens per GPU
     python bench.py --config 4 ...      # configs[4]: experts streamed from pinned host memory
     python bench.py --config 5 ...      # a Kimi-K3 layer at decode (896 experts, top-16, latent
@@ -68,15 +69,15 @@ def parse():
                          "only for small ncu captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
-                    help="BASELINE config: 2 = MoE-layer decode (headline), 3 = MoE-layer prefill "
-                         "(--tokens defaults to 4096), 4 = streamed-expert decode; 5 = Kimi-K3 "
-                         "layer decode (supplementary)")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
+                    help="BASELINE config: 1 = single-expert MXFP4 matvec GB/s, 2 = MoE-layer decode "
+                         "(headline), 3 = MoE-layer prefill (--tokens defaults to 4096), 4 = streamed-expert "
+                         "decode; 5 = Kimi-K3 layer decode (supplementary)")
     ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.tokens is None:
-        args.tokens = {2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
+        args.tokens = {1: 8, 2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
     if args.experts is None:
         args.experts = 896 if args.config == 5 else E
     return args
@@ -124,184 +125,231 @@ def barrier(world: int):
 # ----------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU every 200 ms while the timed region runs."""
+    """SM clocks and throttle reasons while the timed region runs. One GPU: NVML every
+    ~2 ms plus ``nvidia-smi -lms 200``. Several GPUs (one process each): only local rank
+    0 samples, NVML for every GPU of the job every ~10 ms, and the other ranks run no
+    sampler, so the ranks' launch loops do not compete with NVML calls."""
 
     Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, local_rank: int):
+    def __init__(self, local_rank: int, world: int = 1):
         import threading
 
         import torch
         self.proc = None
-        self.nv = []                                  # (sm MHz, max MHz, reasons bitmask)
+        self.nv = []                                  # (gpu, sm MHz, max MHz, reasons bitmask)
         self._stop = threading.Event()
         self._thr = None
+        self.active = world == 1 or local_rank == 0
+        if not self.active:
+            return
+        gpus = [local_rank] if world == 1 else list(range(min(world, torch.cuda.device_count())))
+
+        def uuid_of(i):
+            u = str(torch.cuda.get_device_properties(i).uuid)
+            return u if u.startswith("GPU-") else "GPU-" + u
+
+        period = 0.002 if world == 1 else 0.010
         try:
             import pynvml
             pynvml.nvmlInit()
-            uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
-            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            hs = [(i, pynvml.nvmlDeviceGetHandleByUUID(uuid_of(i))) for i in gpus]
 
             def poll():
                 while not self._stop.is_set():
                     try:
-                        self.nv.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
-                                        pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM),
-                                        pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                        for i, h in hs:
+                            self.nv.append((i, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                            pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                            pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
                     except Exception:
                         return
-                    time.sleep(0.002)
+                    time.sleep(period)
             self._thr = threading.Thread(target=poll, daemon=True)
             self._thr.start()
         except Exception:
             self._thr = None
-        try:
-            uuid = str(torch.cuda.get_device_properties(local_rank).uuid)
-            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={uuid}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+        if world == 1:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={uuid_of(local_rank)}", f"--query-gpu={self.Q}",
+                     "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except Exception:
+                self.proc = None
 
     # NVML clocks-event reason bits (nvml.h): sw power cap 0x4, hw slowdown 0x8,
     # sw thermal 0x20, hw thermal 0x40
     NV_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40}
 
-    def stop(self) -> dict:
+    def stop(self):
+        if not self.active:
+            return None
         self._stop.set()
         if self._thr is not None:
             self._thr.join(timeout=2)
-        if self.proc is None and not self.nv:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        if self.proc is None:
-            reasons = sorted(n for n, b in self.NV_BITS.items() if any(r & b for _, _, r in self.nv))
-            return {"sm_mhz": statistics.median(c for c, _, _ in self.nv),
-                    "sm_max_mhz": max(m for _, m, _ in self.nv), "samples": len(self.nv),
-                    "source": "nvml", "reasons": reasons}
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except Exception:
-            self.proc.kill()
-            out = ""
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            f = [c.strip() for c in line.split(",")]
-            if len(f) < 8:
-                continue
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
             try:
-                sm.append(float(f[0]))
-                mx.append(float(f[1]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[4:8]):
-                if v.lower() == "active":
-                    reasons.add(n)
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in out.strip().splitlines():
+                f = [c.strip() for c in line.split(",")]
+                if len(f) < 8:
+                    continue
+                try:
+                    sm.append(float(f[0]))
+                    mx.append(float(f[1]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[4:8]):
+                    if v.lower() == "active":
+                        reasons.add(n)
         for n, b in self.NV_BITS.items():
-            if any(r & b for _, _, r in self.nv):
+            if any(r & b for _, _, _, r in self.nv):
                 reasons.add(n)
         if self.nv:                                   # in-region NVML samples take precedence
-            sm = [c for c, _, _ in self.nv]
-            mx = mx + [m for _, m, _ in self.nv]
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
-                "source": "nvml+nvidia-smi" if self.nv else "nvidia-smi",
-                "reasons": sorted(reasons)}
+            sm = [c for _, c, _, _ in self.nv]
+            mx = mx + [m for _, _, m, _ in self.nv]
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        gpus = sorted({g for g, _, _, _ in self.nv})
+        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None, "samples": len(sm),
+               "source": ("nvml" if self.proc is None else "nvml+nvidia-smi") if self.nv else "nvidia-smi",
+               "reasons": sorted(reasons)}
+        if len(gpus) > 1:
+            out["per_gpu_sm_mhz"] = {str(g): statistics.median(c for gg, c, _, _ in self.nv if gg == g)
+                                     for g in gpus}
+            out["sampled_by"] = "local rank 0 for every GPU of the job"
+        return out
 
 
 # ------------------------------------------------------------- CPU baseline (oracle)
 
-def cpu_baseline(M: int, seed: int, steps: int, budget_s: float = 20.0):
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:                                       # noqa: BLE001
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(M: int, seed: int, steps: int, budget_s: float = 20.0, layers: int = 1):
     """The reference path restated on the host cores (oracle port): fp32 router in numpy,
-    then the reference fused kernel's loop in C (OpenMP over rows) for every expert the
-    step routes to, plus the shared expert. Weights are a pool of 8 synthetic experts
-    reused by id (the work per expert does not depend on the values); at most
-    ``budget_s`` of expert compute is spent and the step time is extrapolated to all
-    U + 1 experts. Returns (tokens/s, cores, sample description)."""
+    then the reference fused kernel's loop in C (OpenMP over rows, every host core -- the
+    launcher's OMP_NUM_THREADS is overridden) for every expert the step routes to, plus the
+    shared expert. Weights are a pool of 8 synthetic experts reused by id (the work per
+    expert does not depend on the values). Decode steps (M <= 64) run whole, `layers`
+    layers each, until ``budget_s`` is spent (at least one); a prefill step is cut after
+    ``budget_s`` of expert compute and extrapolated to all U + 1 experts. Returns a dict:
+    tokens/s, cores, ISA level, sample description, steps timed, whether they were whole."""
     from oracle import mxfp4_oracle as O
+    cores = host_cores()
+    try:
+        from threadpoolctl import threadpool_limits
+        blas = threadpool_limits(cores)
+    except Exception:                                       # noqa: BLE001
+        blas = None
     rng = np.random.default_rng(seed)
     gate = O.bf16_bits_to_f32(O.f32_to_bf16_bits((rng.standard_normal((E, H)) * 0.02).astype(np.float32)))
     pool = [(O.random_mxfp4(rng, I_, H), O.random_mxfp4(rng, I_, H), O.random_mxfp4(rng, H, I_))
             for _ in range(8)]
-    t_route, t_exp, n_exp, n_steps, U_tot = 0.0, 0.0, 0, 0, 0
-    spent = 0.0
+    whole = M <= 64
+    t_route, t_exp, n_exp, n_steps, U_tot, wall = 0.0, 0.0, 0, 0, 0, 0.0
     for s in range(max(1, steps)):
         x = O.bf16_bits_to_f32(O.f32_to_bf16_bits(rng.standard_normal((M, H)).astype(np.float32)))
-        t0 = time.perf_counter()
-        r = O.route(x, gate, None, TOPK, True, SCALE)
-        t_route += time.perf_counter() - t0
-        experts = sorted(set(r.expert_indices.reshape(-1).tolist()))
-        U_tot += len(experts) + 1
-        n_steps += 1
-        for j, e in enumerate(experts + [-1]):
-            tok = np.arange(M) if e < 0 else np.nonzero(r.expert_indices == e)[0]
-            (p1, s1), (p3, s3), (p2, s2) = pool[j % len(pool)]
+        w0 = time.perf_counter()
+        for _ in range(layers):
             t0 = time.perf_counter()
-            g = O.matvec_fused(x[tok], p1, s1)
-            u = O.matvec_fused(x[tok], p3, s3)
-            O.matvec_fused(O.silu(g) * u, p2, s2)
-            dt = time.perf_counter() - t0
-            t_exp += dt
-            spent += dt
-            n_exp += 1
-            if spent > budget_s:
-                break
-        if spent > budget_s:
+            r = O.route(x, gate, None, TOPK, True, SCALE)
+            t_route += time.perf_counter() - t0
+            experts = sorted(set(r.expert_indices.reshape(-1).tolist()))
+            U_tot += len(experts) + 1
+            y = np.zeros_like(x)
+            for j, e in enumerate(experts + [-1]):
+                tok = np.arange(M) if e < 0 else np.nonzero(r.expert_indices == e)[0]
+                (p1, s1), (p3, s3), (p2, s2) = pool[j % len(pool)]
+                t0 = time.perf_counter()
+                g = O.matvec_fused(x[tok], p1, s1, threads=cores)
+                u = O.matvec_fused(x[tok], p3, s3, threads=cores)
+                y[tok] += O.matvec_fused(O.silu(g) * u, p2, s2, threads=cores)
+                t_exp += time.perf_counter() - t0
+                n_exp += 1
+                if not whole and t_exp > budget_s:
+                    break
+            x = (x + y).astype(np.float32)
+        wall += time.perf_counter() - w0
+        n_steps += 1
+        if t_route + t_exp > budget_s:
             break
-    per_step = t_route / n_steps + (U_tot / n_steps) * (t_exp / n_exp)
-    sample = (f"{n_steps} step(s) of M={M}: numpy fp32 router + C port of the reference "
-              f"fused-kernel loop over {n_exp} expert FFNs (of {U_tot} routed+shared); step time = "
-              f"router + (U+1) x mean expert time")
-    return M / per_step, O.oracle_threads(), sample
+    if blas is not None:
+        blas.restore_original_limits()
+    if whole:
+        per_step = wall / n_steps
+        sample = (f"{n_steps} whole step(s) of M={M} x {layers} layer(s): numpy fp32 router + C port of the "
+                  f"reference fused-kernel loop over every routed expert and the shared one ({n_exp} expert "
+                  f"FFNs); wall time per step")
+    else:
+        per_step = t_route / n_steps + (U_tot / n_steps) * (t_exp / n_exp)
+        sample = (f"1 step of M={M} cut after {n_exp} of {U_tot} routed+shared expert FFNs: numpy fp32 router "
+                  f"+ C port of the reference fused-kernel loop; step time = router + (U+1) x mean expert time")
+    return {"tokens_per_s": M / per_step, "s_per_step": per_step, "cores": cores, "isa": O.oracle_isa(),
+            "sample": sample, "steps_timed": n_steps, "whole_steps": whole}
 
 
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU path (oracle port) on this box's host cores, on
-    the same config and metric as the B200 arm. Each sample is one bounded slice of a step
-    (router + a subset of the step's expert FFNs, extrapolated to all of them); at most 8
-    samples after one warm-up, inside a ~150 s budget."""
+    the same config and metric as the B200 arm, with every host core (whatever
+    OMP_NUM_THREADS the launcher set). Decode configs time whole steps (router + every
+    routed expert + the shared one) after one warm-up step, as many as fit in ~100 s and at
+    most --steps; prefill times one step cut after a bounded share of its experts and
+    extrapolated. Under torchrun rank 0 alone runs it."""
     if rank != 0:
         return
     cfg = args.config
     if cfg == 5:
         print(json.dumps({"impl": "reference", "metric": "k3_layer_decode_tokens_per_s",
                           "unavailable": "config 5 is supplementary (not a BASELINE config); the CPU reference "
-                                         "arm is timed on configs 2-4"}))
+                                         "arm is timed on configs 1-4"}))
+        return
+    t0 = time.perf_counter()
+    if cfg == 1:
+        line = reference_matvec(args)
+        line["wall_s"] = time.perf_counter() - t0
+        print(json.dumps(line))
         return
     M = 1 if cfg == 4 else args.tokens
-    n_s, n_w = max(1, min(args.steps, 8)), min(args.warmup, 1)
-    budget = 150.0 / (n_s + n_w)
-    t0 = time.perf_counter()
-    vals = []
-    for i in range(n_w + n_s):
-        v, cores, sample = cpu_baseline(M, args.seed + i, 1, budget_s=budget)
-        if i >= n_w:
-            vals.append(v)
-    tps = statistics.median(vals) if vals else 0.0
+    layers = args.layers if cfg == 4 else 1
+    cpu_baseline(M, args.seed + 999, 1, budget_s=5.0, layers=layers)              # warm-up
+    res = cpu_baseline(M, args.seed, args.steps, budget_s=100.0, layers=layers)
+    tps = res["tokens_per_s"]
     if cfg == 4:
-        metric, unit, value, hib = "streamed_decode_s_per_token", "s/token", args.layers / tps, False
-        workload = (f"BASELINE configs[4]: M=1 token through {args.layers} MoE layers (expert compute only; "
+        metric, unit, value, hib = "streamed_decode_s_per_token", "s/token", res["s_per_step"], False
+        workload = (f"BASELINE configs[4]: M=1 token through {layers} MoE layers (expert compute only; "
                     "the reference's SSD reads are not timed)")
     else:
         metric = "moe_layer_prefill_tokens_per_s" if cfg == 3 else "moe_layer_decode_tokens_per_s"
         unit, value, hib = "tokens/s", tps, True
         workload = (f"BASELINE configs[{cfg}]: MoE layer {'prefill' if cfg == 3 else 'decode'}, M={M}, "
                     "384+1 MXFP4 experts 7168/2048, top-8")
+    kind = (f"port: numpy router + C restatement of the reference's fused-kernel loop, gcc -O3, "
+            f"{res['isa']} clone, OpenMP on {res['cores']} threads")
     line = {
         "impl": "reference", "metric": metric, "value": value,
-        "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * M / tps if tps else None, "higher_is_better": hib,
+        "unit": unit, "n_gpus": world, "steps": res["steps_timed"], "warmup": 1,
+        "ms_per_step": 1000.0 * res["s_per_step"], "higher_is_better": hib,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload, "tokens": M, "samples": n_s},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port",
-                         "sample": sample},
+        "config": {"workload": workload, "tokens": M, "steps_requested": args.steps,
+                   "whole_steps": res["whole_steps"]},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": res["cores"], "kind": "port",
+                         "build": kind, "sample": res["sample"]},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": time.perf_counter() - t0,
     }
@@ -342,7 +390,7 @@ def run_stream(args, rank, world, local):
     for i in range(W):
         token(i)
     torch.cuda.synchronize()
-    clk = ClockSampler(local)
+    clk = ClockSampler(local, world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(K):
@@ -392,6 +440,12 @@ def run_stream(args, rank, world, local):
     prof = L.profile_collect()
     L.profile_enable(False)
     launches = sum(c for _, c in prof.values())
+    cpu = None
+    if not args.no_cpu_baseline:
+        res = cpu_baseline(1, args.seed, 20, budget_s=15.0, layers=NL)
+        cpu = {"value": res["s_per_step"], "unit": "s/token", "cores": res["cores"], "kind": "port",
+               "build": f"gcc -O3 {res['isa']} clone, OpenMP", "sample": res["sample"] +
+               " (expert compute only: the reference's SSD reads are not timed)"}
     overlap = max(0.0, copy_s + comp_s - s_per_token)
     copied = float(np.mean([sum(len(ids) for ids in per) for per in sets])) * store.nbytes_expert()
     line = {
@@ -416,6 +470,7 @@ def run_stream(args, rank, world, local):
         "gpu_launches": int(launches * K),
         "kernel_ms_per_token": {k: v[0] for k, v in prof.items() if v[1]},
         "clocks": clocks,
+        "cpu_baseline": cpu,
     }
     print(json.dumps(line))
 
@@ -432,6 +487,22 @@ def traffic_from_profiles():
     m = re.search(r"traffic_bytes_per_launch_full:\s*([0-9.eE+]+)", txt)
     a = re.search(r"traffic_launch_algorithmic_bytes:\s*([0-9.eE+]+)", txt)
     return (float(m.group(1)) if m else None), (float(a.group(1)) if a else None)
+
+
+def ep_check(moe, full, x, world):
+    """Expert-parallel output check on the GPUs, outside the timed region: one batch
+    through the expert-parallel layer, and this rank's same tokens through the whole layer
+    (all routed experts + the shared one) on this GPU with the 1-GPU kernels. Returns the
+    largest relative L2 difference over the ranks."""
+    import torch
+    y_ep = moe(x).float()
+    y_one = full(x).float()
+    torch.cuda.synchronize()
+    err = float(torch.linalg.vector_norm((y_ep - y_one).double()) / torch.linalg.vector_norm(y_one.double()))
+    full._pool = None                                       # free the whole-layer pool again
+    torch.cuda.empty_cache()
+    return {"max_rel_l2_over_ranks": dist_max(err, world),
+            "against": "the same tokens through the whole layer on one GPU (LatentMoE, 1-GPU kernels)"}
 
 
 def run_b200(args, rank, world, local):
@@ -457,6 +528,7 @@ def run_b200(args, rank, world, local):
         return synthetic.tokens(args.seed * 7919 + rk * 100003 + i, M, H)
 
     xs = [batch(rank, i) for i in range(R)]
+    check = ep_check(moe, router, xs[0], world) if world > 1 else None
     # experts this rank streams per step: the local experts any rank's tokens route to
     E_loc = args.experts // world
     U = []
@@ -516,8 +588,9 @@ def run_b200(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_baseline(M, args.seed, 2)
-        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+        res = cpu_baseline(M, args.seed, 20, budget_s=15.0)
+        cpu = {"value": res["tokens_per_s"], "unit": "tokens/s", "cores": res["cores"], "kind": "port",
+               "build": f"gcc -O3 {res['isa']} clone, OpenMP", "sample": res["sample"]}
 
     for g in graphs:
         g.reset()
@@ -539,6 +612,7 @@ def run_b200(args, rank, world, local):
                    "l2": f"inputs larger than L2: {9.0 / world:.2f} GB of expert weights per GPU, "
                          "a different token batch every step",
                    "timing": timing + ", events around K steps"},
+        "ep_check": check,
         "unique_experts_mean": float(np.mean(U_t)),
         "unique_experts_per_batch": U[:8],
         "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
@@ -585,7 +659,7 @@ def step_modes(moe, xs, R, world):
             torch.cuda.synchronize()
             graphs = []
             modes.append((f"eager launches ({R} distinct batches as a ring; graph capture failed: "
-                          f"{type(exc).__name__})", [(lambda x=x: moe(x)) for x in xs]))
+                          f"{_exc_text(exc)})", [(lambda x=x: moe(x)) for x in xs]))
     else:
         modes.append((f"eager launches ({R} distinct batches as a ring)", [(lambda x=x: moe(x)) for x in xs]))
         xin = xs[0].clone()
@@ -596,23 +670,28 @@ def step_modes(moe, xs, R, world):
             graphs.append(g)
             modes.append((f"one CUDA graph over a static input ({R} distinct batches copied in as a ring)",
                           [(lambda x=x: (xin.copy_(x, non_blocking=True), g.replay())) for x in xs]))
-        except Exception:                                   # noqa: BLE001 -- the eager mode stands
+        except Exception as exc:                            # noqa: BLE001 -- the eager mode stands, reason kept
             torch.cuda.synchronize()
+            modes[0] = (modes[0][0] + f"; graph capture failed: {_exc_text(exc)}", modes[0][1])
     return graphs, modes
+
+
+def _exc_text(exc: BaseException) -> str:
+    return f"{type(exc).__name__}: {str(exc).splitlines()[0][:240] if str(exc) else ''}"
 
 
 def time_modes(modes, steps, K, W, R, world, local):
     """Times K steps of every mode (W warm-up steps each; events bracketed by barriers and
     synchronisation; max over ranks); returns (ms per step, mode name, clocks) of the
-    fastest."""
+    fastest, with every mode's time in the name when there are several."""
     import torch
-    best = None
+    best, seen = None, []
     for name, run in modes:
         for i in range(W):
             run[i % R]()
         torch.cuda.synchronize()
         barrier(world)
-        clk = ClockSampler(local)
+        clk = ClockSampler(local, world)
         time.sleep(0.3)
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
@@ -624,8 +703,11 @@ def time_modes(modes, steps, K, W, R, world, local):
         clocks = clk.stop()
         barrier(world)
         ms = dist_max(ev0.elapsed_time(ev1) / K, world)
+        seen.append(f"{name.split(' (')[0]} {ms:.4f} ms")
         if best is None or ms < best[0]:
             best = (ms, name, clocks)
+    if len(seen) > 1:
+        best = (best[0], best[1] + " [timed: " + "; ".join(seen) + "]", best[2])
     return best
 
 
@@ -651,6 +733,7 @@ def run_prefill(args, rank, world, local):
         moe = lay.moe()
         _ = moe.pool
     xs = [synthetic.tokens(args.seed * 7919 + rank * 100003 + i, T, H) for i in range(R)]
+    check = ep_check(moe, lay.moe(), xs[0], world) if world > 1 else None
     graphs, modes = step_modes(moe, xs, R, world)
     barrier(world)
     ms, timing, clocks = time_modes(modes, [(W + i) % R for i in range(K)], K, W, R, world, local)
@@ -699,8 +782,9 @@ def run_prefill(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores, sample = cpu_baseline(T, args.seed, 1)
-        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+        res = cpu_baseline(T, args.seed, 1, budget_s=20.0)
+        cpu = {"value": res["tokens_per_s"], "unit": "tokens/s", "cores": res["cores"], "kind": "port",
+               "build": f"gcc -O3 {res['isa']} clone, OpenMP", "sample": res["sample"]}
     for g in graphs:
         g.reset()
     if rank != 0:
@@ -720,6 +804,7 @@ def run_prefill(args, rank, world, local):
                    "l2": f"inputs larger than L2: {w_bytes / 1e9:.2f} GB of expert weights per GPU and "
                          f"{R} token batches of {T * H * 2 / 1e6:.0f} MB",
                    "timing": timing + ", events around K steps"},
+        "ep_check": check,
         "layer_hbm_gbs": w_bytes / (ms / 1e3) / 1e9,
         "layer_tflops_algorithmic": flops / (ms / 1e3) / 1e12,
         "roofline": {"bound": "tensor", "kernel": "prefill_gemm_kernel<gate/up> (block-scaled grouped GEMM, tcgen05)",
@@ -743,6 +828,202 @@ def run_prefill(args, rank, world, local):
         "cpu_baseline": cpu,
     }
     print(json.dumps(line))
+
+
+def run_matvec(args, rank, world, local):
+    """the full-width single-expert MXFP4 decode matvec (hidden 7168,
+    intermediate 2048) at M tokens (--tokens, 1 or 8), pure HBM-bound dequant-matvec
+    bandwidth on one GPU. A step is one expert's SwiGLU FFN through the reference's API
+    ``LatentMoE.expert_forward`` (``moe.py:90-103``): gate and up projections (one
+    block-scaled launch), silu(gate) * up, the down projection -- 23,396,352 B of MXFP4
+    weights -- over a ring of 64 distinct experts (1.5 GB, larger than L2), one CUDA graph
+    per expert. Beside it, the bare ``mxfp4_matvec_fused`` call (``mxfp4_matvec.py:75-96``)
+    on one 7168 -> 2048 projection (7,798,784 B) over a ring of 128 distinct projections."""
+    import torch
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    from kimi_k3_mlx_macmini_b200.mxfp4 import mxfp4_matvec_fused
+
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"metric": "mxfp4_matvec_hbm_gbs", "unavailable": "config 1 runs on one GPU"}))
+        return
+    torch.cuda.set_device(local)
+    M, K, W = args.tokens, args.steps, args.warmup
+    NE = 64
+    lay = synthetic.baseline_layer(seed=args.seed, E=NE, H=H, I=I_, top_k=1, shared=False)
+    moe = lay.moe()
+    _ = moe.pool
+    xs = [synthetic.tokens(args.seed * 7919 + i, M, H) for i in range(NE)]
+    step_e = [(W + i) % NE for i in range(K)]
+    # ---- expert FFN through expert_forward, a CUDA graph per expert
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        for e in range(2):
+            moe.expert_forward(xs[e], e)
+    torch.cuda.synchronize()
+    graphs = []
+    for e in range(NE):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            moe.expert_forward(xs[e], e)
+        graphs.append(g)
+    ms, timing, clocks = time_modes([(f"CUDA graph per expert ({NE} distinct experts replayed as a ring)",
+                                      [g.replay for g in graphs])], step_e, K, W, NE, 1, local)
+    peak, peak_kind = measured_peaks()
+    ffn_bytes = EXPERT_BYTES + M * H * 2
+    gbs = ffn_bytes / (ms / 1e3) / 1e9
+    # ---- per-kernel device time of the same steps
+    n_prof = min(K, 64)
+    L.profile_enable(True)
+    L.profile_collect()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(4e7))
+    for i in range(n_prof):
+        moe.expert_forward(xs[step_e[i]], step_e[i])
+    torch.cuda.synchronize()
+    prof = L.profile_collect()
+    L.profile_enable(False)
+    gu_ms, gu_n = prof["gateup"]
+    gu_bytes = 2 * PROJ_BYTES + M * H * 2
+    gu_gbs = gu_bytes / (gu_ms / gu_n / 1e3) / 1e9
+    dn_ms, dn_n = prof["down"]
+    # ---- the bare mxfp4_matvec_fused call over a ring of 128 projections (w1 and w3 of the experts)
+    projs = []
+    for e in range(NE):
+        for which in ("w1", "w3"):
+            projs.append(moe.pool.get(e, which))
+    NP = len(projs)
+    xp = [synthetic.tokens(args.seed * 31 + i, M, H) for i in range(8)]
+    outs = torch.empty((M, I_), dtype=torch.float32, device="cuda")
+    pgraphs = []
+    with torch.cuda.stream(cap):
+        mxfp4_matvec_fused(xp[0], *projs[0])
+    torch.cuda.synchronize()
+    for j in range(NP):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            outs.copy_(mxfp4_matvec_fused(xp[j % 8], *projs[j]))
+        pgraphs.append(g)
+    K2 = max(K, 64)
+    pms, ptiming, _ = time_modes([("CUDA graph per projection", [g.replay for g in pgraphs])],
+                                 [(W + i) % NP for i in range(K2)], K2, W, NP, 1, local)
+    L.profile_enable(True)
+    L.profile_collect()
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(4e7))
+    for i in range(min(K2, 64)):
+        mxfp4_matvec_fused(xp[i % 8], *projs[(W + i) % NP])
+    torch.cuda.synchronize()
+    pprof = L.profile_collect()
+    L.profile_enable(False)
+    mv_ms, mv_n = pprof["matvec"]
+    # ---- end to end through expert_forward with host buffers
+    xh = torch.stack([x.cpu() for x in xs]).pin_memory()
+    yh = torch.empty((M, H), dtype=torch.float32).pin_memory()
+    xd = torch.empty((M, H), dtype=torch.bfloat16, device="cuda")
+    for i in range(W):
+        xd.copy_(xh[i % NE], non_blocking=True)
+        yh.copy_(moe.expert_forward(xd, i % NE), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(K):
+        xd.copy_(xh[step_e[i]], non_blocking=True)
+        yh.copy_(moe.expert_forward(xd, step_e[i]), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import mxfp4_oracle as O
+        rng = np.random.default_rng(args.seed)
+        (p1, s1), (p3, s3), (p2, s2) = (O.random_mxfp4(rng, I_, H), O.random_mxfp4(rng, I_, H),
+                                        O.random_mxfp4(rng, H, I_))
+        xf = rng.standard_normal((M, H)).astype(np.float32)
+        cores = host_cores()
+        n, t = 0, 0.0
+        while t < 10.0 and n < 50:
+            t0 = time.perf_counter()
+            g_ = O.matvec_fused(xf, p1, s1, threads=cores)
+            u_ = O.matvec_fused(xf, p3, s3, threads=cores)
+            O.matvec_fused(O.silu(g_) * u_, p2, s2, threads=cores)
+            t += time.perf_counter() - t0
+            n += 1
+        cpu = {"value": ffn_bytes / (t / n) / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+               "build": f"gcc -O3 {O.oracle_isa()} clone, OpenMP",
+               "sample": f"{n} expert FFNs (M={M}) through the C port of the reference fused-kernel loop"}
+    for g in graphs + pgraphs:
+        g.reset()
+    line = {
+        "metric": "mxfp4_matvec_hbm_gbs", "value": gbs, "unit": "GB/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1 weights x e2m1 activation pieces, e8m0 block scales, f32 accumulate (tcgen05 kind::mxf4)",
+        "data": "synthetic (seeded random-init MXFP4 experts of the BASELINE shape)",
+        "config": {"workload": f"BASELINE configs[1]: one expert's SwiGLU FFN (7168 -> 2048 -> 7168, MXFP4) "
+                               f"at M={M} through LatentMoE.expert_forward",
+                   "tokens": M,
+                   "l2": f"inputs larger than L2: a ring of {NE} distinct experts ({NE * EXPERT_BYTES / 1e9:.2f} GB)",
+                   "timing": timing + ", events around K steps"},
+        "frac_of_peak": gbs / peak,
+        "roofline": {"bound": "hbm", "kernel": "bs_gemv_kernel<gate/up> (block-scaled MXFP4 matvec, tcgen05)",
+                     "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
+                     "peak_kind": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu_ms / gu_n},
+        "down_kernel": {"launch_ms": dn_ms / max(dn_n, 1),
+                        "achieved": PROJ_BYTES / (dn_ms / max(dn_n, 1) / 1e3) / 1e9},
+        "matvec_fused_projection": {
+            "api": "mxfp4_matvec_fused (k3_mxfp4_matvec), 7168 -> 2048",
+            "gbs": PROJ_BYTES / (pms / 1e3) / 1e9, "frac_of_peak": PROJ_BYTES / (pms / 1e3) / 1e9 / peak,
+            "ms_per_call": pms, "kernel_launch_ms": mv_ms / max(mv_n, 1),
+            "kernel_gbs": PROJ_BYTES / (mv_ms / max(mv_n, 1) / 1e3) / 1e9,
+            "timing": ptiming + f", {K2} calls over a ring of {NP} distinct projections"},
+        "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
+        "e2e": {"value": ffn_bytes / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
+                "ms_per_step": e2e_ms, "api": "LatentMoE.expert_forward (k3_moe_experts_decode)"},
+        "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+
+
+def reference_matvec(args):
+    """--impl reference for configs[1]: one expert FFN per step through the C port of the
+    reference's fused-kernel loop on every host core."""
+    from oracle import mxfp4_oracle as O
+    M = args.tokens
+    rng = np.random.default_rng(args.seed)
+    (p1, s1), (p3, s3), (p2, s2) = (O.random_mxfp4(rng, I_, H), O.random_mxfp4(rng, I_, H),
+                                    O.random_mxfp4(rng, H, I_))
+    xf = rng.standard_normal((M, H)).astype(np.float32)
+    cores = host_cores()
+
+    def step():
+        g_ = O.matvec_fused(xf, p1, s1, threads=cores)
+        u_ = O.matvec_fused(xf, p3, s3, threads=cores)
+        O.matvec_fused(O.silu(g_) * u_, p2, s2, threads=cores)
+
+    for _ in range(max(1, min(args.warmup, 3))):
+        step()
+    n, t = 0, 0.0
+    while n < max(1, args.steps) and t < 60.0:
+        t0 = time.perf_counter()
+        step()
+        t += time.perf_counter() - t0
+        n += 1
+    v = (EXPERT_BYTES + M * H * 2) / (t / n) / 1e9
+    return {"impl": "reference", "metric": "mxfp4_matvec_hbm_gbs", "value": v, "unit": "GB/s", "n_gpus": 1,
+            "steps": n, "warmup": max(1, min(args.warmup, 3)), "ms_per_step": 1e3 * t / n,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"BASELINE configs[1]: one expert's SwiGLU FFN (7168 -> 2048 -> 7168, MXFP4) "
+                                   f"at M={M}", "tokens": M},
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
+                             "build": f"gcc -O3 {O.oracle_isa()} clone, OpenMP",
+                             "sample": f"{n} whole expert FFNs"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def run_k3(args, rank, world, local):
@@ -833,6 +1114,8 @@ def main():
             run_stream(args, rank, world, local)
         elif args.config == 3:
             run_prefill(args, rank, world, local)
+        elif args.config == 1:
+            run_matvec(args, rank, world, local)
         else:
             run_b200(args, rank, world, local)
     finally:

@@ -129,8 +129,10 @@ K3_API int k3_mxfp4_matvec(const void* x, int x_dtype, int64_t M, int64_t K,
  * This call allocates nothing. Its scratch is one file-scope device array of 4 MiB,
  * which every GPU that loads this library holds until the process exits; shapes that
  * need more scratch than that (see k3_mxfp4_matvec_workspace) return K3_ERR_INVALID.
- * The first call on a device looks the array's address up (cudaGetSymbolAddress, with
- * that device current); make that first call before any stream capture. Every call
+ * The first call in a device's context looks the array's address up
+ * (cudaGetSymbolAddress, with that device current) and keeps it for that context; a
+ * cudaDeviceReset replaces the context, and the next call looks the address up again.
+ * Make the first call on each device before any stream capture. Every call
  * shares the one array, so calls that overlap on the GPU (other streams, other host
  * threads) race; each call re-initialises what it reads from the array. Arguments and
  * results are those of k3_mxfp4_matvec. */
@@ -401,6 +403,19 @@ K3_API int k3_file_read_to_device(const char* path, const int64_t* offsets, cons
 /* Device status word of the last prefill call on `workspace` (synchronises `stream`):
  * K3_OK, or K3_ERR_TIMEOUT when a kernel's bounded wait gave up. */
 K3_API int k3_moe_prefill_status(const void* workspace, void* stream);
+
+/* ------------------------------------------------------- failure detection ----- */
+
+/* Self-test of the bounded device-side wait every pipelined kernel here uses (an
+ * mbarrier wait that gives up after a time limit, writes K3_ERR_TIMEOUT into the call's
+ * status word and returns, so the context stays usable). One CTA waits on a barrier whose
+ * completion `mode` decides: 0 = nothing arrives, the wait runs out after limit_ns
+ * (1e3..2e9); 1 = another warp arrives, the wait succeeds; 2 = another warp raises the
+ * abort flag, the wait gives up without a timeout. result (device int32[3]) <- {status
+ * word, 1 if the wait succeeded else 0, nanoseconds waited}. No reference counterpart:
+ * the reference's guards are host-side (air_llm/models/kimi_k3/model.py:211-216,
+ * loader.py:246-247) and it has no device waits. */
+K3_API int k3_wait_selftest(int64_t limit_ns, int mode, int32_t* result, void* stream);
 
 #ifdef __cplusplus
 }

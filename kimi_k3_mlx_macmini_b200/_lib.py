@@ -98,6 +98,7 @@ SIGNATURES = {
     "k3_file_read_to_device": (_i32, [ctypes.c_char_p, _vp, _vp, _i32, _vp, _vp, _sz, _i32, _vp]),
     "k3_lm_head_argmax": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "k3_moe_ep_local_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
+    "k3_wait_selftest": (_i32, [_i64, _i32, _vp, _vp]),
     "k3_moe_ep_local": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                _vp, _i32, _vp, _sz, _vp]),
 }

@@ -38,10 +38,11 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Waits for the phase of `bar` selected by `parity`. Gives up after kWaitLimitNs (records
+// Waits for the phase of `bar` selected by `parity`. Gives up after limit_ns (records
 // K3_ERR_TIMEOUT in *status) or as soon as *abort becomes non-zero (abort may be null).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status,
-                                          const volatile int* abort = nullptr) {
+                                          const volatile int* abort = nullptr,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
@@ -49,7 +50,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         if (abort && *abort) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             atomicExch(status, K3_ERR_TIMEOUT);
             return false;
         }

@@ -530,15 +530,14 @@ int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batc
 template <bool G>
 int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const char* what) {
     if (grid > kBMaxSegments) return fail(K3_ERR_UNSUPPORTED, "block-scaled grid above 256 CTAs");
-    static bool configured = false;
+    static OncePerContext attr;
     constexpr size_t smem = bsmem_bytes<G>();
-    if (!configured) {
-        if (int rc = cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                                what))
-            return rc;
-        configured = true;
-    }
+    if (int rc = attr.run([&] {
+            return cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   int(smem)),
+                              what);
+        }))
+        return rc;
     if (int rc = cuda_check(launch_pdl(bs_gemv_kernel<G>, dim3(unsigned(grid)), dim3(kBThreads), smem, s, maps, a),
                             what))
         return rc;

@@ -3,6 +3,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
+
 #include "k3_common.cuh"
 
 namespace k3 {
@@ -22,10 +24,48 @@ int cuda_check(cudaError_t e, const char* what) {
                                  cudaGetErrorString(e) + ")");
 }
 
+namespace {
+// Driver entry points for the context id, looked up through the runtime (the library
+// links no driver library of its own).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+std::once_flag g_ctx_fns_once;
+}  // namespace
+
+int current_context(int* dev, unsigned long long* ctx_id) {
+    *ctx_id = 0;
+    if (int rc = cuda_check(cudaGetDevice(dev), "cudaGetDevice")) return rc;
+    if (*dev < 0 || *dev >= kMaxDevices)
+        return fail(K3_ERR_UNSUPPORTED, "device ordinal " + std::to_string(*dev) + " beyond " +
+                                            std::to_string(kMaxDevices));
+    std::call_once(g_ctx_fns_once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(f);
+    });
+    if (!g_ctx_get_current || !g_ctx_get_id)
+        return fail(K3_ERR_CUDA, "cuCtxGetCurrent/cuCtxGetId unavailable from the driver");
+    CUcontext ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) return fail(K3_ERR_CUDA, "cuCtxGetCurrent failed");
+    if (!ctx) return K3_OK;
+    unsigned long long id = 0;
+    if (g_ctx_get_id(ctx, &id) != CUDA_SUCCESS) return fail(K3_ERR_CUDA, "cuCtxGetId failed");
+    *ctx_id = id + 1;                                 // 0 stays "no context"
+    return K3_OK;
+}
+
 int num_sms() {
-    static int cached[64] = {0};
+    static int cached[kMaxDevices] = {0};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
     if (!cached[dev]) {
         int v = 0;
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)

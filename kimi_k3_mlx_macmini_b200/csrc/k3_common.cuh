@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 #include <utility>
 
@@ -33,6 +34,39 @@ void prof_end(int kind, cudaStream_t s);
         int _rc = ::k3::cuda_check(cudaGetLastError(), what);              \
         if (_rc != K3_OK) return _rc;                                      \
     } while (0)
+
+constexpr int kMaxDevices = 64;
+
+// The current device and the id of its current context. Function attributes and the
+// device address of a __device__ array belong to a context: a cudaDeviceReset (or a
+// primary context released and created again) gives the device a new context and a new
+// id, and what was set up for the old one is gone. *ctx_id is 0 while the device has no
+// context yet (nothing has run on it in this process).
+int current_context(int* dev, unsigned long long* ctx_id);
+
+// Runs a set-up step (cudaFuncSetAttribute and the like) once for every context it is
+// called under: each device of a process that drives several GPUs, and again after a
+// device's context was replaced. Thread-safe; a failed step is retried by the next call.
+class OncePerContext {
+public:
+    template <class F>
+    int run(F&& fn) {
+        int dev = -1;
+        unsigned long long id = 0;
+        if (int rc = current_context(&dev, &id)) return rc;
+        std::lock_guard<std::mutex> g(mu_);
+        if (id != 0 && done_[dev] == id) return K3_OK;
+        if (int rc = fn()) return rc;
+        if (id == 0)                                  // fn() created the context
+            if (int rc = current_context(&dev, &id)) return rc;
+        done_[dev] = id;
+        return K3_OK;
+    }
+
+private:
+    std::mutex mu_;
+    unsigned long long done_[kMaxDevices] = {};       // context id the step ran under
+};
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -572,15 +572,14 @@ int weight_map(CUtensorMap* m, const uint16_t* w, int64_t rows, int64_t K, int64
 
 template <int MT>
 int launch_dense(const DenseArgs& a, cudaStream_t s) {
-    static bool attr = false;
+    static OncePerContext attr;
     const size_t smem = dense_smem_bytes<MT>();
-    if (!attr) {
-        if (int rc = cuda_check(cudaFuncSetAttribute(dense_matvec_kernel<MT>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
-                                "cudaFuncSetAttribute(dense_matvec_kernel)"))
-            return rc;
-        attr = true;
-    }
+    if (int rc = attr.run([&] {
+            return cuda_check(cudaFuncSetAttribute(dense_matvec_kernel<MT>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                              "cudaFuncSetAttribute(dense_matvec_kernel)");
+        }))
+        return rc;
     const int G = int(std::min<int64_t>(num_sms(), a.U));
     // programmatic dependent launch: the matvec starts streaming weights while the prep
     // kernel runs, and waits for it (griddepcontrol.wait) before touching its outputs

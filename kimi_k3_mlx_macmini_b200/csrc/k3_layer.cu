@@ -114,20 +114,19 @@ extern "C" K3_API int k3_attn_res_norm(const float* prefix_sum, const float* blo
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const size_t smem = sizeof(float) * size_t(H);
     if (smem > 48 * 1024) {
-        static bool attr[2] = {false, false};
+        static OncePerContext attr[2];
         const int i = n_blocks < 8 ? 0 : 1;
-        if (!attr[i]) {
-            const int rc = i == 0 ? cuda_check(cudaFuncSetAttribute(attn_res_norm_kernel<8>,
-                                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                                    48 * 1024 * 4),
-                                               "cudaFuncSetAttribute(attn_res_norm)")
-                                  : cuda_check(cudaFuncSetAttribute(attn_res_norm_kernel<kARMaxVec>,
-                                                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                                    48 * 1024 * 4),
-                                               "cudaFuncSetAttribute(attn_res_norm)");
-            if (rc) return rc;
-            attr[i] = true;
-        }
+        if (int rc = attr[i].run([&] {
+                return i == 0 ? cuda_check(cudaFuncSetAttribute(attn_res_norm_kernel<8>,
+                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                48 * 1024 * 4),
+                                           "cudaFuncSetAttribute(attn_res_norm)")
+                              : cuda_check(cudaFuncSetAttribute(attn_res_norm_kernel<kARMaxVec>,
+                                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                                48 * 1024 * 4),
+                                           "cudaFuncSetAttribute(attn_res_norm)");
+            }))
+            return rc;
     }
     if (n_blocks < 8)
         launch_ar<8>(prefix_sum, block_residual, int(n_blocks), N, H, res_proj, res_norm, post_norm, eps, out,

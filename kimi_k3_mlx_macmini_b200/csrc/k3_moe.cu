@@ -593,16 +593,15 @@ int set_smem(const char* what) {
                       what);
 }
 
-bool smem_configured = false;
+OncePerContext g_smem_attr;
 int configure_smem() {
-    if (smem_configured) return K3_OK;
-    if (int rc = set_smem<true, false, false>("cudaFuncSetAttribute(gemv gate/up bf16)")) return rc;
-    if (int rc = set_smem<true, false, true>("cudaFuncSetAttribute(gemv gate/up f32)")) return rc;
-    if (int rc = set_smem<false, true, true>("cudaFuncSetAttribute(gemv down)")) return rc;
-    if (int rc = set_smem<false, false, false>("cudaFuncSetAttribute(gemv matvec bf16)")) return rc;
-    if (int rc = set_smem<false, false, true>("cudaFuncSetAttribute(gemv matvec f32)")) return rc;
-    smem_configured = true;
-    return K3_OK;
+    return g_smem_attr.run([] {
+        if (int rc = set_smem<true, false, false>("cudaFuncSetAttribute(gemv gate/up bf16)")) return rc;
+        if (int rc = set_smem<true, false, true>("cudaFuncSetAttribute(gemv gate/up f32)")) return rc;
+        if (int rc = set_smem<false, true, true>("cudaFuncSetAttribute(gemv down)")) return rc;
+        if (int rc = set_smem<false, false, false>("cudaFuncSetAttribute(gemv matvec bf16)")) return rc;
+        return set_smem<false, false, true>("cudaFuncSetAttribute(gemv matvec f32)");
+    });
 }
 
 size_t carve(size_t& off, size_t bytes) {

@@ -33,23 +33,28 @@ constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;   // 4 MiB per device
 // handed to a kernel.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device, looked up once per device
-// (with that device current) and cached.
+// Device address of the scratch array in the current device's context. It is looked up
+// once per context (with that device current) and cached; a device whose context was
+// replaced since (cudaDeviceReset) gets a fresh lookup, since the array then lives at
+// an address of the new context.
 int scratch_address(void** out) {
     int dev = -1;
-    if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
-    if (dev < 0 || dev >= kMaxDevices) return fail(K3_ERR_UNSUPPORTED, "device index out of range");
+    unsigned long long ctx = 0;
+    if (int rc = current_context(&dev, &ctx)) return rc;
     std::lock_guard<std::mutex> g(g_mu);
-    if (!g_scratch_addr[dev]) {
+    if (ctx == 0 || g_scratch_ctx[dev] != ctx) {
         void* p = nullptr;
         if (int rc = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                                 "cudaGetSymbolAddress(no-alloc scratch)"))
             return rc;
+        if (ctx == 0)                                  // the lookup created the context
+            if (int rc = current_context(&dev, &ctx)) return rc;
         g_scratch_addr[dev] = p;
+        g_scratch_ctx[dev] = ctx;
     }
     *out = g_scratch_addr[dev];
     return K3_OK;

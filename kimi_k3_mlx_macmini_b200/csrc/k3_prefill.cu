@@ -856,9 +856,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
-bool g_attr_done = false;
-int configure_prefill() {
-    if (g_attr_done) return K3_OK;
+OncePerContext g_prefill_attr;
+int configure_prefill_once() {
     if (int rc = cuda_check(cudaFuncSetAttribute(prefill_gemm_kernel<true, kPPieces / kPStack>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(psmem_bytes())),
                             "cudaFuncSetAttribute(prefill gate/up)"))
@@ -875,9 +874,9 @@ int configure_prefill() {
                                                  int(rg_smem_bytes())),
                             "cudaFuncSetAttribute(router gemm)"))
         return rc;
-    g_attr_done = true;
     return K3_OK;
 }
+int configure_prefill() { return g_prefill_attr.run(configure_prefill_once); }
 
 size_t carve_p(size_t& off, size_t bytes) {
     const size_t o = off;

@@ -345,16 +345,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
 
 template <bool G, bool H, bool T>
 int launch_one(const TMaps& maps, const TArgs& a, int grid, cudaStream_t s, const char* what) {
-    static bool configured = false;
+    static OncePerContext attr;
     constexpr size_t smem = tsmem_bytes<H, T>();
-    if (!configured) {
-        if (int rc = cuda_check(cudaFuncSetAttribute(gemv_tma_kernel<G, H, T>,
-                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     int(smem)),
-                                what))
-            return rc;
-        configured = true;
-    }
+    if (int rc = attr.run([&] {
+            return cuda_check(cudaFuncSetAttribute(gemv_tma_kernel<G, H, T>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
+                              what);
+        }))
+        return rc;
     gemv_tma_kernel<G, H, T><<<grid, kTThreads, smem, s>>>(maps, a);
     K3_CHECK_LAUNCH(what);
     return K3_OK;

@@ -27,6 +27,12 @@ static inline float e8m0_to_f32(uint8_t b) {
     return f;
 }
 
+/* 3 when the x86-64-v3 clone of k3o_mxfp4_matvec runs on this host, else 2. */
+int k3o_isa_level(void) {
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("x86-64-v3") ? 3 : 2;
+}
+
 int k3o_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();
@@ -36,7 +42,11 @@ int k3o_num_threads(void) {
 }
 
 /* x fp32 [M][K]; packed u8 [N][K/2]; scales u8 [N][K/32]; out fp32 [M][N].
- * threads <= 0 uses the OpenMP default. Returns 0, or 1 on a bad shape. */
+ * threads <= 0 uses the OpenMP default. Returns 0, or 1 on a bad shape.
+ * Two clones, picked at load time by the CPU's features: x86-64-v3 (fmaf as the FMA3
+ * instruction) where the host has it, the x86-64-v2 baseline elsewhere. Both compute the
+ * same fused multiply-adds in the same order. */
+__attribute__((target_clones("arch=x86-64-v3", "default")))
 int k3o_mxfp4_matvec(const float* x, int64_t M, int64_t K, const uint8_t* packed,
                      const uint8_t* scales, int64_t N, float* out, int threads) {
     if (M <= 0 || N <= 0 || K <= 0 || (K % 32) != 0) return 1;

@@ -172,6 +172,11 @@ def oracle_threads() -> int:
     return int(_lib().k3o_num_threads())
 
 
+def oracle_isa() -> str:
+    """The instruction-set level of the C restatement's clone that runs on this host."""
+    return f"x86-64-v{int(_lib().k3o_isa_level())}"
+
+
 # ----------------------------------------------------------------------- activations
 
 def silu(x):

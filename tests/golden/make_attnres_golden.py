@@ -3,7 +3,7 @@ OWN CODE: ``x = rmsnorm(apply_attn_res(prefix_sum, block_residual, mlp_res_proj,
 mlp_res_norm), post_attention_layernorm)`` (``k3ref/layers.py:83-96,321-322``, mirroring
 ``air_llm/models/kimi_k3/layer.py:120-121`` and ``ops.py:61-74``).
 
-    python tests/golden/make_attnres_golden.py /path/to/reference
+    python tests/golden/make_attnres_golden.py --ref /path/to/reference
 
 Inputs are regenerated from seeds by ``inputs.attnres_inputs`` (numpy PCG64) and checked
 by digest; the fixture stores the seeds, the digest and the reference's outputs.
@@ -43,4 +43,7 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", type=Path, required=True, help="reference checkout (read-only)")
+    main(str(ap.parse_args().ref))

@@ -2,7 +2,7 @@
 run over the tiny checkpoint of ``tests/ckpt_util.py`` (seed 0). Needs the reference
 tree (read only); run here, not on the GPU box:
 
-    python tests/golden/make_manifest_golden.py /path/to/reference
+    python tests/golden/make_manifest_golden.py --ref /path/to/reference
 
 Writes ``tests/golden/manifest_tiny.json``: the meta record (minus the machine-specific
 checkpoint path) and every tensor record, in the builder's order.
@@ -33,4 +33,7 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", type=Path, required=True, help="reference checkout (read-only)")
+    main(str(ap.parse_args().ref))

@@ -254,9 +254,10 @@ def _oracle_layer_output(lay, x_bits_host, idx, w):
     return y
 
 
-@pytest.mark.parametrize("M", [1, 8])
+@pytest.mark.parametrize("M", [1, 4, 8])
 def test_full_size_decode_layer(k3, full_layer, M):
-    """BASELINE configs[2] at full size (384 + 1 experts, 7168/2048, top-8, x2.5)."""
+    """BASELINE configs[2] at full size (384 + 1 experts, 7168/2048, top-8, x2.5), at each
+    of its token counts M = 1, 4, 8."""
     from kimi_k3_mlx_macmini_b200 import synthetic
     lay, moe = full_layer
     x = synthetic.tokens(1000 + M, M, 7168)
@@ -343,3 +344,37 @@ def test_packed_tiles_layout(k3):
         for rb in range(2):
             for kt in range(2):
                 assert np.array_equal(out[b, rb, kt], p[b, rb * 128:(rb + 1) * 128, kt * 128:(kt + 1) * 128])
+
+
+# ------------------------------------------------------- unfused validation path
+
+def test_unfused_mxfp4_matvec_matches_oracle(k3):
+    """``mxfp4.py:84-92``: decode to bf16 (lossless), x cast to bf16, bf16 GEMM, result
+    widened to fp32 -- the reference's unfused path, whose product is rounded to bf16."""
+    rng = np.random.default_rng(8)
+    p, s = O.random_mxfp4(rng, 2048, 7168)
+    xb = O.f32_to_bf16_bits(rng.standard_normal((4, 7168)).astype(np.float32))
+    got = host(k3.mxfp4_matvec(bf16_cu(xb), cu(p), cu(s)))
+    assert got.dtype == np.float32 and got.shape == (4, 2048)
+    want = O.matvec_fp64(O.bf16_bits_to_f32(xb), p, s)
+    assert O.rel_l2(got, want) < 4e-3                              # bf16 rounding of the product
+    want_b = O.bf16_bits_to_f32(O.f32_to_bf16_bits(want.astype(np.float32)))
+    assert np.mean(got == want_b) > 0.95                           # mostly the correctly rounded bf16
+
+
+@pytest.mark.parametrize("name", ["moe_small_m1", "moe_small_m5"])
+def test_unfused_moe_matches_reference(k3, name):
+    """``LatentMoE(fused=False)`` (``moe.py:86-88``): every projection dequantised to bf16
+    and multiplied in fp32, expert by expert, against the reference's golden output and the
+    fused path on the same layer."""
+    d, g, spec, _, _ = G.moe_case(name)
+    fused = _baseline_moe(k3, d, spec)
+    unfused = _baseline_moe(k3, d, spec)
+    unfused.fused = False
+    x = bf16_cu(d["x_bf16"])
+    y_u, r = unfused(x, return_router=True)
+    assert O.rel_l2(host(y_u), g["y"]) < NORTH_STAR_REL_L2
+    assert O.rel_l2(host(y_u), g["y"]) < EXPECTED_REL_L2
+    assert O.rel_l2(host(y_u), host(fused(x))) < EXPECTED_REL_L2
+    bad, ties = G.index_sets_match(host(r.expert_indices), g["idx_sorted"], g["corrected"], spec.top_k)
+    assert bad == 0 and ties == 0

@@ -6,8 +6,9 @@ memory belongs to another allocator cannot call cudaMalloc (the memory would go 
 that allocator's back or not exist, and cudaMalloc/cudaFree synchronise the device).
 The no-alloc entry point serves them from one 4 MiB device array built into the
 library. These GPU tests call it through the C ABI and check it against the workspace
-entry point ``k3_mxfp4_matvec``, on two calls in a row, and check that a shape needing
-more scratch than the array is refused with a clear error.
+entry point ``k3_mxfp4_matvec`` bit for bit, on two calls in a row and on consecutive
+calls of different shapes, against the CPU oracle at the BASELINE gate/up shape, and that
+a shape needing more scratch than the array is refused with a clear error.
 
 The file is named to be collected last, so a run that stops at the first failure has
 already run every other test; it also passes alone in a fresh process.
@@ -38,43 +39,79 @@ def _inputs(gen, M, K, N, xdt):
     return x, packed, scales
 
 
-def _with_workspace(L, x, packed, scales, N):
+def _with_workspace(L, x, packed, scales, N, odt=torch.float32):
     lib = L.load_library()
     M, K = x.shape
-    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    out = torch.empty((M, N), dtype=odt, device="cuda")
     ws = torch.empty(lib.k3_mxfp4_matvec_workspace(M, K, N), dtype=torch.uint8, device="cuda")
     L.check(lib.k3_mxfp4_matvec(x.data_ptr(), L.dtype_code(x), M, K, packed.data_ptr(),
-                                scales.data_ptr(), N, out.data_ptr(), L.K3_F32, ws.data_ptr(),
+                                scales.data_ptr(), N, out.data_ptr(), L.dtype_code(out), ws.data_ptr(),
                                 ws.numel(), L.stream_of(x)), "k3_mxfp4_matvec")
     return out
 
 
-def _no_alloc(L, x, packed, scales, N):
+def _no_alloc(L, x, packed, scales, N, odt=torch.float32):
     lib = L.load_library()
     M, K = x.shape
-    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    out = torch.empty((M, N), dtype=odt, device="cuda")
     L.check(lib.k3_mxfp4_matvec_noalloc(x.data_ptr(), L.dtype_code(x), M, K, packed.data_ptr(),
-                                        scales.data_ptr(), N, out.data_ptr(), L.K3_F32,
+                                        scales.data_ptr(), N, out.data_ptr(), L.dtype_code(out),
                                         L.stream_of(x)), "k3_mxfp4_matvec_noalloc")
     return out
 
 
-@pytest.mark.parametrize("M,K,N,xdt", [
-    (8, 7168, 2048, torch.bfloat16),     # BASELINE gate/up projection, decode batch
-    (3, 2048, 7168, torch.float32),      # BASELINE down projection, fp32 activations
-    (11, 256, 128, torch.float32),       # more than 8 tokens: chunked launches
+def _rel(got, want):
+    return float(torch.linalg.vector_norm((got.double() - want.double())) / torch.linalg.vector_norm(want.double()))
+
+
+@pytest.mark.parametrize("M,K,N,xdt,odt", [
+    (8, 7168, 2048, torch.bfloat16, torch.float32),    # BASELINE gate/up projection, decode batch
+    (1, 7168, 2048, torch.bfloat16, torch.bfloat16),   # one token, bf16 result
+    (3, 2048, 7168, torch.float32, torch.float32),     # BASELINE down projection, fp32 activations
+    (11, 256, 128, torch.float32, torch.float32),      # more than 8 tokens: chunked launches
 ])
-def test_no_alloc_matches_workspace_entry_point(lib, M, K, N, xdt):
+def test_no_alloc_matches_workspace_entry_point(lib, M, K, N, xdt, odt):
+    """Both entry points run the same kernels, whose split-k partial sums are added in a
+    fixed order, so the results are identical bit for bit -- a leftover of an earlier
+    call's scratch would show as a difference."""
     gen = torch.Generator(device="cuda")
     gen.manual_seed(M * 7919 + K + N)
     for call in range(2):                                # two calls in a row, fresh inputs
         x, packed, scales = _inputs(gen, M, K, N, xdt)
-        want = _with_workspace(lib, x, packed, scales, N)
-        got = _no_alloc(lib, x, packed, scales, N)
+        want = _with_workspace(lib, x, packed, scales, N, odt)
+        got = _no_alloc(lib, x, packed, scales, N, odt)
         torch.cuda.synchronize()
-        rel = float(torch.linalg.vector_norm((got - want).double()) /
-                    torch.linalg.vector_norm(want.double()))
-        assert rel < REL_L2_TOL, f"call {call}: rel-L2 {rel:.3e}"
+        assert _rel(got, want) < REL_L2_TOL, f"call {call}"
+        assert torch.equal(got, want), f"call {call}: not bitwise equal"
+
+
+def test_no_alloc_consecutive_calls_on_different_shapes(lib):
+    """Calls that leave different plans, counters and partial sums in the shared scratch
+    (a tall down-projection shape, then the gate/up shape, then a small one) each match
+    the workspace entry point bit for bit."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(99)
+    for M, K, N, xdt in [(8, 2048, 7168, torch.float32), (5, 7168, 2048, torch.bfloat16),
+                         (2, 512, 256, torch.bfloat16), (8, 7168, 2048, torch.float32)]:
+        x, packed, scales = _inputs(gen, M, K, N, xdt)
+        got = _no_alloc(lib, x, packed, scales, N)
+        want = _with_workspace(lib, x, packed, scales, N)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), (M, K, N)
+
+
+def test_no_alloc_matches_oracle_at_baseline_shape(lib):
+    """The BASELINE gate/up projection (7168 -> 2048) at M = 8 against the C restatement
+    of the reference's fused-kernel loop (``mxfp4_matvec.py:29-63``) and fp64."""
+    from oracle import mxfp4_oracle as O
+    rng = np.random.default_rng(2048)
+    p, s = O.random_mxfp4(rng, 2048, 7168)
+    xb = O.f32_to_bf16_bits(rng.standard_normal((8, 7168)).astype(np.float32))
+    xf = O.bf16_bits_to_f32(xb)
+    x = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    got = _no_alloc(lib, x, torch.from_numpy(p).cuda(), torch.from_numpy(s).cuda(), 2048).cpu().numpy()
+    assert O.rel_l2(got, O.matvec_fused(xf, p, s)) < REL_L2_TOL
+    assert O.rel_l2(got, O.matvec_fp64(xf, p, s)) < REL_L2_TOL
 
 
 def test_no_alloc_refuses_shapes_beyond_its_scratch(lib):
