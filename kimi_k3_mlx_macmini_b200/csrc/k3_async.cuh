@@ -116,6 +116,12 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
         : "memory");
 }
 
+// Brings a tensor-map descriptor (a __grid_constant__ kernel parameter) into the
+// descriptor cache ahead of its first copy.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
 // L2 prefetch of one tensor-map box (no shared memory, no completion tracking).
 __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int c0, int c1, int c2) {
     asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];\n" ::"l"(

@@ -45,11 +45,12 @@ __device__ __forceinline__ float sum8(const float* v) {
 
 }  // namespace
 
-template <bool GATEUP>
+template <bool GATEUP, bool SFRAW>
 __global__ void __launch_bounds__(kBThreads, 1)
     bs_gemv_kernel(const __grid_constant__ BMaps maps, const BArgs a) {
-    using St = BStage<GATEUP>;
-    constexpr int S = bstages<GATEUP>();
+    static_assert(!(GATEUP && SFRAW), "row-major scales are read by the single-projection kernel only");
+    using St = BStage<GATEUP, SFRAW>;
+    constexpr int S = bstages<GATEUP, SFRAW>();
     constexpr uint32_t kCols = btmem_cols<GATEUP>();
     constexpr int kAccW = GATEUP ? 128 : 64;               // TMEM columns per accumulator
     constexpr int kSf0 = 2 * kAccW;                        // first scale column
@@ -76,6 +77,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
+        // the tensor-map descriptors are fetched while the prologue runs, not at the first
+        // copy (about a microsecond each when cold)
+        prefetch_tensormap(&maps.a0);
+        if (GATEUP) prefetch_tensormap(&maps.a1);
+        prefetch_tensormap(&maps.b);
+        if (SFRAW) prefetch_tensormap(&maps.sfa);
+    }
+    if (threadIdx.x == 0) {
         s_abort = 0;
         s_issued = 0;
         for (int s = 0; s < S; ++s) {
@@ -93,10 +102,29 @@ __global__ void __launch_bounds__(kBThreads, 1)
     // copy) now; it waits for this launch before reading anything it writes
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     if (warp == 1) tmem_alloc(&s_tmem, kCols);
-    // the plan was written two launches back (router / plan kernel, then the scale-chunk
-    // gather), which had completed when the previous launch started
-    for (int i = threadIdx.x; i < int(sizeof(Plan) / 4); i += blockDim.x)
-        reinterpret_cast<int*>(&s_plan)[i] = reinterpret_cast<const int*>(a.plan)[i];
+    if (a.identity_m > 0) {
+        // the identity plan (single-matrix matvec): items of 8 tokens, slot 0, weight 1
+        const int Mi = a.identity_m, Vi = (Mi + kBMaxN / kBPieces - 1) / (kBMaxN / kBPieces);
+        if (threadIdx.x == 0) {
+            s_plan.n_active = Vi;
+            s_plan.n_pairs = Mi;
+            s_plan.M = Mi;
+            s_plan.status = K3_OK;
+        }
+        for (int v = threadIdx.x; v <= Vi; v += blockDim.x) {
+            if (v < Vi) s_plan.expert[v] = 0;
+            s_plan.pair_start[v] = min(v * (kBMaxN / kBPieces), Mi);
+        }
+        for (int q = threadIdx.x; q < Mi; q += blockDim.x) {
+            s_plan.pair_tok[q] = q;
+            s_plan.pair_w[q] = 1.0f;
+        }
+    } else {
+        // the plan was written two launches back (router / plan kernel, then the scale-chunk
+        // gather), which had completed when the previous launch started
+        for (int i = threadIdx.x; i < int(sizeof(Plan) / 4); i += blockDim.x)
+            reinterpret_cast<int*>(&s_plan)[i] = reinterpret_cast<const int*>(a.plan)[i];
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -120,53 +148,110 @@ __global__ void __launch_bounds__(kBThreads, 1)
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint64_t stream_once = l2_evict_first();
+            // what the stages of one item share (computed once per item: 64-bit divisions)
+            struct Item {
+                int v, rb, slot, ps, np, r0, tb;
+                int64_t kbase;
+                uint32_t bytes;
+            };
+            auto item_at = [&](int64_t i) {
+                Item it;
+                const int64_t key = i / ipk;
+                it.v = int(key % V);
+                it.rb = int(key / V);
+                it.slot = P->expert[it.v];
+                it.ps = P->pair_start[it.v];
+                it.np = P->pair_start[it.v + 1] - it.ps;
+                it.r0 = it.rb * kBRows;
+                it.tb = it.slot * int(nRb) + it.rb;
+                it.kbase = int64_t(i % ipk) * kchunk;
+                it.bytes = uint32_t((GATEUP ? 2 : 1) * (kBRows * 128 + (SFRAW ? kBRows * 16 : 2 * kBChunk)) +
+                                    it.np * kBPieces * 128 + 2 * kBChunk);
+                return it;
+            };
+            // the weight tiles and their scales of k-step s
+            auto stage_a = [&](const Item& it, int s, int si) {
+                St& st = ring[si];
+                const int64_t k = it.kbase + int64_t(s) * kBStageK;
+                const int64_t sfo = int64_t(it.slot) * a.sf_slot + (int64_t(it.rb) * kcks + k / 128) * kBChunk;
+                if (a.tiled)
+                    tma_4d_hint(&st.a[0][0][0], &maps.a0, 0, 0, int(k / kBStageK), it.tb, &full[si], stream_once);
+                else
+                    tma_3d_hint(&st.a[0][0][0], &maps.a0, int(k / 2), it.r0, it.slot, &full[si], stream_once);
+                if constexpr (SFRAW)      // the 512-k scale box holding this stage's 256 k
+                    tma_2d(&st.sfraw[0][0], &maps.sfa, int(k / 512) * 16, it.slot * int(a.rows) + it.r0, &full[si]);
+                else
+                    bulk_g2s_hint(&st.sfa[0][0], a.sfa0 + sfo, 2 * kBChunk, &full[si], stream_once);
+                if (GATEUP) {
+                    if (a.tiled)
+                        tma_4d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), it.tb,
+                                    &full[si], stream_once);
+                    else
+                        tma_3d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), it.r0, it.slot, &full[si],
+                                    stream_once);
+                    bulk_g2s_hint(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si], stream_once);
+                }
+            };
+            // the activation pieces and their scale chunks of k-step s (written by the
+            // previous launch)
+            auto stage_b = [&](const Item& it, int s, int si) {
+                St& st = ring[si];
+                const int64_t k = it.kbase + int64_t(s) * kBStageK;
+                if (GATEUP) {
+                    for (int pi = 0; pi < it.np; ++pi)      // one token's 8 piece rows per pair
+                        tma_2d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * P->pair_tok[it.ps + pi],
+                               &full[si]);
+                } else {
+                    for (int pi = 0; pi < it.np; ++pi)      // pair pi's 8 piece rows
+                        tma_3d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * pi, it.v, &full[si]);
+                }
+                bulk_g2s(&st.sfb[0], a.sfb + (int64_t(it.v) * kcks + k / 128) * kBChunk, 2 * kBChunk, &full[si]);
+            };
+            // Nothing of the weights comes from the previous launch: when allowed, request
+            // the first stages' weight tiles and scales (the ring starts empty) before
+            // waiting for it. (ie, se) is the first stage not yet requested.
+            int64_t ie = i0;
+            int se = 0;
+            uint32_t pre = 0;
+            if (a.identity_m > 0 || a.early_a) {
+                while (ie < i1 && pre < uint32_t(S)) {
+                    const Item it = item_at(ie);
+                    for (; se < nst && pre < uint32_t(S); ++se, ++pre) {
+                        mbar_expect_tx(&full[pre], it.bytes);
+                        stage_a(it, se, int(pre));
+                    }
+                    if (se == nst) {
+                        se = 0;
+                        ++ie;
+                    }
+                }
+            }
             // The B operand (token or activation pieces and their scale chunks) comes from
             // the previous launch, which may still be running (programmatic dependent
-            // launch): wait for it before the first request.
+            // launch): wait for it before the first request of it.
             asm volatile("griddepcontrol.wait;\n" ::: "memory");
-            uint32_t gs = 0;
-            for (int64_t i = i0; i < i1 && !s_abort; ++i) {
-                const int64_t key = i / ipk;
-                const int v = int(key % V), rb = int(key / V), kc = int(i % ipk);
-                const int slot = P->expert[v];
-                const int ps = P->pair_start[v], np = P->pair_start[v + 1] - ps;
-                const uint32_t bytes = uint32_t((GATEUP ? 2 : 1) * (kBRows * 128 + 2 * kBChunk) +
-                                                np * kBPieces * 128 + 2 * kBChunk);
-                const int r0 = rb * kBRows;
-                const int tb = slot * int(nRb) + rb;                         // tile row block
-                for (int s = 0; s < nst; ++s, ++gs) {
+            {
+                uint32_t g = 0;
+                for (int64_t i = i0; g < pre; ++i) {
+                    const Item it = item_at(i);
+                    for (int s = 0; s < nst && g < pre; ++s, ++g) {
+                        stage_b(it, s, int(g));
+                        s_issued = g + 1;
+                    }
+                }
+            }
+            uint32_t gs = pre;
+            for (int64_t i = ie; i < i1 && !s_abort; ++i) {
+                const Item it = item_at(i);
+                for (int s = (i == ie ? se : 0); s < nst; ++s, ++gs) {
                     const int si = int(gs % S);
                     if (!mbar_wait(&empty[si], ((gs / S) & 1) ^ 1, a.status, &s_abort)) {
                         s_abort = 1;
                         break;
                     }
-                    St& st = ring[si];
-                    const int64_t k = int64_t(kc) * kchunk + int64_t(s) * kBStageK;
-                    mbar_expect_tx(&full[si], bytes);
-                    const int64_t sfo = int64_t(slot) * a.sf_slot + (int64_t(rb) * kcks + k / 128) * kBChunk;
-                    if (a.tiled)
-                        tma_4d_hint(&st.a[0][0][0], &maps.a0, 0, 0, int(k / kBStageK), tb, &full[si], stream_once);
-                    else
-                        tma_3d_hint(&st.a[0][0][0], &maps.a0, int(k / 2), r0, slot, &full[si], stream_once);
-                    bulk_g2s_hint(&st.sfa[0][0], a.sfa0 + sfo, 2 * kBChunk, &full[si], stream_once);
-                    if (GATEUP) {
-                        if (a.tiled)
-                            tma_4d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, 0, 0, int(k / kBStageK), tb,
-                                        &full[si], stream_once);
-                        else
-                            tma_3d_hint(&st.a[GATEUP ? 1 : 0][0][0], &maps.a1, int(k / 2), r0, slot, &full[si],
-                                        stream_once);
-                        bulk_g2s_hint(&st.sfa[GATEUP ? 1 : 0][0], a.sfa1 + sfo, 2 * kBChunk, &full[si], stream_once);
-                    }
-                    if (GATEUP) {
-                        for (int pi = 0; pi < np; ++pi)      // one token's 8 piece rows per pair
-                            tma_2d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * P->pair_tok[ps + pi],
-                                   &full[si]);
-                    } else {
-                        for (int pi = 0; pi < np; ++pi)      // pair pi's 8 piece rows
-                            tma_3d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * pi, v, &full[si]);
-                    }
-                    bulk_g2s(&st.sfb[0], a.sfb + (int64_t(v) * kcks + k / 128) * kBChunk, 2 * kBChunk, &full[si]);
+                    mbar_expect_tx(&full[si], it.bytes);
+                    stage_a(it, s, si);
+                    stage_b(it, s, si);
                     s_issued = gs + 1;
                 }
             }
@@ -179,6 +264,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
             const int v = int((i / ipk) % V);
             const int np = P->pair_start[v + 1] - P->pair_start[v];
             const int nb = kBPieces * np;                                // MMA N
+            // SFRAW: parity of the item's first 256-k step (which half of a 512-k scale box)
+            const int half0 = SFRAW ? int((int64_t(i % ipk) * nst) & 1) : 0;
             const uint32_t buf = ib & 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&acce[buf], ((ib >> 1) & 1) ^ 1, a.status, &s_abort))) {
                 s_abort = 1;
@@ -195,7 +282,24 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const St& st = ring[si];
+                St& st = ring[si];
+                if constexpr (SFRAW) {
+                    // the stage's two scale chunks from its 8 bytes of every row of the raw
+                    // box: lane l writes rows l + 32c, byte j of chunk h at l*16 + 4c + j
+                    const int half = (half0 + s) & 1;
+                    uint32_t w0[4], w1[4];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint2 v2 = *reinterpret_cast<const uint2*>(&st.sfraw[32 * c + lane][8 * half]);
+                        w0[c] = v2.x;
+                        w1[c] = v2.y;
+                    }
+                    *reinterpret_cast<uint4*>(&st.sfa[0][16 * lane]) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+                    *reinterpret_cast<uint4*>(&st.sfa[0][kBChunk + 16 * lane]) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+                    // generic-proxy writes, read next by tcgen05.cp (async proxy)
+                    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                    __syncwarp();
+                }
                 const uint32_t sf = tm + kSf0 + kSfW * si;
                 const uint32_t sfa0 = sf, sfa1 = sf + 8, sfb = sf + (GATEUP ? 16 : 8);
                 if (elect_one()) {
@@ -319,16 +423,29 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 __threadfence();
 #pragma unroll
                 for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
-                for (int sg = 0; sg < s_nseg; ++sg) {       // segment order: deterministic sums
+                // segment order: deterministic sums; the next segment's loads are in flight
+                // while one is added (two register buffers)
+                const int nseg = s_nseg;
+                float xa[kPW], xb[kPW];
+                auto load_seg = [&](float (&x)[kPW], int sg) {
                     const float* sp = kpart + int64_t(s_seg[sg]) * (kPW * kBRows);
-                    float x[kPW];
 #pragma unroll
                     for (int c = 0; c < kPW; ++c) x[c] = __ldcg(sp + c * kBRows + r);
+                };
+                auto add_seg = [&](const float (&x)[kPW]) {
 #pragma unroll
                     for (int pi = 0; pi < kMaxPr; ++pi) {
                         acc0[pi] += x[pi];
                         if (GATEUP) acc1[pi] += x[(GATEUP ? kMaxPr : 0) + pi];
                     }
+                };
+                if (nseg > 0) load_seg(xa, 0);
+                for (int sg = 0; sg < nseg; sg += 2) {
+                    if (sg + 1 < nseg) load_seg(xb, sg + 1);
+                    add_seg(xa);
+                    if (sg + 1 >= nseg) break;
+                    if (sg + 2 < nseg) load_seg(xa, sg + 2);
+                    add_seg(xb);
                 }
             }
             if (GATEUP) {
@@ -359,7 +476,13 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 const int64_t row = int64_t(rb) * kBRows + r;
 #pragma unroll
                 for (int pi = 0; pi < kMaxPr; ++pi)
-                    if (pi < np) a.y_pair[int64_t(ps + pi) * a.rows + row] = acc0[pi];
+                    if (pi < np) {
+                        if (a.y_bf16)
+                            reinterpret_cast<__nv_bfloat16*>(a.y_pair)[int64_t(ps + pi) * a.rows + row] =
+                                __float2bfloat16_rn(acc0[pi]);
+                        else
+                            a.y_pair[int64_t(ps + pi) * a.rows + row] = acc0[pi];
+                    }
             }
             if (!local && et == 0) a.cnt[key] = 0u;        // ready for the next call
             if (!local) epi_sync();                          // s_seg is rewritten by the next key
@@ -527,18 +650,19 @@ int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batc
 
 // ------------------------------------------------------------------ launches
 
-template <bool G>
+template <bool G, bool SFRAW = false>
 int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const char* what) {
     if (grid > kBMaxSegments) return fail(K3_ERR_UNSUPPORTED, "block-scaled grid above 256 CTAs");
     static OncePerContext attr;
-    constexpr size_t smem = bsmem_bytes<G>();
+    constexpr size_t smem = bsmem_bytes<G, SFRAW>();
     if (int rc = attr.run([&] {
-            return cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   int(smem)),
+            return cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G, SFRAW>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
                               what);
         }))
         return rc;
-    if (int rc = cuda_check(launch_pdl(bs_gemv_kernel<G>, dim3(unsigned(grid)), dim3(kBThreads), smem, s, maps, a),
+    if (int rc = cuda_check(launch_pdl(bs_gemv_kernel<G, SFRAW>, dim3(unsigned(grid)), dim3(kBThreads), smem, s,
+                                       maps, a),
                             what))
         return rc;
     return K3_OK;
@@ -549,6 +673,9 @@ int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s
 }
 int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
     return launch_bs<false>(maps, a, grid, s, "bs_gemv<down>");
+}
+int launch_bs_proj_rawsf(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
+    return launch_bs<false, true>(maps, a, grid, s, "bs_gemv<projection, stored scales>");
 }
 
 }  // namespace k3

@@ -33,32 +33,45 @@ __host__ __device__ __forceinline__ int sf_chunk_offset(int n, int j) {
 }
 
 // One pipeline stage. Gate/up: the 128-row gate tile and the 128-row up tile of one
-// expert block share the B tile; down: one 128-row tile.
+// expert block share the B tile; down: one 128-row tile. SFRAW stages (weights with their
+// scales as stored, row-major [rows][K/32]) also hold the TMA box of those scales: 16
+// bytes (512 k) of each of the 128 rows, from which the MMA warp writes the stage's two
+// scale chunks.
 template <bool GATEUP>
-struct alignas(1024) BStage {
+struct alignas(1024) BStageBase {
     uint8_t a[GATEUP ? 2 : 1][kBRows][128];     // E2M1 weights, SW128
     uint8_t b[kBMaxN][128];                     // E2M1 activation pieces, SW128
     uint8_t sfa[GATEUP ? 2 : 1][2 * kBChunk];   // weight scales, two chunks (256 k)
     uint8_t sfb[2 * kBChunk];                   // piece scales, two chunks
 };
-
+template <bool GATEUP, bool SFRAW = false>
+struct alignas(1024) BStage : BStageBase<GATEUP> {};
 template <bool GATEUP>
-constexpr int bstages() { return GATEUP ? 5 : 8; }
+struct alignas(1024) BStage<GATEUP, true> : BStageBase<GATEUP> {
+    uint8_t sfraw[kBRows][16];                  // row-major scale box (512 k)
+};
+static_assert(sizeof(BStage<false>) == sizeof(BStageBase<false>) && sizeof(BStage<true>) == sizeof(BStageBase<true>),
+              "the stored-layout stages carry no raw scale box");
+
+template <bool GATEUP, bool SFRAW = false>
+constexpr int bstages() { return GATEUP ? 5 : (SFRAW ? 7 : 8); }
 template <bool GATEUP>
 constexpr uint32_t btmem_cols() { return GATEUP ? 512 : 256; }
-template <bool GATEUP>
+template <bool GATEUP, bool SFRAW = false>
 constexpr size_t bsmem_bytes() {
-    return sizeof(BStage<GATEUP>) * bstages<GATEUP>() + 1024 /*align*/ + 256 /*barriers*/;
+    return sizeof(BStage<GATEUP, SFRAW>) * bstages<GATEUP, SFRAW>() + 1024 /*align*/ + 256 /*barriers*/;
 }
-static_assert(bsmem_bytes<true>() + 4096 <= 227 * 1024 && bsmem_bytes<false>() + 4096 <= 227 * 1024,
+static_assert(bsmem_bytes<true>() + 4096 <= 227 * 1024 && bsmem_bytes<false>() + 4096 <= 227 * 1024 &&
+                  bsmem_bytes<false, true>() + 4096 <= 227 * 1024,
               "block-scaled ring exceeds shared memory");
 
 // Tensor maps: a0/a1 = packed weight pools, row-major [slot][rows][K/2] (box 128 B x 128
 // rows) or tiled [slot * rows/128][K/256][128][128] (box = one contiguous tile);
 // b = activation pieces, gate/up x [8T][K/2] (box 128 B x 8 rows: one token's pieces),
-// down act [v][64][K/2] (box 128 B x 8 rows: one pair's pieces).
+// down act [v][64][K/2] (box 128 B x 8 rows: one pair's pieces); sfa (SFRAW only) = the
+// weight scales as stored, [slot * rows][K/32] (box 16 B x 128 rows).
 struct BMaps {
-    CUtensorMap a0, a1, b;
+    CUtensorMap a0, a1, b, sfa;
 };
 
 struct BArgs {
@@ -82,12 +95,24 @@ struct BArgs {
     uint8_t* act_sf;
     int act_kind;
     float beta, lbeta;
-    // down epilogue: one f32 output row per pair, y_pair [pairs][H]
+    // down epilogue: one f32 output row per pair, y_pair [pairs][H] (bf16 when y_bf16)
     float* y_pair;
+    int y_bf16;
+    // > 0: the plan is the identity plan of identity_m tokens (items of 8 tokens of slot 0,
+    // weight 1), built by each CTA itself; the weights and their scales are then requested
+    // before the wait for the previous launch (which writes only the activation operand)
+    int identity_m;
+    // request the first stages' weights before waiting for the previous launch (the weights
+    // and the plan never come from it): set for the down phase, whose CTAs start on the SMs
+    // that the gate/up launch's early finishers leave
+    int early_a;
 };
 
 int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
 int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
+// The down-phase kernel over a weight matrix whose scales are row-major as stored
+// (maps.sfa), for the single-matrix matvec.
+int launch_bs_proj_rawsf(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
 // Per-item B scale chunks of the gate/up phase from the per-row x piece scales.
 int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
                       cudaStream_t s);

@@ -1,4 +1,5 @@
 // C-ABI plumbing: error state, device queries, and the fused-matvec entry point.
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -128,6 +129,11 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
                 const uint8_t* scales, int64_t N, void* out, int odt, uint8_t* ws, cudaStream_t s);
 int launch_matvec_simple(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* packed,
                          const uint8_t* scales, int64_t N, void* out, int odt, cudaStream_t s);
+// defined in k3_mv.cu
+bool matvec_bs_ok(int64_t K, int64_t N, const uint8_t* packed, const uint8_t* scales);
+size_t matvec_bs_workspace(int64_t M, int64_t K, int64_t N);
+int matvec_bs(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* packed, const uint8_t* scales,
+              int64_t N, void* out, int odt, uint8_t* ws, cudaStream_t s);
 
 }  // namespace k3
 
@@ -172,8 +178,10 @@ extern "C" K3_API int k3_profile_collect(double* ms_out, int64_t* launches_out, 
 
 extern "C" K3_API size_t k3_mxfp4_matvec_workspace(int64_t M, int64_t K, int64_t N) {
     if (M < 1 || K < 32 || N < 1) return 0;
-    if (K % 128 == 0 && N % 64 == 0) return matvec_fast_workspace(M, K, N);
-    return 256;
+    size_t need = 256;
+    if (K % 128 == 0 && N % 64 == 0) need = std::max(need, matvec_fast_workspace(M, K, N));
+    if (K % 512 == 0 && N % 128 == 0) need = std::max(need, matvec_bs_workspace(M, K, N));
+    return need;
 }
 
 extern "C" K3_API int k3_mxfp4_matvec(const void* x, int x_dtype, int64_t M, int64_t K,
@@ -186,6 +194,13 @@ extern "C" K3_API int k3_mxfp4_matvec(const void* x, int x_dtype, int64_t M, int
     if (M < 1 || N < 1 || K < 32 || K % 32)
         return fail(K3_ERR_INVALID, "k3_mxfp4_matvec: need M, N >= 1 and K a positive multiple of 32 (K=" + std::to_string(K) + ")");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (matvec_bs_ok(K, N, packed, scales)) {           // block-scaled tensor cores (tcgen05)
+        const size_t need = matvec_bs_workspace(M, K, N);
+        if (!workspace) return fail(K3_ERR_WORKSPACE, "k3_mxfp4_matvec: workspace is NULL");
+        if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(K3_ERR_WORKSPACE, "k3_mxfp4_matvec: workspace must be 256-byte aligned");
+        if (workspace_bytes < need) return fail(K3_ERR_WORKSPACE, "k3_mxfp4_matvec: workspace too small: need " + std::to_string(need));
+        return matvec_bs(x, x_dtype, M, K, packed, scales, N, out, out_dtype, static_cast<uint8_t*>(workspace), s);
+    }
     if (matvec_fast_ok(K, N, x, packed, scales)) {
         const size_t need = matvec_fast_workspace(M, K, N);
         if (!workspace) return fail(K3_ERR_WORKSPACE, "k3_mxfp4_matvec: workspace is NULL");

@@ -206,14 +206,16 @@ struct PrepArgs {
 __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (blockIdx.x > 0) {
-        if (a.xp) {                        // CTA 1+kb: 32-blocks 16kb.. of token `warp`
-            const int64_t g0 = int64_t(blockIdx.x - 1) * 16;
-            if (warp < a.M)
-                for (int64_t g = g0; g < g0 + 16 && g < a.K / 32; ++g) {
-                    const float v = load_as_f32(a.x, a.x_dtype, int64_t(warp) * a.K + 32 * g + lane);
-                    split_pieces(v, lane, a.xp + int64_t(kBPieces * warp) * (a.K / 2) + 16 * g, a.K / 2,
-                                 a.xsf + int64_t(kBPieces * warp) * (a.K / 32) + g, a.K / 32);
-                }
+        if (a.xp) {                        // one warp per (token, 32-block): the piece split is a
+                                           // serial chain, so it is spread over many CTAs
+            const int64_t G = a.K / 32;
+            const int64_t task = int64_t(blockIdx.x - 1) * (blockDim.x >> 5) + warp;
+            if (task < int64_t(a.M) * G) {
+                const int64_t t = task / G, g = task % G;
+                const float v = load_as_f32(a.x, a.x_dtype, t * a.K + 32 * g + lane);
+                split_pieces(v, lane, a.xp + int64_t(kBPieces) * t * (a.K / 2) + 16 * g, a.K / 2,
+                             a.xsf + int64_t(kBPieces) * t * G + g, G);
+            }
             return;
         }
         if (a.blocked) {                   // CTA 1+kb: block kb of every token (warp t)
@@ -988,6 +990,7 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     tb.sf_slot = (L.H / 128) * (L.I / 128) * kBChunk;
     tb.sfb = act_sf;
     tb.y_pair = reinterpret_cast<float*>(ws + L.y_pair);
+    tb.early_a = 1;     // W2 tiles stream on the SMs the gate/up launch's early finishers free
     prof_begin(K3_PROF_DOWN, s);
     rc = launch_bs_down(mb, tb, sms, s);
     prof_end(K3_PROF_DOWN, s);
@@ -1079,7 +1082,8 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
     pa.xp = L.bs ? ws + L.xq_hi : nullptr;
     pa.xsf = L.bs ? ws + L.xq_ts : nullptr;
     prof_begin(K3_PROF_TOPK, s);
-    prep_kernel<<<1 + (L.tma ? int((L.H + 511) / 512) : int(M)), 256, 0, s>>>(pa);
+    const int prep_ctas = L.bs ? int((M * (L.H / 32) + 7) / 8) : L.tma ? int((L.H + 511) / 512) : int(M);
+    prep_kernel<<<1 + prep_ctas, 256, 0, s>>>(pa);
     prof_end(K3_PROF_TOPK, s);
     K3_CHECK_LAUNCH("prep_kernel");
     if (L.bs) return decode_bs(p, L, ws, int(M), y, ydt, sms, s);

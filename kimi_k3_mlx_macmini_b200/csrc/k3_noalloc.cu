@@ -23,6 +23,11 @@ int matvec_fast(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* pac
                 const uint8_t* scales, int64_t N, void* out, int odt, uint8_t* ws, cudaStream_t s);
 int launch_matvec_simple(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* packed,
                          const uint8_t* scales, int64_t N, void* out, int odt, cudaStream_t s);
+// defined in k3_mv.cu
+bool matvec_bs_ok(int64_t K, int64_t N, const uint8_t* packed, const uint8_t* scales);
+size_t matvec_bs_workspace(int64_t M, int64_t K, int64_t N);
+int matvec_bs(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* packed, const uint8_t* scales,
+              int64_t N, void* out, int odt, uint8_t* ws, cudaStream_t s);
 
 namespace {
 
@@ -74,9 +79,10 @@ extern "C" K3_API int k3_mxfp4_matvec_noalloc(const void* x, int x_dtype, int64_
     if (M < 1 || N < 1 || K < 32 || K % 32)
         return fail(K3_ERR_INVALID, "k3_mxfp4_matvec_noalloc: need M, N >= 1 and K a positive multiple of 32");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (!matvec_fast_ok(K, N, x, packed, scales))        // the generic kernel needs no scratch
+    const bool bs = matvec_bs_ok(K, N, packed, scales);
+    if (!bs && !matvec_fast_ok(K, N, x, packed, scales))  // the generic kernel needs no scratch
         return launch_matvec_simple(x, x_dtype, M, K, packed, scales, N, out, out_dtype, s);
-    const size_t need = matvec_fast_workspace(M, K, N);
+    const size_t need = bs ? matvec_bs_workspace(M, K, N) : matvec_fast_workspace(M, K, N);
     if (need > kNoAllocScratchBytes)
         return fail(K3_ERR_INVALID, "k3_mxfp4_matvec_noalloc: M=" + std::to_string(M) + " K=" +
                                         std::to_string(K) + " N=" + std::to_string(N) + " needs " +
@@ -85,9 +91,11 @@ extern "C" K3_API int k3_mxfp4_matvec_noalloc(const void* x, int x_dtype, int64_
                                         "-byte no-alloc limit; use k3_mxfp4_matvec with a workspace");
     void* scratch = nullptr;
     if (int rc = scratch_address(&scratch)) return rc;
-    // The prep kernel rewrites the plan and the converted x and zeroes the arrival
+    // The prep kernel rewrites the converted x (and the plan) and zeroes the arrival
     // counters; every partial sum is written before it is read. Nothing of a previous
     // call's contents is used.
+    if (bs)
+        return matvec_bs(x, x_dtype, M, K, packed, scales, N, out, out_dtype, static_cast<uint8_t*>(scratch), s);
     return matvec_fast(x, x_dtype, M, K, packed, scales, N, out, out_dtype,
                        static_cast<uint8_t*>(scratch), s);
 }

@@ -168,9 +168,9 @@ class ExpertParallelMoE:
         return y
 
     def _forward_nccl(self, flat: torch.Tensor) -> torch.Tensor:
-        """One step with two all_gathers (tokens; routing packed as [M][2k] int32: expert
-        ids, then the weights' bits) and the local experts taken straight from the
-        gathered routing on the device (``k3_moe_ep_local``)."""
+        """One step with two all_gathers issued as one NCCL group (tokens; routing packed
+        as [M][2k] int32: expert ids, then the weights' bits) and the local experts taken
+        straight from the gathered routing on the device (``k3_moe_ep_local``)."""
         lib = L.load_library()
         c = self.cfg
         M, H = flat.shape
@@ -188,8 +188,10 @@ class ExpertParallelMoE:
         routing = torch.cat([idx, w.view(torch.int32)], dim=1)
         x_all = torch.empty((W * M, H), dtype=flat.dtype, device=dev)
         r_all = torch.empty((W * M, 2 * k), dtype=torch.int32, device=dev)
-        dist.all_gather_into_tensor(x_all, flat, group=self.group)
-        dist.all_gather_into_tensor(r_all, routing, group=self.group)
+        # both gathers in one NCCL group: one collective launch per step instead of two
+        with dist._coalescing_manager(group=self.group, device=dev):
+            dist.all_gather_into_tensor(x_all, flat, group=self.group)
+            dist.all_gather_into_tensor(r_all, routing, group=self.group)
         y_part = torch.empty((W * M, H), dtype=torch.float32, device=dev)
         w_all = r_all[:, k:].view(torch.float32)
         shared_n = M if self.with_shared else 0
