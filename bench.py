@@ -106,6 +106,20 @@ def dist_init(args):
     return rank, world, local
 
 
+# CUDA graphs that hold NCCL calls, and layers that keep such graphs: released before the
+# process group is destroyed, on every exit path (a live one makes the teardown wait)
+_NCCL_GRAPHS: list = []
+
+
+def release_nccl_graphs():
+    for o in _NCCL_GRAPHS:
+        if hasattr(o, "release_graphs"):
+            o.release_graphs()
+        else:
+            o.reset()
+    _NCCL_GRAPHS.clear()
+
+
 def dist_max(v: float, world: int) -> float:
     if world == 1:
         return v
@@ -505,6 +519,50 @@ def ep_check(moe, full, x, world):
             "against": "the same tokens through the whole layer on one GPU (LatentMoE, 1-GPU kernels)"}
 
 
+def e2e_loop(call, xh, order, K, W, out_shape, world):
+    """End to end through the public API, as a serving loop runs it: per step, the
+    host->device copy of that step's tokens from pinned memory (copy stream), the layer
+    call (compute stream), and the device->host copy of its output into pinned memory
+    (copy stream); two buffers each way, so a step's copies overlap its neighbours'
+    compute. Timed with CUDA events on the compute stream, which waits for the last copy
+    before the closing event; max over ranks. Returns ms per step."""
+    import torch
+    comp = torch.cuda.current_stream()
+    cs = torch.cuda.Stream()
+    xd = [torch.empty(tuple(xh.shape[1:]), dtype=xh.dtype, device="cuda") for _ in range(2)]
+    yh = [torch.empty(out_shape, dtype=torch.float32).pin_memory() for _ in range(2)]
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+
+    def step(i):
+        b = i % 2
+        with torch.cuda.stream(cs):
+            cs.wait_event(ev_done[b])                   # step i-2 has finished with xd[b]
+            xd[b].copy_(xh[order(i)], non_blocking=True)
+            ev_in[b].record(cs)
+        comp.wait_event(ev_in[b])
+        y = call(xd[b])
+        ev_done[b].record(comp)
+        with torch.cuda.stream(cs):
+            cs.wait_event(ev_done[b])
+            y.record_stream(cs)
+            yh[b].copy_(y, non_blocking=True)
+
+    for i in range(W):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(comp)
+    for i in range(K):
+        step(W + i)
+    comp.wait_stream(cs)
+    e1.record(comp)
+    torch.cuda.synchronize()
+    barrier(world)
+    return dist_max(e0.elapsed_time(e1) / K, world)
+
+
 def run_b200(args, rank, world, local):
     import torch
     from kimi_k3_mlx_macmini_b200 import _lib as L
@@ -520,6 +578,7 @@ def run_b200(args, rank, world, local):
         from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
         moe = ExpertParallelMoE(lay.cfg, 0, {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias},
                                 lay.source)
+        _NCCL_GRAPHS.append(moe)
     else:
         moe = router
         _ = moe.pool
@@ -545,8 +604,12 @@ def run_b200(args, rank, world, local):
     ms, timing, clocks = time_modes(modes, step_x, K, W, R, world, local)
     value = world * M / (ms / 1e3)
 
-    # ---- per-kernel timing of the same batches (eager launches, events per kernel)
+    # ---- per-kernel timing of the same batches (eager launches, events per kernel; an
+    # expert-parallel layer launches its step itself rather than replaying it)
     n_prof = min(K, 50)
+    api_graphs = getattr(moe, "graphs", None)
+    if api_graphs is not None:
+        moe.graphs = False
     L.profile_enable(True)
     L.profile_collect()
     torch.cuda.synchronize()
@@ -557,8 +620,11 @@ def run_b200(args, rank, world, local):
     torch.cuda.synchronize()
     prof = L.profile_collect()
     L.profile_enable(False)
+    if api_graphs is not None:
+        moe.graphs = api_graphs
     gu_ms, gu_n = prof["gateup"]
     dn_ms, dn_n = prof["down"]
+    gu_n, dn_n = max(gu_n, 1), max(dn_n, 1)
     U_t = [U[step_x[i]] for i in range(n_prof)]
     gu_bytes = np.mean([(u + 1) * 2 * PROJ_BYTES for u in U_t]) + M * H * 2
     dn_bytes = np.mean([(u + 1) * PROJ_BYTES for u in U_t])
@@ -569,22 +635,7 @@ def run_b200(args, rank, world, local):
 
     # ---- end to end through the public API with host buffers
     xh = torch.stack([x.cpu() for x in xs]).pin_memory()
-    yh = torch.empty((M, H), dtype=torch.float32).pin_memory()
-    xd = torch.empty((M, H), dtype=torch.bfloat16, device="cuda")
-    for i in range(W):
-        xd.copy_(xh[i % R], non_blocking=True)
-        yh.copy_(moe(xd), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(K):
-        xd.copy_(xh[step_x[i]], non_blocking=True)
-        yh.copy_(moe(xd), non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    e2e_ms = dist_max(e0.elapsed_time(e1) / K, world)
+    e2e_ms = e2e_loop(moe, xh, lambda i: i % R, K, W, (M, H), world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -594,6 +645,9 @@ def run_b200(args, rank, world, local):
 
     for g in graphs:
         g.reset()
+    graph_error = getattr(moe, "graph_error", None)
+    if world > 1:
+        release_nccl_graphs()                               # NCCL graphs go before the process group
     if rank != 0:
         return
     line = {
@@ -611,7 +665,8 @@ def run_b200(args, rank, world, local):
                                   "all_gather dispatch, reduce_scatter combine (NCCL)",
                    "l2": f"inputs larger than L2: {9.0 / world:.2f} GB of expert weights per GPU, "
                          "a different token batch every step",
-                   "timing": timing + ", events around K steps"},
+                   "timing": timing + ", events around K steps",
+                   "api_graph_error": graph_error},
         "ep_check": check,
         "unique_experts_mean": float(np.mean(U_t)),
         "unique_experts_per_batch": U[:8],
@@ -626,7 +681,10 @@ def run_b200(args, rank, world, local):
         "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
         "e2e": {"value": world * M / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
-                "ms_per_step": e2e_ms, "api": "LatentMoE.__call__ (k3_moe_decode)"},
+                "ms_per_step": e2e_ms,
+                "api": ("LatentMoE.__call__ (k3_moe_decode)" if world == 1 else
+                        "ExpertParallelMoE.__call__ (captured step replayed per call)"),
+                "copies": "copy stream, two buffers each way (overlapping the neighbouring steps)"},
         "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -661,10 +719,13 @@ def step_modes(moe, xs, R, world):
             modes.append((f"eager launches ({R} distinct batches as a ring; graph capture failed: "
                           f"{_exc_text(exc)})", [(lambda x=x: moe(x)) for x in xs]))
     else:
-        modes.append((f"eager launches ({R} distinct batches as a ring)", [(lambda x=x: moe(x)) for x in xs]))
+        api = ("public API calls (the layer replays its captured step)" if getattr(moe, "graphs", False)
+               else "eager launches")
+        modes.append((f"{api} ({R} distinct batches as a ring)", [(lambda x=x: moe(x)) for x in xs]))
         xin = xs[0].clone()
         try:
             g = torch.cuda.CUDAGraph()
+            _NCCL_GRAPHS.append(g)
             with torch.cuda.graph(g, stream=cap):
                 moe(xin)
             graphs.append(g)
@@ -729,6 +790,7 @@ def run_prefill(args, rank, world, local):
         from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
         moe = ExpertParallelMoE(lay.cfg, 0, {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias},
                                 lay.source)
+        _NCCL_GRAPHS.append(moe)
     else:
         moe = lay.moe()
         _ = moe.pool
@@ -739,8 +801,11 @@ def run_prefill(args, rank, world, local):
     ms, timing, clocks = time_modes(modes, [(W + i) % R for i in range(K)], K, W, R, world, local)
     value = world * T / (ms / 1e3)
 
-    # per-kernel device time (profiling events, outside the timed region)
+    # per-kernel device time (profiling events, outside the timed region; launched, not replayed)
     n_prof = min(K, 10)
+    api_graphs = getattr(moe, "graphs", None)
+    if api_graphs is not None:
+        moe.graphs = False
     L.profile_enable(True)
     L.profile_collect()
     for i in range(n_prof):
@@ -748,8 +813,11 @@ def run_prefill(args, rank, world, local):
     torch.cuda.synchronize()
     prof = L.profile_collect()
     L.profile_enable(False)
+    if api_graphs is not None:
+        moe.graphs = api_graphs
     gu_ms, gu_n = prof["gateup"]
     dn_ms, dn_n = prof["down"]
+    gu_n, dn_n = max(gu_n, 1), max(dn_n, 1)
     peak_hbm, peak_kind = measured_peaks()
     E_loc = args.experts // world
     proj = 7168 * 2048 // 2 + 7168 * 2048 // 32                 # bytes of one MXFP4 projection
@@ -762,23 +830,7 @@ def run_prefill(args, rank, world, local):
 
     # ---- end to end through the public API with host buffers
     xh = torch.stack([x.cpu() for x in xs]).pin_memory()
-    yh = torch.empty((T, H), dtype=torch.float32).pin_memory()
-    xd = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
-    for i in range(2):
-        xd.copy_(xh[i], non_blocking=True)
-        yh.copy_(moe(xd), non_blocking=True)
-    torch.cuda.synchronize()
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_e2e = min(K, 20)
-    e0.record()
-    for i in range(n_e2e):
-        xd.copy_(xh[i % R], non_blocking=True)
-        yh.copy_(moe(xd), non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    barrier(world)
-    e2e_ms = dist_max(e0.elapsed_time(e1) / n_e2e, world)
+    e2e_ms = e2e_loop(moe, xh, lambda i: i % R, min(K, 20), 2, (T, H), world)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -787,6 +839,9 @@ def run_prefill(args, rank, world, local):
                "build": f"gcc -O3 {res['isa']} clone, OpenMP", "sample": res["sample"]}
     for g in graphs:
         g.reset()
+    graph_error = getattr(moe, "graph_error", None)
+    if world > 1:
+        release_nccl_graphs()                               # NCCL graphs go before the process group
     if rank != 0:
         return
     line = {
@@ -803,7 +858,8 @@ def run_prefill(args, rank, world, local):
                                   "all_gather dispatch, reduce_scatter combine (NCCL)",
                    "l2": f"inputs larger than L2: {w_bytes / 1e9:.2f} GB of expert weights per GPU and "
                          f"{R} token batches of {T * H * 2 / 1e6:.0f} MB",
-                   "timing": timing + ", events around K steps"},
+                   "timing": timing + ", events around K steps",
+                   "api_graph_error": graph_error},
         "ep_check": check,
         "layer_hbm_gbs": w_bytes / (ms / 1e3) / 1e9,
         "layer_tflops_algorithmic": flops / (ms / 1e3) / 1e12,
@@ -822,7 +878,10 @@ def run_prefill(args, rank, world, local):
         "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
-                "ms_per_step": e2e_ms, "api": "LatentMoE.__call__ (k3_moe_prefill)"},
+                "ms_per_step": e2e_ms,
+                "api": ("LatentMoE.__call__ (k3_moe_prefill)" if world == 1 else
+                        "ExpertParallelMoE.__call__ (captured step replayed per call)"),
+                "copies": "copy stream, two buffers each way (overlapping the neighbouring steps)"},
         "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -1121,6 +1180,7 @@ def main():
     finally:
         if world > 1:
             import torch.distributed as dist
+            release_nccl_graphs()
             dist.destroy_process_group()
 
 

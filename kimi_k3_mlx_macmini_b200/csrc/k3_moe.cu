@@ -1478,8 +1478,8 @@ int pairs_decode_run(const k3_moe_params* p, const void* x, int x_dtype, int64_t
     pa.cntB = reinterpret_cast<unsigned*>(ws + L.cntB);
     pa.n_cntB = L.U * (L.H / kBRows);
     prof_begin(K3_PROF_TOPK, s);
-    if (int rc = launch_plan_from_pairs(pa, s)) return rc;
-    if (int rc = launch_convert_tokens(x, x_dtype, T, L.H, ws + L.xq_hi, ws + L.xq_ts, s)) return rc;
+    const ConvertArgs conv{x, x_dtype, T, L.H, ws + L.xq_hi, ws + L.xq_ts};
+    if (int rc = launch_plan_from_pairs(pa, conv, s)) return rc;
     prof_end(K3_PROF_TOPK, s);
     return decode_bs(p, L, ws, int(T), y_out, y_dtype, sms, s);
 }

@@ -10,7 +10,17 @@ namespace k3 {
 // [0, T) are skipped. Items: the used slots in ascending order, each split into chunks of
 // at most 8 pairs; a slot's pairs keep their candidate order. Too many items or pairs for
 // a plan set K3_ERR_UNSUPPORTED in plan->status (the surplus is dropped).
-__global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
+__device__ void convert_tokens_body(const void* x, int x_dtype, int64_t T, int64_t K, uint8_t* xp, uint8_t* xsf,
+                                    int64_t first_warp, int64_t n_warps);
+
+// CTA 0 builds the plan; CTAs 1.. convert the tokens to pieces (convert_tokens_body) at
+// the same time, when conv.xp is set.
+__global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a, ConvertArgs conv) {
+    if (blockIdx.x > 0) {
+        convert_tokens_body(conv.x, conv.x_dtype, conv.T, conv.K, conv.xp, conv.xsf,
+                            int64_t(blockIdx.x - 1) * (blockDim.x >> 5), int64_t(gridDim.x - 1) * (blockDim.x >> 5));
+        return;
+    }
     constexpr int kMaxSlots = kMaxExperts + 1;
     __shared__ uint32_t bitmap[(kMaxSlots + 31) / 32];
     __shared__ int cnt_s[kMaxSlots];
@@ -20,6 +30,8 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
     __shared__ int vidx[kMaxPairCandidates];           // valid candidates, in order
     __shared__ int vslot[kMaxPairCandidates];
     __shared__ int chunk_cnt[kMaxPairCandidates / 32];
+    __shared__ int vrank[kMaxPairCandidates];          // rank among the earlier candidates of its slot
+    __shared__ int run_s[kMaxSlots];                   // running count per slot (ranking pass)
     __shared__ int n_valid, n_used, n_items, n_pairs;
     Plan* P = a.plan;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -27,7 +39,10 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
     for (int64_t i = threadIdx.x; i < a.n_cntA; i += blockDim.x) a.cntA[i] = 0;
     for (int64_t i = threadIdx.x; i < a.n_cntB; i += blockDim.x) a.cntB[i] = 0;
     for (int i = threadIdx.x; i < (kMaxSlots + 31) / 32; i += blockDim.x) bitmap[i] = 0;
-    for (int i = threadIdx.x; i < kMaxSlots; i += blockDim.x) cnt_s[i] = 0;
+    for (int i = threadIdx.x; i < kMaxSlots; i += blockDim.x) {
+        cnt_s[i] = 0;
+        run_s[i] = 0;
+    }
     __syncthreads();
     // validity and in-order compaction: ballots per 32 candidates, then a scan of chunk counts
     const int nin = a.n_in;
@@ -141,10 +156,26 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
         }
     }
     const int nv = n_valid;
+    if (warp == 0) {
+        // ranks in candidate order, 32 candidates a step: lanes with the same slot find each
+        // other (match.any), the last of a group advances that slot's running count
+        for (int c0 = 0; c0 < nv; c0 += 32) {
+            const int v = c0 + lane;
+            const bool act = v < nv;
+            const int sl = act ? vslot[v] : -1 - lane;
+            const unsigned grp = __match_any_sync(0xffffffffu, sl);
+            const int before = __popc(grp & ((1u << lane) - 1u));
+            const int base = act ? run_s[sl] : 0;
+            if (act) vrank[v] = base + before;
+            __syncwarp();
+            if (act && (grp >> lane) == 1u) run_s[sl] = base + before + 1;
+            __syncwarp();
+        }
+    }
+    __syncthreads();
     for (int v = threadIdx.x; v < nv; v += blockDim.x) {
         const int sl = vslot[v];
-        int rank = 0;
-        for (int u = 0; u < v; ++u) rank += (vslot[u] == sl);
+        const int rank = vrank[v];
         const int p = pbase[pos_s[sl]] + rank;
         if (p < npairs) {
             int s2, t;
@@ -162,25 +193,32 @@ __global__ void __launch_bounds__(256) plan_from_pairs_kernel(PairsArgs a) {
     }
 }
 
-int launch_plan_from_pairs(const PairsArgs& a, cudaStream_t s) {
+int launch_plan_from_pairs(const PairsArgs& a, const ConvertArgs& conv, cudaStream_t s) {
     if (a.n_in > kMaxPairCandidates) return fail(K3_ERR_UNSUPPORTED, "more than 1024 pair candidates");
-    plan_from_pairs_kernel<<<1, 256, 0, s>>>(a);
+    const int64_t warps = conv.xp ? conv.T * (conv.K / 32) : 0;
+    const int conv_blocks = int(std::min<int64_t>((warps + 7) / 8, int64_t(num_sms()) * 8));
+    plan_from_pairs_kernel<<<1 + conv_blocks, 256, 0, s>>>(a, conv);
     K3_CHECK_LAUNCH("plan_from_pairs_kernel");
     return K3_OK;
 }
 
 // x [T][K] -> E2M1 pieces [8T][K/2] and per-row scales [8T][K/32]; one warp per
-// (token, 32-element block).
-__global__ void __launch_bounds__(256) convert_tokens_kernel(const void* x, int x_dtype, int64_t T, int64_t K,
-                                                             uint8_t* xp, uint8_t* xsf) {
+// (token, 32-element block), warps first_warp, first_warp + n_warps, ...
+__device__ void convert_tokens_body(const void* x, int x_dtype, int64_t T, int64_t K, uint8_t* xp, uint8_t* xsf,
+                                    int64_t first_warp, int64_t n_warps) {
     const int lane = threadIdx.x & 31;
     const int64_t G = K / 32;
-    const int64_t nw = int64_t(gridDim.x) * (blockDim.x >> 5);
-    for (int64_t task = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); task < T * G; task += nw) {
+    for (int64_t task = first_warp + (threadIdx.x >> 5); task < T * G; task += n_warps) {
         const int64_t t = task / G, g = task % G;
         const float v = load_as_f32(x, x_dtype, t * K + 32 * g + lane);
         split_pieces(v, lane, xp + kBPieces * t * (K / 2) + 16 * g, K / 2, xsf + kBPieces * t * G + g, G);
     }
+}
+
+__global__ void __launch_bounds__(256) convert_tokens_kernel(const void* x, int x_dtype, int64_t T, int64_t K,
+                                                             uint8_t* xp, uint8_t* xsf) {
+    convert_tokens_body(x, x_dtype, T, K, xp, xsf, int64_t(blockIdx.x) * (blockDim.x >> 5),
+                        int64_t(gridDim.x) * (blockDim.x >> 5));
 }
 
 int launch_convert_tokens(const void* x, int x_dtype, int64_t T, int64_t K, uint8_t* xp, uint8_t* xsf,

@@ -48,7 +48,16 @@ __device__ __forceinline__ void pair_candidate(const PairsArgs& a, int i, int& s
     if (slot < 0 || slot >= a.num_slots || tok < 0 || tok >= a.T) slot = -1;
 }
 
-int launch_plan_from_pairs(const PairsArgs& a, cudaStream_t s);
+// Tokens to convert to E2M1 pieces alongside the plan (xp == nullptr: none).
+struct ConvertArgs {
+    const void* x;
+    int x_dtype;
+    int64_t T, K;
+    uint8_t* xp;
+    uint8_t* xsf;
+};
+// One launch: CTA 0 builds the plan from the candidates, CTAs 1.. convert the tokens.
+int launch_plan_from_pairs(const PairsArgs& a, const ConvertArgs& conv, cudaStream_t s);
 int launch_convert_tokens(const void* x, int x_dtype, int64_t T, int64_t K, uint8_t* xp, uint8_t* xsf,
                           cudaStream_t s);
 

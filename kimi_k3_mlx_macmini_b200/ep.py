@@ -28,7 +28,7 @@ to the order in which the ranks' partial sums are added.
 from __future__ import annotations
 
 import ctypes
-from typing import Callable, Tuple
+from typing import Callable, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -108,8 +108,14 @@ class ExpertParallelMoE:
     by all ranks of ``group`` (every rank calls with the same M)."""
 
     def __init__(self, cfg, layer: int, w: dict, expert_source: Callable, group=None,
-                 device=None):
+                 device=None, graphs: bool = True):
         self.cfg, self.group = cfg, group
+        # On NCCL, a step (router, collectives, local experts: ~15 launches) is captured
+        # into a CUDA graph per token count at its first call and replayed afterwards, so a
+        # decode loop is not bound by the host's launch rate.
+        self.graphs = graphs
+        self._steps: dict = {}
+        self.graph_error: Optional[str] = None
         self.W = dist.get_world_size(group)
         self.r = dist.get_rank(group)
         E = cfg.num_experts
@@ -203,6 +209,35 @@ class ExpertParallelMoE:
         dist.reduce_scatter_tensor(y, y_part, group=self.group)
         return y
 
+    def _replay(self, flat: torch.Tensor) -> torch.Tensor:
+        """The step as a CUDA graph: captured once per (tokens, dtype) -- every rank at the
+        same call, since all ranks call with the same M -- over static input and output
+        buffers; each call copies x in, replays, and returns a copy of the output."""
+        key = (flat.shape[0], flat.dtype)
+        ent = self._steps.get(key)
+        if ent is None:
+            cur = torch.cuda.current_stream(flat.device)
+            side = torch.cuda.Stream(flat.device)
+            sx = flat.clone()
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self._forward_nccl(sx)               # warm-up: workspaces exist before capture
+            cur.wait_stream(side)
+            torch.cuda.synchronize(flat.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                sy = self._forward_nccl(sx)
+            ent = (g, sx, sy)
+            self._steps[key] = ent
+        g, sx, sy = ent
+        sx.copy_(flat)
+        g.replay()
+        return sy.clone()
+
+    def release_graphs(self) -> None:
+        """Drop the captured steps (before the process group is destroyed)."""
+        self._steps.clear()
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         L.require_cuda(x, "x")
         shape = x.shape
@@ -211,6 +246,13 @@ class ExpertParallelMoE:
             flat = flat.float()
         flat = flat.contiguous()
         if _is_nccl(self.group):
+            if self.graphs and self.graph_error is None and not torch.cuda.is_current_stream_capturing():
+                try:
+                    return self._replay(flat).reshape(shape)
+                except Exception as exc:              # noqa: BLE001 -- kept, then launched eagerly
+                    torch.cuda.synchronize(flat.device)
+                    self.graph_error = f"{type(exc).__name__}: {str(exc).splitlines()[0][:200] if str(exc) else ''}"
+                    self._steps.clear()
             return self._forward_nccl(flat).reshape(shape)
         y = ep_forward(flat, self._route, self._local, group=self.group,
                        num_experts=self.cfg.num_experts, with_shared=self.with_shared)

@@ -125,6 +125,7 @@ def _ep_worker(rank, world, port, q, T=6):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    ep = None
     try:
         from kimi_k3_mlx_macmini_b200 import synthetic
         from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
@@ -132,10 +133,18 @@ def _ep_worker(rank, world, port, q, T=6):
         w = {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias}
         ep = ExpertParallelMoE(lay.cfg, 0, w, lay.source)
         x = synthetic.tokens(500 + rank, T, H)
-        y = ep(x)
+        y = ep(x)                             # captures the step, then replays it
+        x2 = synthetic.tokens(900 + rank, T, H)
+        y2 = ep(x2)                           # replay on new tokens
+        assert ep.graph_error is None, ep.graph_error
         ref = lay.moe()(x)                    # the whole layer on this GPU
-        q.put((rank, O.rel_l2(y.cpu().numpy(), ref.float().cpu().numpy())))
+        ref2 = lay.moe()(x2)
+        err = max(O.rel_l2(y.cpu().numpy(), ref.float().cpu().numpy()),
+                  O.rel_l2(y2.cpu().numpy(), ref2.float().cpu().numpy()))
+        q.put((rank, err))
     finally:
+        if ep is not None:
+            ep.release_graphs()               # graphs holding NCCL calls go before the group
         dist.destroy_process_group()
 
 
