@@ -520,12 +520,14 @@ def ep_check(moe, full, x, world):
 
 
 def e2e_loop(call, xh, order, K, W, out_shape, world):
-    """End to end through the public API, as a serving loop runs it: per step, the
-    host->device copy of that step's tokens from pinned memory (copy stream), the layer
-    call (compute stream), and the device->host copy of its output into pinned memory
-    (copy stream); two buffers each way, so a step's copies overlap its neighbours'
-    compute. Timed with CUDA events on the compute stream, which waits for the last copy
-    before the closing event; max over ranks. Returns ms per step."""
+    """End to end through the public API, as a serving loop runs it. Every step copies its
+    tokens host->device from pinned memory and its output device->host into pinned
+    memory, on one copy stream beside the compute stream, with two buffers each way: the
+    next step's upload is queued ahead of this step's download, so both copies overlap the
+    neighbouring steps' compute without running against each other on the bus. Timed
+    with CUDA events on the compute stream (the first timed upload starts after the
+    opening event; the compute stream waits for the last download before the closing
+    one); max over ranks. Returns ms per step."""
     import torch
     comp = torch.cuda.current_stream()
     cs = torch.cuda.Stream()
@@ -534,28 +536,39 @@ def e2e_loop(call, xh, order, K, W, out_shape, world):
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
 
-    def step(i):
+    def upload_on_cs(i):                                # step i's tokens into xd[i % 2]
         b = i % 2
+        cs.wait_event(ev_done[b])                       # the step that last read xd[b] is done
+        xd[b].copy_(xh[order(i)], non_blocking=True)
+        ev_in[b].record(cs)
+
+    def upload(i):
         with torch.cuda.stream(cs):
-            cs.wait_event(ev_done[b])                   # step i-2 has finished with xd[b]
-            xd[b].copy_(xh[order(i)], non_blocking=True)
-            ev_in[b].record(cs)
+            upload_on_cs(i)
+
+    def run(i, last):
+        b = i % 2
         comp.wait_event(ev_in[b])
         y = call(xd[b])
         ev_done[b].record(comp)
-        with torch.cuda.stream(cs):
+        with torch.cuda.stream(cs):                     # one stream switch a step
+            if not last:
+                upload_on_cs(i + 1)
             cs.wait_event(ev_done[b])
             y.record_stream(cs)
             yh[b].copy_(y, non_blocking=True)
 
+    upload(0)
     for i in range(W):
-        step(i)
+        run(i, i == W - 1)
     torch.cuda.synchronize()
     barrier(world)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(comp)
+    cs.wait_stream(comp)
+    upload(W)
     for i in range(K):
-        step(W + i)
+        run(W + i, i == K - 1)
     comp.wait_stream(cs)
     e1.record(comp)
     torch.cuda.synchronize()
@@ -684,7 +697,7 @@ def run_b200(args, rank, world, local):
                 "ms_per_step": e2e_ms,
                 "api": ("LatentMoE.__call__ (k3_moe_decode)" if world == 1 else
                         "ExpertParallelMoE.__call__ (captured step replayed per call)"),
-                "copies": "copy stream, two buffers each way (overlapping the neighbouring steps)"},
+                "copies": "one copy stream, two buffers each way: the next upload ahead of this download, both overlapping the neighbouring steps"},
         "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,
         "cpu_baseline": cpu,
@@ -881,7 +894,7 @@ def run_prefill(args, rank, world, local):
                 "ms_per_step": e2e_ms,
                 "api": ("LatentMoE.__call__ (k3_moe_prefill)" if world == 1 else
                         "ExpertParallelMoE.__call__ (captured step replayed per call)"),
-                "copies": "copy stream, two buffers each way (overlapping the neighbouring steps)"},
+                "copies": "one copy stream, two buffers each way: the next upload ahead of this download, both overlapping the neighbouring steps"},
         "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,
         "cpu_baseline": cpu,

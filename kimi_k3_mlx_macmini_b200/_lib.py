@@ -110,6 +110,8 @@ _lock = threading.Lock()
 def load_library(path: Path = LIB_PATH):
     """Load the shared library and bind every declared symbol (no GPU needed)."""
     global _lib
+    if _lib is not None:                # every call of the layer comes here: no lock once loaded
+        return _lib
     with _lock:
         if _lib is None:
             if not path.exists():
@@ -160,9 +162,10 @@ def stream_of(t: torch.Tensor) -> int:
 _ws: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-(device, stream) scratch buffer, grown on demand (stream-ordered reuse)."""
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+def workspace(device: torch.device, nbytes: int, stream: int = None) -> torch.Tensor:
+    """Per-(device, stream) scratch buffer, grown on demand (stream-ordered reuse);
+    ``stream`` is the current stream's handle when the caller already has it."""
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream if stream is None else stream)
     buf = _ws.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)

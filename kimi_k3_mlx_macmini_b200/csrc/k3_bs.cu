@@ -423,29 +423,27 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 __threadfence();
 #pragma unroll
                 for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
-                // segment order: deterministic sums; the next segment's loads are in flight
-                // while one is added (two register buffers)
+                // segment order: deterministic sums. Four segments' loads are in flight at
+                // once, and only the values of the key's np pairs are read.
                 const int nseg = s_nseg;
-                float xa[kPW], xb[kPW];
-                auto load_seg = [&](float (&x)[kPW], int sg) {
-                    const float* sp = kpart + int64_t(s_seg[sg]) * (kPW * kBRows);
+                for (int sg0 = 0; sg0 < nseg; sg0 += 4) {
+                    float x[4][kPW];
 #pragma unroll
-                    for (int c = 0; c < kPW; ++c) x[c] = __ldcg(sp + c * kBRows + r);
-                };
-                auto add_seg = [&](const float (&x)[kPW]) {
+                    for (int u = 0; u < 4; ++u) {
+                        const float* sp = kpart + int64_t(s_seg[min(sg0 + u, nseg - 1)]) * (kPW * kBRows);
 #pragma unroll
-                    for (int pi = 0; pi < kMaxPr; ++pi) {
-                        acc0[pi] += x[pi];
-                        if (GATEUP) acc1[pi] += x[(GATEUP ? kMaxPr : 0) + pi];
+                        for (int c = 0; c < kPW; ++c)
+                            x[u][c] = (sg0 + u < nseg && (c % kMaxPr) < np) ? __ldcg(sp + c * kBRows + r) : 0.0f;
                     }
-                };
-                if (nseg > 0) load_seg(xa, 0);
-                for (int sg = 0; sg < nseg; sg += 2) {
-                    if (sg + 1 < nseg) load_seg(xb, sg + 1);
-                    add_seg(xa);
-                    if (sg + 1 >= nseg) break;
-                    if (sg + 2 < nseg) load_seg(xa, sg + 2);
-                    add_seg(xb);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        if (sg0 + u >= nseg) break;
+#pragma unroll
+                        for (int pi = 0; pi < kMaxPr; ++pi) {
+                            acc0[pi] += x[u][pi];
+                            if (GATEUP) acc1[pi] += x[u][(GATEUP ? kMaxPr : 0) + pi];
+                        }
+                    }
                 }
             }
             if (GATEUP) {

@@ -149,6 +149,17 @@ __device__ __forceinline__ float warp_max_nonneg(float v) {
     return __uint_as_float(r);
 }
 
+// E8M0 byte of the smallest power of two S with m <= 6 S, for the non-negative block
+// maximum m given as its bit pattern: the exponent field minus 2, plus one when the
+// significand is above 1.5, clamped to 1..253 (a zero block keeps byte 1). The same byte
+// as frexp(m) = f * 2^E -> E - 3 + (f > 0.75) + 127, read off the bits: m = 0, subnormal
+// m and NaN give 1, +inf 125 (frexp's exponent 0 for it).
+__device__ __forceinline__ int e8m0_cover6(uint32_t mb) {
+    if (mb >= 0x7f800000u) return mb == 0x7f800000u ? 125 : 1;
+    const int b = int(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
+    return mb == 0u ? 1 : (b < 1 ? 1 : (b > 253 ? 253 : b));
+}
+
 // Warp-wide: lane l holds element l of a 32-element block of NV values (independent
 // chains, interleaved); splits each into NP (default kBPieces) E2M1 pieces. Piece p of value i: its
 // 16 packed bytes go to data[i] + p*row_stride (element 2j in the low nibble of byte j)
@@ -166,15 +177,9 @@ __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, u
     for (int p = 0; p < NP; ++p) {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            const float m = warp_max_nonneg(fabsf(res[i]));
-            // smallest power of two S with m <= 6 S, as E8M0 byte b (S = 2^(b-127))
-            int b = 1;
-            if (m > 0.0f) {
-                int E;
-                const float f = frexpf(m, &E);
-                b = E - 3 + (f > 0.75f ? 1 : 0) + 127;
-                b = b < 1 ? 1 : (b > 253 ? 253 : b);
-            }
+            // smallest power of two S with max|res| <= 6 S, as E8M0 byte b (S = 2^(b-127)),
+            // from the bits of the block maximum (frexpf cost half the split)
+            const int b = e8m0_cover6(__float_as_uint(warp_max_nonneg(fabsf(res[i]))));
             const float S = __int_as_float(b << 23);
             const float inv = __int_as_float((254 - b) << 23);
             const float a = fabsf(res[i]) * inv;

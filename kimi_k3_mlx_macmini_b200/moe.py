@@ -216,6 +216,16 @@ class LatentMoE:
                 and c.num_experts_per_token <= 16)
 
     def _params(self, *, num_experts=None, top_k=None, has_shared=None) -> L.K3MoEParams:
+        """The call's k3_moe_params, built once per variant (a decode call is short enough
+        that rebuilding the ctypes struct every time shows in its host time)."""
+        key = (num_experts, top_k, has_shared, self.block_scaled, self.use_pool)
+        cache = self.__dict__.setdefault("_pcache", {})
+        hit = cache.get(key)
+        if hit is None:
+            hit = cache[key] = self._make_params(num_experts=num_experts, top_k=top_k, has_shared=has_shared)
+        return hit
+
+    def _make_params(self, *, num_experts=None, top_k=None, has_shared=None) -> L.K3MoEParams:
         c, pool = self.cfg, self.pool
         lb = getattr(c, "situ_linear_beta", None)
         return L.K3MoEParams(
@@ -371,19 +381,25 @@ class LatentMoE:
         lib = L.load_library()
         params = self._params()
         k = self.cfg.num_experts_per_token
-        y = torch.empty((flat.shape[0], self.pool.hidden), dtype=torch.float32, device=flat.device)
-        idx = torch.empty((flat.shape[0], k), dtype=torch.int32, device=flat.device)
-        w = torch.empty((flat.shape[0], k), dtype=torch.float32, device=flat.device)
-        for m0 in range(0, flat.shape[0], MAX_DECODE_TOKENS):
-            xc = flat[m0:m0 + MAX_DECODE_TOKENS]
-            M = xc.shape[0]
-            ws = L.workspace(flat.device, lib.k3_moe_decode_workspace(params, M))
-            L.check(lib.k3_moe_decode(params, xc.data_ptr(), L.dtype_code(xc), M,
-                                      self.gate_w.data_ptr(),
-                                      None if self.gate_b is None else self.gate_b.data_ptr(),
-                                      y[m0:m0 + M].data_ptr(), L.K3_F32, idx[m0:m0 + M].data_ptr(),
-                                      w[m0:m0 + M].data_ptr(), ws.data_ptr(), ws.numel(),
-                                      L.stream_of(xc)), "k3_moe_decode")
+        T, dev = flat.shape[0], flat.device
+        y = torch.empty((T, self.pool.hidden), dtype=torch.float32, device=dev)
+        idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        stream = L.stream_of(flat)
+        wsz = self.__dict__.setdefault("_wsz", {})
+        xdt, xsz = L.dtype_code(flat), flat.element_size()
+        gb = None if self.gate_b is None else self.gate_b.data_ptr()
+        for m0 in range(0, T, MAX_DECODE_TOKENS):
+            M = min(MAX_DECODE_TOKENS, T - m0)
+            need = wsz.get(M)
+            if need is None:
+                need = wsz[M] = lib.k3_moe_decode_workspace(params, M)
+            ws = L.workspace(dev, need, stream)
+            H = flat.shape[1]
+            L.check(lib.k3_moe_decode(params, flat.data_ptr() + m0 * H * xsz, xdt, M, self.gate_w.data_ptr(), gb,
+                                      y.data_ptr() + m0 * y.shape[1] * 4, L.K3_F32, idx.data_ptr() + m0 * k * 4,
+                                      w.data_ptr() + m0 * k * 4, ws.data_ptr(), ws.numel(), stream),
+                    "k3_moe_decode")
         return y, idx, w
 
     def _fused_prefill(self, flat: torch.Tensor):
