@@ -359,6 +359,19 @@ K3_API int k3_dense_matvec(const k3_dense_seg* segs, int nseg, int64_t M, int64_
                            int out_dtype, int64_t ldo, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* The same dense projections for many tokens (a Kimi-K3 layer above 8 tokens: latent down
+ * and up, shared expert -- air_llm/models/kimi_k3/moe.py:105-107,116,128-131, where MLX
+ * multiplies the layer's bf16 weights with fp32 activations): out [M][N] (row stride ldo)
+ * = X [M][K] . W [N][K]^T, or out += that when `accumulate` is set (a second segment into
+ * the same output). W bf16 with row stride ldw; X f32 or bf16 with row stride ldx. fp32 X
+ * enters the bf16 tensor cores (tcgen05 kind::f16) as two bf16 pieces (hi, lo) with fp32
+ * accumulation (~16 significant bits of x); bf16 X is exact. K must be a multiple of 64
+ * and W's rows 16-byte aligned. Deterministic (fixed k order). */
+K3_API size_t k3_dense_gemm_workspace(int64_t M, int64_t K);
+K3_API int k3_dense_gemm(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K, const uint16_t* w,
+                         int64_t ldw, int64_t N, float* out, int64_t ldo, int accumulate, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
 /* Streamed lm_head argmax (`KimiK3.logits`, air_llm/models/kimi_k3/model.py:111-133): for
  * one hidden row h [H] (f32 or bf16) and W bf16 [V][H], idx_out = argmax_n h . W[n]
  * (lowest n on ties, as the reference's first-occurrence argmax over ascending chunks)

@@ -99,6 +99,8 @@ SIGNATURES = {
     "k3_lm_head_argmax": (_i32, [_vp, _i32, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "k3_moe_ep_local_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64, _i64]),
     "k3_wait_selftest": (_i32, [_i64, _i32, _vp, _vp]),
+    "k3_dense_gemm_workspace": (_sz, [_i64, _i64]),
+    "k3_dense_gemm": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i32, _vp, _sz, _vp]),
     "k3_moe_ep_local": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                _vp, _i32, _vp, _sz, _vp]),
 }

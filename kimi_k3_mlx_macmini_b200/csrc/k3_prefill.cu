@@ -6,8 +6,8 @@
 // matvec launch per projection; here one launch per phase covers every (expert, token)
 // pair of the call:
 //
-//   router_gemm_kernel    logits [T][E] = x . W_g^T on tcgen05 kind::f16 (bf16 x bf16 ->
-//                         fp32 in TMEM), then the shared sigmoid top-k kernel;
+//   gemm_bf16_kernel      logits [T][E] = x . W_g^T on tcgen05 kind::f16 (bf16 x bf16 ->
+//                         fp32 in TMEM; k3_gemm.cu), then the shared sigmoid top-k kernel;
 //   prefill_count/scan/place_kernel
 //                         the pairs grouped by slot (experts ascending, shared last),
 //                         candidates in order within a slot, cut into chunks of <= kPN
@@ -19,6 +19,7 @@
 //                         double-buffered TMEM accumulators, epilogue warps draining the
 //                         other buffer.
 #include "k3_async.cuh"
+#include "k3_gemm.cuh"
 #include "k3_pairs.cuh"
 #include "k3_prefill.cuh"
 #include "k3_tma.cuh"
@@ -50,136 +51,7 @@ __device__ __forceinline__ uint64_t l2_evict_last() {
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
     return p;
 }
-// Instruction descriptor of kind::f16: bf16 x bf16 -> fp32, M = 128, N = n, both K-major.
-__device__ __forceinline__ uint32_t bf16_idesc(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
-}
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
 
-
-// ------------------------------------------------------------------ router GEMM
-
-constexpr int kRGN = 96;          // tokens per CTA (MMA N)
-constexpr int kRGStages = 6;
-constexpr int kRGThreads = 192;   // producer, MMA, 4 epilogue warps
-struct alignas(1024) RGStage {
-    uint8_t a[kBRows][128];       // 128 router rows x 64 k (bf16), SW128
-    uint8_t b[kRGN][128];         // kRGN tokens x 64 k
-};
-constexpr size_t rg_smem_bytes() { return sizeof(RGStage) * kRGStages + 1024 + 256; }
-static_assert(rg_smem_bytes() <= 227 * 1024, "router ring exceeds shared memory");
-
-// logits[t][e] for e in [128 bx, +128), t in [kRGN by, +kRGN): fp32 accumulation of the
-// exact bf16 products in the tensor core, in a fixed k order (deterministic).
-__global__ void __launch_bounds__(kRGThreads, 1)
-    router_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap,
-                       int T, int E, int64_t H, float* __restrict__ logits, int* status) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-    RGStage* ring = reinterpret_cast<RGStage*>(base);
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + sizeof(RGStage) * kRGStages);
-    uint64_t* empty = full + kRGStages;
-    uint64_t* accf = empty + kRGStages;
-    uint64_t* drain = accf + 1;
-    __shared__ uint32_t s_tmem;
-    __shared__ volatile int s_abort;
-    __shared__ volatile unsigned s_issued;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        s_abort = 0;
-        s_issued = 0;
-        for (int s = 0; s < kRGStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        mbar_init(accf, 1);
-        mbar_init(drain, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
-    if (warp == 1) tmem_alloc(&s_tmem, 128);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tm = s_tmem;
-    const int e0 = blockIdx.x * kBRows, t0 = blockIdx.y * kRGN;
-    const int nst = int(H / 64);
-
-    if (warp == 0) {
-        if (lane == 0) {
-            for (int s = 0; s < nst; ++s) {
-                const int si = s % kRGStages;
-                if (!mbar_wait(&empty[si], ((s / kRGStages) & 1) ^ 1, status, &s_abort)) {
-                    s_abort = 1;
-                    break;
-                }
-                mbar_expect_tx(&full[si], uint32_t(sizeof(RGStage)));
-                tma_2d(&ring[si].a[0][0], &wmap, 64 * s, e0, &full[si]);
-                tma_2d(&ring[si].b[0][0], &xmap, 64 * s, t0, &full[si]);
-                s_issued = unsigned(s + 1);
-            }
-        }
-    } else if (warp == 1) {
-        const uint32_t idesc = bf16_idesc(kRGN);
-        int s = 0;
-        for (; s < nst; ++s) {
-            const int si = s % kRGStages;
-            if (!__all_sync(0xffffffffu, mbar_wait(&full[si], (s / kRGStages) & 1, status, &s_abort))) {
-                s_abort = 1;
-                break;
-            }
-            tc_fence_after();
-            if (elect_one()) {
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_bf16(tm, sw128_desc(&ring[si].a[0][0], 32 * kk), sw128_desc(&ring[si].b[0][0], 32 * kk),
-                             idesc, (s > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(&empty[si]);
-            }
-            __syncwarp();
-        }
-        if (s == nst) {
-            if (elect_one()) tc_commit(accf);
-            __syncwarp();
-        } else {
-            const unsigned issued = s_issued;
-            for (unsigned k = unsigned(s); k < issued; ++k)
-                if (!mbar_wait(&full[k % kRGStages], (k / kRGStages) & 1, status)) break;
-        }
-        if (elect_one()) tc_commit(drain);
-        __syncwarp();
-        mbar_wait(drain, 0, status);
-    } else {
-        const int q = warp & 3;
-        if (__all_sync(0xffffffffu, mbar_wait(accf, 0, status, &s_abort))) {
-            tc_fence_after();
-            const int e = e0 + 32 * q + lane;
-            const uint32_t taddr = tm + (uint32_t(32 * q) << 16);
-#pragma unroll 1
-            for (int j0 = 0; j0 < kRGN; j0 += 16) {
-                float v[16];
-                tmem_ld16(taddr + j0, v);
-#pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
-                    const int t = t0 + j0 + jj;
-                    if (t < T && e < E) logits[int64_t(t) * E + e] = v[jj];
-                }
-            }
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tm, 128);
-    }
-}
 
 // ------------------------------------------------------------------ routing plan
 
@@ -870,10 +742,6 @@ int configure_prefill_once() {
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, int(psmem_bytes())),
                             "cudaFuncSetAttribute(prefill down)"))
         return rc;
-    if (int rc = cuda_check(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 int(rg_smem_bytes())),
-                            "cudaFuncSetAttribute(router gemm)"))
-        return rc;
     return K3_OK;
 }
 int configure_prefill() { return g_prefill_attr.run(configure_prefill_once); }
@@ -1121,27 +989,8 @@ bool router_gemm_ok(int xdt, int64_t H, const void* x, const void* gate_w) {
 
 int launch_router_gemm(const void* x, int64_t T, int64_t H, const uint16_t* gate_w, int64_t E, float* logits,
                        int* status, cudaStream_t s) {
-    if (int rc = configure_prefill()) return rc;
-    CUtensorMap wmap, xmap;
-    {
-        const uint64_t d[2] = {uint64_t(H), uint64_t(E)};
-        const uint64_t st[1] = {uint64_t(H) * 2};
-        const uint32_t b[2] = {64, uint32_t(kBRows)};
-        if (int rc = encode_map(&wmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, gate_w, d, st, b,
-                                CU_TENSOR_MAP_SWIZZLE_128B))
-            return rc;
-    }
-    {
-        const uint64_t d[2] = {uint64_t(H), uint64_t(T)};
-        const uint64_t st[1] = {uint64_t(H) * 2};
-        const uint32_t b[2] = {64, uint32_t(kRGN)};
-        if (int rc = encode_map(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, d, st, b, CU_TENSOR_MAP_SWIZZLE_128B))
-            return rc;
-    }
-    const dim3 grid(unsigned((E + kBRows - 1) / kBRows), unsigned((T + kRGN - 1) / kRGN));
-    router_gemm_kernel<<<grid, kRGThreads, rg_smem_bytes(), s>>>(wmap, xmap, int(T), int(E), H, logits, status);
-    K3_CHECK_LAUNCH("router_gemm_kernel");
-    return K3_OK;
+    // logits [T][E] = x [T][H] . W_gate [E][H]^T: the dense tcgen05 GEMM, one bf16 piece
+    return launch_gemm_bf16(static_cast<const uint16_t*>(x), nullptr, H, T, H, gate_w, H, E, logits, E, 0, status, s);
 }
 
 }  // namespace k3

@@ -55,24 +55,39 @@ def _rmsnorm(x: torch.Tensor, norm_w: torch.Tensor, eps: float) -> torch.Tensor:
     return norm_w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps))
 
 
-_MM_OUT_DTYPE: Optional[bool] = None
+def _gemm(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 out [M][N] (+)= x [M][K] . W [N][K]^T on this library's tcgen05 GEMM
+    (``k3_dense_gemm``): bf16 W, fp32 x as bf16 hi + lo pieces; ``out`` given: accumulate
+    into it."""
+    xc = x if x.dtype in (torch.float32, torch.bfloat16) else x.float()
+    if xc.stride(-1) != 1:
+        xc = xc.contiguous()
+    M, K = xc.shape
+    N = w.shape[0]
+    acc = out is not None
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    lib = L.load_library()
+    ws = L.workspace(x.device, lib.k3_dense_gemm_workspace(M, K))
+    L.check(lib.k3_dense_gemm(xc.data_ptr(), L.dtype_code(xc), xc.stride(0), M, K, w.data_ptr(), w.stride(0), N,
+                              out.data_ptr(), out.stride(0), int(acc), ws.data_ptr(), ws.numel(), L.stream_of(xc)),
+            "k3_dense_gemm")
+    return out
 
 
-def _mm_f32(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """fp32 x [M][K] times bf16 W [N][K]^T in fp32: two bf16 tensor-core GEMMs (hi and lo
-    pieces of x, fp32 outputs) when torch offers them, else the fp32 GEMM."""
-    global _MM_OUT_DTYPE
-    xf = x.float()
-    if w.dtype == torch.bfloat16 and _MM_OUT_DTYPE is not False:
-        hi = xf.to(torch.bfloat16)
-        lo = (xf - hi.float()).to(torch.bfloat16)
-        try:
-            y = torch.mm(torch.cat([hi, lo]), w.t(), out_dtype=torch.float32)
-            _MM_OUT_DTYPE = True
-            return y[:xf.shape[0]] + y[xf.shape[0]:]
-        except (RuntimeError, TypeError):
-            _MM_OUT_DTYPE = False
-    return xf @ w.float().t()
+def _gemm_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    return (w.is_cuda and x.is_cuda and w.dtype == torch.bfloat16 and w.dim() == 2 and w.stride(1) == 1 and w.shape[1] % 64 == 0
+            and w.stride(0) % 8 == 0 and w.data_ptr() % 16 == 0 and x.shape[-1] == w.shape[1])
+
+
+def _mm_f32(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp32 x [M][K] times bf16 W [N][K]^T in fp32 (added into ``out`` when given): the
+    library's tcgen05 GEMM for bf16 weights whose K is a multiple of 64; other shapes (the
+    reference's tiny test models) multiply in fp32 on the GPU."""
+    if _gemm_ok(x, w):
+        return _gemm(x, w, out)
+    y = x.float() @ w.float().t()
+    return y if out is None else out.add_(y)
 
 
 def _activation(kind: int, g: torch.Tensor, u: torch.Tensor, beta: float, lbeta: float) -> torch.Tensor:
@@ -115,20 +130,22 @@ def matvec(segs: Sequence[Seg], N: int, combine: int = L.K3_DENSE_SUM, activatio
                                     float(situ_linear_beta), out.data_ptr(), L.dtype_code(out), N,
                                     ws.data_ptr(), ws.numel(), L.stream_of(x0)), "k3_dense_matvec")
         return out
-    # more than 8 tokens (or weights that are not bf16): cuBLAS GEMMs
-    parts = []
-    for sg in segs:
+    # more than 8 tokens: GEMMs on the tensor cores (k3_dense_gemm); summed segments
+    # accumulate into one output in segment order
+    def seg_input(sg):
         w, x, nw, eps = sg[:4]
         if len(sg) > 4 and sg[4]:
             K = w.shape[1]
             x = _activation(activation, x[:, :K].float(), x[:, K:2 * K].float(), situ_beta, situ_linear_beta)
-        parts.append(_mm_f32(x if nw is None else _rmsnorm(x, nw, eps), w))
+        return x if nw is None else _rmsnorm(x, nw, eps)
+
     if combine == L.K3_DENSE_ACT:
-        y = _activation(activation, parts[0], parts[1], situ_beta, situ_linear_beta)
+        g, u = (_mm_f32(seg_input(sg), sg[0]) for sg in segs[:2])
+        y = _activation(activation, g, u, situ_beta, situ_linear_beta)
     else:
-        y = parts[0]
-        for p in parts[1:]:
-            y = y + p
+        y = None
+        for sg in segs:
+            y = _mm_f32(seg_input(sg), sg[0], y)
     return y.to(out_dtype)
 
 

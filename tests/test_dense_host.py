@@ -1,5 +1,5 @@
-"""Host-side pieces of the dense path (``dense.py``) that run without a GPU: the split
-bf16 GEMM helper's fp32 result, rmsnorm and the gate/up activations against numpy
+"""Host-side pieces of the dense path (``dense.py``) that run without a GPU: the GEMM
+helper's fp32 result for shapes the tensor-core GEMM does not take, rmsnorm and the gate/up activations against numpy
 (``ops.py:11-28``), and the dispatch between the library matvec and the GEMM path."""
 import numpy as np
 import torch

@@ -262,3 +262,69 @@ def test_k3_layer_prefill_agrees_with_decode(k3, k3_layer):
     yd = torch.cat([moe(x[m:m + 8]) for m in range(0, 40, 8)])
     torch.cuda.synchronize()
     assert O.rel_l2(y.cpu().numpy(), yd.cpu().numpy()) < 5e-4
+
+
+# ---------------------------------------------------- dense GEMM (more than 8 tokens)
+
+def _gemm_call(x, w, out, accumulate, ldo=None):
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    lib = L.load_library()
+    M, K = x.shape
+    N = w.shape[0]
+    ws = L.workspace(x.device, lib.k3_dense_gemm_workspace(M, K))
+    L.check(lib.k3_dense_gemm(x.data_ptr(), L.dtype_code(x), x.stride(0), M, K, w.data_ptr(), w.stride(0), N,
+                              out.data_ptr(), out.stride(0) if ldo is None else ldo, int(accumulate), ws.data_ptr(),
+                              ws.numel(), L.stream_of(x)), "k3_dense_gemm")
+
+
+@pytest.mark.parametrize("M,K,N,xdt", [
+    (40, 3584, 7168, torch.float32),     # Kimi-K3 latent up above 8 tokens
+    (200, 7168, 3584, torch.float32),    # latent down, ragged token tiles (200 = 2 x 96 + 8)
+    (97, 1024, 300, torch.bfloat16),     # ragged rows of W (300 = 2 x 128 + 44), bf16 x exact
+])
+def test_dense_gemm_against_fp64(k3, M, K, N, xdt):
+    """k3_dense_gemm (tcgen05 kind::f16): fp32 x as bf16 hi + lo pieces keeps ~16 bits of
+    every input (bar 2e-5 relative L2); bf16 x is exact in fp32 accumulation (2e-6)."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(M + K + N)
+    x = (torch.randn((M, K), generator=gen, device="cuda") * 2.0).to(xdt)
+    w = (torch.randn((N, K), generator=gen, device="cuda") * K ** -0.5).to(torch.bfloat16)
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    _gemm_call(x, w, out, False)
+    want = x.double().cpu().numpy() @ w.double().cpu().numpy().T
+    err = O.rel_l2(out.cpu().numpy(), want)
+    assert err < (2e-5 if xdt == torch.float32 else 2e-6), err
+    again = torch.empty_like(out)
+    _gemm_call(x, w, again, False)
+    assert torch.equal(out, again)                         # fixed k order: bitwise repeatable
+
+
+def test_dense_gemm_accumulates_into_strided_output(k3):
+    """Two segments into one output (row stride above N), views with row strides above K."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11)
+    base_x = torch.randn((33, 1024 + 64), generator=gen, device="cuda")
+    x0 = base_x[:, :1024]                                   # row stride 1088
+    x1 = torch.randn((33, 512), generator=gen, device="cuda")
+    w0 = (torch.randn((130, 1024), generator=gen, device="cuda") * 0.03).to(torch.bfloat16)
+    w1 = (torch.randn((130, 512), generator=gen, device="cuda") * 0.04).to(torch.bfloat16)
+    big = torch.full((33, 160), 7.0, device="cuda")
+    out = big[:, :130]                                      # row stride 160
+    _gemm_call(x0, w0, out, False)
+    _gemm_call(x1, w1, out, True)
+    want = (x0.double().cpu().numpy() @ w0.double().cpu().numpy().T
+            + x1.double().cpu().numpy() @ w1.double().cpu().numpy().T)
+    assert O.rel_l2(out.cpu().numpy(), want) < 2e-5
+    assert torch.all(big[:, 130:] == 7.0)                   # untouched beyond N
+
+
+def test_dense_gemm_rejects_bad_shapes(k3):
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    lib = L.load_library()
+    x = torch.zeros((4, 96), device="cuda")
+    w = torch.zeros((8, 96), dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros((4, 8), device="cuda")
+    ws = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    rc = lib.k3_dense_gemm(x.data_ptr(), L.K3_F32, 96, 4, 96, w.data_ptr(), 96, 8, out.data_ptr(), 8, 0,
+                           ws.data_ptr(), ws.numel(), None)
+    assert rc == L.K3_ERR_UNSUPPORTED and b"multiple of 64" in lib.k3_last_error()
