@@ -65,8 +65,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=None,
                     help="tokens per GPU (default: 8 for config 2, 4096 for 3, 1 for 4 and 5)")
     ap.add_argument("--experts", type=int, default=None,
-                    help="routed experts in the layer (default 384 = BASELINE, 896 for config 5; fewer "
-                         "only for small ncu captures)")
+                    help="routed experts in the layer (default 384 = BASELINE, 896 for config 5; for "
+                         "config 1 the size of the expert ring, default 64; fewer only for small ncu "
+                         "captures)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
@@ -79,7 +80,7 @@ def parse():
     if args.tokens is None:
         args.tokens = {1: 8, 2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
     if args.experts is None:
-        args.experts = 896 if args.config == 5 else E
+        args.experts = {1: 64, 5: 896}.get(args.config, E)
     return args
 
 
@@ -424,14 +425,22 @@ def run_stream(args, rank, world, local):
             x = (x.float() + m(x)).to(torch.bfloat16)
         sets.append(per)
     torch.cuda.synchronize()
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    c0.record(layers[0].copy_stream)
+    # copies of one layer at a time, as the token's layers order them (each layer's copy
+    # stream is its own, so queuing them back to back would run layers' copies side by
+    # side): from an event on the compute stream before the layer's copies are queued to
+    # one after it joined the copy stream
+    copy_ms = 0.0
+    cur = torch.cuda.current_stream()
     for per in sets:
         for m, ids in zip(layers, per):
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(cur)
             m.stage(ids)
-    c1.record(layers[-1].copy_stream)
-    torch.cuda.synchronize()
-    copy_s = c0.elapsed_time(c1) / 1e3 / K
+            cur.wait_stream(m.copy_stream)
+            c1.record(cur)
+            torch.cuda.synchronize()
+            copy_ms += c0.elapsed_time(c1)
+    copy_s = copy_ms / 1e3 / K
     comp_ms = 0.0
     for i, per in enumerate(sets):
         x = synthetic.tokens(args.seed * 7919 + W + i, 1, H)
@@ -908,9 +917,10 @@ def run_matvec(args, rank, world, local):
     bandwidth on one GPU. A step is one expert's SwiGLU FFN through the reference's API
     ``LatentMoE.expert_forward`` (``moe.py:90-103``): gate and up projections (one
     block-scaled launch), silu(gate) * up, the down projection -- 23,396,352 B of MXFP4
-    weights -- over a ring of 64 distinct experts (1.5 GB, larger than L2), one CUDA graph
-    per expert. Beside it, the bare ``mxfp4_matvec_fused`` call (``mxfp4_matvec.py:75-96``)
-    on one 7168 -> 2048 projection (7,798,784 B) over a ring of 128 distinct projections."""
+    weights -- over a ring of --experts distinct experts (default 64: 1.5 GB, larger than
+    L2), one CUDA graph per expert. Beside it, the bare ``mxfp4_matvec_fused`` call (``mxfp4_matvec.py:75-96``)
+    on one 7168 -> 2048 projection (7,798,784 B) over a ring of the experts' 2 x --experts
+    distinct projections."""
     import torch
     from kimi_k3_mlx_macmini_b200 import _lib as L
     from kimi_k3_mlx_macmini_b200 import synthetic
@@ -922,7 +932,9 @@ def run_matvec(args, rank, world, local):
         return
     torch.cuda.set_device(local)
     M, K, W = args.tokens, args.steps, args.warmup
-    NE = 64
+    NE = args.experts
+    if NE < 8:
+        raise SystemExit("config 1 needs a ring of at least 8 experts (larger than L2 from 8 on)")
     lay = synthetic.baseline_layer(seed=args.seed, E=NE, H=H, I=I_, top_k=1, shared=False)
     moe = lay.moe()
     _ = moe.pool
@@ -960,7 +972,7 @@ def run_matvec(args, rank, world, local):
     gu_bytes = 2 * PROJ_BYTES + M * H * 2
     gu_gbs = gu_bytes / (gu_ms / gu_n / 1e3) / 1e9
     dn_ms, dn_n = prof["down"]
-    # ---- the bare mxfp4_matvec_fused call over a ring of 128 projections (w1 and w3 of the experts)
+    # ---- the bare mxfp4_matvec_fused call over a ring of the experts' w1 and w3 projections
     projs = []
     for e in range(NE):
         for which in ("w1", "w3"):

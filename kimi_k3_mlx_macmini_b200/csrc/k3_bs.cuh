@@ -151,53 +151,117 @@ __device__ __forceinline__ float warp_max_nonneg(float v) {
 
 // E8M0 byte of the smallest power of two S with m <= 6 S, for the non-negative block
 // maximum m given as its bit pattern: the exponent field minus 2, plus one when the
-// significand is above 1.5, clamped to 1..253 (a zero block keeps byte 1). The same byte
-// as frexp(m) = f * 2^E -> E - 3 + (f > 0.75) + 127, read off the bits: m = 0, subnormal
-// m and NaN give 1, +inf 125 (frexp's exponent 0 for it).
+// significand is above 1.5, clamped to 1..253 (zero and subnormal m give 1). The same byte
+// as frexp(m) = f * 2^E -> E - 3 + (f > 0.75) + 127, read off the bits; NaN gives 1 and
+// +inf 125 (frexp's exponent 0 for it). Selects only, no branch: the split's unrolled
+// chains of independent values interleave across it.
 __device__ __forceinline__ int e8m0_cover6(uint32_t mb) {
-    if (mb >= 0x7f800000u) return mb == 0x7f800000u ? 125 : 1;
-    const int b = int(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
-    return mb == 0u ? 1 : (b < 1 ? 1 : (b > 253 ? 253 : b));
+    int b = int(mb >> 23) - 2 + ((mb & 0x7fffffu) > 0x400000u ? 1 : 0);
+    b = min(max(b, 1), 253);
+    b = mb > 0x7f800000u ? 1 : b;                        // NaN
+    return mb == 0x7f800000u ? 125 : b;                  // +inf
+}
+
+// E2M1 codes of two floats, round to nearest even with saturation at +-6 (the block scale
+// keeps |value| <= 6): code of a in bits 0-3, of b in bits 4-7.
+__device__ __forceinline__ uint32_t e2m1x2_codes(float a, float b) {
+    uint32_t r;
+    asm("{\n"
+        ".reg .b8 c;\n"
+        "cvt.rn.satfinite.e2m1x2.f32 c, %2, %1;\n"
+        "cvt.u32.u8 %0, c;\n"
+        "}\n"
+        : "=r"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// The values of two E2M1 codes packed as e2m1x2_codes returns them (exact in f16).
+__device__ __forceinline__ float2 e2m1x2_values(uint32_t codes) {
+    uint32_t h;
+    asm("{\n"
+        ".reg .b8 c;\n"
+        "cvt.u8.u32 c, %1;\n"
+        "cvt.rn.f16x2.e2m1x2 %0, c;\n"
+        "}\n"
+        : "=r"(h) : "r"(codes));
+    return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// Within each group of 8 lanes, lane j holds 8 nibbles (nibble p at bits 4p); returns the
+// transpose: lane p of the group gets nibble p of every lane j of the group at bits 4j.
+// Three butterfly stages: in stage d, the nibbles whose position and lane differ in bit d
+// swap across lanes j and j ^ d.
+__device__ __forceinline__ uint32_t transpose_nibbles8(uint32_t n, int lane) {
+#pragma unroll
+    for (int d = 1; d < 8; d <<= 1) {
+        const uint32_t m = d == 1 ? 0xF0F0F0F0u : (d == 2 ? 0xFF00FF00u : 0xFFFF0000u);
+        const uint32_t o = __shfl_xor_sync(0xffffffffu, n, d);
+        n = (lane & d) ? ((n & m) | ((o & m) >> (4 * d))) : ((n & ~m) | ((o & ~m) << (4 * d)));
+    }
+    return n;
 }
 
 // Warp-wide: lane l holds element l of a 32-element block of NV values (independent
-// chains, interleaved); splits each into NP (default kBPieces) E2M1 pieces. Piece p of value i: its
-// 16 packed bytes go to data[i] + p*row_stride (element 2j in the low nibble of byte j)
-// and its E8M0 scale to sf[i][p*sf_stride]. Values with sf[i] == nullptr are skipped.
-// Both scale layouts in use are affine in p: natural per-row scales ([row][block],
-// stride = blocks per row) and the tensor-core chunk (sf_chunk_offset(8*col + p, j),
-// stride 16 since the 8 rows of one column share a 32-row group).
+// chains, interleaved); splits each into NP (default kBPieces, at most 8) E2M1 pieces.
+// Piece p of value i: its 16 packed bytes go to data[i] + p*row_stride (element 2j in the
+// low nibble of byte j) and its E8M0 scale to sf[i][p*sf_stride]. Values with sf[i] ==
+// nullptr are skipped. Both scale layouts in use are affine in p: natural per-row scales
+// ([row][block], stride = blocks per row) and the tensor-core chunk
+// (sf_chunk_offset(8*col + p, j), stride 16 since the 8 rows of one column share a
+// 32-row group).
+// Piece p: S = the smallest power of two with max|res| <= 6 S over the block (one warp
+// reduction), codes = E2M1(res / S) rounded to nearest even, res -= value(codes) * S
+// (exact: value * S is on res's grid). The hardware conversions give the codes and their
+// values; every lane keeps its codes of all pieces in one word, and one nibble transpose
+// per 8 lanes turns those into the pieces' packed rows, written once at the end. A
+// negative value that rounds to zero gets code 0 (not -0), and NaN codes as 0.
 template <int NV, int NP = kBPieces>
 __device__ __forceinline__ void split_pieces_n(const float (&v)[NV], int lane, uint8_t* const (&data)[NV],
                                                int64_t row_stride, uint8_t* const (&sf)[NV], int64_t sf_stride) {
+    static_assert(NP >= 1 && NP <= 8, "a lane keeps at most 8 pieces' codes in one word");
     float res[NV];
+    uint32_t nib[NV];
+    int sfv[NV];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) res[i] = v[i];
-#pragma unroll 1
+    for (int i = 0; i < NV; ++i) {
+        res[i] = v[i];
+        nib[i] = 0u;
+        sfv[i] = 1;
+    }
+#pragma unroll
     for (int p = 0; p < NP; ++p) {
+        float a[NV + 1], S[NV];
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
-            // smallest power of two S with max|res| <= 6 S, as E8M0 byte b (S = 2^(b-127)),
-            // from the bits of the block maximum (frexpf cost half the split)
             const int b = e8m0_cover6(__float_as_uint(warp_max_nonneg(fabsf(res[i]))));
-            const float S = __int_as_float(b << 23);
-            const float inv = __int_as_float((254 - b) << 23);
-            const float a = fabsf(res[i]) * inv;
-            // round to the E2M1 grid {0, .5, 1, 1.5, 2, 3, 4, 6}, ties to the even code
-            const int c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
-                          (a >= 3.5f) + (a > 5.0f);
-            const float q = c <= 4 ? 0.5f * float(c) : (c == 5 ? 3.0f : (c == 6 ? 4.0f : 6.0f));
-            const bool neg = res[i] < 0.0f;
-            res[i] -= (neg ? -q : q) * S;                // exact: q*S is on res's grid
-            uint32_t w = uint32_t(c | ((neg && c) ? 8 : 0)) << (4 * (lane & 7));
-            w |= __shfl_xor_sync(0xffffffffu, w, 1);
-            w |= __shfl_xor_sync(0xffffffffu, w, 2);
-            w |= __shfl_xor_sync(0xffffffffu, w, 4);
-            if (sf[i]) {
-                if ((lane & 7) == 0)
-                    *reinterpret_cast<uint32_t*>(data[i] + p * row_stride + 4 * (lane >> 3)) = w;
-                if (lane == 0) sf[i][p * sf_stride] = uint8_t(b);
+            S[i] = __int_as_float(b << 23);
+            const float t = res[i] * __int_as_float((254 - b) << 23);
+            a[i] = t == t ? t : 0.0f;
+            sfv[i] = lane == p ? b : sfv[i];
+        }
+        a[NV] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; i += 2) {
+            const uint32_t c = e2m1x2_codes(a[i], a[i + 1]);
+            const float2 q = e2m1x2_values(c);
+            res[i] = fmaf(-q.x, S[i], res[i]);
+            nib[i] |= (c & 0xFu) << (4 * p);
+            if (i + 1 < NV) {
+                res[i + 1] = fmaf(-q.y, S[i + 1], res[i + 1]);
+                nib[i + 1] |= (c >> 4) << (4 * p);
             }
+        }
+    }
+    const int p = lane & 7, g = lane >> 3;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        // -0 codes (a negative value rounded to zero) become 0
+        const uint32_t t = nib[i] ^ 0x88888888u;
+        const uint32_t nz = (t | (t >> 1) | (t >> 2) | (t >> 3)) & 0x11111111u;
+        const uint32_t w = transpose_nibbles8(nib[i] & ~((~nz & 0x11111111u) << 3), lane);
+        if (sf[i]) {
+            if (p < NP) *reinterpret_cast<uint32_t*>(data[i] + p * row_stride + 4 * g) = w;
+            if (lane < NP) sf[i][lane * sf_stride] = uint8_t(sfv[i]);
         }
     }
 }

@@ -701,6 +701,8 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms, int64_t H
         }
         L.logit_part = carve(off, sizeof(float) * L.KQ * M * L.E);
         L.route_done = carve(off, sizeof(unsigned) * (2 + (L.E + 15) / 16));   // + piece-task counter
+        L.route_keys = carve(off, sizeof(uint32_t) * M * L.E);
+        L.route_scores = carve(off, sizeof(float) * M * L.E);
         L.act_hi = carve(off, size_t(L.U) * kBMaxN * (L.I / 2));        // act pieces
         L.act_ts = carve(off, size_t(L.U) * (L.I / 128) * kBChunk);
         L.partA = carve(off, sizeof(float) * L.U * (L.I / kBRows) * L.CA * 2 * kMaxTok * kBRows);
@@ -732,6 +734,8 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms, int64_t H
         }
         L.logit_part = carve(off, sizeof(float) * L.KQ * M * L.E);
         L.route_done = carve(off, sizeof(unsigned) * (2 + (L.E + 15) / 16));   // + piece-task counter
+        L.route_keys = carve(off, sizeof(uint32_t) * M * L.E);
+        L.route_scores = carve(off, sizeof(float) * M * L.E);
         L.act_hi = carve(off, sizeof(__half) * L.ppad * L.I);
         L.act_lo = carve(off, sizeof(__half) * L.ppad * L.I);
         L.act_ts = carve(off, sizeof(float) * L.ppad * L.tspad);
@@ -955,6 +959,10 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     ta.act_kind = p->activation;
     ta.beta = p->situ_beta;
     ta.lbeta = p->situ_linear_beta;
+    // the weights do not come from the previous launch (the scale gather), and the plan
+    // was complete before it started: request the first stages' weight tiles before
+    // waiting for it
+    ta.early_a = 1;
     prof_begin(K3_PROF_TOPK, s);
     int rc = launch_gather_sfb(plan, ws + L.xq_ts, L.H, int(L.U), ws + L.sfb_x, s);
     prof_end(K3_PROF_TOPK, s);
@@ -1046,6 +1054,8 @@ int decode_impl(const k3_moe_params* p, const void* x, int xdt, int64_t M,
         ra.E = L.E;
         ra.logit_part = reinterpret_cast<float*>(ws + L.logit_part);
         ra.logits = logits;
+        pl.keys = reinterpret_cast<uint32_t*>(ws + L.route_keys);
+        pl.scores = reinterpret_cast<float*>(ws + L.route_scores);
         ra.done = reinterpret_cast<unsigned*>(ws + L.route_done);
         ra.xq_hi = xq_hi;
         ra.xq_lo = x_hilo ? xq_lo : nullptr;

@@ -100,30 +100,23 @@ __device__ inline void topk_row(const float* __restrict__ lrow, const float* __r
     __syncwarp();
 }
 
-// One warp per token row: the row's scores live in registers (lane l holds experts
-// l, l+32, ...; NE = ceil(E/32) slots), loaded with one round trip; k rounds of argmax on
-// (corrected desc, index asc) retire the winners and pick up their raw scores from the
-// owning lane; the weights are those raw scores, renormalised (sum in selection order)
-// and scaled as topk_row does.
+// One warp per token row from its precomputed keys (order_key(sigmoid(logit) + bias)) and
+// sigmoid scores: lane l holds experts l, l+32, ... (NE = ceil(E/32) slots), loaded with
+// one round trip; k rounds of argmax on (key desc, index asc) retire the winners and pick
+// up their raw scores from the owning lane; the weights are those raw scores,
+// renormalised (sum in selection order) and scaled as topk_row does. Results go to
+// idx_out / w_out and to the CTA's shared copies si / sw.
 template <int NE>
-__device__ __noinline__ void topk_warp_regs(const float* __restrict__ lrow, const float* __restrict__ bias, int E,
-                                            int k, int renorm, float scale, int32_t* __restrict__ idx_out,
-                                            float* __restrict__ w_out, int lane, int* status) {
+__device__ __noinline__ void topk_warp_regs(const uint32_t* __restrict__ krow, const float* __restrict__ srow,
+                                            int E, int k, int renorm, float scale, int32_t* __restrict__ idx_out,
+                                            float* __restrict__ w_out, int* si, float* sw, int lane, int* status) {
     float raw[NE];
     uint32_t key[NE];
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
         const int e = lane + 32 * i;
-        raw[i] = e < E ? __ldcg(lrow + e) : 0.0f;             // logits from other CTAs
-        key[i] = (bias && e < E) ? __float_as_uint(__ldg(bias + e)) : 0u;
-    }
-#pragma unroll
-    for (int i = 0; i < NE; ++i) {
-        const int e = lane + 32 * i;
-        const float r = 1.0f / (1.0f + expf(-raw[i]));
-        const float c = r + __uint_as_float(key[i]);
-        raw[i] = r;
-        key[i] = e < E ? order_key(c) : 0u;
+        key[i] = e < E ? __ldcg(krow + e) : 0u;               // written by other CTAs
+        raw[i] = e < E ? __ldcg(srow + e) : 0.0f;
     }
     int mine = -1;
     float wmine = 0.0f;
@@ -160,26 +153,29 @@ __device__ __noinline__ void topk_warp_regs(const float* __restrict__ lrow, cons
 #pragma unroll 1
     for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, wmine, s);
     if (lane < k) {
+        const float wo = ((k > 1 && renorm) ? wmine / (sum + 1e-20f) : wmine) * scale;
         idx_out[lane] = mine;
-        w_out[lane] = ((k > 1 && renorm) ? wmine / (sum + 1e-20f) : wmine) * scale;
+        w_out[lane] = wo;
+        si[lane] = mine;
+        sw[lane] = wo;
     }
 }
 
 // Top-k of one token row by one warp, from keys the CTA staged in shared memory (row[e] =
-// order_key(sigmoid(logit) + bias), 1 for NaN). The selection is that of k rounds of argmax
+// order_key(sigmoid(logit) + bias), 1 for NaN) and the row's sigmoid scores srow. The selection is that of k rounds of argmax
 // on (key desc, index asc), found without the rounds' serial chains: T, the k-th largest
 // key, by a bitwise search on counts (keys >= candidate; lane l holds keys l, l+32, ... in
 // NE registers, so each step is NE independent compares and one warp reduction, over only
 // the bits below the common prefix of the row's largest and smallest key); then one pass in
 // index order takes the keys above T and the lowest-index keys equal to T; then each winner's
 // rank by counting. Weights are the winners' raw scores, renormalised (sum in rank order) and
-// scaled as topk_row does. For wide routers (E > 512) this beats k argmax rounds over 24-32
+// scaled as topk_row does; results go to idx_out / w_out and the shared copies si / sw. For wide routers (E > 512) this beats k argmax rounds over 24-32
 // registers per lane; up to 512 experts the rounds are faster.
 template <int NE>
-__device__ __noinline__ void topk_warp_count(const uint32_t* row, const float* __restrict__ lrow, int E, int k,
+__device__ __noinline__ void topk_warp_count(const uint32_t* row, const float* __restrict__ srow, int E, int k,
                                              int renorm, float scale, int32_t* __restrict__ idx_out,
-                                             float* __restrict__ w_out, int* cand_e, uint32_t* cand_k,
-                                             int lane, int* status) {
+                                             float* __restrict__ w_out, int* si, float* sw, int* cand_e,
+                                             uint32_t* cand_k, int lane, int* status) {
     uint32_t key[NE];
     uint32_t hi = 0u, lo = 0xffffffffu;
 #pragma unroll
@@ -247,67 +243,76 @@ __device__ __noinline__ void topk_warp_count(const uint32_t* row, const float* _
     if (lane < k) cand_e[rank] = ej;
     __syncwarp();
     const int mine = lane < k ? cand_e[lane] : 0;
-    const float w = lane < k ? 1.0f / (1.0f + expf(-__ldcg(lrow + mine))) : 0.0f;
+    const float w = lane < k ? __ldcg(srow + mine) : 0.0f;
     float sum = 0.0f;
 #pragma unroll 1
     for (int s = 0; s < k; ++s) sum += __shfl_sync(0xffffffffu, w, s);
     if (lane < k) {
+        const float wo = ((k > 1 && renorm) ? w / (sum + 1e-20f) : w) * scale;
         idx_out[lane] = mine;
-        w_out[lane] = ((k > 1 && renorm) ? w / (sum + 1e-20f) : w) * scale;
+        w_out[lane] = wo;
+        si[lane] = mine;
+        sw[lane] = wo;
     }
 }
 
-// Whole-CTA top-k of M token rows (M <= 8), warp t selecting token t's k experts. Up to
-// E = 512 the warp holds its row in registers and runs k argmax rounds; wider rows are
-// first staged as keys in s_key by every thread (M * E words of shared scratch; eight
-// logit loads in flight per thread per pass, the logits coming from other CTAs) for the
+// Whole-CTA top-k of M token rows (M <= 8) from precomputed keys and sigmoid scores
+// ([M][E] each, written by other CTAs), warp t selecting token t's k experts into
+// idx_out / w_out and the shared copies si / sw ([M][k]). Up to E = 512 the warp holds
+// its row in registers and runs k argmax rounds; wider rows are first staged in s_key
+// (M * E words of shared scratch; eight loads in flight per thread per pass) for the
 // counting search.
-__device__ inline void topk_cta(const float* __restrict__ logits, const float* __restrict__ bias, int M,
+__device__ inline void topk_cta(const uint32_t* __restrict__ keys, const float* __restrict__ scores, int M,
                                 int E, int k, int renorm, float scale, int32_t* __restrict__ idx_out,
-                                float* __restrict__ w_out, uint32_t* s_key, int warp, int lane, int* status) {
+                                float* __restrict__ w_out, int* si, float* sw, uint32_t* s_key, int warp,
+                                int lane, int* status) {
     __shared__ int cand_e[kMaxTok][kMaxTopK];
     __shared__ uint32_t cand_k[kMaxTok][kMaxTopK];
     if (E <= 512) {
         if (warp >= M) return;
-        const float* lrow = logits + int64_t(warp) * E;
+        const uint32_t* krow = keys + int64_t(warp) * E;
+        const float* srow = scores + int64_t(warp) * E;
         int32_t* io = idx_out + warp * k;
         float* wo = w_out + warp * k;
-        if (E <= 128) topk_warp_regs<4>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-        else if (E <= 256) topk_warp_regs<8>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-        else if (E <= 384) topk_warp_regs<12>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
-        else topk_warp_regs<16>(lrow, bias, E, k, renorm, scale, io, wo, lane, status);
+        int* sio = si + warp * k;
+        float* swo = sw + warp * k;
+        if (E <= 128) topk_warp_regs<4>(krow, srow, E, k, renorm, scale, io, wo, sio, swo, lane, status);
+        else if (E <= 256) topk_warp_regs<8>(krow, srow, E, k, renorm, scale, io, wo, sio, swo, lane, status);
+        else if (E <= 384) topk_warp_regs<12>(krow, srow, E, k, renorm, scale, io, wo, sio, swo, lane, status);
+        else topk_warp_regs<16>(krow, srow, E, k, renorm, scale, io, wo, sio, swo, lane, status);
         return;
     }
 #pragma unroll 1
     for (int i0 = threadIdx.x; i0 < M * E; i0 += 8 * blockDim.x) {
-        float l[8], b[8];
+        uint32_t v[8];
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-            const int i = min(i0 + h * int(blockDim.x), M * E - 1);
-            l[h] = __ldcg(logits + i);
-            b[h] = bias ? __ldg(bias + i % E) : 0.0f;
-        }
+        for (int h = 0; h < 8; ++h) v[h] = __ldcg(keys + min(i0 + h * int(blockDim.x), M * E - 1));
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
             const int i = i0 + h * int(blockDim.x);
-            if (i < M * E) s_key[i] = order_key(1.0f / (1.0f + expf(-l[h])) + b[h]);
+            if (i < M * E) s_key[i] = v[h];
         }
     }
     __syncthreads();
     if (warp >= M) return;
     const uint32_t* row = s_key + warp * E;
-    const float* lrow = logits + int64_t(warp) * E;
+    const float* srow = scores + int64_t(warp) * E;
     int32_t* io = idx_out + warp * k;
     float* wo = w_out + warp * k;
+    int* sio = si + warp * k;
+    float* swo = sw + warp * k;
     int* ce = cand_e[warp];
     uint32_t* ck = cand_k[warp];
-    if (E <= 768) topk_warp_count<24>(row, lrow, E, k, renorm, scale, io, wo, ce, ck, lane, status);
-    else topk_warp_count<32>(row, lrow, E, k, renorm, scale, io, wo, ce, ck, lane, status);
+    if (E <= 768) topk_warp_count<24>(row, srow, E, k, renorm, scale, io, wo, sio, swo, ce, ck, lane, status);
+    else topk_warp_count<32>(row, srow, E, k, renorm, scale, io, wo, sio, swo, ce, ck, lane, status);
 }
 
 // The routing part of a decode call.
 struct PlanArgs {
     const float* bias;
+    // fused router only: the top-k keys and sigmoid scores [M][E] (see topk_cta)
+    uint32_t* keys;
+    float* scores;
     int E, k, renorm;
     float scale;
     int32_t* idx;                  // [M][k]: written here when logits are given, else read
@@ -321,14 +326,16 @@ struct PlanArgs {
     int M;
 };
 
-// Whole-CTA: zero the counters, run the top-k when `logits` is given (warp t: token t),
+// Whole-CTA: zero the counters, run the top-k (warp t: token t; kSharedKeys: always,
+// from a.keys / a.scores; otherwise when `logits` is given),
 // then build the plan: active experts in ascending id order (moe.py:120), per expert its
 // (token, weight) pairs in ascending token order, the shared expert last. Every routing
 // entry finds its expert's slot and its rank among the same expert's earlier entries in
 // parallel.
-// kSharedKeys: the top-k stages its keys in s_key (M * E words of shared scratch) and runs
-// topk_cta; otherwise warp t runs topk_row on token t. A compile-time choice, so a kernel
-// carries the registers of only the form it uses.
+// kSharedKeys: the top-k runs topk_cta on the precomputed a.keys / a.scores (s_key: M * E
+// words of shared scratch for wide routers) and leaves its results in shared memory as
+// well; otherwise warp t runs topk_row on token t's logits. A compile-time choice, so a
+// kernel carries the registers of only the form it uses.
 template <bool kSharedKeys = false>
 __device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, int warp, int lane,
                                       uint32_t* s_key = nullptr) {
@@ -347,9 +354,8 @@ __device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, in
     for (int i = threadIdx.x; i < kMaxActive; i += blockDim.x) cnt[i] = 0;
     __syncthreads();
     if constexpr (kSharedKeys) {
-        if (logits)
-            topk_cta(logits, a.bias, a.M, a.E, a.k, a.renorm, a.scale, a.idx, a.w, s_key, warp, lane,
-                     &P->status);
+        topk_cta(a.keys, a.scores, a.M, a.E, a.k, a.renorm, a.scale, a.idx, a.w, s_idx, s_w, s_key, warp,
+                 lane, &P->status);
     } else {
         if (logits && warp < a.M)
             topk_row(logits + int64_t(warp) * a.E, a.bias, a.E, a.k, a.renorm, a.scale,
@@ -358,9 +364,14 @@ __device__ inline void build_plan_cta(const PlanArgs& a, const float* logits, in
     __syncthreads();                               // top-k results visible
     const int nsel = a.M * a.k;
     for (int i = threadIdx.x; i < nsel; i += blockDim.x) {
-        const int e = a.idx[i];
-        s_idx[i] = e;
-        s_w[i] = a.w[i];
+        int e;
+        if constexpr (kSharedKeys) {
+            e = s_idx[i];                          // the top-k's shared copy
+        } else {
+            e = a.idx[i];
+            s_idx[i] = e;
+            s_w[i] = a.w[i];
+        }
         if (e < 0 || e >= a.E)
             P->status = K3_ERR_INVALID;
         else

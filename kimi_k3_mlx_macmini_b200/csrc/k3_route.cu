@@ -6,8 +6,10 @@
 // (x bf16 is exact; fp32 x is split into bf16 hi + lo), its 8 warps taking equal parts
 // of the slice and meeting in shared memory in warp order. Slice partials are summed
 // in slice order by the last CTA of each row block to arrive, so the logits are
-// deterministic; the last row block to finish runs the top-k and builds the plan. The
-// CTAs of the first row blocks also convert x, one exponent per (token, 512-k block).
+// deterministic; that CTA also turns its logits into the top-k's keys and sigmoid scores.
+// The last row block to finish runs the top-k and builds the plan. The other CTAs
+// split the expert input into E2M1 pieces (block-scaled path) or convert x to f16
+// pieces.
 #include "k3_route.cuh"
 
 namespace k3 {
@@ -150,7 +152,15 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
 #pragma unroll
             for (int s = 0; s < kMaxSlices; ++s)
                 if (s < int(gridDim.y)) v += pv[s];
-            a.logits[int64_t(t) * a.E + e] = v;
+            const int64_t o = int64_t(t) * a.E + e;
+            a.logits[o] = v;
+            // the top-k's inputs, here where 16 x M threads per row block compute them in
+            // parallel instead of in the one CTA that runs the selection: raw = sigmoid,
+            // key of raw + bias (moe.py:65-76)
+            const float raw = 1.0f / (1.0f + expf(-v));
+            const float* bias = a.plan_args.bias;
+            a.plan_args.keys[o] = order_key(raw + (bias ? __ldg(bias + e) : 0.0f));
+            a.plan_args.scores[o] = raw;
         }
     }
     __threadfence();
@@ -164,7 +174,7 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     }
     __threadfence();
     extern __shared__ uint32_t s_key[];                      // M * E top-k keys
-    build_plan_cta<true>(a.plan_args, a.logits, warp, lane, s_key);
+    build_plan_cta<true>(a.plan_args, nullptr, warp, lane, s_key);
     do_pieces();                                             // whatever the others left
 }
 

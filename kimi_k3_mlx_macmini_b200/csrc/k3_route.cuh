@@ -29,6 +29,9 @@ struct RouteArgs {
     // (replaces xq_* when non-null)
     uint8_t* xp;
     uint8_t* xsf;
+    // plan_args.keys / .scores [M][E]: written by the row blocks' finishing CTAs (the
+    // top-k keys order_key(sigmoid(logit) + bias) and the sigmoid scores), read by the
+    // CTA that runs the top-k
     PlanArgs plan_args;
     Plan* plan;
 };
