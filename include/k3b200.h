@@ -249,6 +249,17 @@ K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* x, int x_dt
                                  const int32_t* idx, const float* w, void* y_out, int y_dtype,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* One expert's unweighted SwiGLU FFN: LatentMoE.expert_forward (air_llm/models/kimi_k3/
+ * moe.py:90-103), y [M][H] = act(x W1^T, x W3^T) W2^T of pool slot `expert` (a routed
+ * expert id, or num_experts for an MXFP4 shared expert). Three launches (x pieces,
+ * gate/up, down) on the block-scaled pool; no routing plan. Limits: 1 <= M <= 8, H % 512
+ * == 0, I % 512 == 0, a block-scaled pool (p->experts may be NULL). x f32|bf16, y
+ * f32|bf16. */
+K3_API size_t k3_moe_expert_forward_workspace(const k3_moe_params* p, int64_t M);
+K3_API int k3_moe_expert_forward(const k3_moe_params* p, const void* x, int x_dtype, int64_t M,
+                                 int64_t expert, void* y_out, int y_dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ prefill --- */
 
 /* Prefill (any number of tokens T, meant for T in the hundreds to thousands) MoE block

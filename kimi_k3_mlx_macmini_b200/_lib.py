@@ -76,6 +76,9 @@ SIGNATURES = {
                              _vp, _vp, _vp, _sz, _vp]),
     "k3_moe_experts_decode": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp,
                                      _i32, _vp, _sz, _vp]),
+    "k3_moe_expert_forward_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64]),
+    "k3_moe_expert_forward": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _i64, _vp, _i32, _vp,
+                                     _sz, _vp]),
     "k3_moe_prefill_workspace": (_sz, [ctypes.POINTER(K3MoEParams), _i64]),
     "k3_moe_prefill": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _vp, _i32,
                               _vp, _vp, _vp, _sz, _vp]),

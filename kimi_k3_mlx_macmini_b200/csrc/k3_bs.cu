@@ -34,7 +34,9 @@ __device__ __forceinline__ void epi_sync() {
 }
 
 
-__device__ __forceinline__ int64_t owner_of(int64_t i, int64_t n, int64_t g) {
+// CTA owning item i of n items split over g CTAs in contiguous ranges [b n / g, (b+1) n / g)
+// (32-bit: the host keeps n * g below 2^32)
+__device__ __forceinline__ uint32_t owner_of(uint32_t i, uint32_t n, uint32_t g) {
     return ((i + 1) * g - 1) / n;
 }
 
@@ -45,12 +47,46 @@ __device__ __forceinline__ float sum8(const float* v) {
 
 }  // namespace
 
-template <bool GATEUP, bool SFRAW>
+// The last CTA of a split key sums the key's segment partials (each [PW][128] floats:
+// per pair the gate or down value, then for gate/up the up value) in segment order into
+// acc0 / acc1 for row r: G segments' values of the first NPM pairs in flight at once
+// (np <= NPM; pairs past np read nothing and add zeros).
+template <int G, int NPM, bool GATEUP>
+__device__ __forceinline__ void sum_segments(const float* kpart, const int* segs, int nseg, int np, int r,
+                                             float (&acc0)[kBMaxN / kBPieces], float (&acc1)[kBMaxN / kBPieces]) {
+    constexpr int kMaxPr = kBMaxN / kBPieces;
+    constexpr int kPW = GATEUP ? 2 * kMaxPr : kMaxPr;
+    for (int sg0 = 0; sg0 < nseg; sg0 += G) {
+        float x0[G][NPM], x1[G][NPM];
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            const float* sp = kpart + int64_t(segs[min(sg0 + u, nseg - 1)]) * (kPW * kBRows);
+#pragma unroll
+            for (int pi = 0; pi < NPM; ++pi) {
+                const bool ok = sg0 + u < nseg && pi < np;
+                x0[u][pi] = ok ? __ldcg(sp + pi * kBRows + r) : 0.0f;
+                x1[u][pi] = (GATEUP && ok) ? __ldcg(sp + (kMaxPr + pi) * kBRows + r) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            if (sg0 + u >= nseg) break;
+#pragma unroll
+            for (int pi = 0; pi < NPM; ++pi) {
+                acc0[pi] += x0[u][pi];
+                if (GATEUP) acc1[pi] += x1[u][pi];
+            }
+        }
+    }
+}
+
+template <bool GATEUP, bool SFRAW, bool SFBRAW>
 __global__ void __launch_bounds__(kBThreads, 1)
     bs_gemv_kernel(const __grid_constant__ BMaps maps, const BArgs a) {
     static_assert(!(GATEUP && SFRAW), "row-major scales are read by the single-projection kernel only");
-    using St = BStage<GATEUP, SFRAW>;
-    constexpr int S = bstages<GATEUP, SFRAW>();
+    static_assert(!SFBRAW || GATEUP, "raw piece scales are read by the gate/up kernel only");
+    using St = BStage<GATEUP, SFRAW, SFBRAW>;
+    constexpr int S = bstages<GATEUP, SFRAW, SFBRAW>();
     constexpr uint32_t kCols = btmem_cols<GATEUP>();
     constexpr int kAccW = GATEUP ? 128 : 64;               // TMEM columns per accumulator
     constexpr int kSf0 = 2 * kAccW;                        // first scale column
@@ -83,6 +119,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
         if (GATEUP) prefetch_tensormap(&maps.a1);
         prefetch_tensormap(&maps.b);
         if (SFRAW) prefetch_tensormap(&maps.sfa);
+        if (SFBRAW) prefetch_tensormap(&maps.sfb);
     }
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -121,7 +158,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
         }
     } else {
         // the plan was written two launches back (router / plan kernel, then the scale-chunk
-        // gather), which had completed when the previous launch started
+        // gather), which had completed when the previous launch started -- or by the
+        // previous launch itself (plan_in_prev): wait for it first
+        if (a.plan_in_prev) asm volatile("griddepcontrol.wait;\n" ::: "memory");
         for (int i = threadIdx.x; i < int(sizeof(Plan) / 4); i += blockDim.x)
             reinterpret_cast<int*>(&s_plan)[i] = reinterpret_cast<const int*>(a.plan)[i];
     }
@@ -133,16 +172,19 @@ __global__ void __launch_bounds__(kBThreads, 1)
     // Keys: (128-row block rb, expert item v), key = rb * V + v (row-block major, so heavy
     // experts spread over CTAs); items = the key's C k-chunks.
     const Plan* P = &s_plan;
+    // Item indices in 32-bit arithmetic (a 64-bit division by a runtime divisor is a long
+    // dependent sequence, and the producer does four per item before its first request);
+    // the host keeps (items) x (grid) below 2^32.
     const int V = P->n_active;
-    const int64_t nRb = a.rows / kBRows;
-    const int64_t ipk = a.C;
-    const int64_t n = int64_t(V) * nRb * ipk;
-    const int64_t grid = gridDim.x, bid = blockIdx.x;
-    const int64_t i0 = bid * n / grid, i1 = (bid + 1) * n / grid;
+    const uint32_t uV = uint32_t(V);
+    const uint32_t nRb = uint32_t(a.rows / kBRows);
+    const uint32_t ipk = uint32_t(a.C);
+    const uint32_t n = uV * nRb * ipk;
+    const uint32_t grid = gridDim.x, bid = blockIdx.x;
+    const uint32_t i0 = bid * n / grid, i1 = (bid + 1) * n / grid;
     const int64_t kchunk = a.K / a.C;
     const int nst = int(kchunk / kBStageK);
     const int64_t kcks = a.K / 128;                                   // scale chunks per row block
-    const int64_t G = a.K / 32;                                       // scale blocks per row
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -154,11 +196,11 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 int64_t kbase;
                 uint32_t bytes;
             };
-            auto item_at = [&](int64_t i) {
+            auto item_at = [&](uint32_t i) {
                 Item it;
-                const int64_t key = i / ipk;
-                it.v = int(key % V);
-                it.rb = int(key / V);
+                const uint32_t key = i / ipk;
+                it.v = int(key % uV);
+                it.rb = int(key / uV);
                 it.slot = P->expert[it.v];
                 it.ps = P->pair_start[it.v];
                 it.np = P->pair_start[it.v + 1] - it.ps;
@@ -166,7 +208,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 it.tb = it.slot * int(nRb) + it.rb;
                 it.kbase = int64_t(i % ipk) * kchunk;
                 it.bytes = uint32_t((GATEUP ? 2 : 1) * (kBRows * 128 + (SFRAW ? kBRows * 16 : 2 * kBChunk)) +
-                                    it.np * kBPieces * 128 + 2 * kBChunk);
+                                    it.np * kBPieces * 128 + (SFBRAW ? it.np * kBPieces * 16 : 2 * kBChunk));
                 return it;
             };
             // the weight tiles and their scales of k-step s
@@ -198,19 +240,23 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 St& st = ring[si];
                 const int64_t k = it.kbase + int64_t(s) * kBStageK;
                 if (GATEUP) {
-                    for (int pi = 0; pi < it.np; ++pi)      // one token's 8 piece rows per pair
-                        tma_2d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * P->pair_tok[it.ps + pi],
-                               &full[si]);
+                    for (int pi = 0; pi < it.np; ++pi) {    // one token's 8 piece rows per pair
+                        const int row = kBPieces * P->pair_tok[it.ps + pi];
+                        tma_2d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), row, &full[si]);
+                        if constexpr (SFBRAW)                // and their scales' 512-k box
+                            tma_2d(&st.sfbraw[kBPieces * pi][0], &maps.sfb, int(k / 512) * 16, row, &full[si]);
+                    }
                 } else {
                     for (int pi = 0; pi < it.np; ++pi)      // pair pi's 8 piece rows
                         tma_3d(&st.b[kBPieces * pi][0], &maps.b, int(k / 2), kBPieces * pi, it.v, &full[si]);
                 }
-                bulk_g2s(&st.sfb[0], a.sfb + (int64_t(it.v) * kcks + k / 128) * kBChunk, 2 * kBChunk, &full[si]);
+                if constexpr (!SFBRAW)
+                    bulk_g2s(&st.sfb[0], a.sfb + (int64_t(it.v) * kcks + k / 128) * kBChunk, 2 * kBChunk, &full[si]);
             };
             // Nothing of the weights comes from the previous launch: when allowed, request
             // the first stages' weight tiles and scales (the ring starts empty) before
             // waiting for it. (ie, se) is the first stage not yet requested.
-            int64_t ie = i0;
+            uint32_t ie = i0;
             int se = 0;
             uint32_t pre = 0;
             if (a.identity_m > 0 || a.early_a) {
@@ -232,7 +278,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
             asm volatile("griddepcontrol.wait;\n" ::: "memory");
             {
                 uint32_t g = 0;
-                for (int64_t i = i0; g < pre; ++i) {
+                for (uint32_t i = i0; g < pre; ++i) {
                     const Item it = item_at(i);
                     for (int s = 0; s < nst && g < pre; ++s, ++g) {
                         stage_b(it, s, int(g));
@@ -241,7 +287,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 }
             }
             uint32_t gs = pre;
-            for (int64_t i = ie; i < i1 && !s_abort; ++i) {
+            for (uint32_t i = ie; i < i1 && !s_abort; ++i) {
                 const Item it = item_at(i);
                 for (int s = (i == ie ? se : 0); s < nst; ++s, ++gs) {
                     const int si = int(gs % S);
@@ -260,12 +306,12 @@ __global__ void __launch_bounds__(kBThreads, 1)
         // ---------------------------------------------------------- MMA issuer
         // The whole warp runs the loop (warp-uniform descriptors); one elected lane issues.
         uint32_t gs = 0, ib = 0;
-        for (int64_t i = i0; i < i1 && !s_abort; ++i, ++ib) {
-            const int v = int((i / ipk) % V);
+        for (uint32_t i = i0; i < i1 && !s_abort; ++i, ++ib) {
+            const int v = int((i / ipk) % uV);
             const int np = P->pair_start[v + 1] - P->pair_start[v];
             const int nb = kBPieces * np;                                // MMA N
             // SFRAW: parity of the item's first 256-k step (which half of a 512-k scale box)
-            const int half0 = SFRAW ? int((int64_t(i % ipk) * nst) & 1) : 0;
+            const int half0 = (SFRAW || SFBRAW) ? int(((i % ipk) * uint32_t(nst)) & 1u) : 0;
             const uint32_t buf = ib & 1;
             if (!__all_sync(0xffffffffu, mbar_wait(&acce[buf], ((ib >> 1) & 1) ^ 1, a.status, &s_abort))) {
                 s_abort = 1;
@@ -297,6 +343,22 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     *reinterpret_cast<uint4*>(&st.sfa[0][16 * lane]) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
                     *reinterpret_cast<uint4*>(&st.sfa[0][kBChunk + 16 * lane]) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
                     // generic-proxy writes, read next by tcgen05.cp (async proxy)
+                    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                    __syncwarp();
+                }
+                if constexpr (SFBRAW) {
+                    // the same for the piece scales: B row m (pair m / 8, piece m % 8), lane
+                    // l takes rows l and l + 32, its 8 bytes of the stage's half of the box
+                    const int half = (half0 + s) & 1;
+#pragma unroll
+                    for (int c = 0; c < 2; ++c) {
+                        const int m = lane + 32 * c;
+                        if (m < nb) {
+                            const uint2 v2 = *reinterpret_cast<const uint2*>(&st.sfbraw[m][8 * half]);
+                            *reinterpret_cast<uint32_t*>(&st.sfb[sf_chunk_offset(m, 0)]) = v2.x;
+                            *reinterpret_cast<uint32_t*>(&st.sfb[kBChunk + sf_chunk_offset(m, 0)]) = v2.y;
+                        }
+                    }
                     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
                     __syncwarp();
                 }
@@ -349,9 +411,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
 #pragma unroll
         for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
         uint32_t ib = 0;
-        for (int64_t i = i0; i < i1; ++i, ++ib) {
-            const int64_t key = i / ipk;
-            const int v = int(key % V), rb = int(key / V);
+        for (uint32_t i = i0; i < i1; ++i, ++ib) {
+            const uint32_t key = i / ipk;
+            const int v = int(key % uV), rb = int(key / uV);
             const int ps = P->pair_start[v], np = P->pair_start[v + 1] - ps;
             const uint32_t buf = ib & 1;
             const bool ok = mbar_wait(&accf[buf], (ib >> 1) & 1, a.status, &s_abort);
@@ -384,11 +446,11 @@ __global__ void __launch_bounds__(kBThreads, 1)
             if (i + 1 < i1 && (i + 1) / ipk == key) continue;
 
             // ---- flush the key
-            const int64_t ks = key * ipk;
+            const uint32_t ks = key * ipk;
             const bool local = ipk == 1 || (ks >= i0 && ks + ipk <= i1);
-            float* kpart = a.part + key * a.maxseg * (kPW * kBRows);
+            float* kpart = a.part + int64_t(key) * a.maxseg * (kPW * kBRows);
             if (!local) {
-                const int64_t seg = (i0 > ks ? i0 : ks) - ks;
+                const int64_t seg = int64_t((i0 > ks ? i0 : ks) - ks);
                 float* sp = kpart + seg * (kPW * kBRows);
 #pragma unroll
                 for (int pi = 0; pi < kMaxPr; ++pi) {
@@ -400,9 +462,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
                     // the key's segments: one per CTA b owning items of it, starting at that
                     // CTA's first item (CTAs with empty ranges own nothing)
                     int ns = 0;
-                    const int64_t b0 = owner_of(ks, n, grid), b1 = owner_of(ks + ipk - 1, n, grid);
-                    for (int64_t cb = b0; cb <= b1 && ns < kBMaxSegments; ++cb) {
-                        const int64_t f0 = cb * n / grid, f1 = (cb + 1) * n / grid;
+                    const uint32_t b0 = owner_of(ks, n, grid), b1 = owner_of(ks + ipk - 1, n, grid);
+                    for (uint32_t cb = b0; cb <= b1 && ns < kBMaxSegments; ++cb) {
+                        const uint32_t f0 = cb * n / grid, f1 = (cb + 1) * n / grid;
                         if (f1 > f0) s_seg[ns++] = int((f0 > ks ? f0 : ks) - ks);
                     }
                     s_nseg = ns;
@@ -423,28 +485,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
                 __threadfence();
 #pragma unroll
                 for (int pi = 0; pi < kMaxPr; ++pi) acc0[pi] = acc1[pi] = 0.0f;
-                // segment order: deterministic sums. Four segments' loads are in flight at
-                // once, and only the values of the key's np pairs are read.
+                // segment order: deterministic sums. Only the key's np pairs are read; in the
+                // projection kernels, the fewer they are, the more segments' loads are in
+                // flight at once (in gate/up the wider merge's registers cost more than its
+                // round trips save: measured)
                 const int nseg = s_nseg;
-                for (int sg0 = 0; sg0 < nseg; sg0 += 4) {
-                    float x[4][kPW];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float* sp = kpart + int64_t(s_seg[min(sg0 + u, nseg - 1)]) * (kPW * kBRows);
-#pragma unroll
-                        for (int c = 0; c < kPW; ++c)
-                            x[u][c] = (sg0 + u < nseg && (c % kMaxPr) < np) ? __ldcg(sp + c * kBRows + r) : 0.0f;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        if (sg0 + u >= nseg) break;
-#pragma unroll
-                        for (int pi = 0; pi < kMaxPr; ++pi) {
-                            acc0[pi] += x[u][pi];
-                            if (GATEUP) acc1[pi] += x[u][(GATEUP ? kMaxPr : 0) + pi];
-                        }
-                    }
-                }
+                if (GATEUP || np > 4) sum_segments<4, kMaxPr, GATEUP>(kpart, s_seg, nseg, np, r, acc0, acc1);
+                else if (np <= 2) sum_segments<16, 2, GATEUP>(kpart, s_seg, nseg, np, r, acc0, acc1);
+                else sum_segments<8, 4, GATEUP>(kpart, s_seg, nseg, np, r, acc0, acc1);
             }
             if (GATEUP) {
                 // activation x routing weight per pair, split into the down kernel's pieces,
@@ -648,19 +696,22 @@ int launch_scales_tc(const uint8_t* in, int64_t rows, int64_t cols, int64_t batc
 
 // ------------------------------------------------------------------ launches
 
-template <bool G, bool SFRAW = false>
+template <bool G, bool SFRAW = false, bool SFBRAW = false>
 int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const char* what) {
     if (grid > kBMaxSegments) return fail(K3_ERR_UNSUPPORTED, "block-scaled grid above 256 CTAs");
+    // item indices are 32-bit in the kernel: (items of at most kMaxActive experts) x grid
+    if (uint64_t(kMaxActive) * uint64_t(a.rows / kBRows) * uint64_t(a.C) * uint64_t(grid) >= (uint64_t(1) << 32))
+        return fail(K3_ERR_UNSUPPORTED, "block-scaled launch: too many items for 32-bit indices");
     static OncePerContext attr;
-    constexpr size_t smem = bsmem_bytes<G, SFRAW>();
+    constexpr size_t smem = bsmem_bytes<G, SFRAW, SFBRAW>();
     if (int rc = attr.run([&] {
-            return cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G, SFRAW>,
+            return cuda_check(cudaFuncSetAttribute(bs_gemv_kernel<G, SFRAW, SFBRAW>,
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)),
                               what);
         }))
         return rc;
-    if (int rc = cuda_check(launch_pdl(bs_gemv_kernel<G, SFRAW>, dim3(unsigned(grid)), dim3(kBThreads), smem, s,
-                                       maps, a),
+    if (int rc = cuda_check(launch_pdl(bs_gemv_kernel<G, SFRAW, SFBRAW>, dim3(unsigned(grid)), dim3(kBThreads),
+                                       smem, s, maps, a),
                             what))
         return rc;
     return K3_OK;
@@ -668,6 +719,10 @@ int launch_bs(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s, const
 
 int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
     return launch_bs<true>(maps, a, grid, s, "bs_gemv<gate/up>");
+}
+int launch_bs_gateup_rawsfb(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
+    if (!a.plan_in_prev) return fail(K3_ERR_INVALID, "bs_gemv<gate/up, raw piece scales>: plan_in_prev unset");
+    return launch_bs<true, false, true>(maps, a, grid, s, "bs_gemv<gate/up, raw piece scales>");
 }
 int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s) {
     return launch_bs<false>(maps, a, grid, s, "bs_gemv<down>");

@@ -36,7 +36,8 @@ __host__ __device__ __forceinline__ int sf_chunk_offset(int n, int j) {
 // expert block share the B tile; down: one 128-row tile. SFRAW stages (weights with their
 // scales as stored, row-major [rows][K/32]) also hold the TMA box of those scales: 16
 // bytes (512 k) of each of the 128 rows, from which the MMA warp writes the stage's two
-// scale chunks.
+// scale chunks. SFBRAW stages (gate/up) do the same for the activation pieces: per pair
+// the 16-byte (512 k) box of its token's 8 piece rows of the per-row scales [8T][K/32].
 template <bool GATEUP>
 struct alignas(1024) BStageBase {
     uint8_t a[GATEUP ? 2 : 1][kBRows][128];     // E2M1 weights, SW128
@@ -44,34 +45,41 @@ struct alignas(1024) BStageBase {
     uint8_t sfa[GATEUP ? 2 : 1][2 * kBChunk];   // weight scales, two chunks (256 k)
     uint8_t sfb[2 * kBChunk];                   // piece scales, two chunks
 };
-template <bool GATEUP, bool SFRAW = false>
+template <bool GATEUP, bool SFRAW = false, bool SFBRAW = false>
 struct alignas(1024) BStage : BStageBase<GATEUP> {};
 template <bool GATEUP>
-struct alignas(1024) BStage<GATEUP, true> : BStageBase<GATEUP> {
-    uint8_t sfraw[kBRows][16];                  // row-major scale box (512 k)
+struct alignas(1024) BStage<GATEUP, true, false> : BStageBase<GATEUP> {
+    uint8_t sfraw[kBRows][16];                  // row-major weight scale box (512 k)
+};
+template <>
+struct alignas(1024) BStage<true, false, true> : BStageBase<true> {
+    uint8_t sfbraw[kBMaxN][16];                 // per pair: its token's 8 piece-scale rows (512 k)
 };
 static_assert(sizeof(BStage<false>) == sizeof(BStageBase<false>) && sizeof(BStage<true>) == sizeof(BStageBase<true>),
               "the stored-layout stages carry no raw scale box");
 
-template <bool GATEUP, bool SFRAW = false>
+template <bool GATEUP, bool SFRAW = false, bool SFBRAW = false>
 constexpr int bstages() { return GATEUP ? 5 : (SFRAW ? 7 : 8); }
 template <bool GATEUP>
 constexpr uint32_t btmem_cols() { return GATEUP ? 512 : 256; }
-template <bool GATEUP, bool SFRAW = false>
+template <bool GATEUP, bool SFRAW = false, bool SFBRAW = false>
 constexpr size_t bsmem_bytes() {
-    return sizeof(BStage<GATEUP, SFRAW>) * bstages<GATEUP, SFRAW>() + 1024 /*align*/ + 256 /*barriers*/;
+    return sizeof(BStage<GATEUP, SFRAW, SFBRAW>) * bstages<GATEUP, SFRAW, SFBRAW>() + 1024 /*align*/ +
+           256 /*barriers*/;
 }
 static_assert(bsmem_bytes<true>() + 4096 <= 227 * 1024 && bsmem_bytes<false>() + 4096 <= 227 * 1024 &&
-                  bsmem_bytes<false, true>() + 4096 <= 227 * 1024,
+                  bsmem_bytes<false, true>() + 4096 <= 227 * 1024 &&
+                  bsmem_bytes<true, false, true>() + 5 * 1024 + 512 <= 227 * 1024,
               "block-scaled ring exceeds shared memory");
 
 // Tensor maps: a0/a1 = packed weight pools, row-major [slot][rows][K/2] (box 128 B x 128
 // rows) or tiled [slot * rows/128][K/256][128][128] (box = one contiguous tile);
 // b = activation pieces, gate/up x [8T][K/2] (box 128 B x 8 rows: one token's pieces),
 // down act [v][64][K/2] (box 128 B x 8 rows: one pair's pieces); sfa (SFRAW only) = the
-// weight scales as stored, [slot * rows][K/32] (box 16 B x 128 rows).
+// weight scales as stored, [slot * rows][K/32] (box 16 B x 128 rows); sfb (SFBRAW only) =
+// the per-row scales of the x pieces [8T][K/32] (box 16 B x 8 rows: one token's pieces).
 struct BMaps {
-    CUtensorMap a0, a1, b, sfa;
+    CUtensorMap a0, a1, b, sfa, sfb;
 };
 
 struct BArgs {
@@ -104,15 +112,27 @@ struct BArgs {
     int identity_m;
     // request the first stages' weights before waiting for the previous launch (the weights
     // and the plan never come from it): set for the down phase, whose CTAs start on the SMs
-    // that the gate/up launch's early finishers leave
+    // that the gate/up launch's early finishers leave. (Measured slower for the gate/up
+    // phase when its previous launch was the short scale gather.)
     int early_a;
+    // the previous launch writes the plan (the gate/up launch with raw piece scales follows
+    // the plan producer directly): every thread waits for it before copying the plan
+    int plan_in_prev;
 };
 
 int launch_bs_gateup(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
+// The gate/up kernel reading the x pieces' per-row scales through maps.sfb (no scale
+// gather launch before it); a.plan_in_prev must be set.
+int launch_bs_gateup_rawsfb(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
 int launch_bs_down(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
 // The down-phase kernel over a weight matrix whose scales are row-major as stored
 // (maps.sfa), for the single-matrix matvec.
 int launch_bs_proj_rawsf(const BMaps& maps, const BArgs& a, int grid, cudaStream_t s);
+// x [M][K] -> E2M1 pieces [8M][K/2] and their scale chunks for identity-plan items of 8
+// tokens [M/8][K/128][512]; zeroes ncnt arrival counters and sets *status = K3_OK (the
+// launch a projection with identity_m = M depends on).
+int launch_mv_prep(const void* x, int xdt, int M, int64_t K, uint8_t* xp, uint8_t* sfb, unsigned* cnt, int ncnt,
+                   int* status, cudaStream_t s);
 // Per-item B scale chunks of the gate/up phase from the per-row x piece scales.
 int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
                       cudaStream_t s);

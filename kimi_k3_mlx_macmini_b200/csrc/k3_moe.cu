@@ -940,6 +940,14 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
                                 CU_TENSOR_MAP_SWIZZLE_128B))
             return rc;
     }
+    {   // the pieces' per-row scales [8M][H/32]: one token's 8 rows x 16 bytes (512 k) a box
+        const uint64_t d[2] = {uint64_t(L.H / 32), uint64_t(kBPieces * M)};
+        const uint64_t st[1] = {uint64_t(L.H / 32)};
+        const uint32_t b[2] = {16, uint32_t(kBPieces)};
+        if (int rc = encode_map(&ma.sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + L.xq_ts, d, st, b,
+                                CU_TENSOR_MAP_SWIZZLE_NONE))
+            return rc;
+    }
     BArgs ta{};
     ta.plan = plan;
     ta.K = L.H;
@@ -959,16 +967,12 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     ta.act_kind = p->activation;
     ta.beta = p->situ_beta;
     ta.lbeta = p->situ_linear_beta;
-    // the weights do not come from the previous launch (the scale gather), and the plan
-    // was complete before it started: request the first stages' weight tiles before
-    // waiting for it
-    ta.early_a = 1;
-    prof_begin(K3_PROF_TOPK, s);
-    int rc = launch_gather_sfb(plan, ws + L.xq_ts, L.H, int(L.U), ws + L.sfb_x, s);
-    prof_end(K3_PROF_TOPK, s);
-    if (rc) return rc;
+    // the gate/up launch follows the plan producer (router, prep or pairs plan) directly:
+    // it waits for it before copying the plan, and its producer loads each pair's piece
+    // scales as stored, from which the MMA warp writes the scale chunks (no gather launch)
+    ta.plan_in_prev = 1;
     prof_begin(K3_PROF_GATEUP, s);
-    rc = launch_bs_gateup(ma, ta, sms, s);
+    int rc = launch_bs_gateup_rawsfb(ma, ta, sms, s);
     prof_end(K3_PROF_GATEUP, s);
     if (rc) return rc;
 
@@ -1006,6 +1010,129 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     prof_begin(K3_PROF_OTHER, s);
     rc = launch_combine(plan, tb.y_pair, L.H, M, y, ydt, s);
     prof_end(K3_PROF_OTHER, s);
+    return rc;
+}
+
+// One expert's SwiGLU FFN for M <= 8 tokens (LatentMoE.expert_forward, moe.py:90-103):
+// three launches -- x pieces (launch_mv_prep), gate/up, down -- over the identity plan
+// (one item of M tokens, weight 1), which both block-scaled launches build themselves, so
+// neither waits for a plan and both request their first weight stages at once. The
+// expert's pools are addressed as one-slot pools at its slot; the down launch writes the
+// tokens' rows of y directly (the identity plan's pair t is token t), so no combine runs.
+struct FfnLayout {
+    int64_t U, keysA, keysB;
+    int CA, CB;
+    size_t status, xp, sfb, act_p, act_sf, partA, partB, cnt, total;
+};
+
+FfnLayout ffn_layout(const k3_moe_params& p, int64_t M, int sms) {
+    FfnLayout L{};
+    L.U = (M + kMaxTok - 1) / kMaxTok;
+    L.keysA = L.U * (p.inter / kBRows);
+    L.keysB = L.U * (p.hidden / kBRows);
+    L.CA = choose_split_bs(L.keysA, p.hidden, sms);
+    L.CB = choose_split_bs(L.keysB, p.inter, sms);
+    size_t off = 0;
+    L.status = carve(off, sizeof(int));
+    L.xp = carve(off, size_t(L.U) * kBMaxN * (p.hidden / 2));
+    L.sfb = carve(off, size_t(L.U) * (p.hidden / 128) * kBChunk);
+    L.act_p = carve(off, size_t(L.U) * kBMaxN * (p.inter / 2));
+    L.act_sf = carve(off, size_t(L.U) * (p.inter / 128) * kBChunk);
+    L.partA = carve(off, sizeof(float) * size_t(L.keysA) * L.CA * 2 * kMaxTok * kBRows);
+    L.partB = carve(off, sizeof(float) * size_t(L.keysB) * L.CB * kMaxTok * kBRows);
+    L.cnt = carve(off, sizeof(unsigned) * size_t(L.keysA + L.keysB));   // gate/up keys, then down keys
+    L.total = off;
+    return L;
+}
+
+int expert_ffn_bs(const k3_moe_params* p, const void* x, int xdt, int64_t M, int64_t e, void* y, int ydt,
+                  uint8_t* ws, const FfnLayout& L, cudaStream_t s) {
+    int rc = configure_smem();
+    if (rc) return rc;
+    const int sms = num_sms();
+    const k3_expert_pool& pl = *p->pool;
+    const int64_t H = p->hidden, I = p->inter;
+    const bool tiled = pl.w1_tiles && pl.w3_tiles && pl.w2_tiles;
+    const size_t sfA = size_t(I / 128) * (H / 128) * kBChunk;     // scale-chunk bytes of one slot
+    const size_t sfB = size_t(H / 128) * (I / 128) * kBChunk;
+    const size_t codes = size_t(I) * (H / 2);                      // code bytes of one slot
+    int* status = reinterpret_cast<int*>(ws + L.status);
+    unsigned* cnt = reinterpret_cast<unsigned*>(ws + L.cnt);
+    BMaps ma{};
+    if (tiled) {
+        if ((rc = tiles_map(&ma.a0, pl.w1_tiles + e * codes, I, H, 1))) return rc;
+        if ((rc = tiles_map(&ma.a1, pl.w3_tiles + e * codes, I, H, 1))) return rc;
+    } else {
+        if ((rc = packed_map(&ma.a0, pl.w1_packed + e * codes, I, H, 1))) return rc;
+        if ((rc = packed_map(&ma.a1, pl.w3_packed + e * codes, I, H, 1))) return rc;
+    }
+    {
+        const uint64_t d[2] = {uint64_t(H / 2), uint64_t(kBPieces * M)};
+        const uint64_t st[1] = {uint64_t(H / 2)};
+        const uint32_t b[2] = {128, uint32_t(kBPieces)};                // one token's pieces
+        if ((rc = encode_map(&ma.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, ws + L.xp, d, st, b,
+                             CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+    }
+    BMaps mb{};
+    if ((rc = tiled ? tiles_map(&mb.a0, pl.w2_tiles + e * codes, H, I, 1)
+                    : packed_map(&mb.a0, pl.w2_packed + e * codes, H, I, 1)))
+        return rc;
+    {
+        const uint64_t d[3] = {uint64_t(I / 2), uint64_t(kBMaxN), uint64_t(L.U)};
+        const uint64_t st[2] = {uint64_t(I / 2), uint64_t(kBMaxN) * uint64_t(I / 2)};
+        const uint32_t b[3] = {128, uint32_t(kBPieces), 1};
+        if ((rc = encode_map(&mb.b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, ws + L.act_p, d, st, b,
+                             CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+    }
+    prof_begin(K3_PROF_TOPK, s);
+    rc = launch_mv_prep(x, xdt, int(M), H, ws + L.xp, ws + L.sfb, cnt, int(L.keysA + L.keysB), status, s);
+    prof_end(K3_PROF_TOPK, s);
+    if (rc) return rc;
+
+    BArgs ta{};
+    ta.K = H;
+    ta.rows = I;
+    ta.C = L.CA;
+    ta.status = status;
+    ta.part = reinterpret_cast<float*>(ws + L.partA);
+    ta.cnt = cnt;
+    ta.maxseg = L.CA;
+    ta.sfa0 = pl.w1_scales_tc + e * sfA;
+    ta.sfa1 = pl.w3_scales_tc + e * sfA;
+    ta.tiled = tiled ? 1 : 0;
+    ta.sf_slot = int64_t(sfA);
+    ta.sfb = ws + L.sfb;
+    ta.act_p = ws + L.act_p;
+    ta.act_sf = ws + L.act_sf;
+    ta.act_kind = p->activation;
+    ta.beta = p->situ_beta;
+    ta.lbeta = p->situ_linear_beta;
+    ta.identity_m = int(M);
+    prof_begin(K3_PROF_GATEUP, s);
+    rc = launch_bs_gateup(ma, ta, sms, s);
+    prof_end(K3_PROF_GATEUP, s);
+    if (rc) return rc;
+
+    BArgs tb{};
+    tb.K = I;
+    tb.rows = H;
+    tb.C = L.CB;
+    tb.status = status;
+    tb.part = reinterpret_cast<float*>(ws + L.partB);
+    tb.cnt = cnt + L.keysA;
+    tb.maxseg = L.CB;
+    tb.sfa0 = pl.w2_scales_tc + e * sfB;
+    tb.tiled = tiled ? 1 : 0;
+    tb.sf_slot = int64_t(sfB);
+    tb.sfb = ws + L.act_sf;
+    tb.y_pair = static_cast<float*>(y);
+    tb.y_bf16 = ydt == K3_BF16 ? 1 : 0;
+    tb.identity_m = int(M);
+    prof_begin(K3_PROF_DOWN, s);
+    rc = launch_bs_down(mb, tb, sms, s);
+    prof_end(K3_PROF_DOWN, s);
     return rc;
 }
 
@@ -1400,6 +1527,31 @@ extern "C" K3_API int k3_moe_experts_decode(const k3_moe_params* p, const void* 
     return decode_impl(p, x, x_dtype, M, nullptr, nullptr, const_cast<int32_t*>(idx),
                        const_cast<float*>(w), y_out, y_dtype, static_cast<uint8_t*>(workspace), L,
                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" K3_API size_t k3_moe_expert_forward_workspace(const k3_moe_params* p, int64_t M) {
+    if (!p || M < 1 || M > kMaxTok || p->hidden <= 0 || p->inter <= 0) return 0;
+    return ffn_layout(*p, M, num_sms()).total;
+}
+
+extern "C" K3_API int k3_moe_expert_forward(const k3_moe_params* p, const void* x, int x_dtype, int64_t M,
+                                            int64_t expert, void* y_out, int y_dtype, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+    if (!p) return fail(K3_ERR_INVALID, "k3_moe_expert_forward: params is NULL");
+    if (M < 1 || M > kMaxTok) return fail(K3_ERR_UNSUPPORTED, "k3_moe_expert_forward takes 1..8 tokens, got M=" + std::to_string(M));
+    if (!x || !y_out) return fail(K3_ERR_INVALID, "k3_moe_expert_forward: NULL tensor");
+    if (x_dtype != K3_F32 && x_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_expert_forward: x must be f32 or bf16");
+    if (y_dtype != K3_F32 && y_dtype != K3_BF16) return fail(K3_ERR_INVALID, "k3_moe_expert_forward: y must be f32 or bf16");
+    if (p->activation != K3_ACT_SILU && p->activation != K3_ACT_SITU) return fail(K3_ERR_INVALID, "unknown activation");
+    if (p->hidden % 512 || p->inter % 512)
+        return fail(K3_ERR_UNSUPPORTED, "k3_moe_expert_forward: hidden and inter must be multiples of 512");
+    if (!pool_bs(*p)) return fail(K3_ERR_UNSUPPORTED, "k3_moe_expert_forward needs the block-scaled expert pool");
+    if (expert < 0 || expert >= p->pool->num_slots)
+        return fail(K3_ERR_INVALID, "k3_moe_expert_forward: expert " + std::to_string(expert) + " is not a pool slot");
+    const FfnLayout L = ffn_layout(*p, M, num_sms());
+    if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
+    return expert_ffn_bs(p, x, x_dtype, M, expert, y_out, y_dtype, static_cast<uint8_t*>(workspace), L,
+                         static_cast<cudaStream_t>(stream));
 }
 
 // ------------------------------------------------------------ pairs (expert parallel)

@@ -92,11 +92,20 @@ __global__ void __launch_bounds__(256) mv_prep_kernel(const void* __restrict__ x
 
 }  // namespace
 
+int launch_mv_prep(const void* x, int xdt, int M, int64_t K, uint8_t* xp, uint8_t* sfb, unsigned* cnt, int ncnt,
+                   int* status, cudaStream_t s) {
+    const int64_t tasks = int64_t(M) * (K / 32);
+    mv_prep_kernel<<<unsigned(1 + (tasks + 7) / 8), 256, 0, s>>>(x, xdt, M, K, xp, sfb, cnt, ncnt, status);
+    K3_CHECK_LAUNCH("mv_prep_kernel");
+    return K3_OK;
+}
+
 // Shapes the block-scaled projection takes: K a multiple of 512 (the scale boxes and
 // their 16-byte row stride), N a multiple of 128, 16-byte aligned matrices.
 bool matvec_bs_ok(int64_t K, int64_t N, const uint8_t* packed, const uint8_t* scales) {
     return K % 512 == 0 && N % kBRows == 0 && (reinterpret_cast<uintptr_t>(packed) & 15) == 0 &&
-           (reinterpret_cast<uintptr_t>(scales) & 15) == 0 && K / 2 <= (int64_t(1) << 31);
+           (reinterpret_cast<uintptr_t>(scales) & 15) == 0 && K / 2 <= (int64_t(1) << 31) &&
+           (N / kBRows) * (K / kBStageK) < 65536;     // the kernel's 32-bit item indices
 }
 
 size_t matvec_bs_workspace(int64_t M, int64_t K, int64_t N) {
@@ -136,13 +145,12 @@ int matvec_bs(const void* x, int xdt, int64_t M, int64_t K, const uint8_t* packe
                 return rc;
         }
         const int64_t keys = L.U * (N / kBRows);
-        const int64_t tasks = Mc * (K / 32);
         prof_begin(K3_PROF_TOPK, s);
-        mv_prep_kernel<<<unsigned(1 + (tasks + 7) / 8), 256, 0, s>>>(
-            static_cast<const uint8_t*>(x) + size_t(m0) * K * esz, xdt, int(Mc), K, ws + L.xp, ws + L.sfb,
-            reinterpret_cast<unsigned*>(ws + L.cnt), int(keys), reinterpret_cast<int*>(ws + L.status));
+        const int prc = launch_mv_prep(static_cast<const uint8_t*>(x) + size_t(m0) * K * esz, xdt, int(Mc), K,
+                                       ws + L.xp, ws + L.sfb, reinterpret_cast<unsigned*>(ws + L.cnt), int(keys),
+                                       reinterpret_cast<int*>(ws + L.status), s);
         prof_end(K3_PROF_TOPK, s);
-        K3_CHECK_LAUNCH("mv_prep_kernel");
+        if (prc) return prc;
         BArgs a{};
         a.plan = nullptr;
         a.K = K;

@@ -334,10 +334,28 @@ class LatentMoE:
         if h2.dtype not in (torch.float32, torch.bfloat16):
             h2 = h2.float()
         M = h2.shape[0]
+        if self._ffn_ok(M):
+            # the expert's FFN alone: no routing plan, three launches
+            lib = L.load_library()
+            h2 = h2.contiguous()
+            params = self._params(top_k=1, has_shared=0)
+            y = torch.empty((M, self.pool.hidden), dtype=torch.float32, device=h.device)
+            ws = L.workspace(h.device, lib.k3_moe_expert_forward_workspace(params, M))
+            L.check(lib.k3_moe_expert_forward(params, h2.data_ptr(), L.dtype_code(h2), M, int(e), y.data_ptr(),
+                                              L.K3_F32, ws.data_ptr(), ws.numel(), L.stream_of(h2)),
+                    "k3_moe_expert_forward")
+            return y.reshape(*h.shape[:-1], y.shape[-1])
         idx = torch.full((M, 1), int(e), dtype=torch.int32, device=h.device)
         w = torch.ones((M, 1), dtype=torch.float32, device=h.device)
         y = self._experts_decode(h2, idx, w, self._params(top_k=1, has_shared=0))
         return y.reshape(*h.shape[:-1], y.shape[-1])
+
+    def _ffn_ok(self, M: int) -> bool:
+        """True when ``expert_forward`` of M tokens runs ``k3_moe_expert_forward``: at most
+        8 tokens on the block-scaled pool, H and I multiples of 512."""
+        p = self.pool
+        return (M <= MAX_DECODE_TOKENS and self.use_pool and self.block_scaled and p.scales_tc is not None
+                and p.hidden % 512 == 0 and p.inter % 512 == 0)
 
     def _act_args(self):
         c = self.cfg

@@ -276,6 +276,36 @@ def test_full_size_decode_layer(k3, full_layer, M):
     assert O.rel_l2(host(yf), host(y)) < 1e-6
 
 
+@pytest.mark.parametrize("M,xdt", [(1, "bf16"), (8, "bf16"), (3, "f32")])
+def test_full_size_expert_forward(k3, full_layer, M, xdt):
+    """LatentMoE.expert_forward (moe.py:90-103) at BASELINE configs[1] width through the
+    three-launch k3_moe_expert_forward path, for a routed expert and the shared slot,
+    against the C oracle of the reference's fused kernel; and against the routed-decode
+    path (k3_moe_experts_decode with every token on that expert, weight 1)."""
+    from kimi_k3_mlx_macmini_b200 import synthetic
+    lay, moe = full_layer
+    assert moe._ffn_ok(M)
+    x = synthetic.tokens(3100 + M, M, 7168)
+    if xdt == "f32":
+        x = x.float() * 1.37
+    xf = O.bf16_bits_to_f32(x.view(torch.uint16).cpu().numpy()) if xdt == "bf16" else host(x)
+    for e in (5, synthetic.SHARED):
+        slot = lay.cfg.num_experts if e == synthetic.SHARED else e
+        y = host(moe.expert_forward(x, slot))
+        (p1, s1), (p3, s3), (p2, s2) = lay.expert(e)
+        h = lambda t: t.cpu().numpy()  # noqa: E731
+        want = O.matvec_fused(O.silu(O.matvec_fused(xf, h(p1), h(s1))) * O.matvec_fused(xf, h(p3), h(s3)),
+                              h(p2), h(s2))
+        assert y.shape == (M, 7168)
+        assert O.rel_l2(y, want) < NORTH_STAR_REL_L2
+        assert O.rel_l2(y, want) < EXPECTED_REL_L2
+        idx = torch.full((M, 1), slot, dtype=torch.int32, device="cuda")
+        w = torch.ones((M, 1), dtype=torch.float32, device="cuda")
+        params = moe._params(num_experts=lay.cfg.num_experts + 1, top_k=1, has_shared=0)   # shared slot too
+        routed = host(moe._experts_decode(x.contiguous(), idx, w, params))
+        assert O.rel_l2(y, routed) < 1e-6
+
+
 def test_full_size_decode_deterministic(k3, full_layer):
     from kimi_k3_mlx_macmini_b200 import synthetic
     _, moe = full_layer
