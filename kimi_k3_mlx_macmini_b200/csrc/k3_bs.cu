@@ -157,9 +157,9 @@ __global__ void __launch_bounds__(kBThreads, 1)
             s_plan.pair_w[q] = 1.0f;
         }
     } else {
-        // the plan was written two launches back (router / plan kernel, then the scale-chunk
-        // gather), which had completed when the previous launch started -- or by the
-        // previous launch itself (plan_in_prev): wait for it first
+        // gate/up (plan_in_prev): the previous launch (router, prep or pairs plan) writes
+        // the plan -- wait for it first. down: the plan is two launches old and was
+        // complete when the previous launch (gate/up) started.
         if (a.plan_in_prev) asm volatile("griddepcontrol.wait;\n" ::: "memory");
         for (int i = threadIdx.x; i < int(sizeof(Plan) / 4); i += blockDim.x)
             reinterpret_cast<int*>(&s_plan)[i] = reinterpret_cast<const int*>(a.plan)[i];
@@ -541,41 +541,6 @@ __global__ void __launch_bounds__(kBThreads, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tm, kCols);
-}
-
-// -------------------------------------------------------------- x scale gather
-
-// Scale chunks of each expert item's B operand: chunk c of item v holds, for its pair i
-// and piece p (row 8i + p), the E8M0 bytes of k-blocks 4c..4c+3 of token pair_tok's
-// piece row, gathered from the per-row scales xsf [8T][K/32]. One thread per 4-byte word.
-__global__ void gather_sfb_kernel(const Plan* __restrict__ plan, const uint8_t* __restrict__ xsf, int64_t K,
-                                  uint8_t* __restrict__ sfb) {
-    // launched as a programmatic dependent of the route launch: wait for its plan and scales,
-    // then let the gate/up launch start (it copies the plan before its own wait)
-    asm volatile("griddepcontrol.wait;\n" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    const int v = blockIdx.y;
-    if (v >= plan->n_active) return;
-    const int ps = plan->pair_start[v], np = plan->pair_start[v + 1] - ps;
-    const int64_t nc = K / 128, G = K / 32;
-    for (int64_t w = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; w < nc * np * kBPieces;
-         w += int64_t(gridDim.x) * blockDim.x) {
-        const int64_t c = w / (np * kBPieces);
-        const int r = int(w % (np * kBPieces));                 // row 8i + p of the chunk
-        const int t = plan->pair_tok[ps + r / kBPieces];
-        const uint32_t word =
-            __ldg(reinterpret_cast<const uint32_t*>(xsf + (int64_t(kBPieces) * t + r % kBPieces) * G + 4 * c));
-        *reinterpret_cast<uint32_t*>(sfb + (int64_t(v) * nc + c) * kBChunk + sf_chunk_offset(r, 0)) = word;
-    }
-}
-
-int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
-                      cudaStream_t s) {
-    const dim3 grid(unsigned((K / 128 * kBMaxN + 255) / 256), unsigned(max_items));
-    if (int rc = cuda_check(launch_pdl(gather_sfb_kernel, grid, dim3(256), 0, s, plan, xsf, K, sfb),
-                            "gather_sfb_kernel"))
-        return rc;
-    return K3_OK;
 }
 
 // ------------------------------------------------------------------- combine

@@ -95,8 +95,9 @@ struct BArgs {
     const uint8_t* sfa1;    // of pool a1 (gate/up)
     int tiled;              // a0/a1 are tile pools (4-D maps) rather than row-major pools
     int64_t sf_slot;        // bytes per slot of a scale-chunk pool
-    const uint8_t* sfb;     // B scale chunks per expert item [v][K/128][512] (gate/up: x
-                            // pieces gathered per pair; down: act pieces)
+    const uint8_t* sfb;     // B scale chunks per expert item [v][K/128][512] (gate/up
+                            // over the identity plan: x pieces, from launch_mv_prep; down:
+                            // act pieces); unused by the raw-scale gate/up (maps.sfb)
     // gate/up epilogue: act pieces of expert v's pair i, piece p at row v*64 + 8i + p of
     // act_p [.][I/2]; their scale chunks act_sf [v][I/128][512]
     uint8_t* act_p;
@@ -113,7 +114,7 @@ struct BArgs {
     // request the first stages' weights before waiting for the previous launch (the weights
     // and the plan never come from it): set for the down phase, whose CTAs start on the SMs
     // that the gate/up launch's early finishers leave. (Measured slower for the gate/up
-    // phase when its previous launch was the short scale gather.)
+    // phase when a short scale-gather launch preceded it.)
     int early_a;
     // the previous launch writes the plan (the gate/up launch with raw piece scales follows
     // the plan producer directly): every thread waits for it before copying the plan
@@ -133,9 +134,6 @@ int launch_bs_proj_rawsf(const BMaps& maps, const BArgs& a, int grid, cudaStream
 // launch a projection with identity_m = M depends on).
 int launch_mv_prep(const void* x, int xdt, int M, int64_t K, uint8_t* xp, uint8_t* sfb, unsigned* cnt, int ncnt,
                    int* status, cudaStream_t s);
-// Per-item B scale chunks of the gate/up phase from the per-row x piece scales.
-int launch_gather_sfb(const Plan* plan, const uint8_t* xsf, int64_t K, int max_items, uint8_t* sfb,
-                      cudaStream_t s);
 // y[t] = sum over the pairs of token t, in plan order, of y_pair[pair] (weights are
 // already applied); y [M][H] f32 or bf16.
 int launch_combine(const Plan* plan, const float* y_pair, int64_t H, int M, void* y, int y_dtype,

@@ -208,10 +208,10 @@ __global__ void __launch_bounds__(256) prep_kernel(PrepArgs a) {
     if (blockIdx.x > 0) {
         if (a.xp) {                        // one warp per (token, 32-block): the piece split is a
                                            // serial chain, so it is spread over many CTAs
-            const int64_t G = a.K / 32;
-            const int64_t task = int64_t(blockIdx.x - 1) * (blockDim.x >> 5) + warp;
-            if (task < int64_t(a.M) * G) {
-                const int64_t t = task / G, g = task % G;
+            const uint32_t G = uint32_t(a.K / 32);            // 32-bit: no 64-bit division per warp
+            const uint32_t task = (blockIdx.x - 1) * (blockDim.x >> 5) + warp;
+            if (task < uint32_t(a.M) * G) {
+                const int64_t t = task / G, g = task - uint32_t(t) * G;
                 const float v = load_as_f32(a.x, a.x_dtype, t * a.K + 32 * g + lane);
                 split_pieces(v, lane, a.xp + int64_t(kBPieces) * t * (a.K / 2) + 16 * g, a.K / 2,
                              a.xsf + int64_t(kBPieces) * t * G + g, G);
@@ -692,7 +692,6 @@ DecodeLayout decode_layout(const k3_moe_params& p, int64_t M, int sms, int64_t H
         L.route_w = carve(off, sizeof(float) * M * p.top_k);
         L.xq_hi = carve(off, size_t(kBMaxN) * (L.H / 2));              // x pieces
         L.xq_ts = carve(off, size_t(kBMaxN) * (L.H / 32));              // their per-row scales
-        L.sfb_x = carve(off, size_t(L.U) * (L.H / 128) * kBChunk);      // per-item B scale chunks
         L.KQ = 1;
         for (int64_t c = 1; c <= H_router / 512 && c <= 16; ++c) {  // router k-slices: >= one CTA per SM
             if ((H_router / 512) % c) continue;
@@ -961,7 +960,6 @@ int decode_bs(const k3_moe_params* p, const DecodeLayout& L, uint8_t* ws, int M,
     ta.sfa1 = pl.w3_scales_tc;
     ta.tiled = tiled ? 1 : 0;
     ta.sf_slot = (L.I / 128) * (L.H / 128) * kBChunk;
-    ta.sfb = ws + L.sfb_x;
     ta.act_p = act_p;
     ta.act_sf = act_sf;
     ta.act_kind = p->activation;
@@ -1469,10 +1467,8 @@ extern "C" K3_API int k3_moe_decode(const k3_moe_params* p, const void* x, int x
     if (int rc = check_ws(workspace, workspace_bytes, L.total)) return rc;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    float* logits = reinterpret_cast<float*>(ws + L.logits);
     int32_t* idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + L.route_idx);
     float* w = weight_out ? weight_out : reinterpret_cast<float*>(ws + L.route_w);
-    (void)logits;
     return decode_impl(p, x, x_dtype, M, gate_w_bf16, bias, idx, w, y_out, y_dtype, ws, L, s);
 }
 
@@ -1597,7 +1593,6 @@ DecodeLayout pairs_layout(const k3_moe_params& p, int64_t T, int64_t n_in, int s
     L.plan = carve(off, sizeof(Plan));
     L.xq_hi = carve(off, size_t(kBPieces) * T * (L.H / 2));
     L.xq_ts = carve(off, size_t(kBPieces) * T * (L.H / 32));
-    L.sfb_x = carve(off, size_t(L.U) * (L.H / 128) * kBChunk);
     L.act_hi = carve(off, size_t(L.U) * kBMaxN * (L.I / 2));
     L.act_ts = carve(off, size_t(L.U) * (L.I / 128) * kBChunk);
     L.partA = carve(off, sizeof(float) * L.U * (L.I / kBRows) * L.CA * 2 * kMaxTok * kBRows);

@@ -65,7 +65,7 @@ struct DecodeLayout {
     bool bs;                       // ... on the block-scaled (kind::mxf4) tensor-core path
     int64_t ppad, tspad;           // column strides of the blocked activation buffers
     int KQ;                        // router k-slices (fused router)
-    size_t y_pair, sfb_x;          // block-scaled path: pair outputs, gate/up B scale chunks
+    size_t y_pair;                 // block-scaled path: one output row per pair
     size_t plan, logits, logit_part, route_done, route_idx, route_w, xq_hi, xq_lo, xq_ts, act_hi, act_lo, act_ts, partA, cntA, partB,
         cntB, total;
     size_t route_keys, route_scores;   // fused router: top-k keys and sigmoid scores [M][E]

@@ -79,10 +79,10 @@ __global__ void __launch_bounds__(256) mv_prep_kernel(const void* __restrict__ x
         for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0u;
         return;
     }
-    const int64_t G = K / 32;
-    const int64_t task = int64_t(blockIdx.x - 1) * (blockDim.x >> 5) + warp;
-    if (task >= int64_t(M) * G) return;
-    const int64_t t = task / G, g = task % G;
+    const uint32_t G = uint32_t(K / 32);                  // 32-bit: no 64-bit division per warp
+    const uint32_t task = (blockIdx.x - 1) * (blockDim.x >> 5) + warp;
+    if (task >= uint32_t(M) * G) return;
+    const int64_t t = task / G, g = task - uint32_t(t) * G;
     const float v = load_as_f32(x, x_dtype, t * K + 32 * g + lane);
     // piece p of token t: row 8t + p of the pieces (pair t % 8 of item t / 8); its scale
     // at row 8 (t % 8) + p, k-block g % 4 of chunk g / 4 of the item (16 bytes per piece)

@@ -207,9 +207,9 @@ int launch_plan_from_pairs(const PairsArgs& a, const ConvertArgs& conv, cudaStre
 __device__ void convert_tokens_body(const void* x, int x_dtype, int64_t T, int64_t K, uint8_t* xp, uint8_t* xsf,
                                     int64_t first_warp, int64_t n_warps) {
     const int lane = threadIdx.x & 31;
-    const int64_t G = K / 32;
-    for (int64_t task = first_warp + (threadIdx.x >> 5); task < T * G; task += n_warps) {
-        const int64_t t = task / G, g = task % G;
+    const uint32_t G = uint32_t(K / 32);                  // 32-bit: no 64-bit division per task
+    for (uint32_t task = uint32_t(first_warp) + (threadIdx.x >> 5); task < uint32_t(T) * G; task += uint32_t(n_warps)) {
+        const int64_t t = task / G, g = task - uint32_t(t) * G;
         const float v = load_as_f32(x, x_dtype, t * K + 32 * g + lane);
         split_pieces(v, lane, xp + kBPieces * t * (K / 2) + 16 * g, K / 2, xsf + kBPieces * t * G + g, G);
     }

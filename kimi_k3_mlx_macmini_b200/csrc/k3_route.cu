@@ -36,8 +36,9 @@ template <bool XF32>
 __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
     __shared__ float red[8][16][kMaxTok];
     __shared__ int s_last;
-    // the next launch (the scale gather, a programmatic dependent that waits for this grid
-    // before reading anything) may be scheduled as soon as every CTA here is resident
+    // the next launch (gate/up, a programmatic dependent that waits for this grid before
+    // reading the plan) may be scheduled as soon as every CTA here is resident: its CTAs
+    // set up on the SMs this grid's early finishers leave
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
@@ -95,21 +96,27 @@ __global__ void __launch_bounds__(256) route_fused_kernel(RouteArgs a) {
             const void* xe = a.xe ? a.xe : a.x;
             const int xedt = a.xe ? a.xe_dtype : a.x_dtype;
             const int64_t He = a.xe ? a.He : a.H;
-            const int64_t ng = He / 32;
-            const int64_t ntask = a.M * ng;
+            const uint32_t ng = uint32_t(He / 32);
+            const uint32_t ntask = uint32_t(a.M) * ng;
             unsigned* claim = a.done + 1 + gridDim.x;
             for (;;) {
                 unsigned t0 = 0;
                 if (lane == 0) t0 = atomicAdd(claim, 4u);
                 t0 = __shfl_sync(0xffffffffu, t0, 0);
-                if (int64_t(t0) >= ntask) break;
-                for (int64_t task = t0; task < int64_t(t0) + 4 && task < ntask; ++task) {
-                    const int t = int(task / ng);
-                    const int64_t g = task % ng;
-                    const float v = load_as_f32(xe, xedt, int64_t(t) * He + 32 * g + lane);
-                    split_pieces(v, lane, a.xp + int64_t(kBPieces * t) * (He / 2) + 16 * g, He / 2,
-                                 a.xsf + int64_t(kBPieces * t) * ng + g, ng);
+                if (t0 >= ntask) break;
+                // the four claimed (token, 32-block) tasks split as four interleaved chains
+                float v[4];
+                uint8_t* d[4];
+                uint8_t* sf[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const uint32_t task = min(t0 + uint32_t(h), ntask - 1u);
+                    const uint32_t t = task / ng, g = task - t * ng;
+                    v[h] = load_as_f32(xe, xedt, int64_t(t) * He + 32 * int64_t(g) + lane);
+                    d[h] = a.xp + int64_t(kBPieces * t) * (He / 2) + 16 * int64_t(g);
+                    sf[h] = t0 + uint32_t(h) < ntask ? a.xsf + int64_t(kBPieces * t) * ng + g : nullptr;
                 }
+                split_pieces_n<4>(v, lane, d, He / 2, sf, int64_t(ng));
             }
         } else {
             // ---- x -> f16 pieces: the CTAs of the first row blocks split the slice's 512-blocks
