@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
             }
             if (GATEUP) {
                 // activation x routing weight per pair, split into the down kernel's pieces,
-                // four pairs interleaved
+                // up to four pairs interleaved
                 const int64_t rowb = a.rows / 2;                            // bytes per act row (I/2)
                 uint8_t* sfc = a.act_sf + (int64_t(v) * (a.rows / 128) + rb) * kBChunk;
 #pragma unroll 1
@@ -515,7 +515,16 @@ __global__ void __launch_bounds__(kBThreads, 1)
                         d[h] = a.act_p + (int64_t(v) * kBMaxN + kBPieces * pi) * rowb + (int64_t(rb) * kBRows + 32 * q) / 2;
                         sf[h] = pi < np ? sfc + sf_chunk_offset(kBPieces * pi, q) : nullptr;
                     }
-                    split_pieces_n<4>(xv, lane, d, rowb, sf, 16);
+                    // a single pair (every routed expert at M = 1): one chain, not four
+                    // with three idle (the last item's split is the launch's tail)
+                    if (np - p0 == 1) {
+                        const float x1[1] = {xv[0]};
+                        uint8_t* const d1[1] = {d[0]};
+                        uint8_t* const s1[1] = {sf[0]};
+                        split_pieces_n<1>(x1, lane, d1, rowb, s1, 16);
+                    } else {
+                        split_pieces_n<4>(xv, lane, d, rowb, sf, 16);
+                    }
                 }
             } else {
                 // one output row per pair (the combine kernel sums a token's pairs)
