@@ -500,16 +500,16 @@ def run_stream(args, rank, world, local):
 
 # ------------------------------------------------------------------ B200 arm
 
-def traffic_from_profiles():
-    """(DRAM bytes, algorithmic bytes) of one full-size gate/up launch from the committed
-    ncu summary (dram__bytes_read.sum + dram__bytes_write.sum)."""
+def traffic_ratio_from_profiles():
+    """DRAM bytes / algorithmic bytes of a gate/up launch, from the committed ncu summary
+    of the small case (dram__bytes_read.sum + dram__bytes_write.sum of a 32-expert launch);
+    the full launch's traffic is this ratio x its algorithmic bytes (every weight byte is
+    read once, so the traffic grows with the bytes streamed)."""
     f = ROOT / "profiles" / "bs_gemv_gateup_config2.md"
     if not f.exists():
-        return None, None
-    txt = f.read_text()
-    m = re.search(r"traffic_bytes_per_launch_full:\s*([0-9.eE+]+)", txt)
-    a = re.search(r"traffic_launch_algorithmic_bytes:\s*([0-9.eE+]+)", txt)
-    return (float(m.group(1)) if m else None), (float(a.group(1)) if a else None)
+        return None
+    m = re.search(r"traffic_ratio_small_case:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
 
 
 def ep_check(moe, full, x, world):
@@ -695,8 +695,11 @@ def run_b200(args, rank, world, local):
         "layer_hbm_gbs": layer_bytes / (ms / 1e3) / 1e9,
         "roofline": {"bound": "hbm", "kernel": "bs_gemv_kernel<gate/up> (block-scaled grouped MXFP4 matvec, tcgen05)",
                      "achieved": gu_gbs, "peak": peak, "unit": "GB/s", "frac": gu_gbs / peak,
-                     "peak_kind": peak_kind, "traffic": traffic_from_profiles()[0],
-                     "traffic_launch_algorithmic_bytes": traffic_from_profiles()[1],
+                     "peak_kind": peak_kind,
+                     "traffic": (None if traffic_ratio_from_profiles() is None
+                                 else traffic_ratio_from_profiles() * gu_bytes),
+                     "traffic_source": "ncu dram bytes / algorithmic bytes of a 32-expert launch "
+                                       "(profiles/bs_gemv_gateup_config2.md) x this launch's algorithmic bytes",
                      "algorithmic_bytes_per_launch": gu_bytes,
                      "launch_ms": gu_ms / gu_n},
         "down_kernel": {"achieved": dn_gbs, "frac": dn_gbs / peak, "launch_ms": dn_ms / dn_n},
