@@ -76,6 +76,9 @@ def parse():
                          "decode; 5 = Kimi-K3 layer decode (supplementary)")
     ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "gather", "a2a"],
+                    help="N > 1: the expert-parallel token exchange (auto = gather: all_gather + "
+                         "reduce_scatter; a2a: the counted all_to_all)")
     args = ap.parse_args()
     if args.tokens is None:
         args.tokens = {1: 8, 2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
@@ -599,7 +602,7 @@ def run_b200(args, rank, world, local):
         # expert parallel: this rank holds experts [rank*E/W, (rank+1)*E/W) + the shared one
         from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
         moe = ExpertParallelMoE(lay.cfg, 0, {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias},
-                                lay.source)
+                                lay.source, exchange=args.exchange)
         _NCCL_GRAPHS.append(moe)
     else:
         moe = router
@@ -684,7 +687,8 @@ def run_b200(args, rank, world, local):
                    "tokens_per_gpu": M,
                    "parallelism": "single GPU" if world == 1 else
                                   f"ep{world}: {args.experts // world} routed experts per rank + replicated shared, "
-                                  "all_gather dispatch, reduce_scatter combine (NCCL)",
+                                  + ("counted all_to_all dispatch and combine (NCCL)" if moe.uses_a2a(M) else
+                                     "all_gather dispatch, reduce_scatter combine (NCCL)"),
                    "l2": f"inputs larger than L2: {9.0 / world:.2f} GB of expert weights per GPU, "
                          "a different token batch every step",
                    "timing": timing + ", events around K steps",
@@ -708,7 +712,8 @@ def run_b200(args, rank, world, local):
                 "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
                 "ms_per_step": e2e_ms,
                 "api": ("LatentMoE.__call__ (k3_moe_decode)" if world == 1 else
-                        "ExpertParallelMoE.__call__ (captured step replayed per call)"),
+                        "ExpertParallelMoE.__call__ (counted all-to-all step, launched per call)"
+                        if moe.uses_a2a(M) else "ExpertParallelMoE.__call__ (captured step replayed per call)"),
                 "copies": "one copy stream, two buffers each way: the next upload ahead of this download, both overlapping the neighbouring steps"},
         "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,
@@ -747,6 +752,10 @@ def step_modes(moe, xs, R, world):
         api = ("public API calls (the layer replays its captured step)" if getattr(moe, "graphs", False)
                else "eager launches")
         modes.append((f"{api} ({R} distinct batches as a ring)", [(lambda x=x: moe(x)) for x in xs]))
+        if not moe.capturable(xs[0].shape[0]):
+            modes[0] = ("eager launches: the counted all-to-all step reads its split sizes on the host "
+                        f"({R} distinct batches as a ring)", modes[0][1])
+            return graphs, modes
         xin = xs[0].clone()
         try:
             g = torch.cuda.CUDAGraph()
@@ -800,8 +809,8 @@ def time_modes(modes, steps, K, W, R, world, local):
 def run_prefill(args, rank, world, local):
     """one MoE layer at prefill, T = 4096 tokens per GPU (x bf16,
     top-8 of 384 + shared), the whole layer in one library call (router GEMM, grouped
-    block-scaled GEMMs); at N > 1 the experts are sharded (all_gather dispatch,
-    reduce_scatter combine)."""
+    block-scaled GEMMs); at N > 1 the experts are sharded (all_gather dispatch and
+    reduce_scatter combine, or with --exchange a2a the counted all-to-all)."""
     import torch
     from kimi_k3_mlx_macmini_b200 import _lib as L
     from kimi_k3_mlx_macmini_b200 import synthetic
@@ -814,7 +823,7 @@ def run_prefill(args, rank, world, local):
     if world > 1:
         from kimi_k3_mlx_macmini_b200.ep import ExpertParallelMoE
         moe = ExpertParallelMoE(lay.cfg, 0, {"gate.weight": lay.gate, "gate.e_score_correction_bias": lay.bias},
-                                lay.source)
+                                lay.source, exchange=args.exchange)
         _NCCL_GRAPHS.append(moe)
     else:
         moe = lay.moe()
@@ -880,7 +889,8 @@ def run_prefill(args, rank, world, local):
                    "tokens_per_gpu": T,
                    "parallelism": "single GPU" if world == 1 else
                                   f"ep{world}: {E_loc} routed experts per rank + replicated shared, "
-                                  "all_gather dispatch, reduce_scatter combine (NCCL)",
+                                  + ("counted all_to_all dispatch and combine (NCCL)" if moe.uses_a2a(T) else
+                                     "all_gather dispatch, reduce_scatter combine (NCCL)"),
                    "l2": f"inputs larger than L2: {w_bytes / 1e9:.2f} GB of expert weights per GPU and "
                          f"{R} token batches of {T * H * 2 / 1e6:.0f} MB",
                    "timing": timing + ", events around K steps",
@@ -905,7 +915,8 @@ def run_prefill(args, rank, world, local):
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
                 "ms_per_step": e2e_ms,
                 "api": ("LatentMoE.__call__ (k3_moe_prefill)" if world == 1 else
-                        "ExpertParallelMoE.__call__ (captured step replayed per call)"),
+                        "ExpertParallelMoE.__call__ (counted all-to-all step, launched per call)"
+                        if moe.uses_a2a(T) else "ExpertParallelMoE.__call__ (captured step replayed per call)"),
                 "copies": "one copy stream, two buffers each way: the next upload ahead of this download, both overlapping the neighbouring steps"},
         "gpu_launches": int(round(sum(c for _, c in prof.values()) / n_prof * K)),
         "clocks": clocks,

@@ -312,6 +312,37 @@ K3_API int k3_moe_ep_local(const k3_moe_params* p, const void* x, int x_dtype, i
                            int32_t shared_t0, int32_t shared_n, void* y_out, int y_dtype,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* Counted all-to-all token exchange of an expert-parallel step (prefill sizes). The
+ * reference runs every routed expert in one process (air_llm/models/kimi_k3/moe.py:119-127:
+ * per-expert gather of its tokens, weighted scatter-add of the outputs); these three calls
+ * split that loop over ranks, rank d owning experts [d*experts_per_rank, (d+1)*experts_per_rank).
+ *
+ * k3_ep_a2a_plan: from this rank's routing idx [M][route_stride] (top_k ids per row), the
+ * send plan: token t goes once to every rank owning one of its experts and always to its
+ * own rank. send_counts[W] / send_offs[W] (int64: the collective's split sizes and their
+ * exclusive prefix), send_rows[offs[d] + i] = the i-th token for rank d (ascending), and
+ * tok_slot[t][W] = t's row in the send buffer for rank d, or -1. send_rows needs M*W
+ * entries. *status (device int) becomes K3_ERR_INVALID for an expert id outside
+ * [0, experts_per_rank * world) (the id is skipped). */
+K3_API int k3_ep_a2a_plan(const int32_t* idx, int64_t route_stride, int64_t M, int top_k,
+                          int experts_per_rank, int world, int rank, int64_t* send_counts,
+                          int64_t* send_offs, int32_t* send_rows, int32_t* tok_slot, int32_t* status,
+                          void* stream);
+/* dst[i] = src[rows[i]] for n rows of row_bytes bytes (a multiple of 4; src and dst 4-byte
+ * aligned): packs the send buffer (tokens and their routing rows). *status becomes
+ * K3_ERR_INVALID for a row index outside [0, n_src). */
+K3_API int k3_ep_gather_rows(const void* src, int64_t n_src, int64_t row_bytes, const int32_t* rows,
+                             int64_t n, void* dst, int32_t* status, void* stream);
+/* y_out[t] = base[t] + the sum over d = 0..world-1 of (d == rank and own given ? own[t] :
+ * part[tok_slot[t][d]]) (rows with -1 skipped), in that order, in fp32: a token's shared
+ * expert output (base), its own rank's partial row (own: the rank's own token rows, which
+ * need not travel) and the partial rows the reverse all-to-all returned (part, in the send
+ * buffer's layout). base and own are optional [M][H] (NULL: absent); part [n_part][H]
+ * fp32; all 16-byte aligned, H % 4 == 0, y f32/bf16. */
+K3_API int k3_ep_a2a_combine(const float* base, const float* own, int rank, const float* part,
+                             int64_t n_part, const int32_t* tok_slot, int64_t M, int world, int64_t H,
+                             void* y_out, int y_dtype, int32_t* status, void* stream);
+
 /* Latent MoE decode (Kimi-K3, air_llm/models/kimi_k3/moe.py:110-127): the router reads
  * x_router [M][H_router] (the hidden state), the routed experts read x_expert [M][hidden]
  * (the latent state, p->hidden wide); y_out [M][hidden] = the weighted sum of the routed

@@ -106,6 +106,9 @@ SIGNATURES = {
     "k3_dense_gemm": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i32, _vp, _sz, _vp]),
     "k3_moe_ep_local": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                _vp, _i32, _vp, _sz, _vp]),
+    "k3_ep_a2a_plan": (_i32, [_vp, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "k3_ep_gather_rows": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "k3_ep_a2a_combine": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i64, _i32, _i64, _vp, _i32, _vp, _vp]),
 }
 
 _lib = None

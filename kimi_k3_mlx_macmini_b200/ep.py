@@ -14,12 +14,36 @@ shared expert; the router is replicated. Every rank brings M tokens. A step:
    gathered token (zero for tokens that touch none of its experts);
 4. combine: ``reduce_scatter`` (sum) returns to each rank the total of its own M rows.
 
-At prefill (thousands of tokens per rank) the same steps run with the local expert
-computation on the grouped-GEMM kernels (``k3_moe_pairs_prefill``).
-
-All transfers have fixed sizes, so a step captures into one CUDA graph with its NCCL
-collectives. Compared with W replicas of the whole layer, each rank streams only the
+At decode all transfers have fixed sizes, so a step captures into one CUDA graph with its
+NCCL collectives. Compared with W replicas of the whole layer, each rank streams only the
 experts its share is routed to by all W*M tokens, once.
+
+The counted all-to-all exchange (``exchange="a2a"``) sends a token once to each rank
+that owns one of its experts (and to its own rank, for the shared expert), not to every
+rank, and returns only the partial rows of those tokens:
+
+1. route, then ``k3_ep_a2a_plan`` builds the send plan on the device (rows per
+   destination, tokens ascending; each token's row per destination);
+2. the row counts go through one ``all_to_all_single`` and to the host (the split sizes
+   of the next collectives: one host synchronisation per step, so the step is launched
+   eagerly); meanwhile the shared expert runs over the own tokens;
+3. ``k3_ep_gather_rows`` packs the tokens and routing rows bound for other ranks; two
+   ``all_to_all`` deliver them (the own tokens go straight from the input), so the
+   receive buffer is [rows from rank 0][rows from rank 1]..., the own segment holding all
+   own tokens in order;
+4. ``k3_moe_ep_local`` runs this rank's routed experts over the received rows;
+5. the reverse ``all_to_all`` returns each partial row to its token's rank (the own rows
+   stay), and ``k3_ep_a2a_combine`` sums a token's shared-expert row and its rows in
+   ascending rank order.
+
+With top-8 of 384 experts over 8 ranks a token reaches ~4.6 other ranks instead of 7, so
+the exchange moves ~0.66 of the gather's token bytes and of the reduce-scatter's fp32
+bytes. Measured at prefill (T = 4096 per GPU, BASELINE layer) it is not faster on B200
+over NVSwitch: 4.36 against 4.09 ms per step at N = 2 and 6.09 against 5.99 ms at N = 8
+(the packing, the ordered combine, a second GEMM launch set for the shared expert and
+the host synchronisation cost about what the smaller transfers save). ``exchange="auto"``
+(the default) therefore runs the gather step at every size; ``"a2a"`` selects the
+all-to-all.
 
 The reference has no multi-device path (``air_llm/models/kimi_k3/moe.py:110-132`` runs
 every expert of one process); the per-token result equals its ``LatentMoE.__call__`` up
@@ -34,7 +58,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib as L
-from .moe import SHARED, ExpertPool, LatentMoE
+from .moe import MAX_DECODE_TOKENS, SHARED, ExpertPool, LatentMoE
 
 PAIRS_DECODE_MAX = 1024      # candidates one k3_moe_pairs_decode call takes
 
@@ -47,11 +71,14 @@ def _is_nccl(group) -> bool:
 
 
 def pair_candidates(idx_all: torch.Tensor, w_all: torch.Tensor, rank: int, world: int,
-                    num_experts: int, with_shared: bool, M: int):
-    """(slot, token row, weight) candidates of rank ``rank``: every routed pair of the W*M
-    gathered tokens, with slot = expert - first local expert when the expert is local and
-    -1 otherwise, then the shared expert (slot E/W) for this rank's own M tokens."""
+                    num_experts: int, with_shared: bool, M: int, own_t0: Optional[int] = None):
+    """(slot, token row, weight) candidates of rank ``rank``: every routed pair of the
+    gathered (or received) token rows, with slot = expert - first local expert when the
+    expert is local and -1 otherwise, then the shared expert (slot E/W) for this rank's own
+    M token rows, which start at row ``own_t0`` (default rank * M: the gathered layout)."""
     E_loc = num_experts // world
+    if own_t0 is None:
+        own_t0 = rank * M
     lo = rank * E_loc
     k = idx_all.shape[1]
     T = idx_all.shape[0]
@@ -61,24 +88,129 @@ def pair_candidates(idx_all: torch.Tensor, w_all: torch.Tensor, rank: int, world
     tok = torch.arange(T, device=dev, dtype=torch.int32).repeat_interleave(k)
     w = w_all.reshape(-1).to(torch.float32)
     if with_shared:
-        own = torch.arange(rank * M, rank * M + M, device=dev, dtype=torch.int32)
+        own = torch.arange(own_t0, own_t0 + M, device=dev, dtype=torch.int32)
         slot = torch.cat([slot, torch.full((M,), E_loc, device=dev, dtype=torch.int32)])
         tok = torch.cat([tok, own])
         w = torch.cat([w, torch.ones(M, device=dev, dtype=torch.float32)])
     return slot.contiguous(), tok.contiguous(), w.contiguous()
 
 
+def a2a_plan(idx: torch.Tensor, rank: int, world: int, experts_per_rank: int):
+    """The send plan of the counted all-to-all (what ``k3_ep_a2a_plan`` computes on the
+    device), from this rank's routing idx [M, k]: per destination d the rows of the tokens
+    that have an expert on rank d, or that are this rank's own (d == rank), ascending.
+    Returns (counts: list of W ints, rows: int32 [sum(counts)] destination-major,
+    tok_slot: int32 [M, W], the send row of (t, d) or -1)."""
+    M = idx.shape[0]
+    dev = idx.device
+    ids = idx.long()
+    valid = (ids >= 0) & (ids < experts_per_rank * world)
+    dest = torch.where(valid, ids // experts_per_rank, torch.full_like(ids, rank))   # invalid ids: skipped
+    mask = torch.zeros((M, world), dtype=torch.bool, device=dev)
+    mask.scatter_(1, dest, True)
+    mask[:, rank] = True
+    counts = mask.sum(0).tolist()
+    dt = mask.t().nonzero()                                   # (d, t), d-major, t ascending
+    rows = dt[:, 1].to(torch.int32).contiguous()
+    tok_slot = torch.full((M, world), -1, dtype=torch.int32, device=dev)
+    tok_slot[dt[:, 1], dt[:, 0]] = torch.arange(dt.shape[0], dtype=torch.int32, device=dev)
+    return counts, rows, tok_slot
+
+
+def a2a_plan_dev(routing: torch.Tensor, k: int, experts_per_rank: int, world: int, rank: int):
+    """``k3_ep_a2a_plan`` on this rank's routing rows (device, int32 [M, >= k], expert ids
+    first). Returns (meta int64 [2W]: send counts then their exclusive prefix, rows int32
+    [M*W]: the send rows' tokens, destination-major, tok_slot int32 [M, W], status int32
+    [4]: the status words of the plan, the two packings and the combine)."""
+    lib = L.load_library()
+    M = routing.shape[0]
+    dev = routing.device
+    meta = torch.empty(2 * world, dtype=torch.int64, device=dev)
+    rows = torch.empty(M * world, dtype=torch.int32, device=dev)
+    tok_slot = torch.empty((M, world), dtype=torch.int32, device=dev)
+    status = torch.zeros(4, dtype=torch.int32, device=dev)
+    L.check(lib.k3_ep_a2a_plan(routing.data_ptr(), routing.stride(0), M, k, experts_per_rank, world, rank,
+                               meta.data_ptr(), meta[world:].data_ptr(), rows.data_ptr(), tok_slot.data_ptr(),
+                               status.data_ptr(), L.stream_of(routing)), "k3_ep_a2a_plan")
+    return meta, rows, tok_slot, status
+
+
+def gather_rows_dev(src: torch.Tensor, rows: torch.Tensor, n: int, status: torch.Tensor,
+                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``k3_ep_gather_rows``: src[rows[:n]] for a row-major device tensor src, into
+    ``out`` (contiguous, n rows) when given; a bad row index sets status[0] (a device
+    word)."""
+    lib = L.load_library()
+    dst = torch.empty((n,) + tuple(src.shape[1:]), dtype=src.dtype, device=src.device) if out is None else out
+    row_bytes = src[0].numel() * src.element_size()
+    L.check(lib.k3_ep_gather_rows(src.data_ptr(), src.shape[0], row_bytes, rows.data_ptr(), n, dst.data_ptr(),
+                                  status.data_ptr(), L.stream_of(src)), "k3_ep_gather_rows")
+    return dst
+
+
+def a2a_combine_dev(part: torch.Tensor, tok_slot: torch.Tensor, status: torch.Tensor,
+                    dtype: torch.dtype = torch.float32, base: Optional[torch.Tensor] = None,
+                    own: Optional[torch.Tensor] = None, rank: int = 0) -> torch.Tensor:
+    """``k3_ep_a2a_combine``: y[t] = base[t] + sum over d ascending of (own[t] when d ==
+    rank and own is given, else part[tok_slot[t, d]]), fp32 rows [., H]; a bad slot sets
+    status[0]."""
+    lib = L.load_library()
+    M, W = tok_slot.shape
+    H = part.shape[1]
+    y = torch.empty((M, H), dtype=dtype, device=part.device)
+    L.check(lib.k3_ep_a2a_combine(None if base is None else base.data_ptr(), None if own is None else own.data_ptr(),
+                                  rank, part.data_ptr(), part.shape[0], tok_slot.data_ptr(), M, W, H, y.data_ptr(),
+                                  L.dtype_code(y), status.data_ptr(), L.stream_of(part)), "k3_ep_a2a_combine")
+    return y
+
+
+def _ep_forward_a2a(x, idx, w, local_fn, group, num_experts, with_shared):
+    """The counted all-to-all step on any backend (torch ops for the plan, packing and
+    combine; ``ExpertParallelMoE`` runs the same data flow on its CUDA kernels)."""
+    W = dist.get_world_size(group)
+    r = dist.get_rank(group)
+    M, H = x.shape
+    k = idx.shape[1]
+    E_loc = num_experts // W
+    counts, rows, tok_slot = a2a_plan(idx, r, W, E_loc)
+    cnt = torch.tensor(counts, dtype=torch.int64)
+    rcnt = torch.empty_like(cnt)
+    dist.all_to_all_single(rcnt, cnt, group=group)
+    recv = rcnt.tolist()
+    routing = torch.cat([idx, w.view(torch.int32)], dim=1)
+    x_recv = torch.empty((sum(recv), H), dtype=x.dtype)
+    r_recv = torch.empty((sum(recv), 2 * k), dtype=torch.int32)
+    dist.all_to_all_single(x_recv, x[rows.long()].contiguous(), recv, counts, group=group)
+    dist.all_to_all_single(r_recv, routing[rows.long()].contiguous(), recv, counts, group=group)
+    own_t0 = sum(recv[:r])
+    slot, tok, wt = pair_candidates(r_recv[:, :k], r_recv[:, k:].view(torch.float32), r, W, num_experts,
+                                    with_shared, M, own_t0=own_t0)
+    y_part = local_fn(x_recv, slot, tok, wt).to(torch.float32).contiguous()
+    y_back = torch.empty((sum(counts), H), dtype=torch.float32)
+    dist.all_to_all_single(y_back, y_part, counts, recv, group=group)
+    y = torch.zeros((M, H), dtype=torch.float32)
+    for d in range(W):                                         # ascending rank: a fixed order
+        sel = tok_slot[:, d] >= 0
+        y[sel] += y_back[tok_slot[sel, d].long()]
+    return y
+
+
 def ep_forward(x: torch.Tensor, route_fn: RouteFn, local_fn: LocalFn, *, group=None,
-               num_experts: int, with_shared: bool) -> torch.Tensor:
+               num_experts: int, with_shared: bool, exchange: str = "gather") -> torch.Tensor:
     """One expert-parallel step for this rank's tokens x [M, H]; returns y [M, H] f32.
-    ``route_fn(x) -> (idx [M, k] int32, w [M, k] f32)``; ``local_fn(x_all, slot, tok, w)
-    -> [W*M, H] f32`` computes this rank's experts over the candidate pairs."""
+    ``route_fn(x) -> (idx [M, k] int32, w [M, k] f32)``; ``local_fn(x_rows, slot, tok, w)
+    -> [rows, H] f32`` computes this rank's experts over the candidate pairs of the
+    gathered (``exchange="gather"``) or received (``"a2a"``, host tensors) token rows."""
     W = dist.get_world_size(group)
     r = dist.get_rank(group)
     M, H = x.shape
     idx, w = route_fn(x)
     idx = idx.to(torch.int32).contiguous()
     w = w.to(torch.float32).contiguous()
+    if exchange == "a2a":
+        return _ep_forward_a2a(x.contiguous(), idx, w, local_fn, group, num_experts, with_shared)
+    if exchange != "gather":
+        raise ValueError(f"exchange must be 'gather' or 'a2a', not {exchange!r}")
     nccl = _is_nccl(group)
     if nccl:
         x_all = torch.empty((W * M, H), dtype=x.dtype, device=x.device)
@@ -108,7 +240,13 @@ class ExpertParallelMoE:
     by all ranks of ``group`` (every rank calls with the same M)."""
 
     def __init__(self, cfg, layer: int, w: dict, expert_source: Callable, group=None,
-                 device=None, graphs: bool = True):
+                 device=None, graphs: bool = True, exchange: str = "auto"):
+        if exchange not in ("auto", "gather", "a2a"):
+            raise ValueError(f"exchange must be 'auto', 'gather' or 'a2a', not {exchange!r}")
+        # "gather": all_gather + reduce_scatter (fixed sizes, captured as a CUDA graph);
+        # "a2a": the counted all-to-all (one host synchronisation per step, launched
+        # eagerly; NCCL only); "auto": the gather step, the faster of the two as measured.
+        self.exchange = exchange
         self.cfg, self.group = cfg, group
         # On NCCL, a step (router, collectives, local experts: ~15 launches) is captured
         # into a CUDA graph per token count at its first call and replayed afterwards, so a
@@ -173,14 +311,22 @@ class ExpertParallelMoE:
                                         L.stream_of(x_all)), "k3_moe_pairs_decode")
         return y
 
-    def _forward_nccl(self, flat: torch.Tensor) -> torch.Tensor:
-        """One step with two all_gathers issued as one NCCL group (tokens; routing packed
-        as [M][2k] int32: expert ids, then the weights' bits) and the local experts taken
-        straight from the gathered routing on the device (``k3_moe_ep_local``)."""
+    def uses_a2a(self, M: int) -> bool:
+        """Whether a call with M tokens per rank runs the counted all-to-all step."""
+        return self.exchange == "a2a" and _is_nccl(self.group)
+
+    def capturable(self, M: int) -> bool:
+        """Whether a call with M tokens per rank can be captured into a CUDA graph (the
+        all-to-all step reads its split sizes on the host)."""
+        return not self.uses_a2a(M)
+
+    def _route_packed(self, flat: torch.Tensor) -> torch.Tensor:
+        """The router on this rank's tokens; routing packed as [M][2k] int32 (expert ids,
+        then the weights' bits)."""
         lib = L.load_library()
         c = self.cfg
         M, H = flat.shape
-        k, E, W = c.num_experts_per_token, c.num_experts, self.W
+        k, E = c.num_experts_per_token, c.num_experts
         dev = flat.device
         idx = torch.empty((M, k), dtype=torch.int32, device=dev)
         w = torch.empty((M, k), dtype=torch.float32, device=dev)
@@ -191,7 +337,123 @@ class ExpertParallelMoE:
                                  int(bool(c.moe_renormalize)), float(c.routed_scaling_factor),
                                  idx.data_ptr(), w.data_ptr(), None, None, ws.data_ptr(), ws.numel(),
                                  L.stream_of(flat)), "k3_moe_route")
-        routing = torch.cat([idx, w.view(torch.int32)], dim=1)
+        return torch.cat([idx, w.view(torch.int32)], dim=1)
+
+    def _forward_a2a(self, flat: torch.Tensor) -> torch.Tensor:
+        """One step with the counted all-to-all exchange (module docstring, steps 1-5), on
+        two streams: the shared expert over the own tokens runs on the caller's stream
+        while the host waits for the row counts and while the tokens travel; the packing,
+        the exchanges and the routed local experts run on a side stream. A rank's own rows
+        do not travel back: the combine reads them from the local partial rows."""
+        lib = L.load_library()
+        k, W, r = self.cfg.num_experts_per_token, self.W, self.r
+        M, H = flat.shape
+        dev = flat.device
+        main = torch.cuda.current_stream(dev)
+        side = self._side_stream(dev)
+        routing = self._route_packed(flat)
+        meta, rows, tok_slot, status = a2a_plan_dev(routing, k, self.E_loc, W, r)
+        rcnt = torch.empty(W, dtype=torch.int64, device=dev)
+        dist.all_to_all_single(rcnt, meta[:W], group=self.group)
+        host = self._pinned_counts(W)
+        host.copy_(torch.cat([meta[:W], rcnt, status[:1].to(torch.int64)]), non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        y_shared = None
+        if self.with_shared:                                   # overlaps the host's wait below
+            y_shared = self._shared_part(flat)
+        ready.synchronize()                                    # the step's one host synchronisation
+        counts = host.tolist()
+        send, recv = counts[:W], counts[W:2 * W]
+        if counts[2 * W]:
+            raise ValueError("k3_ep_a2a_plan: the routing holds an expert id outside the layer")
+        S, R = sum(send), sum(recv)
+        soff = [sum(send[:d]) for d in range(W)]
+        roff = [sum(recv[:d]) for d in range(W)]
+        side.wait_event(ready)
+        with torch.cuda.stream(side):
+            x_send = torch.empty((S, H), dtype=flat.dtype, device=dev)
+            r_send = torch.empty((S, 2 * k), dtype=torch.int32, device=dev)
+            # the send buffers keep the plan's layout; the own segment is not packed (the own
+            # tokens go from flat / routing straight into the receive buffers)
+            for lo, hi in ((0, soff[r]), (soff[r] + send[r], S)):
+                if hi > lo:
+                    gather_rows_dev(flat, rows[lo:hi], hi - lo, status[1:], out=x_send[lo:hi])
+                    gather_rows_dev(routing, rows[lo:hi], hi - lo, status[2:], out=r_send[lo:hi])
+            x_recv = torch.empty((R, H), dtype=flat.dtype, device=dev)
+            r_recv = torch.empty((R, 2 * k), dtype=torch.int32, device=dev)
+            ins_x = [flat if d == r else x_send[soff[d]:soff[d] + send[d]] for d in range(W)]
+            ins_r = [routing if d == r else r_send[soff[d]:soff[d] + send[d]] for d in range(W)]
+            dist.all_to_all([x_recv[roff[d]:roff[d] + recv[d]] for d in range(W)], ins_x, group=self.group)
+            dist.all_to_all([r_recv[roff[d]:roff[d] + recv[d]] for d in range(W)], ins_r, group=self.group)
+            y_part = torch.empty((R, H), dtype=torch.float32, device=dev)
+            ws = L.workspace(dev, lib.k3_moe_ep_local_workspace(self.params, R, 0))
+            L.check(lib.k3_moe_ep_local(self.params, x_recv.data_ptr(), L.dtype_code(x_recv), R, r_recv.data_ptr(),
+                                        r_recv.data_ptr() + 4 * k, 2 * k, self.lo, 0, 0, y_part.data_ptr(), L.K3_F32,
+                                        ws.data_ptr(), ws.numel(), L.stream_of(x_recv)), "k3_moe_ep_local")
+            # the own rows do not travel back: zero-size slots for this rank
+            y_back = torch.empty((S, H), dtype=torch.float32, device=dev)
+            none = y_part[:0]
+            dist.all_to_all([none if d == r else y_back[soff[d]:soff[d] + send[d]] for d in range(W)],
+                            [none if d == r else y_part[roff[d]:roff[d] + recv[d]] for d in range(W)],
+                            group=self.group)
+        main.wait_stream(side)
+        for t in (y_part, y_back):                             # read below on the caller's stream
+            t.record_stream(main)
+        y = a2a_combine_dev(y_back, tok_slot, status[3:], base=y_shared, own=y_part[roff[r]:roff[r] + M], rank=r)
+        # the status words of the packing and the combine (non-zero only for a plan that
+        # points outside its buffers); read by the tests, not per step
+        self.last_a2a_status = status
+        return y
+
+    def _side_stream(self, dev: torch.device) -> torch.cuda.Stream:
+        st = getattr(self, "_side", None)
+        if st is None:
+            st = self._side = torch.cuda.Stream(dev)
+        return st
+
+    def _pinned_counts(self, W: int) -> torch.Tensor:
+        buf = getattr(self, "_counts_host", None)
+        if buf is None:
+            buf = self._counts_host = torch.empty(2 * W + 1, dtype=torch.int64).pin_memory()
+        return buf
+
+    def _shared_part(self, flat: torch.Tensor) -> torch.Tensor:
+        """The shared expert over this rank's M own tokens (slot E/W of the pool, weight 1),
+        fp32 [M, H]: on the prefill kernels above MAX_DECODE_TOKENS tokens and on the decode
+        kernels up to it, as the one-GPU layer runs it."""
+        lib = L.load_library()
+        M, H = flat.shape
+        dev = flat.device
+        cache = self.__dict__.setdefault("_shared_cand", {})
+        c = cache.get(M)
+        if c is None:
+            c = cache[M] = (torch.full((M,), self.E_loc, dtype=torch.int32, device=dev),
+                            torch.arange(M, dtype=torch.int32, device=dev),
+                            torch.ones(M, dtype=torch.float32, device=dev))
+        y = torch.empty((M, H), dtype=torch.float32, device=dev)
+        args = (flat.data_ptr(), L.dtype_code(flat), M, c[0].data_ptr(), c[1].data_ptr(), c[2].data_ptr(), M,
+                y.data_ptr(), L.K3_F32)
+        if M > MAX_DECODE_TOKENS:
+            ws = L.workspace(dev, lib.k3_moe_pairs_prefill_workspace(self.params, M, M))
+            L.check(lib.k3_moe_pairs_prefill(self.params, *args, ws.data_ptr(), ws.numel(), L.stream_of(flat)),
+                    "k3_moe_pairs_prefill")
+        else:
+            ws = L.workspace(dev, lib.k3_moe_pairs_workspace(self.params, M, M))
+            L.check(lib.k3_moe_pairs_decode(self.params, *args, ws.data_ptr(), ws.numel(), L.stream_of(flat)),
+                    "k3_moe_pairs_decode")
+        return y
+
+    def _forward_nccl(self, flat: torch.Tensor) -> torch.Tensor:
+        """One step with two all_gathers issued as one NCCL group (tokens; routing packed
+        as [M][2k] int32: expert ids, then the weights' bits) and the local experts taken
+        straight from the gathered routing on the device (``k3_moe_ep_local``)."""
+        lib = L.load_library()
+        c = self.cfg
+        M, H = flat.shape
+        k, W = c.num_experts_per_token, self.W
+        dev = flat.device
+        routing = self._route_packed(flat)
         x_all = torch.empty((W * M, H), dtype=flat.dtype, device=dev)
         r_all = torch.empty((W * M, 2 * k), dtype=torch.int32, device=dev)
         # both gathers in one NCCL group: one collective launch per step instead of two
@@ -245,6 +507,11 @@ class ExpertParallelMoE:
         if flat.dtype not in (torch.float32, torch.bfloat16):
             flat = flat.float()
         flat = flat.contiguous()
+        if self.uses_a2a(flat.shape[0]):
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("the all-to-all step reads its split sizes on the host and cannot be "
+                                   "captured; use exchange='gather' for a capturable layer")
+            return self._forward_a2a(flat).reshape(shape)
         if _is_nccl(self.group):
             if self.graphs and self.graph_error is None and not torch.cuda.is_current_stream_capturing():
                 try:
@@ -264,4 +531,5 @@ class ExpertParallelMoE:
         return self._local(x_all, slot, tok, w)
 
 
-__all__ = ["ExpertParallelMoE", "ep_forward", "pair_candidates"]
+__all__ = ["ExpertParallelMoE", "a2a_combine_dev", "a2a_plan", "a2a_plan_dev", "ep_forward",
+           "gather_rows_dev", "pair_candidates"]

@@ -25,7 +25,7 @@ def _layer(seed=11):
     return gate, bias, experts
 
 
-def _worker(rank, world, port, out_q):
+def _worker(rank, world, port, out_q, exchange="gather"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -54,7 +54,8 @@ def _worker(rank, world, port, out_q):
                 y[t] += (out[0] * float(w[i])).astype(np.float32)
             return torch.from_numpy(y)
 
-        y = ep_forward(torch.from_numpy(x), route_fn, local_fn, num_experts=E, with_shared=True)
+        y = ep_forward(torch.from_numpy(x), route_fn, local_fn, num_experts=E, with_shared=True,
+                       exchange=exchange)
         ref, _ = O.moe_forward(x, O.MoESpec(E, K, SCALE, True, "silu"), gate, bias,
                                lambda e, w: experts[e][w],
                                shared={"kind": "mxfp4", **{w: experts["shared"][w] for w in ("w1", "w3", "w2")}})
@@ -69,21 +70,51 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ep_forward_gloo_two_ranks():
-    world = 2
+def _run(world, exchange):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=120) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert set(res) == {0, 1}
+    assert set(res) == set(range(world))
     for rank, err in res.items():
         assert err < 1e-5, (rank, err)
+
+
+def test_ep_forward_gloo_two_ranks():
+    _run(2, "gather")
+
+
+def test_ep_forward_a2a_gloo_two_ranks():
+    """The counted all-to-all exchange (send plan, row counts, tokens and routing out,
+    partial rows back, ordered per-token sum) on gloo ranks."""
+    _run(2, "a2a")
+
+
+def test_ep_forward_a2a_gloo_four_ranks():
+    """Four ranks of two experts each: tokens reach some ranks and not others, so the
+    split sizes differ per pair of ranks."""
+    _run(4, "a2a")
+
+
+def test_a2a_plan_layout():
+    from kimi_k3_mlx_macmini_b200.ep import a2a_plan
+    # 4 tokens, top-2 of 8 experts over 4 ranks (2 each); this is rank 1
+    idx = torch.tensor([[0, 1], [2, 7], [6, 3], [5, 4]], dtype=torch.int32)
+    counts, rows, slot = a2a_plan(idx, rank=1, world=4, experts_per_rank=2)
+    # rank 0: token 0; rank 1 (own): all tokens; rank 2: tokens 3; rank 3: tokens 1, 2
+    assert counts == [1, 4, 1, 2]
+    assert rows.tolist() == [0, 0, 1, 2, 3, 3, 1, 2]
+    assert slot.tolist() == [[0, 1, -1, -1], [-1, 2, -1, 6], [-1, 3, -1, 7], [-1, 4, 5, -1]]
+    # an expert id outside the layer is skipped (the device plan also flags the call)
+    counts, rows, slot = a2a_plan(torch.tensor([[9, -1]], dtype=torch.int32), rank=0, world=4,
+                                  experts_per_rank=2)
+    assert counts == [1, 0, 0, 0] and rows.tolist() == [0] and slot.tolist() == [[0, -1, -1, -1]]
 
 
 def test_pair_candidates_layout():
