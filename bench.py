@@ -76,9 +76,11 @@ def parse():
                          "decode; 5 = Kimi-K3 layer decode (supplementary)")
     ap.add_argument("--layers", type=int, default=4, help="config 4: consecutive streamed layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="auto", choices=["auto", "gather", "a2a"],
-                    help="N > 1: the expert-parallel token exchange (auto = gather: all_gather + "
-                         "reduce_scatter; a2a: the counted all_to_all)")
+    ap.add_argument("--exchange", default="auto", choices=["auto", "gather", "a2a", "p2p"],
+                    help="N > 1: the expert-parallel token exchange (gather: NCCL all_gather + "
+                         "reduce_scatter; a2a: the counted NCCL all_to_all; p2p: the decode step's gather "
+                         "and reduce-scatter as kernels over NVLink peer memory; auto: p2p at decode, "
+                         "gather at prefill)")
     args = ap.parse_args()
     if args.tokens is None:
         args.tokens = {1: 8, 2: 8, 3: 4096, 4: 1, 5: 1}[args.config]
@@ -527,8 +529,13 @@ def ep_check(moe, full, x, world):
     err = float(torch.linalg.vector_norm((y_ep - y_one).double()) / torch.linalg.vector_norm(y_one.double()))
     full._pool = None                                       # free the whole-layer pool again
     torch.cuda.empty_cache()
-    return {"max_rel_l2_over_ranks": dist_max(err, world),
-            "against": "the same tokens through the whole layer on one GPU (LatentMoE, 1-GPU kernels)"}
+    p2p = getattr(moe, "p2p", None)
+    st = float(p2p.status.max().item()) if p2p is not None else 0.0
+    out = {"max_rel_l2_over_ranks": dist_max(err, world),
+           "against": "the same tokens through the whole layer on one GPU (LatentMoE, 1-GPU kernels)"}
+    if p2p is not None:
+        out["p2p_status_max_over_ranks"] = int(dist_max(st, world))
+    return out
 
 
 def e2e_loop(call, xh, order, K, W, out_shape, world):
@@ -637,6 +644,9 @@ def run_b200(args, rank, world, local):
         moe.graphs = False
     L.profile_enable(True)
     L.profile_collect()
+    if world > 1:
+        moe.collective_timing = True
+        moe.collective_ms()
     torch.cuda.synchronize()
     # keep the GPU busy while the host enqueues, so each event pair brackets device time
     torch.cuda._sleep(int(4e7))
@@ -645,6 +655,10 @@ def run_b200(args, rank, world, local):
     torch.cuda.synchronize()
     prof = L.profile_collect()
     L.profile_enable(False)
+    coll = None
+    if world > 1:
+        coll = {k: v / n_prof for k, v in moe.collective_ms().items()}
+        moe.collective_timing = False
     if api_graphs is not None:
         moe.graphs = api_graphs
     gu_ms, gu_n = prof["gateup"]
@@ -688,11 +702,14 @@ def run_b200(args, rank, world, local):
                    "parallelism": "single GPU" if world == 1 else
                                   f"ep{world}: {args.experts // world} routed experts per rank + replicated shared, "
                                   + ("counted all_to_all dispatch and combine (NCCL)" if moe.uses_a2a(M) else
+                                     "all-gather dispatch and reduce-scatter combine as kernels over NVLink "
+                                     "peer memory (CUDA IPC)" if moe.exchange_used(M) == "p2p" else
                                      "all_gather dispatch, reduce_scatter combine (NCCL)"),
                    "l2": f"inputs larger than L2: {9.0 / world:.2f} GB of expert weights per GPU, "
                          "a different token batch every step",
                    "timing": timing + ", events around K steps",
-                   "api_graph_error": graph_error},
+                   "api_graph_error": graph_error,
+                   "p2p_error": getattr(moe, "p2p_error", None)},
         "ep_check": check,
         "unique_experts_mean": float(np.mean(U_t)),
         "unique_experts_per_batch": U[:8],
@@ -708,6 +725,7 @@ def run_b200(args, rank, world, local):
                      "launch_ms": gu_ms / gu_n},
         "down_kernel": {"achieved": dn_gbs, "frac": dn_gbs / peak, "launch_ms": dn_ms / dn_n},
         "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
+        "collective_ms_per_step": coll,
         "e2e": {"value": world * M / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": M * H * 4,
                 "ms_per_step": e2e_ms,
@@ -842,11 +860,18 @@ def run_prefill(args, rank, world, local):
         moe.graphs = False
     L.profile_enable(True)
     L.profile_collect()
+    if world > 1:
+        moe.collective_timing = True
+        moe.collective_ms()
     for i in range(n_prof):
         moe(xs[i % R])
     torch.cuda.synchronize()
     prof = L.profile_collect()
     L.profile_enable(False)
+    coll = None
+    if world > 1:
+        coll = {k: v / n_prof for k, v in moe.collective_ms().items()}
+        moe.collective_timing = False
     if api_graphs is not None:
         moe.graphs = api_graphs
     gu_ms, gu_n = prof["gateup"]
@@ -911,6 +936,7 @@ def run_prefill(args, rank, world, local):
         "down_kernel": {"launch_ms": dn_ms / max(dn_n, 1),
                         "achieved_tflops": flops / 3 / (dn_ms / max(dn_n, 1) / 1e3) / 1e12},
         "kernel_ms_per_step": {k: v[0] / n_prof for k, v in prof.items() if v[1]},
+        "collective_ms_per_step": coll,
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 4,
                 "ms_per_step": e2e_ms,

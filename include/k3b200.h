@@ -343,6 +343,37 @@ K3_API int k3_ep_a2a_combine(const float* base, const float* own, int rank, cons
                              int64_t n_part, const int32_t* tok_slot, int64_t M, int world, int64_t H,
                              void* y_out, int y_dtype, int32_t* status, void* stream);
 
+/* Expert-parallel exchanges over NVLink peer memory (an alternative to the NCCL
+ * all_gather / reduce_scatter of a decode step; the reference has one process and no
+ * exchange: air_llm/models/kimi_k3/moe.py:119-127). Every rank owns one exchange buffer of
+ * k3_p2p_buffer_bytes (zeroed before first use) and maps every peer's through CUDA IPC
+ * (k3_p2p_export on the owner, k3_p2p_open on the others). Layout: a 1 KB header, then
+ * gather areas 0 and 1 and the reduce area, world slots each (k3_p2p_area_offsets). Waits
+ * are bounded (2 s, then K3_ERR_TIMEOUT in *status; the group must then be rebuilt). */
+typedef struct {
+    int32_t world, rank;
+    int64_t gather_bytes, gather2_bytes, reduce_bytes;   /* slot capacities */
+    void* base[32];        /* every rank's buffer as mapped in this process (own at [rank]) */
+} k3_p2p_group;
+K3_API size_t k3_p2p_buffer_bytes(int world, int64_t gather_bytes, int64_t gather2_bytes, int64_t reduce_bytes);
+/* offsets_out[4]: gather area 0, gather area 1, reduce area, total bytes. */
+K3_API int k3_p2p_area_offsets(int world, int64_t gather_bytes, int64_t gather2_bytes, int64_t reduce_bytes,
+                               int64_t* offsets_out);
+/* IPC handle (64 bytes) of the allocation holding ptr, and ptr's offset in it. */
+K3_API int k3_p2p_export(const void* ptr, uint8_t* handle_out, int64_t* offset_out);
+K3_API int k3_p2p_open(const uint8_t* handle, int64_t offset, void** ptr_out);
+K3_API int k3_p2p_close(void* ptr, int64_t offset);
+/* All-gather: src (bytes) and src2 (bytes2), multiples of 16, go to slot `rank` of gather
+ * areas 0 and 1 of every rank (slot stride = this call's size, so each area holds the
+ * world's rows contiguously); mode 1 = put and publish, 2 = wait for the peers, 3 = both. */
+K3_API int k3_p2p_allgather(const k3_p2p_group* g, const void* src, int64_t bytes, const void* src2,
+                            int64_t bytes2, int mode, int32_t* status, void* stream);
+/* Reduce-scatter: src holds world chunks of n floats (chunk d for rank d); out[i] = sum over
+ * ranks s ascending of rank s's chunk for this rank, fp32. Modes as for the all-gather
+ * (2: wait and sum). */
+K3_API int k3_p2p_reduce_scatter(const k3_p2p_group* g, const float* src, int64_t n, float* out, int mode,
+                                 int32_t* status, void* stream);
+
 /* Latent MoE decode (Kimi-K3, air_llm/models/kimi_k3/moe.py:110-127): the router reads
  * x_router [M][H_router] (the hidden state), the routed experts read x_expert [M][hidden]
  * (the latent state, p->hidden wide); y_out [M][hidden] = the weighted sum of the routed

@@ -51,6 +51,12 @@ class K3DenseSeg(ctypes.Structure):
                 ("norm_w", ctypes.c_void_p), ("eps", ctypes.c_float), ("act_input", ctypes.c_int32)]
 
 
+class K3P2PGroup(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("gather_bytes", ctypes.c_int64),
+                ("gather2_bytes", ctypes.c_int64), ("reduce_bytes", ctypes.c_int64),
+                ("base", ctypes.c_void_p * 32)]
+
+
 # name -> (restype, argtypes); mirrors include/k3b200.h
 SIGNATURES = {
     "k3_abi_version": (_i32, []),
@@ -106,6 +112,13 @@ SIGNATURES = {
     "k3_dense_gemm": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i32, _vp, _sz, _vp]),
     "k3_moe_ep_local": (_i32, [ctypes.POINTER(K3MoEParams), _vp, _i32, _i64, _vp, _vp, _i64, _i32, _i32, _i32,
                                _vp, _i32, _vp, _sz, _vp]),
+    "k3_p2p_buffer_bytes": (_sz, [_i32, _i64, _i64, _i64]),
+    "k3_p2p_area_offsets": (_i32, [_i32, _i64, _i64, _i64, _vp]),
+    "k3_p2p_export": (_i32, [_vp, _vp, _vp]),
+    "k3_p2p_open": (_i32, [_vp, _i64, _vp]),
+    "k3_p2p_close": (_i32, [_vp, _i64]),
+    "k3_p2p_allgather": (_i32, [ctypes.POINTER(K3P2PGroup), _vp, _i64, _vp, _i64, _i32, _vp, _vp]),
+    "k3_p2p_reduce_scatter": (_i32, [ctypes.POINTER(K3P2PGroup), _vp, _i64, _vp, _i32, _vp, _vp]),
     "k3_ep_a2a_plan": (_i32, [_vp, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "k3_ep_gather_rows": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "k3_ep_a2a_combine": (_i32, [_vp, _vp, _i32, _vp, _i64, _vp, _i64, _i32, _i64, _vp, _i32, _vp, _vp]),
@@ -136,6 +149,11 @@ def load_library(path: Path = LIB_PATH):
 
 class K3Error(RuntimeError):
     """A CUDA or workspace failure reported by the library."""
+
+
+def last_error() -> str:
+    """The calling thread's last library error message."""
+    return (load_library().k3_last_error() or b"").decode(errors="replace")
 
 
 def check(rc: int, what: str) -> None:

@@ -52,6 +52,7 @@ to the order in which the ranks' partial sums are added.
 from __future__ import annotations
 
 import ctypes
+import hashlib
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -234,6 +235,124 @@ def ep_forward(x: torch.Tensor, route_fn: RouteFn, local_fn: LocalFn, *, group=N
     return y_part[r * M:(r + 1) * M].clone()
 
 
+class P2PUnavailable(RuntimeError):
+    """Peer-memory exchange not possible for this group (ranks sharing a GPU, no CUDA IPC
+    between the ranks' GPUs, ...); every rank of the group raises it together."""
+
+
+class P2PExchange:
+    """Exchange buffers of an expert-parallel group over NVLink peer memory (CUDA IPC):
+    a decode step's all-gather of the tokens and routing and its reduce-scatter of the
+    partial rows as ``k3_p2p_*`` kernels that store straight into the peers' buffers,
+    instead of NCCL collectives. Built collectively (every rank of ``group`` at once):
+    each rank allocates its buffer, exports its IPC handle, receives every peer's (one
+    NCCL all_gather) and maps them; the ranks agree on the outcome (one all_reduce), so
+    either all use it or all raise ``P2PUnavailable``. The kernels wait on flags that
+    other ranks set, so the group needs one GPU per rank: ranks that share a GPU make it
+    unavailable. Capacities are per rank and call."""
+
+    def __init__(self, group, device: torch.device, gather_bytes: int, gather2_bytes: int, reduce_bytes: int):
+        lib = L.load_library()
+        self.group = group
+        self.W, self.r = dist.get_world_size(group), dist.get_rank(group)
+        self.caps = (int(gather_bytes), int(gather2_bytes), int(reduce_bytes))
+        self._opened = []
+        nbytes = int(lib.k3_p2p_buffer_bytes(self.W, *self.caps))
+        if nbytes == 0:
+            raise ValueError("k3_p2p_buffer_bytes: bad world size or capacities")
+        self._buf = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+        skew = (-self._buf.data_ptr()) % 256
+        self.own = self._buf[skew:skew + nbytes]
+        offs = (ctypes.c_int64 * 4)()
+        L.check(lib.k3_p2p_area_offsets(self.W, *self.caps, offs), "k3_p2p_area_offsets")
+        self.offsets = list(offs)
+        torch.cuda.synchronize(device)                       # zeroed before any peer maps it
+        why = ""
+        handle = (ctypes.c_uint8 * 64)()
+        ioff = ctypes.c_int64()
+        if lib.k3_p2p_export(self.own.data_ptr(), handle, ctypes.byref(ioff)) != 0:
+            why = f"rank {self.r}: k3_p2p_export: {L.last_error()}"
+        uuid = str(torch.cuda.get_device_properties(device).uuid).encode()
+        gpu_id = int.from_bytes(hashlib.sha1(uuid).digest()[:7], "little")
+        rec = (list(bytes(handle)) + list(int(ioff.value).to_bytes(8, "little", signed=True))
+               + list(gpu_id.to_bytes(8, "little")))
+        allh = torch.empty((self.W, len(rec)), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(allh, torch.tensor(rec, dtype=torch.uint8, device=device), group=group)
+        allh = allh.cpu()
+        gpus = [int.from_bytes(bytes(allh[s, 72:80].tolist()), "little") for s in range(self.W)]
+        if not why and len(set(gpus)) != self.W:
+            why = "two ranks share a GPU"
+        bases = []
+        if not why:
+            for s in range(self.W):
+                if s == self.r:
+                    bases.append(self.own.data_ptr())
+                    continue
+                h = (ctypes.c_uint8 * 64)(*allh[s, :64].tolist())
+                o = int.from_bytes(bytes(allh[s, 64:72].tolist()), "little", signed=True)
+                ptr = ctypes.c_void_p()
+                if lib.k3_p2p_open(h, o, ctypes.byref(ptr)) != 0:
+                    why = f"rank {self.r}: k3_p2p_open of rank {s}'s buffer: {L.last_error()}"
+                    break
+                self._opened.append((ptr.value, o))
+                bases.append(ptr.value)
+        ok = torch.tensor([0 if why else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if not int(ok.item()):
+            self.close()
+            raise P2PUnavailable(why or "another rank could not map the exchange buffers")
+        self.desc = L.K3P2PGroup(world=self.W, rank=self.r, gather_bytes=self.caps[0],
+                                 gather2_bytes=self.caps[1], reduce_bytes=self.caps[2],
+                                 base=(ctypes.c_void_p * 32)(*bases))
+        # status words of the all-gather and the reduce-scatter (K3_ERR_TIMEOUT after a wait
+        # gave up: the group is then out of step and must be rebuilt)
+        self.status = torch.zeros(2, dtype=torch.int32, device=device)
+        dist.barrier(group=group)                            # every buffer mapped everywhere
+
+    def area(self, i: int) -> int:
+        """Device address of this rank's gather area 0, gather area 1 or reduce area."""
+        return self.own.data_ptr() + self.offsets[i]
+
+    def allgather(self, src: torch.Tensor, src2: torch.Tensor) -> None:
+        lib = L.load_library()
+        L.check(lib.k3_p2p_allgather(ctypes.byref(self.desc), src.data_ptr(), src.numel() * src.element_size(),
+                                     src2.data_ptr(), src2.numel() * src2.element_size(), 3,
+                                     self.status.data_ptr(), L.stream_of(src)), "k3_p2p_allgather")
+
+    def reduce_scatter(self, src: torch.Tensor, out: torch.Tensor) -> None:
+        lib = L.load_library()
+        L.check(lib.k3_p2p_reduce_scatter(ctypes.byref(self.desc), src.data_ptr(), out.numel(), out.data_ptr(), 3,
+                                          self.status[1:].data_ptr(), L.stream_of(src)), "k3_p2p_reduce_scatter")
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers (after this rank's work on the device is done; the
+        own buffer lives until the object goes)."""
+        if not self._opened:
+            return
+        torch.cuda.synchronize(self.own.device)
+        lib = L.load_library()
+        for ptr, o in self._opened:
+            lib.k3_p2p_close(ptr, o)
+        self._opened = []
+
+
+class _CollTimer:
+    def __init__(self, owner, name: str):
+        self.owner, self.name, self.ev = owner, name, None
+
+    def __enter__(self):
+        if self.owner.collective_timing and not torch.cuda.is_current_stream_capturing():
+            self.ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self.ev[0].record()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ev is not None:
+            self.ev[1].record()
+            self.owner._coll_events.append((self.name, *self.ev))
+        return False
+
+
 class ExpertParallelMoE:
     """This rank's share of an expert-parallel MoE layer on its GPU; ``__call__(x)`` is
     ``LatentMoE.__call__`` (``moe.py:110-132``) for this rank's tokens, computed jointly
@@ -241,11 +360,14 @@ class ExpertParallelMoE:
 
     def __init__(self, cfg, layer: int, w: dict, expert_source: Callable, group=None,
                  device=None, graphs: bool = True, exchange: str = "auto"):
-        if exchange not in ("auto", "gather", "a2a"):
-            raise ValueError(f"exchange must be 'auto', 'gather' or 'a2a', not {exchange!r}")
-        # "gather": all_gather + reduce_scatter (fixed sizes, captured as a CUDA graph);
-        # "a2a": the counted all-to-all (one host synchronisation per step, launched
-        # eagerly; NCCL only); "auto": the gather step, the faster of the two as measured.
+        if exchange not in ("auto", "gather", "a2a", "p2p"):
+            raise ValueError(f"exchange must be 'auto', 'gather', 'a2a' or 'p2p', not {exchange!r}")
+        # "gather": NCCL all_gather + reduce_scatter (fixed sizes, captured as a CUDA
+        # graph); "a2a": the counted NCCL all-to-all (one host synchronisation per step,
+        # launched eagerly); "p2p": the gather step's two exchanges as kernels over NVLink
+        # peer memory up to MAX_DECODE_TOKENS tokens per rank (one GPU per rank, CUDA IPC
+        # between them; otherwise, and above that size, the NCCL gather step); "auto": as
+        # "p2p" -- the fastest measured at decode, and the gather step at prefill.
         self.exchange = exchange
         self.cfg, self.group = cfg, group
         # On NCCL, a step (router, collectives, local experts: ~15 launches) is captured
@@ -254,6 +376,12 @@ class ExpertParallelMoE:
         self.graphs = graphs
         self._steps: dict = {}
         self.graph_error: Optional[str] = None
+        # set by a profiling caller: CUDA events around each collective of eagerly launched
+        # steps (never inside a captured graph), summed by collective_ms()
+        self.collective_timing = False
+        self._coll_events: list = []
+        self.p2p: Optional[P2PExchange] = None
+        self.p2p_error: Optional[str] = None             # why the peer-memory exchange is off
         self.W = dist.get_world_size(group)
         self.r = dist.get_rank(group)
         E = cfg.num_experts
@@ -311,6 +439,22 @@ class ExpertParallelMoE:
                                         L.stream_of(x_all)), "k3_moe_pairs_decode")
         return y
 
+    def _coll(self, name: str):
+        """Context for one collective: with ``collective_timing`` set (and not capturing),
+        events on the launching stream before and after it -- the collective's exposed
+        time on that stream, waits for slower ranks included."""
+        return _CollTimer(self, name)
+
+    def collective_ms(self) -> dict:
+        """{collective: total ms} of the timed collectives since the last call (waits for
+        their events)."""
+        out: dict = {}
+        for name, e0, e1 in self._coll_events:
+            e1.synchronize()
+            out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+        self._coll_events = []
+        return out
+
     def uses_a2a(self, M: int) -> bool:
         """Whether a call with M tokens per rank runs the counted all-to-all step."""
         return self.exchange == "a2a" and _is_nccl(self.group)
@@ -354,7 +498,8 @@ class ExpertParallelMoE:
         routing = self._route_packed(flat)
         meta, rows, tok_slot, status = a2a_plan_dev(routing, k, self.E_loc, W, r)
         rcnt = torch.empty(W, dtype=torch.int64, device=dev)
-        dist.all_to_all_single(rcnt, meta[:W], group=self.group)
+        with self._coll("a2a_counts"):
+            dist.all_to_all_single(rcnt, meta[:W], group=self.group)
         host = self._pinned_counts(W)
         host.copy_(torch.cat([meta[:W], rcnt, status[:1].to(torch.int64)]), non_blocking=True)
         ready = torch.cuda.Event()
@@ -384,8 +529,9 @@ class ExpertParallelMoE:
             r_recv = torch.empty((R, 2 * k), dtype=torch.int32, device=dev)
             ins_x = [flat if d == r else x_send[soff[d]:soff[d] + send[d]] for d in range(W)]
             ins_r = [routing if d == r else r_send[soff[d]:soff[d] + send[d]] for d in range(W)]
-            dist.all_to_all([x_recv[roff[d]:roff[d] + recv[d]] for d in range(W)], ins_x, group=self.group)
-            dist.all_to_all([r_recv[roff[d]:roff[d] + recv[d]] for d in range(W)], ins_r, group=self.group)
+            with self._coll("a2a_dispatch"):
+                dist.all_to_all([x_recv[roff[d]:roff[d] + recv[d]] for d in range(W)], ins_x, group=self.group)
+                dist.all_to_all([r_recv[roff[d]:roff[d] + recv[d]] for d in range(W)], ins_r, group=self.group)
             y_part = torch.empty((R, H), dtype=torch.float32, device=dev)
             ws = L.workspace(dev, lib.k3_moe_ep_local_workspace(self.params, R, 0))
             L.check(lib.k3_moe_ep_local(self.params, x_recv.data_ptr(), L.dtype_code(x_recv), R, r_recv.data_ptr(),
@@ -394,9 +540,10 @@ class ExpertParallelMoE:
             # the own rows do not travel back: zero-size slots for this rank
             y_back = torch.empty((S, H), dtype=torch.float32, device=dev)
             none = y_part[:0]
-            dist.all_to_all([none if d == r else y_back[soff[d]:soff[d] + send[d]] for d in range(W)],
-                            [none if d == r else y_part[roff[d]:roff[d] + recv[d]] for d in range(W)],
-                            group=self.group)
+            with self._coll("a2a_combine"):
+                dist.all_to_all([none if d == r else y_back[soff[d]:soff[d] + send[d]] for d in range(W)],
+                                [none if d == r else y_part[roff[d]:roff[d] + recv[d]] for d in range(W)],
+                                group=self.group)
         main.wait_stream(side)
         for t in (y_part, y_back):                             # read below on the caller's stream
             t.record_stream(main)
@@ -454,22 +601,54 @@ class ExpertParallelMoE:
         k, W = c.num_experts_per_token, self.W
         dev = flat.device
         routing = self._route_packed(flat)
-        x_all = torch.empty((W * M, H), dtype=flat.dtype, device=dev)
-        r_all = torch.empty((W * M, 2 * k), dtype=torch.int32, device=dev)
-        # both gathers in one NCCL group: one collective launch per step instead of two
-        with dist._coalescing_manager(group=self.group, device=dev):
-            dist.all_gather_into_tensor(x_all, flat, group=self.group)
-            dist.all_gather_into_tensor(r_all, routing, group=self.group)
+        p2p = self._p2p_for(M, dev)
+        if p2p is not None:
+            # both gathers as one peer-memory kernel: rows land in this rank's gather areas
+            with self._coll("p2p_allgather"):
+                p2p.allgather(flat, routing)
+            x_ptr, r_ptr = p2p.area(0), p2p.area(1)
+        else:
+            x_all = torch.empty((W * M, H), dtype=flat.dtype, device=dev)
+            r_all = torch.empty((W * M, 2 * k), dtype=torch.int32, device=dev)
+            # both gathers in one NCCL group: one collective launch per step instead of two
+            with self._coll("all_gather"), dist._coalescing_manager(group=self.group, device=dev):
+                dist.all_gather_into_tensor(x_all, flat, group=self.group)
+                dist.all_gather_into_tensor(r_all, routing, group=self.group)
+            x_ptr, r_ptr = x_all.data_ptr(), r_all.data_ptr()
         y_part = torch.empty((W * M, H), dtype=torch.float32, device=dev)
-        w_all = r_all[:, k:].view(torch.float32)
         shared_n = M if self.with_shared else 0
         ws2 = L.workspace(dev, lib.k3_moe_ep_local_workspace(self.params, W * M, shared_n))
-        L.check(lib.k3_moe_ep_local(self.params, x_all.data_ptr(), L.dtype_code(x_all), W * M, r_all.data_ptr(),
-                                    w_all.data_ptr(), 2 * k, self.lo, self.r * M, shared_n, y_part.data_ptr(),
-                                    L.K3_F32, ws2.data_ptr(), ws2.numel(), L.stream_of(x_all)), "k3_moe_ep_local")
+        L.check(lib.k3_moe_ep_local(self.params, x_ptr, L.dtype_code(flat), W * M, r_ptr, r_ptr + 4 * k, 2 * k,
+                                    self.lo, self.r * M, shared_n, y_part.data_ptr(), L.K3_F32, ws2.data_ptr(),
+                                    ws2.numel(), L.stream_of(flat)), "k3_moe_ep_local")
         y = torch.empty((M, H), dtype=torch.float32, device=dev)
-        dist.reduce_scatter_tensor(y, y_part, group=self.group)
+        if p2p is not None:
+            with self._coll("p2p_reduce_scatter"):
+                p2p.reduce_scatter(y_part, y)
+        else:
+            with self._coll("reduce_scatter"):
+                dist.reduce_scatter_tensor(y, y_part, group=self.group)
         return y
+
+    def _p2p_for(self, M: int, dev: torch.device) -> Optional[P2PExchange]:
+        """The peer-memory exchange for a step of M tokens per rank, built at its first use
+        (collectively: every rank calls with the same M), or None for the NCCL step."""
+        if self.exchange not in ("p2p", "auto") or M > MAX_DECODE_TOKENS or not _is_nccl(self.group):
+            return None
+        if self.p2p is None and self.p2p_error is None:
+            H, k = self.pool.hidden, self.cfg.num_experts_per_token
+            try:
+                self.p2p = P2PExchange(self.group, dev, MAX_DECODE_TOKENS * H * 4, MAX_DECODE_TOKENS * 2 * k * 4,
+                                       MAX_DECODE_TOKENS * H * 4)
+            except P2PUnavailable as exc:                    # every rank: the NCCL step instead
+                self.p2p_error = str(exc)
+        return self.p2p
+
+    def exchange_used(self, M: int) -> str:
+        """The exchange a call with M tokens per rank runs: "a2a", "p2p" or "gather"."""
+        if self.uses_a2a(M):
+            return "a2a"
+        return "p2p" if (self.p2p is not None and M <= MAX_DECODE_TOKENS) else "gather"
 
     def _replay(self, flat: torch.Tensor) -> torch.Tensor:
         """The step as a CUDA graph: captured once per (tokens, dtype) -- every rank at the
@@ -497,8 +676,12 @@ class ExpertParallelMoE:
         return sy.clone()
 
     def release_graphs(self) -> None:
-        """Drop the captured steps (before the process group is destroyed)."""
+        """Drop the captured steps and unmap the peers' exchange buffers (before the
+        process group is destroyed)."""
         self._steps.clear()
+        if self.p2p is not None:
+            self.p2p.close()
+            self.p2p = None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         L.require_cuda(x, "x")
@@ -531,5 +714,5 @@ class ExpertParallelMoE:
         return self._local(x_all, slot, tok, w)
 
 
-__all__ = ["ExpertParallelMoE", "a2a_combine_dev", "a2a_plan", "a2a_plan_dev", "ep_forward",
+__all__ = ["ExpertParallelMoE", "P2PExchange", "P2PUnavailable", "a2a_combine_dev", "a2a_plan", "a2a_plan_dev", "ep_forward",
            "gather_rows_dev", "pair_candidates"]

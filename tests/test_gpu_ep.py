@@ -137,6 +137,10 @@ def _ep_worker(rank, world, port, q, T=6, exchange="auto"):
         x2 = synthetic.tokens(900 + rank, T, H)
         y2 = ep(x2)                           # replay on new tokens
         assert ep.graph_error is None, ep.graph_error
+        if exchange in ("p2p", "auto") and T <= 8:
+            assert ep.p2p is not None, ep.p2p_error       # one GPU per rank: the peer-memory step
+        if ep.p2p is not None:
+            assert ep.p2p.status.tolist() == [0, 0]
         ref = lay.moe()(x)                    # the whole layer on this GPU
         ref2 = lay.moe()(x2)
         err = max(O.rel_l2(y.cpu().numpy(), ref.float().cpu().numpy()),
@@ -180,6 +184,17 @@ def test_expert_parallel_prefill():
     two agree to the unordered fp32 adds into y."""
     world = min(4, torch.cuda.device_count())
     for rank, err in _run_ep(world, 300).items():
+        assert err < 1e-5, (rank, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("exchange,T", [("p2p", 8), ("gather", 6)])
+def test_expert_parallel_decode_exchanges(exchange, T):
+    """The decode step with its all-gather and reduce-scatter as kernels over NVLink peer
+    memory (exchange="p2p", also the default at decode) and as NCCL collectives
+    ("gather"), both captured and replayed."""
+    world = min(4, torch.cuda.device_count())
+    for rank, err in _run_ep(world, T, exchange).items():
         assert err < 1e-5, (rank, err)
 
 
