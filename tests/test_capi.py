@@ -74,3 +74,31 @@ def test_python_layer_refuses_cpu_tensors():
     with pytest.raises(ValueError, match="CUDA"):
         mxfp4_matvec_fused(torch.zeros(1, 64), torch.zeros(4, 32, dtype=torch.uint8),
                            torch.zeros(4, 2, dtype=torch.uint8))
+
+
+def test_exchange_layouts_and_validation(lib):
+    """The expert-parallel exchange entry points: the peer-memory buffer layout (a 1 KB
+    header, then world slots per area, each slot 16-byte aligned) and argument checks that
+    answer before any CUDA call."""
+    import ctypes as C
+    from kimi_k3_mlx_macmini_b200 import _lib as L
+    for W, g0, g1, rb in ((2, 114688, 512, 229376), (8, 229376, 1024, 229376), (3, 100, 36, 20)):
+        offs = (C.c_int64 * 4)()
+        assert lib.k3_p2p_area_offsets(W, g0, g1, rb, offs) == 0
+        r16 = lambda v: (v + 15) // 16 * 16  # noqa: E731
+        assert list(offs) == [1024, 1024 + W * r16(g0), 1024 + W * (r16(g0) + r16(g1)),
+                              1024 + W * (r16(g0) + r16(g1) + r16(rb))]
+        assert lib.k3_p2p_buffer_bytes(W, g0, g1, rb) == offs[3]
+    assert lib.k3_p2p_buffer_bytes(0, 16, 16, 16) == 0 and lib.k3_p2p_buffer_bytes(33, 16, 16, 16) == 0
+    g = L.K3P2PGroup(world=2, rank=2, gather_bytes=64, gather2_bytes=64, reduce_bytes=64,
+                     base=(C.c_void_p * 32)(256, 512))
+    fake = C.c_void_p(256)
+    assert lib.k3_p2p_allgather(C.byref(g), fake, 16, fake, 16, 3, fake, None) == L.K3_ERR_INVALID   # rank >= world
+    g.rank = 0
+    assert lib.k3_p2p_allgather(C.byref(g), fake, 80, fake, 16, 3, fake, None) == L.K3_ERR_INVALID   # > capacity
+    assert lib.k3_p2p_allgather(C.byref(g), fake, 24, fake, 16, 3, fake, None) == L.K3_ERR_INVALID   # not 16-multiple
+    assert lib.k3_p2p_reduce_scatter(C.byref(g), fake, 6, fake, 3, fake, None) == L.K3_ERR_INVALID   # n % 4
+    assert lib.k3_ep_a2a_plan(fake, 8, 4, 8, 48, 33, 0, fake, fake, fake, fake, fake, None) == L.K3_ERR_UNSUPPORTED
+    assert lib.k3_ep_a2a_plan(fake, 4, 4, 8, 48, 8, 0, fake, fake, fake, fake, fake, None) == L.K3_ERR_INVALID
+    assert lib.k3_ep_gather_rows(fake, 4, 6, fake, 4, fake, fake, None) == L.K3_ERR_INVALID          # row bytes % 4
+    assert lib.k3_ep_a2a_combine(None, None, 0, fake, 4, fake, 4, 2, 6, fake, L.K3_F32, fake, None) == L.K3_ERR_INVALID
