@@ -601,7 +601,7 @@ class ExpertParallelMoE:
         k, W = c.num_experts_per_token, self.W
         dev = flat.device
         routing = self._route_packed(flat)
-        p2p = self._p2p_for(M, dev)
+        p2p = self._p2p_for(flat)
         if p2p is not None:
             # both gathers as one peer-memory kernel: rows land in this rank's gather areas
             with self._coll("p2p_allgather"):
@@ -630,13 +630,20 @@ class ExpertParallelMoE:
                 dist.reduce_scatter_tensor(y, y_part, group=self.group)
         return y
 
-    def _p2p_for(self, M: int, dev: torch.device) -> Optional[P2PExchange]:
-        """The peer-memory exchange for a step of M tokens per rank, built at its first use
-        (collectively: every rank calls with the same M), or None for the NCCL step."""
+    def _p2p_for(self, flat: torch.Tensor) -> Optional[P2PExchange]:
+        """The peer-memory exchange for a step over this rank's tokens ``flat`` [M, H],
+        built at its first use (collectively: every rank calls with the same M and dtype),
+        or None for the NCCL step (too many tokens, or rows whose sizes are not multiples
+        of 16 bytes, as the exchange kernels copy 16-byte words)."""
+        M, H = flat.shape
+        dev = flat.device
+        k = self.cfg.num_experts_per_token
         if self.exchange not in ("p2p", "auto") or M > MAX_DECODE_TOKENS or not _is_nccl(self.group):
             return None
+        if (M * H * flat.element_size()) % 16 or (M * 2 * k * 4) % 16:
+            return None
         if self.p2p is None and self.p2p_error is None:
-            H, k = self.pool.hidden, self.cfg.num_experts_per_token
+            H = self.pool.hidden
             try:
                 self.p2p = P2PExchange(self.group, dev, MAX_DECODE_TOKENS * H * 4, MAX_DECODE_TOKENS * 2 * k * 4,
                                        MAX_DECODE_TOKENS * H * 4)
@@ -645,10 +652,12 @@ class ExpertParallelMoE:
         return self.p2p
 
     def exchange_used(self, M: int) -> str:
-        """The exchange a call with M tokens per rank runs: "a2a", "p2p" or "gather"."""
+        """The exchange a call with M bf16 tokens per rank runs: "a2a", "p2p" or "gather"."""
         if self.uses_a2a(M):
             return "a2a"
-        return "p2p" if (self.p2p is not None and M <= MAX_DECODE_TOKENS) else "gather"
+        k = self.cfg.num_experts_per_token
+        fits = M <= MAX_DECODE_TOKENS and (M * 2 * k * 4) % 16 == 0
+        return "p2p" if (self.p2p is not None and fits) else "gather"
 
     def _replay(self, flat: torch.Tensor) -> torch.Tensor:
         """The step as a CUDA graph: captured once per (tokens, dtype) -- every rank at the
