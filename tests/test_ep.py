@@ -126,3 +126,32 @@ def test_pair_candidates_layout():
     assert slot.tolist() == [-1, 1, -1, 0, 3, -1, 4]
     assert tok.tolist() == [0, 0, 1, 1, 2, 2, 1]
     assert wt.tolist() == [0, 1, 2, 3, 4, 5, 1]
+
+
+def test_a2a_plan_properties():
+    """For random routings: every (token, destination) that needs a row gets exactly one,
+    rows are destination-major with tokens ascending, the own destination holds every
+    token, and tok_slot points back at the rows."""
+    from kimi_k3_mlx_macmini_b200.ep import a2a_plan
+    rng = np.random.default_rng(17)
+    for trial in range(20):
+        W = int(rng.choice([1, 2, 3, 4, 8]))
+        E_loc = int(rng.integers(1, 6))
+        M = int(rng.integers(1, 40))
+        k = int(rng.integers(1, min(4, W * E_loc) + 1))
+        rank = int(rng.integers(0, W))
+        idx = np.stack([rng.choice(W * E_loc, size=k, replace=False) for _ in range(M)]).astype(np.int32)
+        counts, rows, slot = a2a_plan(torch.from_numpy(idx), rank, W, E_loc)
+        need = np.zeros((M, W), bool)
+        for t in range(M):
+            need[t, idx[t] // E_loc] = True
+            need[t, rank] = True
+        assert counts == need.sum(0).tolist()
+        rows, slot = rows.numpy(), slot.numpy()
+        off = np.concatenate([[0], np.cumsum(counts)])
+        for d in range(W):
+            seg = rows[off[d]:off[d + 1]]
+            assert seg.tolist() == np.flatnonzero(need[:, d]).tolist()        # ascending tokens
+            for i, t in enumerate(seg):
+                assert slot[t, d] == off[d] + i
+        assert ((slot >= 0) == need).all()
