@@ -155,3 +155,43 @@ def test_a2a_plan_properties():
             for i, t in enumerate(seg):
                 assert slot[t, d] == off[d] + i
         assert ((slot >= 0) == need).all()
+
+
+def _leaver(rank, world, port, out_q):
+    """Rank 1 leaves before the step; rank 0's step must end with an error (the peer is
+    gone or the short process-group timeout runs out), not wait for good."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        out_q.put((rank, "left"))
+        return                                              # exits without joining the step
+    from kimi_k3_mlx_macmini_b200.ep import ep_forward
+    time.sleep(0.5)
+    x = torch.zeros((M, H))
+    t0 = time.time()
+    try:
+        ep_forward(x, lambda xt: (torch.zeros((M, K), dtype=torch.int32), torch.ones((M, K))),
+                   lambda xa, s, t, w: torch.zeros((xa.shape[0], H)), num_experts=E, with_shared=True,
+                   exchange="a2a")
+        out_q.put((rank, "no error"))
+    except Exception as exc:                                # noqa: BLE001 -- the outcome under test
+        out_q.put((rank, f"error after {time.time() - t0:.1f}s: {type(exc).__name__}"))
+
+
+def test_step_fails_fast_when_a_rank_leaves():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2].rstrip("s:")) < 30.0, res[0]
