@@ -1,10 +1,10 @@
-"""Expert-parallel MoE layer at decode (BASELINE configs[2] at 2/4/8 GPUs).
+"""Expert-parallel MoE layer (BASELINE configs[2] and [3] at 2/4/8 GPUs).
 
 One process per GPU. Rank r owns routed experts [r*E/W, (r+1)*E/W) and a copy of the
 shared expert; the router is replicated. Every rank brings M tokens. A step:
 
 1. route: each rank runs the router on its own M tokens (top-k ids and weights);
-2. dispatch: ``all_gather`` of the tokens (bf16 [W*M, H]) and of their routing (one
+2. dispatch: an all-gather of the tokens (bf16 [W*M, H]) and of their routing (one
    [M, 2k] int32 block: expert ids, then the weights' bits) -- at decode M is at most 8,
    so broadcasting every token to every rank is smaller than a counted all-to-all and
    needs no host synchronisation;
@@ -12,11 +12,14 @@ shared expert; the router is replicated. Every rank brings M tokens. A step:
    to them, plus the shared expert for its own tokens (``k3_moe_ep_local``: the pairs
    are taken from the gathered routing on the device), producing one f32 partial row per
    gathered token (zero for tokens that touch none of its experts);
-4. combine: ``reduce_scatter`` (sum) returns to each rank the total of its own M rows.
+4. combine: a reduce-scatter (sum) returns to each rank the total of its own M rows.
 
-At decode all transfers have fixed sizes, so a step captures into one CUDA graph with its
-NCCL collectives. Compared with W replicas of the whole layer, each rank streams only the
-experts its share is routed to by all W*M tokens, once.
+At decode (up to MAX_DECODE_TOKENS tokens per rank) the all-gather and the reduce-scatter
+are two kernels over NVLink peer memory by default (``P2PExchange``: IPC-mapped buffers,
+flags with bounded waits); above that, or where peer memory is unavailable, they are the
+NCCL collectives (``exchange="gather"`` forces those). All transfers have fixed sizes, so
+a step captures into one CUDA graph. Compared with W replicas of the whole layer, each
+rank streams only the experts its share is routed to by all W*M tokens, once.
 
 The counted all-to-all exchange (``exchange="a2a"``) sends a token once to each rank
 that owns one of its experts (and to its own rank, for the shared expert), not to every
